@@ -1,0 +1,327 @@
+#!/usr/bin/env python
+"""Value-and-grad throughput of Sheaf's nanoGPT training step on B200.
+
+Workload (default): the nanoGPT-style model of examples/nanoGPT/model.shf
+(6 layers, d_model 384, 6 heads, ctx 256, vocab 65), value-and-grad of the
+cross-entropy loss on shifted tokens, global batch 64 x 256 split over the
+ranks (strong scaling); lowered to StableHLO as Sheaf's JIT lowers it and run
+through libsheafb200's C ABI.  `--workload gpt2` selects the GPT-2-small
+shape (12 layers, d768, ctx 1024, vocab 50304, batch 8 per GPU, weak scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  Device time: CUDA events on the session's
+stream around K steps, max over ranks.  Inputs (weights, activations) are far
+larger than the 126 MB L2, so no flush is needed between steps.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "value-and-grad steps/s & tokens/s at 1/2/4/8 B200; % of TC/HBM roofline"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
+                   choices=["fp32", "tf32", "bf16"])
+    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "gpt2"])
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-profile", action="store_true")
+    return p.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def workload(name, world):
+    from sheaf_b200.programs import models as M
+    if name == "nanogpt":
+        c = M.NANOGPT
+        gb = c.batch
+        if gb % world:
+            raise SystemExit(f"global batch {gb} is not divisible by {world} ranks")
+        return c, gb, gb // world, "strong"
+    c = M.GPT2_SMALL
+    return c, c.batch * world, c.batch, "weak"
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (clock and throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.device), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.rows.append([x.strip() for x in ln.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for k, n in enumerate(names):
+                if len(r) > 5 + k and r[5 + k].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1400.0, "fallback"
+
+
+def cpu_baseline(c, steps=2):
+    """The oracle port (numpy f32) on a bounded sample: 2 sequences of the same model."""
+    from oracle.stablehlo_ref import evaluate, parse_module
+    from sheaf_b200.programs import models as M
+    b = 2
+    low = M.gpt_vag(c, batch=b) if c.T <= 256 else M.gpt_vag(M.GPTConfig(c.n_layer, c.n_head, c.n_embd, c.block_size,
+                                                                         c.vocab_size, 1, 256), batch=1)
+    f = parse_module(low.text)[low.qualified]
+    inp = M.gpt_inputs(c, batch=b) if c.T <= 256 else None
+    if inp is None:
+        cc = M.GPTConfig(c.n_layer, c.n_head, c.n_embd, c.block_size, c.vocab_size, 1, 256)
+        inp = M.gpt_inputs(cc, batch=1)
+        b, T = 1, 256
+    else:
+        T = c.T
+    ins = [inp[n] for n in low.arg_names]
+    evaluate(f, ins, dtype=np.float32)
+    t0 = time.time()
+    for _ in range(steps):
+        evaluate(f, ins, dtype=np.float32)
+    dt = (time.time() - t0) / steps
+    return {"value": b * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{b} sequence(s) x {T} tokens of the same model per step, numpy float32 "
+                      f"interpretation of the same StableHLO (oracle/stablehlo_ref.py), mean of {steps} steps"}
+
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return
+    from sheaf_b200.programs import models as M
+    c, gb, _, scaling = workload(args.workload, world)
+    res = cpu_baseline(c, steps=max(1, min(args.steps, 3)))
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.workload} value-and-grad", "global_batch": gb, "seq_len": c.T,
+                       "parallelism": f"dp{world}"},
+            "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's IREE llvm-cpu path cannot be built here (no Rust toolchain, no IREE); "
+                    "this times the CPU restatement of the same graphs on the host cores"}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    rank, local, world = env_rank()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from sheaf_b200 import build
+    from sheaf_b200.programs import models as M
+    from sheaf_b200.session import B200Session, nccl_unique_id
+    build.build()
+    c, gb, b, scaling = workload(args.workload, world)
+    low = M.gpt_vag(c, batch=b)
+    inp = M.gpt_inputs(c, batch=gb, seed=0)
+    shard = {"x": inp["x"][rank * b:(rank + 1) * b], "y": inp["y"][rank * b:(rank + 1) * b]}
+    nid = None
+    if world > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    sess = B200Session(device=local, precision=args.precision, rank=rank, world_size=world, nccl_id=nid,
+                       timeout_ms=300000)
+    t0 = time.time()
+    sess.load_stablehlo(low.text)
+    load_s = time.time() - t0
+    names = low.arg_names
+    bufs = [sess.buffer(shard[n] if n in shard else inp[n]) for n in names]
+    q = low.qualified
+    reduce = ["mean"] * len(low.result_types) if world > 1 else None
+
+    def step(buffers):
+        outs = sess.call_device(q, buffers, reduce)
+        return outs
+
+    def barrier():
+        sess.synchronize()
+        if dist:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        for o in step(bufs):
+            o.release()
+    barrier()
+    stream = torch.cuda.ExternalStream(sess.cuda_stream, device=torch.device("cuda", local))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            for o in step(bufs):
+                o.release()
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    barrier()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    tokens = gb * c.T
+    value = tokens / (ms_step / 1e3)
+
+    # end to end: per step, H2D of the step's tokens from pinned host memory,
+    # the call, and the loss read back to the host (as Sheaf's VAG dispatch does)
+    e2e = None
+    if not args.no_e2e:
+        px = torch.from_numpy(shard["x"]).pin_memory().numpy()
+        py = torch.from_numpy(shard["y"]).pin_memory().numpy()
+        ix, iy = names.index("x"), names.index("y")
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.time()
+        e0.record(stream)
+        for _ in range(args.steps):
+            bx, by = sess.buffer(px), sess.buffer(py)
+            bb = list(bufs)
+            bb[ix], bb[iy] = bx, by
+            outs = step(bb)
+            loss = outs[0].to_host()
+            for o in outs:
+                o.release()
+            bx.release()
+            by.release()
+        e1.record(stream)
+        e1.synchronize()
+        ems = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ems], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": tokens / (ems / args.steps / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(px.nbytes + py.nbytes) * world, "d2h_bytes_per_step": 4 * world,
+               "steps_per_s": 1e3 / (ems / args.steps), "loss": float(loss)}
+
+    # per-kernel device time (separate pass of the same steps, CUDA events per launch)
+    roof, launches, breakdown = None, None, None
+    if not args.no_profile:
+        sess.set_profiling(True)
+        for _ in range(args.steps):
+            for o in step(bufs):
+                o.release()
+        rows = sess.profile_report()
+        sess.set_profiling(False)
+        calls = max(1, rows[0]["calls"]) if rows else 1
+        launches = sum(r["launches_per_call"] for r in rows if r["function"] == q)
+        tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in ("gemm", "loop", "reduce")}
+        allms = sum(tot.values())
+        breakdown = {k: {"ms_per_step": v, "share": v / allms if allms else 0} for k, v in tot.items()}
+        hbm, tc, src = peaks()
+        gem = [r for r in rows if r["kind"] == "gemm"]
+        gflops = sum(r["flops"] for r in gem) / calls
+        gms = tot["gemm"]
+        if gem and gms > 0:
+            ach = gflops / (gms / 1e3) / 1e12
+            roof = {"bound": "tensor", "kernel": "gemm (all dot_general launches)", "achieved": ach, "peak": tc,
+                    "unit": "TFLOP/s", "frac": ach / tc, "traffic": None, "peak_source": src,
+                    "flops_per_step": gflops, "launches_per_step": len(gem), "share_of_step": gms / allms}
+    result = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": ms_step, "steps_per_s": 1e3 / ms_step,
+              "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+              "contraction": args.precision,
+              "data": "synthetic: seeded N(0,0.02) weights, uniform tokens",
+              "config": {"workload": f"{args.workload} value-and-grad (configs[2])" if args.workload == "nanogpt"
+                         else "gpt2-small value-and-grad (configs[3])",
+                         "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
+                         "global_batch": gb, "seq_len": c.T, "parallelism": f"dp{world}",
+                         "l2": "inputs and activations exceed L2; no flush"},
+              "clocks": clk.summary(), "e2e": e2e, "gpu_launches": (launches or 0) * args.steps,
+              "roofline": roof, "breakdown": breakdown, "module_load_s": load_s}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            result["cpu_baseline"] = cpu_baseline(c)
+        except Exception as ex:  # reported, not fatal
+            result["cpu_baseline"] = {"error": str(ex)[:200]}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    sess.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,168 @@
+/*
+ * sheaf_b200.h - C ABI of libsheafb200, the B200 (sm_100a) execution backend
+ * for Sheaf's JIT-compiled StableHLO graphs.
+ *
+ * The library takes the place of the IREE compile-and-run layer that Sheaf
+ * drives through its hand-written FFI (sheaf/src/runtime/iree_ffi.rs:133-275).
+ * Conventions kept from that interface:
+ *   - status objects: a NULL `sb_status*` means success; a non-NULL status is
+ *     heap-allocated and owned by the caller, who frees it with
+ *     sb_status_free (iree_status_t, iree_ffi.rs:17, 129-131);
+ *   - element type codes are IREE's (iree_ffi.rs:32-34);
+ *   - buffers are reference counted (retain/release) like
+ *     iree_hal_buffer_view_t;
+ *   - functions are called by qualified name "<module>.<function>"
+ *     (iree_runtime_session_call_by_name, iree_ffi.rs:190-195).
+ * Instead of a precompiled .vmfb, a module is loaded from the StableHLO text
+ * that Sheaf emits (sheaf/src/lowering/stablehlo/emit.rs:253-273); the library
+ * plans, fuses and compiles it for the GPU itself.
+ */
+#ifndef SHEAF_B200_H_
+#define SHEAF_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_API __attribute__((visibility("default")))
+
+typedef struct sb_status sb_status;
+typedef struct sb_session sb_session;
+typedef struct sb_buffer sb_buffer;
+
+typedef enum sb_status_code {
+  SB_STATUS_OK = 0,
+  SB_STATUS_INVALID_ARGUMENT = 3,
+  SB_STATUS_DEADLINE_EXCEEDED = 4,
+  SB_STATUS_NOT_FOUND = 5,
+  SB_STATUS_RESOURCE_EXHAUSTED = 8,
+  SB_STATUS_FAILED_PRECONDITION = 9,
+  SB_STATUS_UNIMPLEMENTED = 12,
+  SB_STATUS_INTERNAL = 13,
+  SB_STATUS_UNAVAILABLE = 14,
+} sb_status_code;
+
+/* Element types: the IREE HAL codes (iree_ffi.rs:32-34). */
+#define SB_ELEMENT_TYPE_FLOAT_32 ((0x21u << 24) | 32u)
+#define SB_ELEMENT_TYPE_BFLOAT_16 ((0x31u << 24) | 16u)
+#define SB_ELEMENT_TYPE_INT_32 ((0x11u << 24) | 32u)
+
+/* Arithmetic used for dot_general contractions.  Non-contraction ops are
+ * always computed in f32. */
+typedef enum sb_precision {
+  SB_PRECISION_FP32 = 0, /* f32 FMA on CUDA cores */
+  SB_PRECISION_TF32 = 1, /* tcgen05 kind::tf32, f32 accumulate */
+  SB_PRECISION_BF16 = 2, /* tcgen05 kind::f16 on bf16 operands, f32 accumulate */
+} sb_precision;
+
+/* How an output of a data-parallel call is combined across ranks. */
+typedef enum sb_reduce_op {
+  SB_REDUCE_NONE = 0, /* keep the local value */
+  SB_REDUCE_SUM = 1,
+  SB_REDUCE_MEAN = 2,
+} sb_reduce_op;
+
+typedef struct sb_session_options {
+  int32_t device_ordinal;       /* CUDA device used by this session */
+  int32_t precision;            /* sb_precision */
+  int32_t rank;                 /* data-parallel rank (0 when world_size == 1) */
+  int32_t world_size;           /* number of ranks; 1 = single GPU, no NCCL */
+  uint8_t nccl_unique_id[128];  /* from sb_nccl_get_unique_id on rank 0 */
+  int64_t collective_timeout_ms;/* host deadline for collectives; <= 0 = 600000 */
+  const char* kernel_cache_dir; /* compiled-kernel cache; NULL = $SHEAF_B200_CACHE or default */
+  uint32_t flags;               /* SB_SESSION_FLAG_* */
+} sb_session_options;
+
+#define SB_SESSION_FLAG_NO_CUDA_GRAPH 1u /* launch kernels one by one instead of replaying a graph */
+
+typedef struct sb_allocator_stats {
+  /* field meaning follows iree_hal_allocator_statistics_t as read by
+   * sheaf/src/interpreter/mem_profile.rs:123 */
+  uint64_t host_bytes_peak, host_bytes_allocated, host_bytes_freed;
+  uint64_t device_bytes_peak, device_bytes_allocated, device_bytes_freed;
+} sb_allocator_stats;
+
+/* --- status (iree_status_t: iree_ffi.rs:17, 129-131, 268-269) ------------ */
+SB_API sb_status_code sb_status_code_of(const sb_status* status);
+SB_API const char* sb_status_message(const sb_status* status);
+SB_API void sb_status_free(sb_status* status);
+
+/* --- session (iree_runtime_instance/session_create*: iree_ffi.rs:141-177;
+ *     IreeSession::new, sheaf/src/runtime/iree_session.rs:174) ----------- */
+SB_API void sb_session_options_initialize(sb_session_options* options);
+SB_API sb_status* sb_session_create(const sb_session_options* options, sb_session** out_session);
+SB_API void sb_session_release(sb_session* session);
+SB_API sb_status* sb_session_synchronize(sb_session* session);
+SB_API sb_status* sb_session_allocator_stats(sb_session* session, sb_allocator_stats* out_stats);
+/* The cudaStream_t all of the session's work is ordered on (for event timing
+ * and for ordering work of other CUDA users against the session). */
+SB_API void* sb_session_cuda_stream(sb_session* session);
+/* Per-step CUDA-event timing (the B200 counterpart of `--jit-profile`,
+ * sheaf/src/runtime/iree_session.rs:158-167, 813-849).  While enabled, every
+ * kernel launch of every call is bracketed by events on the session stream. */
+SB_API sb_status* sb_session_set_profiling(sb_session* session, int enable);
+/* CSV, one row per plan step with accumulated device time:
+ * function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call
+ * Synchronizes the stream.  `reset` clears the accumulators afterwards. */
+SB_API sb_status* sb_session_profile_report(sb_session* session, int reset, char* out, size_t capacity,
+                                            size_t* out_length);
+
+/* --- module loading (replaces `iree-compile` + append_bytecode_module_from_memory:
+ *     sheaf/src/runtime/jit/vag.rs:726-794, iree_ffi.rs:180-184,
+ *     IreeSession::load_vmfb, iree_session.rs:373) ------------------------ */
+SB_API sb_status* sb_session_load_stablehlo(sb_session* session, const char* text, size_t length);
+SB_API int sb_session_has_function(sb_session* session, const char* qualified_name);
+
+/* --- calls (iree_runtime_session_call_by_name: iree_ffi.rs:187-192;
+ *     IreeSession::call_device, iree_session.rs:574) ---------------------- *
+ * inputs are borrowed; each returned output carries one reference owned by the
+ * caller.  `output_reduce` (may be NULL) gives an sb_reduce_op per output for
+ * data-parallel sessions; NULL means SB_REDUCE_NONE for every output. */
+SB_API sb_status* sb_session_call(sb_session* session, const char* qualified_name,
+                                  sb_buffer* const* inputs, size_t input_count,
+                                  const int32_t* output_reduce,
+                                  sb_buffer** outputs, size_t output_capacity,
+                                  size_t* out_output_count);
+
+/* --- buffers (iree_hal_buffer_view_*: iree_ffi.rs:195-242) --------------- */
+SB_API sb_status* sb_buffer_allocate_copy(sb_session* session, size_t rank, const uint64_t* shape,
+                                          uint32_t element_type, const void* host_data,
+                                          size_t byte_length, sb_buffer** out_buffer);
+/* Wraps caller-owned device memory without copying; the caller keeps it alive. */
+SB_API sb_status* sb_buffer_wrap_device(sb_session* session, size_t rank, const uint64_t* shape,
+                                        uint32_t element_type, void* device_ptr, size_t byte_length,
+                                        sb_buffer** out_buffer);
+/* Blocking device-to-host copy (iree_hal_device_transfer_d2h, iree_ffi.rs:223-231),
+ * bounded by timeout_ms (<= 0: no bound). */
+SB_API sb_status* sb_buffer_d2h(sb_session* session, sb_buffer* buffer, void* host_data,
+                                size_t byte_length, int64_t timeout_ms);
+SB_API void sb_buffer_retain(sb_buffer* buffer);
+SB_API void sb_buffer_release(sb_buffer* buffer);
+SB_API size_t sb_buffer_rank(const sb_buffer* buffer);
+SB_API uint64_t sb_buffer_dim(const sb_buffer* buffer, size_t index);
+SB_API uint32_t sb_buffer_element_type(const sb_buffer* buffer);
+SB_API size_t sb_buffer_byte_length(const sb_buffer* buffer);
+SB_API void* sb_buffer_device_pointer(const sb_buffer* buffer);
+
+/* --- collectives ---------------------------------------------------------- */
+SB_API sb_status* sb_nccl_get_unique_id(uint8_t out_id[128]);
+
+/* --- host-only inspection (no GPU needed) --------------------------------- *
+ * Parses and plans `text`, compiles its fused kernels, and writes a one-line
+ * summary per function into `report` (NUL-terminated, truncated to capacity). */
+SB_API sb_status* sb_module_inspect(const char* text, size_t length, int32_t precision,
+                                    char* report, size_t report_capacity);
+/* Writes the generated CUDA source of one function (for diagnostics). */
+SB_API sb_status* sb_module_kernel_source(const char* text, size_t length, const char* function,
+                                          char* out, size_t capacity, size_t* out_length);
+
+/* Library version string. */
+SB_API const char* sb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SHEAF_B200_H_ */

@@ -363,10 +363,11 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
             r = v[0][sl]
         elif k == "pad":
             lo, hi, it = op.attrs["lo"], op.attrs["hi"], op.attrs["in"]
-            if any(it):
-                raise NotImplementedError("interior padding")
+            if any(l < 0 for l in lo) or any(h < 0 for h in hi):
+                raise NotImplementedError("negative padding")
             r = np.full(oshape, v[1], dtype=v[0].dtype)
-            sl = tuple(slice(l, l + s) for l, s in zip(lo, v[0].shape))
+            sl = tuple(slice(l, l + (s - 1) * (i + 1) + 1, i + 1) if s else slice(l, l)
+                       for l, s, i in zip(lo, v[0].shape, it))
             r[sl] = v[0]
         elif k == "concatenate":
             r = np.concatenate(v, axis=op.attrs["dim"])

@@ -1,0 +1,610 @@
+// Kernel text generation for fused clusters.  Each cluster node is evaluated at
+// a coordinate tuple (C integer expressions); index maps (broadcast, transpose,
+// reshape, slice, reverse, pad, concatenate, gather) rewrite the tuple, and
+// elementwise nodes combine operand values.  Values are memoized per
+// (node, coordinates) so a node shared inside one cluster is computed once.
+#include "codegen.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+namespace sb {
+
+const char* ctype_of(DType t) {
+  switch (t) {
+    case DType::F32: return "float";
+    case DType::BF16: return "float";
+    case DType::F64: return "double";
+    case DType::I32: return "int";
+    case DType::I64: return "long long";
+    case DType::I1: return "bool";
+  }
+  return "float";
+}
+
+namespace {
+
+constexpr int kDup = -2, kConst = -3, kParam = -4;
+constexpr int kThreads = 256;
+constexpr int64_t kMaxGrid = 148 * 16;
+
+std::string join(const std::vector<std::string>& v, const char* sep) {
+  std::string s;
+  for (size_t i = 0; i < v.size(); ++i) {
+    if (i) s += sep;
+    s += v[i];
+  }
+  return s;
+}
+
+std::string f32_literal(double x) {
+  float f = (float)x;
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  char buf[48];
+  std::snprintf(buf, sizeof buf, "__int_as_float(0x%08x)", u);
+  return buf;
+}
+
+std::string literal(double x, const std::string& ctype) {
+  if (ctype == "float") return f32_literal(x);
+  if (ctype == "bool") return x != 0 ? "true" : "false";
+  if (ctype == "double") {
+    char buf[48];
+    std::snprintf(buf, sizeof buf, "%.17g", x);
+    return buf;
+  }
+  return std::to_string((long long)x) + (ctype == "long long" ? "LL" : "");
+}
+
+// coordinate arithmetic helpers that keep literal zeros simple
+std::string c_mul(const std::string& c, int64_t k) {
+  if (c == "0" || k == 0) return "0";
+  if (k == 1) return c;
+  return "(" + c + ")*" + std::to_string(k);
+}
+std::string c_add(const std::string& a, const std::string& b) {
+  if (a == "0") return b;
+  if (b == "0") return a;
+  return a + "+" + b;
+}
+
+}  // namespace
+
+bool CodeGen::is_materialized_for(const Ctx& c, int v) const {
+  int cl = cluster_[v];
+  if (cl == kParam || cl == kConst) return true;
+  return cl == v && v != c.root;
+}
+
+std::string CodeGen::index_type(const Op& root, int64_t extra) const {
+  int64_t mx = std::max(root.type.numel(), extra);
+  for (auto& t : f_.value_types) mx = std::max(mx, t.numel());
+  return mx >= (int64_t(1) << 31) - 1 ? "long long" : "int";
+}
+
+CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& coords) {
+  auto it = c.leaf_index.find(v);
+  int li;
+  if (it == c.leaf_index.end()) {
+    li = (int)c.leaves.size();
+    c.leaves.push_back(v);
+    c.leaf_index[v] = li;
+  } else {
+    li = it->second;
+  }
+  const Type& t = f_.value_types[v];
+  auto st = row_major(t.shape);
+  std::string off = "0";
+  for (size_t i = 0; i < coords.size(); ++i) off = c_add(off, c_mul(coords[i], st[i]));
+  Val r{fresh(c), ctype_of(t.dtype)};
+  if (t.dtype == DType::BF16) throw std::runtime_error("bf16 buffers are not supported in fused kernels");
+  c.body << c.pad() << "const " << r.ctype << " " << r.name << " = L" << li << "[" << off << "];\n";
+  return r;
+}
+
+CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords) {
+  std::string key = std::to_string(v) + "@" + join(coords, ",");
+  for (int s = (int)c.memo.size() - 1; s >= 0; --s) {
+    auto it = c.memo[s].find(key);
+    if (it != c.memo[s].end()) return it->second;
+  }
+  Val out;
+  if (is_materialized_for(c, v)) {
+    out = leaf_load(c, v, coords);
+    c.memo.back()[key] = out;
+    return out;
+  }
+  int pi = f_.producer[v];
+  if (pi < 0) throw std::runtime_error("codegen: value without producer is not materialized");
+  const Op& op = f_.ops[pi];
+  if (!(cluster_[v] == c.root || cluster_[v] == kDup))
+    throw std::runtime_error(std::string("codegen: node outside cluster (") + opkind_name(op.kind) + ")");
+  std::string ct = ctype_of(op.type.dtype);
+  auto emit = [&](const std::string& expr) {
+    Val r{fresh(c), ct};
+    c.body << c.pad() << "const " << ct << " " << r.name << " = " << expr << ";\n";
+    return r;
+  };
+  const auto& osh = op.type.shape;
+  switch (op.kind) {
+    case OpKind::Constant:
+      out = Val{literal(op.values[0], ct), ct};
+      break;
+    case OpKind::Iota:
+      out = emit("(" + ct + ")(" + coords[op.axis] + ")");
+      break;
+    case OpKind::BroadcastInDim: {
+      const auto& ish = f_.value_types[op.operands[0]].shape;
+      std::vector<std::string> ic(ish.size());
+      for (size_t i = 0; i < ish.size(); ++i)
+        ic[i] = (ish[i] == 1 && osh[op.dims[i]] != 1) ? "0" : coords[op.dims[i]];
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
+    case OpKind::Transpose: {
+      std::vector<std::string> ic(op.dims.size());
+      for (size_t i = 0; i < op.dims.size(); ++i) ic[op.dims[i]] = coords[i];
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
+    case OpKind::Reshape: {
+      const auto& ish = f_.value_types[op.operands[0]].shape;
+      std::vector<int64_t> inz, outz;
+      std::vector<size_t> outpos;
+      for (auto d : ish) if (d != 1) inz.push_back(d);
+      for (size_t i = 0; i < osh.size(); ++i) if (osh[i] != 1) { outz.push_back(osh[i]); outpos.push_back(i); }
+      std::vector<std::string> ic(ish.size(), "0");
+      if (inz == outz) {
+        size_t k = 0;
+        for (size_t i = 0; i < ish.size(); ++i) if (ish[i] != 1) ic[i] = coords[outpos[k++]];
+      } else {
+        auto so = row_major(osh);
+        std::string lin = "0";
+        for (size_t i = 0; i < osh.size(); ++i) lin = c_add(lin, c_mul(coords[i], so[i]));
+        std::string ln = fresh(c, "lin");
+        c.body << c.pad() << "const " << c.idx << " " << ln << " = " << lin << ";\n";
+        auto si = row_major(ish);
+        for (size_t i = 0; i < ish.size(); ++i) {
+          if (ish[i] == 1) continue;
+          std::string e = si[i] == 1 ? ln : "(" + ln + "/" + std::to_string(si[i]) + ")";
+          bool first_nontrivial = true;
+          for (size_t j = 0; j < i; ++j) if (ish[j] != 1) first_nontrivial = false;
+          if (!first_nontrivial) e = "(" + e + "%" + std::to_string(ish[i]) + ")";
+          ic[i] = e;
+        }
+      }
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
+    case OpKind::Slice: {
+      std::vector<std::string> ic(coords.size());
+      for (size_t i = 0; i < coords.size(); ++i)
+        ic[i] = c_add(std::to_string(op.a0[i]) == "0" ? "0" : std::to_string(op.a0[i]), c_mul(coords[i], op.a2[i]));
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
+    case OpKind::Reverse: {
+      std::vector<std::string> ic = coords;
+      for (auto d : op.dims) ic[d] = "(" + std::to_string(osh[d] - 1) + "-(" + coords[d] + "))";
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
+    case OpKind::Pad: {
+      const auto& ish = f_.value_types[op.operands[0]].shape;
+      Val pv = eval(c, op.operands[1], {});
+      out = Val{fresh(c), ct};
+      c.body << c.pad() << ct << " " << out.name << " = " << pv.name << ";\n";
+      std::vector<std::string> conds, ic(ish.size());
+      for (size_t i = 0; i < ish.size(); ++i) {
+        int64_t step = op.a2[i] + 1;
+        std::string rel = "(" + coords[i] + "-(" + std::to_string(op.a0[i]) + "))";
+        conds.push_back(rel + ">=0");
+        conds.push_back(rel + "<" + std::to_string((ish[i] - 1) * step + 1));
+        if (step != 1) {
+          conds.push_back(rel + "%" + std::to_string(step) + "==0");
+          ic[i] = "(" + rel + "/" + std::to_string(step) + ")";
+        } else {
+          ic[i] = rel;
+        }
+      }
+      c.body << c.pad() << "if (" << (conds.empty() ? "true" : join(conds, " && ")) << ") {\n";
+      c.indent++;
+      c.memo.emplace_back();
+      Val in = eval(c, op.operands[0], ic);
+      c.body << c.pad() << out.name << " = " << in.name << ";\n";
+      c.memo.pop_back();
+      c.indent--;
+      c.body << c.pad() << "}\n";
+      break;
+    }
+    case OpKind::Concatenate: {
+      out = Val{fresh(c), ct};
+      c.body << c.pad() << ct << " " << out.name << ";\n";
+      int64_t base = 0;
+      for (size_t j = 0; j < op.operands.size(); ++j) {
+        int64_t ext = f_.value_types[op.operands[j]].shape[op.axis];
+        std::vector<std::string> ic = coords;
+        ic[op.axis] = "(" + coords[op.axis] + "-" + std::to_string(base) + ")";
+        bool last = j + 1 == op.operands.size();
+        c.body << c.pad() << (j ? "else " : "") << (last ? "{\n" : "if ((" + coords[op.axis] + ")<" + std::to_string(base + ext) + ") {\n");
+        c.indent++;
+        c.memo.emplace_back();
+        Val in = eval(c, op.operands[j], ic);
+        c.body << c.pad() << out.name << " = " << in.name << ";\n";
+        c.memo.pop_back();
+        c.indent--;
+        c.body << c.pad() << "}\n";
+        base += ext;
+      }
+      break;
+    }
+    case OpKind::Gather: {
+      const auto& tsh = f_.value_types[op.operands[0]].shape;
+      const auto& ish = f_.value_types[op.operands[1]].shape;
+      int ivd = (int)op.axis;
+      std::vector<std::string> batch;
+      for (size_t d = 0; d < osh.size(); ++d)
+        if (!std::count(op.offset_dims.begin(), op.offset_dims.end(), (int64_t)d)) batch.push_back(coords[d]);
+      std::vector<std::string> starts(tsh.size(), "0");
+      int64_t nidx = ivd < (int)ish.size() ? ish[ivd] : 1;
+      for (int64_t k = 0; k < (int64_t)op.start_index_map.size() && k < nidx; ++k) {
+        std::vector<std::string> icoord;
+        size_t b = 0;
+        for (size_t d = 0; d < ish.size(); ++d) icoord.push_back((int)d == ivd ? std::to_string(k) : batch[b++]);
+        if (ivd >= (int)ish.size()) { /* implicit trailing index dim */ }
+        Val iv = eval(c, op.operands[1], icoord);
+        int64_t od = op.start_index_map[k];
+        int64_t hi = tsh[od] - op.slice_sizes[od];
+        std::string s = fresh(c, "g");
+        c.body << c.pad() << "const " << c.idx << " " << s << " = min(max((" << c.idx << ")(" << iv.name
+               << "), (" << c.idx << ")0), (" << c.idx << ")" << hi << ");\n";
+        starts[od] = s;
+      }
+      std::vector<std::string> tc(tsh.size());
+      size_t oo = 0;
+      std::vector<std::string> offs;
+      for (auto d : op.offset_dims) offs.push_back(coords[d]);
+      for (size_t d = 0; d < tsh.size(); ++d) {
+        if (std::count(op.collapsed.begin(), op.collapsed.end(), (int64_t)d)) tc[d] = starts[d];
+        else tc[d] = c_add(starts[d], offs[oo++]);
+      }
+      out = eval(c, op.operands[0], tc);
+      break;
+    }
+    case OpKind::Select: {
+      Val p = eval(c, op.operands[0], coords);
+      Val a = eval(c, op.operands[1], coords);
+      Val b = eval(c, op.operands[2], coords);
+      out = emit("(" + p.name + " ? " + a.name + " : " + b.name + ")");
+      break;
+    }
+    case OpKind::Clamp: {
+      Val lo = eval(c, op.operands[0], f_.value_types[op.operands[0]].shape.empty() ? std::vector<std::string>{} : coords);
+      Val x = eval(c, op.operands[1], coords);
+      Val hi = eval(c, op.operands[2], f_.value_types[op.operands[2]].shape.empty() ? std::vector<std::string>{} : coords);
+      if (ct == "float") out = emit("fminf(fmaxf(" + x.name + ", " + lo.name + "), " + hi.name + ")");
+      else out = emit("min(max(" + x.name + ", " + lo.name + "), " + hi.name + ")");
+      break;
+    }
+    case OpKind::Compare: {
+      Val a = eval(c, op.operands[0], coords);
+      Val b = eval(c, op.operands[1], coords);
+      static const char* ops[] = {"==", "!=", "<", "<=", ">", ">="};
+      out = emit("(" + a.name + " " + ops[(int)op.cmp] + " " + b.name + ")");
+      break;
+    }
+    case OpKind::Convert: {
+      Val a = eval(c, op.operands[0], coords);
+      if (ct == "bool") out = emit("(" + a.name + " != 0)");
+      else if (a.ctype == "bool") out = emit("(" + a.name + " ? (" + ct + ")1 : (" + ct + ")0)");
+      else out = emit("(" + ct + ")(" + a.name + ")");
+      break;
+    }
+    default: {
+      if (is_binary_elementwise(op.kind)) {
+        Val a = eval(c, op.operands[0], coords);
+        Val b = eval(c, op.operands[1], coords);
+        const std::string& x = a.name;
+        const std::string& y = b.name;
+        bool fl = ct == "float" || ct == "double";
+        switch (op.kind) {
+          case OpKind::Add: out = emit(x + " + " + y); break;
+          case OpKind::Sub: out = emit(x + " - " + y); break;
+          case OpKind::Mul: out = emit(x + " * " + y); break;
+          case OpKind::Div: out = emit(fl ? x + " / " + y : "(" + y + " != 0 ? " + x + " / " + y + " : 0)"); break;
+          case OpKind::Pow: out = emit(fl ? "powf(" + x + ", " + y + ")" : "(" + ct + ")powf((float)" + x + ", (float)" + y + ")"); break;
+          case OpKind::Max: out = emit(fl ? "fmaxf(" + x + ", " + y + ")" : "max(" + x + ", " + y + ")"); break;
+          case OpKind::Min: out = emit(fl ? "fminf(" + x + ", " + y + ")" : "min(" + x + ", " + y + ")"); break;
+          case OpKind::Rem: out = emit(fl ? "fmodf(" + x + ", " + y + ")" : "(" + y + " != 0 ? " + x + " % " + y + " : 0)"); break;
+          case OpKind::And: out = emit(ct == "bool" ? x + " && " + y : x + " & " + y); break;
+          case OpKind::Or: out = emit(ct == "bool" ? x + " || " + y : x + " | " + y); break;
+          default: throw std::runtime_error("codegen: unhandled binary op");
+        }
+      } else if (is_unary_elementwise(op.kind)) {
+        Val a = eval(c, op.operands[0], coords);
+        const std::string& x = a.name;
+        switch (op.kind) {
+          case OpKind::Tanh: out = emit("tanhf(" + x + ")"); break;
+          case OpKind::Sqrt: out = emit("sqrtf(" + x + ")"); break;
+          case OpKind::Rsqrt: out = emit("rsqrtf(" + x + ")"); break;
+          case OpKind::Exp: out = emit("expf(" + x + ")"); break;
+          case OpKind::Log: out = emit("logf(" + x + ")"); break;
+          case OpKind::Abs: out = emit(ct == "float" ? "fabsf(" + x + ")" : "abs(" + x + ")"); break;
+          case OpKind::Neg: out = emit("-" + x); break;
+          case OpKind::Sin: out = emit("sinf(" + x + ")"); break;
+          case OpKind::Cos: out = emit("cosf(" + x + ")"); break;
+          case OpKind::Not: out = emit(ct == "bool" ? "!" + x : "~" + x); break;
+          case OpKind::Sign:
+            out = emit(ct == "float" ? "(" + x + " > 0.f ? 1.f : (" + x + " < 0.f ? -1.f : " + x + "))"
+                                     : "((" + x + " > 0) - (" + x + " < 0))");
+            break;
+          case OpKind::Floor: out = emit("floorf(" + x + ")"); break;
+          case OpKind::Ceil: out = emit("ceilf(" + x + ")"); break;
+          case OpKind::Logistic: out = emit("1.f / (1.f + expf(-" + x + "))"); break;
+          default: throw std::runtime_error("codegen: unhandled unary op");
+        }
+      } else {
+        throw std::runtime_error(std::string("codegen: cannot fuse ") + opkind_name(op.kind));
+      }
+    }
+  }
+  c.memo.back()[key] = out;
+  return out;
+}
+
+std::string CodeGen::header(const std::string& name, const Ctx& c, int extra_ptrs) const {
+  std::ostringstream h;
+  int np = (int)c.leaves.size() + 1 + extra_ptrs;
+  h << "struct __align__(8) A_" << name << " { const void* p[" << np << "]; };\n";
+  h << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << name << "(const A_" << name
+    << " a) {\n";
+  for (size_t i = 0; i < c.leaves.size(); ++i) {
+    const Type& t = f_.value_types[c.leaves[i]];
+    h << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+      << "*)a.p[" << i << "];\n";
+  }
+  return h.str();
+}
+
+void CodeGen::gen_loop(const Op& root, Step* st) {
+  const std::string start_text = src_.str();
+  struct Snip {
+    CodeGen* g; size_t start;
+    ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
+  } snip{this, start_text.size()};
+  if (root.type.numel() == 0) {
+    std::string name = "k" + std::to_string(names_.size());
+    src_ << "extern \"C\" __global__ void " << name << "(const void* p) {}\n\n";
+    names_.push_back(name);
+    st->kernel = name;
+    st->grid = 1;
+    st->block = 32;
+    return;
+  }
+  Ctx c;
+  c.root = root.result;
+  c.idx = index_type(root, 0);
+  c.memo.emplace_back();
+  const auto& sh = root.type.shape;
+  int r = (int)sh.size();
+  std::vector<std::string> coords(r);
+  c.indent = 2;
+  std::ostringstream pre;
+  if (r > 0) {
+    pre << "    " << c.idx << " r_ = i;\n";
+    for (int d = r - 1; d >= 0; --d) {
+      coords[d] = "c" + std::to_string(d);
+      if (d == 0) pre << "    const " << c.idx << " c0 = r_;\n";
+      else pre << "    const " << c.idx << " c" << d << " = r_ % " << sh[d] << "; r_ /= " << sh[d] << ";\n";
+    }
+  }
+  // The root itself is evaluated as a cluster node: force non-materialized view.
+  Val v = eval(c, root.result, coords);
+  std::string name = "k" + std::to_string(names_.size());
+  const char* ot = ctype_of(root.type.dtype);
+  int64_t n = root.type.numel();
+  src_ << header(name, c, 0);
+  src_ << "  " << ot << "* __restrict__ O = (" << ot << "*)a.p[" << c.leaves.size() << "];\n";
+  src_ << "  for (" << c.idx << " i = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; i < ("
+       << c.idx << ")" << n << "; i += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+  src_ << pre.str();
+  c.indent = 2;
+  src_ << c.body.str();
+  src_ << "    O[i] = " << v.name << ";\n  }\n}\n\n";
+  names_.push_back(name);
+  st->kernel = name;
+  st->leaves = c.leaves;
+  st->block = kThreads;
+  st->grid = std::max<int64_t>(1, std::min<int64_t>((n + kThreads - 1) / kThreads, kMaxGrid));
+  int64_t bytes = n * dtype_bytes(root.type.dtype);
+  for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
+  st->bytes_moved = bytes;
+}
+
+void CodeGen::gen_reduce(const Op& root, Step* st) {
+  const std::string start_text = src_.str();
+  struct Snip {
+    CodeGen* g; size_t start;
+    ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
+  } snip{this, start_text.size()};
+  const Type& in = f_.value_types[root.operands[0]];
+  const auto& ish = in.shape;
+  int r = (int)ish.size();
+  std::vector<int64_t> rd(root.dims.begin(), root.dims.end());
+  std::sort(rd.begin(), rd.end());
+  std::vector<int64_t> kd;  // kept dims
+  for (int d = 0; d < r; ++d) if (!std::count(rd.begin(), rd.end(), d)) kd.push_back(d);
+  int64_t R = 1, O = 1;
+  for (auto d : rd) R *= ish[d];
+  for (auto d : kd) O *= ish[d];
+  bool trailing = true;
+  for (size_t i = 0; i < rd.size(); ++i) if (rd[rd.size() - 1 - i] != r - 1 - (int64_t)i) trailing = false;
+  const char* ident = root.body == ReduceBody::Add ? "0.f"
+                      : root.body == ReduceBody::Max ? "__int_as_float(0xff800000)"
+                      : root.body == ReduceBody::Min ? "__int_as_float(0x7f800000)" : "1.f";
+  auto combine = [&](const std::string& a, const std::string& b) {
+    switch (root.body) {
+      case ReduceBody::Add: return a + " + " + b;
+      case ReduceBody::Max: return "fmaxf(" + a + ", " + b + ")";
+      case ReduceBody::Min: return "fminf(" + a + ", " + b + ")";
+      case ReduceBody::Mul: return a + " * " + b;
+    }
+    return a;
+  };
+  if (root.type.dtype != DType::F32 || in.dtype != DType::F32)
+    throw std::runtime_error("reduce: only f32 reductions are supported");
+
+  Ctx c;
+  c.root = root.result;
+  c.idx = index_type(root, 0);
+  c.memo.emplace_back();
+  std::string name = "k" + std::to_string(names_.size());
+  std::ostringstream body;  // assembled kernel body after leaves are known
+  auto out_coords = [&](std::ostringstream& os, const std::string& oi, std::vector<std::string>& oc,
+                        const std::string& ind) {
+    oc.assign(kd.size(), "0");
+    if (kd.empty()) return;
+    os << ind << c.idx << " ro_ = " << oi << ";\n";
+    for (int j = (int)kd.size() - 1; j >= 0; --j) {
+      oc[j] = "o" + std::to_string(j);
+      if (j == 0) os << ind << "const " << c.idx << " o0 = ro_;\n";
+      else os << ind << "const " << c.idx << " o" << j << " = ro_ % " << ish[kd[j]] << "; ro_ /= " << ish[kd[j]] << ";\n";
+    }
+  };
+  auto red_coords = [&](std::ostringstream& os, std::vector<std::string>& kc, const std::string& ind) {
+    kc.assign(rd.size(), "0");
+    os << ind << c.idx << " rk_ = k;\n";
+    for (int j = (int)rd.size() - 1; j >= 0; --j) {
+      kc[j] = "q" + std::to_string(j);
+      if (j == 0) os << ind << "const " << c.idx << " q0 = rk_;\n";
+      else os << ind << "const " << c.idx << " q" << j << " = rk_ % " << ish[rd[j]] << "; rk_ /= " << ish[rd[j]] << ";\n";
+    }
+  };
+  auto merged = [&](const std::vector<std::string>& oc, const std::vector<std::string>& kc) {
+    std::vector<std::string> ic(r);
+    for (size_t j = 0; j < kd.size(); ++j) ic[kd[j]] = oc[j];
+    for (size_t j = 0; j < rd.size(); ++j) ic[rd[j]] = kc[j];
+    return ic;
+  };
+
+  std::ostringstream pre, loopb, post;
+  std::vector<std::string> oc, kc;
+  int64_t splits = 1, chunk = R;
+  int mode;  // 0 warp/row, 1 block/row, 2 column
+  if (trailing && R <= 4096) mode = 0;
+  else if (trailing) mode = 1;
+  else mode = 2;
+  if (mode == 2) {
+    int64_t target = 148 * 2048;
+    if (O < target && R >= 64) {
+      splits = std::min<int64_t>((target + O - 1) / O, R / 32);
+      splits = std::max<int64_t>(splits, 1);
+      chunk = (R + splits - 1) / splits;
+      splits = (R + chunk - 1) / chunk;
+    }
+  }
+  // body of the accumulation loop (input expression at merged coords)
+  c.indent = 3;
+  red_coords(loopb, kc, "      ");
+  c.body.str("");
+  out_coords(pre, mode == 2 ? "o" : "o", oc, "    ");
+  Val v = eval(c, root.operands[0], merged(oc, kc));
+  std::string loop_code = loopb.str() + c.body.str();
+  // init value (scalar expression), evaluated in its own scope
+  c.body.str("");
+  auto saved_memo = std::move(c.memo);
+  c.memo.assign(1, {});
+  c.indent = 3;
+  Val init = eval(c, root.operands[1], {});
+  std::string init_code = c.body.str();
+  c.memo = std::move(saved_memo);
+
+  src_ << header(name, c, mode == 2 && splits > 1 ? 1 : 0);
+  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  if (mode == 0) {
+    src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+    src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; o < " << O
+         << "; o += (" << c.idx << ")gridDim.x * " << kThreads / 32 << ") {\n";
+    src_ << pre.str();
+    src_ << "    float acc = " << ident << ";\n";
+    src_ << "    for (" << c.idx << " k = lane; k < " << R << "; k += 32) {\n" << loop_code;
+    src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
+    src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+         << combine("acc", "y_") << "; }\n";
+    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+    st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
+  } else if (mode == 1) {
+    src_ << "  __shared__ float red_[" << kThreads / 32 << "];\n";
+    src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+    src_ << "  for (" << c.idx << " o = blockIdx.x; o < " << O << "; o += gridDim.x) {\n";
+    src_ << pre.str();
+    src_ << "    float acc = " << ident << ";\n";
+    src_ << "    for (" << c.idx << " k = threadIdx.x; k < " << R << "; k += " << kThreads << ") {\n" << loop_code;
+    src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
+    src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+         << combine("acc", "y_") << "; }\n";
+    src_ << "    if (lane == 0) red_[warp] = acc;\n    __syncthreads();\n";
+    src_ << "    if (warp == 0) {\n      acc = lane < " << kThreads / 32 << " ? red_[lane] : " << ident << ";\n";
+    src_ << "      for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+         << combine("acc", "y_") << "; }\n";
+    src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << combine("acc", init.name) << ";\n      }\n    }\n";
+    src_ << "    __syncthreads();\n  }\n}\n\n";
+    st->grid = std::max<int64_t>(1, std::min<int64_t>(O, kMaxGrid));
+  } else {
+    if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
+    src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
+         << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+    src_ << pre.str();
+    src_ << "    float acc = " << ident << ";\n";
+    src_ << "    const " << c.idx << " k0 = (" << c.idx << ")blockIdx.y * " << chunk << ";\n";
+    src_ << "    const " << c.idx << " k1 = min((" << c.idx << ")" << R << ", k0 + (" << c.idx << ")" << chunk << ");\n";
+    src_ << "    for (" << c.idx << " k = k0; k < k1; ++k) {\n" << loop_code;
+    src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
+    if (splits > 1) {
+      src_ << "    S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n  }\n}\n\n";
+    } else {
+      src_ << "    {\n" << init_code << "    O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+    }
+    st->grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
+    st->grid_y = splits;
+    if (splits > 1) {
+      std::string fin = name + "f";
+      src_ << "struct __align__(8) A_" << fin << " { const void* p[" << c.leaves.size() + 2 << "]; };\n";
+      src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
+           << " a) {\n";
+      for (size_t i = 0; i < c.leaves.size(); ++i) {
+        const Type& t = f_.value_types[c.leaves[i]];
+        src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+             << "*)a.p[" << i << "];\n";
+      }
+      src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+      src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
+      src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
+           << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+      src_ << "    float acc = " << ident << ";\n";
+      src_ << "    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = " << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
+      src_ << "    {\n" << init_code << "    O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+      names_.push_back(fin);
+      st->finish_kernel = fin;
+      st->finish_grid = st->grid;
+      st->splits = splits;
+      st->scratch_elems = splits * O;
+    }
+  }
+  names_.push_back(name);
+  st->kernel = name;
+  st->leaves = c.leaves;
+  st->block = kThreads;
+  int64_t bytes = O * 4;
+  for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
+  st->bytes_moved = bytes;
+}
+
+std::string CodeGen::prelude() { return "// generated by sheaf_b200 for sm_100a\n"; }
+
+std::string CodeGen::source() const { return prelude() + src_.str(); }
+
+}  // namespace sb

@@ -1,0 +1,60 @@
+// CUDA C++ generation for fused clusters (loop fusion and reduction input fusion).
+// Shapes are static, so every extent and stride is baked into the kernel text.
+#pragma once
+#include <map>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+#include "plan.h"
+
+namespace sb {
+
+class CodeGen {
+ public:
+  // cluster[v]: root value id for fused/root nodes, negative for duplicable (-2),
+  // dense constant (-3) and parameter (-4) values.
+  CodeGen(const Function& f, const std::vector<int>& cluster) : f_(f), cluster_(cluster) {}
+
+  void gen_loop(const Op& root, Step* st);
+  void gen_reduce(const Op& root, Step* st);
+  std::string source() const;
+  static std::string prelude();
+  std::vector<std::string> kernel_names() const { return names_; }
+  const std::vector<std::string>& snippets() const { return snippets_; }
+
+ private:
+  struct Val {
+    std::string name;
+    std::string ctype;
+  };
+  struct Ctx {
+    int root = -1;
+    std::vector<int> leaves;
+    std::map<int, int> leaf_index;
+    std::ostringstream body;
+    int tmp = 0;
+    int indent = 2;
+    std::string idx;  // index C type
+    std::vector<std::map<std::string, Val>> memo;
+    std::string pad() const { return std::string(indent * 2, ' '); }
+  };
+
+  Val eval(Ctx& c, int v, const std::vector<std::string>& coords);
+  Val leaf_load(Ctx& c, int v, const std::vector<std::string>& coords);
+  std::string fresh(Ctx& c, const char* p = "t") { return p + std::to_string(c.tmp++); }
+  bool is_materialized_for(const Ctx& c, int v) const;
+  std::string header(const std::string& name, const Ctx& c, int extra_ptrs) const;
+  std::string index_type(const Op& root, int64_t extra) const;
+
+  const Function& f_;
+  const std::vector<int>& cluster_;
+  std::ostringstream src_;
+  std::vector<std::string> names_;
+  std::vector<std::string> snippets_;
+};
+
+const char* ctype_of(DType t);
+
+}  // namespace sb

@@ -1,0 +1,32 @@
+// Hand-written CUDA kernels of the backend (compiled by nvcc for sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace sb {
+
+// Strided batched GEMM: C[b,m,n] = sum_k A[b,m,k] * B[b,k,n] (all f32 in memory).
+// Strides are in elements; C is written, never accumulated.
+struct GemmArgs {
+  const float* a;
+  const float* b;
+  float* c;
+  int64_t batch, M, N, K;
+  int64_t sab, sam, sak;
+  int64_t sbb, sbk, sbn;
+  int64_t scb, scm, scn;
+};
+
+// f32 FMA on CUDA cores; any strides.
+cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream);
+
+// tcgen05 tensor-core GEMM (kind::tf32 on f32 operands, or kind::f16 on bf16
+// copies when bf16 == true).  Returns cudaErrorNotSupported when the operand
+// layout is outside what the kernel handles; the caller then uses gemm_simt.
+cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream);
+// Workspace the tcgen05 path needs for this problem (bf16 operand copies).
+size_t gemm_tcgen05_workspace(const GemmArgs& g, bool bf16);
+
+}  // namespace sb

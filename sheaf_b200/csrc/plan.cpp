@@ -1,0 +1,587 @@
+// Planner: dead-code elimination, fusion clustering, GEMM operand views,
+// split-reduction sizing and the liveness-based arena layout.
+//
+// Fusion model.  Every live value is one of
+//   * materialized: a parameter, a dense constant (uploaded at load), or the
+//     root of a step (written to memory);
+//   * duplicable: splat constants, iota and the pure index maps (broadcast,
+//     reshape, transpose, slice, reverse).  These are never written to memory;
+//     each consumer cluster re-evaluates them from coordinates;
+//   * fused: an expression node evaluated inside the single cluster that
+//     consumes it.
+// A non-duplicable node joins its consumer's cluster when all of its uses (seen
+// through duplicable nodes) lie in one cluster and none of them is a GEMM
+// operand or a gather table; otherwise it becomes the root of a new cluster.
+// Reductions, dot_generals and returned values are always roots.
+#include "plan.h"
+
+#include <algorithm>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+
+#include "codegen.h"
+
+namespace sb {
+
+std::vector<int64_t> row_major(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> s(shape.size(), 1);
+  for (int i = (int)shape.size() - 2; i >= 0; --i) s[i] = s[i + 1] * shape[i + 1];
+  return s;
+}
+
+namespace {
+
+constexpr int kDup = -2;   // duplicable (never materialized)
+constexpr int kConst = -3; // dense constant buffer
+constexpr int kParam = -4;
+
+bool is_dup_kind(const Op& op) {
+  switch (op.kind) {
+    case OpKind::BroadcastInDim: case OpKind::Reshape: case OpKind::Transpose:
+    case OpKind::Slice: case OpKind::Reverse: case OpKind::Iota:
+      return true;
+    case OpKind::Constant:
+      return op.values.size() == 1;
+    default:
+      return false;
+  }
+}
+
+[[noreturn]] void fail(const Op& op, const std::string& msg) {
+  throw std::runtime_error("line " + std::to_string(op.line) + " (" + opkind_name(op.kind) + "): " + msg);
+}
+
+// numpy-style no-copy reshape of a strided view; returns false if impossible.
+bool reshape_view(const std::vector<int64_t>& oshape, const std::vector<int64_t>& ostr,
+                  const std::vector<int64_t>& nshape, std::vector<int64_t>* nstr) {
+  std::vector<int64_t> os, ost;
+  for (size_t i = 0; i < oshape.size(); ++i)
+    if (oshape[i] != 1) { os.push_back(oshape[i]); ost.push_back(ostr[i]); }
+  nstr->assign(nshape.size(), 0);
+  size_t oi = 0, ni = 0;
+  int on = (int)os.size(), nn = (int)nshape.size();
+  while (ni < (size_t)nn && oi < (size_t)on) {
+    if (nshape[ni] == 1) { (*nstr)[ni] = 0; ++ni; continue; }
+    int64_t np = nshape[ni], op = os[oi];
+    size_t nj = ni + 1, oj = oi + 1;
+    while (np != op) {
+      if (np < op) {
+        if (nj >= (size_t)nn) return false;
+        np *= nshape[nj++];
+      } else {
+        if (oj >= (size_t)on) return false;
+        op *= os[oj++];
+      }
+    }
+    for (size_t k = oi; k + 1 < oj; ++k)
+      if (ost[k] != ost[k + 1] * os[k + 1]) return false;
+    (*nstr)[nj - 1] = ost[oj - 1];
+    for (size_t k = nj - 1; k > ni; --k) (*nstr)[k - 1] = (*nstr)[k] * nshape[k];
+    ni = nj;
+    oi = oj;
+  }
+  for (; ni < (size_t)nn; ++ni) {
+    if (nshape[ni] != 1) return false;
+    (*nstr)[ni] = 0;
+  }
+  return oi == (size_t)on;
+}
+
+struct Planner {
+  const Function& f;
+  Precision prec;
+  int NV, P;
+  std::vector<char> live;
+  std::vector<std::vector<std::pair<int, int>>> consumers;  // value -> (op index, slot)
+  std::vector<int> cluster;  // root id, kDup, kConst, kParam
+  std::set<int> forced;
+  std::vector<char> returned;
+
+  Planner(const Function& fn, Precision p) : f(fn), prec(p) {
+    NV = f.num_values();
+    P = (int)f.params.size();
+  }
+
+  const Op* producer(int v) const { return f.producer[v] >= 0 ? &f.ops[f.producer[v]] : nullptr; }
+
+  void liveness() {
+    live.assign(NV, 0);
+    returned.assign(NV, 0);
+    for (int r : f.returns) { live[r] = 1; returned[r] = 1; }
+    for (int i = (int)f.ops.size() - 1; i >= 0; --i) {
+      const Op& op = f.ops[i];
+      if (!live[op.result]) continue;
+      for (int o : op.operands) live[o] = 1;
+    }
+    consumers.assign(NV, {});
+    for (int i = 0; i < (int)f.ops.size(); ++i) {
+      const Op& op = f.ops[i];
+      if (!live[op.result]) continue;
+      for (int s = 0; s < (int)op.operands.size(); ++s) consumers[op.operands[s]].push_back({i, s});
+    }
+  }
+
+  void collect(int v, std::set<int>& cs, bool& blocked, std::set<int>& seen) {
+    for (auto [oi, slot] : consumers[v]) {
+      const Op& c = f.ops[oi];
+      if (c.kind == OpKind::DotGeneral) { blocked = true; continue; }
+      if (c.kind == OpKind::Gather && slot == 0) { blocked = true; continue; }
+      int cv = c.result;
+      if (cluster[cv] == kDup) {
+        if (seen.insert(cv).second) collect(cv, cs, blocked, seen);
+      } else {
+        cs.insert(cluster[cv]);
+      }
+    }
+  }
+
+  void clusterize() {
+    cluster.assign(NV, -1);
+    for (int p = 0; p < P; ++p) cluster[p] = kParam;
+    for (int i = (int)f.ops.size() - 1; i >= 0; --i) {
+      const Op& op = f.ops[i];
+      int v = op.result;
+      if (!live[v]) continue;
+      if (op.kind == OpKind::Constant && op.values.size() != 1) { cluster[v] = kConst; continue; }
+      if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral) {
+        cluster[v] = v;
+        continue;
+      }
+      if (is_dup_kind(op)) { cluster[v] = kDup; continue; }
+      std::set<int> cs, seen;
+      bool blocked = false;
+      collect(v, cs, blocked, seen);
+      cluster[v] = (!blocked && cs.size() == 1) ? *cs.begin() : v;
+    }
+  }
+
+  bool materialized(int v) const { return cluster[v] == kParam || cluster[v] == kConst || cluster[v] == v; }
+
+  // View of v over a materialized buffer, through duplicable index maps.
+  bool view_of(int v, View* out) {
+    if (materialized(v)) {
+      out->value = v;
+      out->offset = 0;
+      out->shape = f.value_types[v].shape;
+      out->strides = row_major(out->shape);
+      return true;
+    }
+    const Op* op = producer(v);
+    if (!op || cluster[v] != kDup) return false;
+    View in;
+    switch (op->kind) {
+      case OpKind::Transpose: {
+        if (!view_of(op->operands[0], &in)) return false;
+        *out = in;
+        out->shape = op->type.shape;
+        for (size_t i = 0; i < op->dims.size(); ++i) out->strides[i] = in.strides[op->dims[i]];
+        return true;
+      }
+      case OpKind::BroadcastInDim: {
+        if (!view_of(op->operands[0], &in)) return false;
+        *out = in;
+        out->shape = op->type.shape;
+        out->strides.assign(out->shape.size(), 0);
+        for (size_t i = 0; i < op->dims.size(); ++i)
+          if (in.shape[i] == out->shape[op->dims[i]]) out->strides[op->dims[i]] = in.strides[i];
+        return true;
+      }
+      case OpKind::Slice: {
+        if (!view_of(op->operands[0], &in)) return false;
+        *out = in;
+        out->shape = op->type.shape;
+        for (size_t i = 0; i < in.shape.size(); ++i) {
+          out->offset += op->a0[i] * in.strides[i];
+          out->strides[i] = in.strides[i] * op->a2[i];
+        }
+        return true;
+      }
+      case OpKind::Reverse: {
+        if (!view_of(op->operands[0], &in)) return false;
+        *out = in;
+        for (auto d : op->dims) {
+          out->offset += (in.shape[d] - 1) * in.strides[d];
+          out->strides[d] = -in.strides[d];
+        }
+        return true;
+      }
+      case OpKind::Reshape: {
+        if (!view_of(op->operands[0], &in)) return false;
+        std::vector<int64_t> ns;
+        if (!reshape_view(in.shape, in.strides, op->type.shape, &ns)) return false;
+        *out = in;
+        out->shape = op->type.shape;
+        out->strides = ns;
+        return true;
+      }
+      default:
+        return false;
+    }
+  }
+
+  // Merges dims `ds` (in order) of a view into one extent/stride; false if not mergeable.
+  static bool merge(const View& v, const std::vector<int64_t>& ds, int64_t* ext, int64_t* str) {
+    *ext = 1;
+    *str = 0;
+    std::vector<int64_t> keep;
+    for (auto d : ds) if (v.shape[d] != 1) keep.push_back(d);
+    for (auto d : ds) *ext *= v.shape[d];
+    if (keep.empty()) { *str = 0; return true; }
+    for (size_t i = 0; i + 1 < keep.size(); ++i)
+      if (v.strides[keep[i]] != v.strides[keep[i + 1]] * v.shape[keep[i + 1]]) return false;
+    *str = v.strides[keep.back()];
+    return true;
+  }
+
+  // Tries to describe a dot_general as a strided batched GEMM.
+  bool gemm_of(const Op& op, GemmDesc* g) {
+    View a, b;
+    bool ok = true;
+    if (!view_of(op.operands[0], &a)) { forced.insert(op.operands[0]); ok = false; }
+    if (!view_of(op.operands[1], &b)) { forced.insert(op.operands[1]); ok = false; }
+    if (!ok) return false;
+    int ra = (int)a.shape.size(), rb = (int)b.shape.size();
+    std::vector<int64_t> af, bf;
+    for (int d = 0; d < ra; ++d)
+      if (!std::count(op.lb.begin(), op.lb.end(), d) && !std::count(op.lc.begin(), op.lc.end(), d)) af.push_back(d);
+    for (int d = 0; d < rb; ++d)
+      if (!std::count(op.rb.begin(), op.rb.end(), d) && !std::count(op.rc.begin(), op.rc.end(), d)) bf.push_back(d);
+    int64_t e1, e2;
+    bool good = true;
+    good &= merge(a, op.lb, &g->batch, &g->sab) && merge(b, op.rb, &e1, &g->sbb) && e1 == g->batch;
+    good &= merge(a, af, &g->M, &g->sam);
+    good &= merge(a, op.lc, &g->K, &g->sak) && merge(b, op.rc, &e2, &g->sbk) && e2 == g->K;
+    good &= merge(b, bf, &g->N, &g->sbn);
+    if (!good) {
+      // materialize both operands contiguously in their own dim order; if the
+      // dims are still not mergeable the dot needs a canonical transpose.
+      bool changed = false;
+      if (!materialized(op.operands[0])) { changed |= forced.insert(op.operands[0]).second; }
+      if (!materialized(op.operands[1])) { changed |= forced.insert(op.operands[1]).second; }
+      if (!changed) fail(op, "dot_general operand layout is not expressible as a strided batched GEMM");
+      return false;
+    }
+    g->a = a;
+    g->b = b;
+    return true;
+  }
+};
+
+// Shape/attribute consistency of every op.  Kernels index buffers from these
+// shapes, so a module that fails here never reaches the GPU.
+void verify(const Function& f) {
+  auto T = [&](int v) -> const Type& { return f.value_types[v]; };
+  for (const Op& op : f.ops) {
+    const auto& rs = op.type.shape;
+    int rr = (int)rs.size();
+    auto need = [&](bool c, const char* what) {
+      if (!c) fail(op, std::string("malformed op: ") + what);
+    };
+    for (auto d : rs) need(d >= 0, "negative extent");
+    if (is_elementwise(op.kind) && op.kind != OpKind::Select && op.kind != OpKind::Clamp) {
+      for (int o : op.operands) need(T(o).shape == rs, "operand shape differs from result shape");
+    }
+    switch (op.kind) {
+      case OpKind::Constant:
+        need(op.values.size() == 1 || (int64_t)op.values.size() == op.type.numel(), "constant payload size");
+        break;
+      case OpKind::Select:
+        need(T(op.operands[0]).shape == rs || T(op.operands[0]).shape.empty(), "select predicate shape");
+        need(T(op.operands[1]).shape == rs && T(op.operands[2]).shape == rs, "select operand shapes");
+        break;
+      case OpKind::Clamp:
+        need(T(op.operands[1]).shape == rs, "clamp operand shape");
+        for (int k : {0, 2}) need(T(op.operands[k]).shape == rs || T(op.operands[k]).shape.empty(), "clamp bound shape");
+        break;
+      case OpKind::BroadcastInDim: {
+        const auto& is = T(op.operands[0]).shape;
+        need(op.dims.size() == is.size(), "broadcast dims arity");
+        for (size_t i = 0; i < is.size(); ++i) {
+          need(op.dims[i] >= 0 && op.dims[i] < rr, "broadcast dim out of range");
+          if (op.dims[i] >= 0 && op.dims[i] < rr) need(is[i] == 1 || is[i] == rs[op.dims[i]], "broadcast extent");
+        }
+        break;
+      }
+      case OpKind::Reshape:
+        need(T(op.operands[0]).numel() == op.type.numel(), "reshape element count");
+        break;
+      case OpKind::Transpose: {
+        const auto& is = T(op.operands[0]).shape;
+        need(op.dims.size() == is.size() && (int)is.size() == rr, "transpose arity");
+        std::vector<int> seen(rr, 0);
+        for (int i = 0; i < rr; ++i) {
+          need(op.dims[i] >= 0 && op.dims[i] < rr && !seen[op.dims[i]]++, "transpose permutation");
+          need(rs[i] == is[op.dims[i]], "transpose extent");
+        }
+        break;
+      }
+      case OpKind::Iota:
+        need(op.axis >= 0 && op.axis < rr, "iota dim");
+        break;
+      case OpKind::Slice: {
+        const auto& is = T(op.operands[0]).shape;
+        need(op.a0.size() == is.size() && op.a1.size() == is.size() && op.a2.size() == is.size() &&
+                 (int)is.size() == rr, "slice arity");
+        for (int i = 0; i < rr; ++i) {
+          need(op.a2[i] >= 1 && op.a0[i] >= 0 && op.a0[i] <= op.a1[i] && op.a1[i] <= is[i], "slice bounds");
+          need(rs[i] == (op.a1[i] - op.a0[i] + op.a2[i] - 1) / op.a2[i], "slice extent");
+        }
+        break;
+      }
+      case OpKind::Pad: {
+        const auto& is = T(op.operands[0]).shape;
+        need(T(op.operands[1]).shape.empty(), "pad value must be a scalar");
+        need(op.a0.size() == is.size() && op.a1.size() == is.size() && op.a2.size() == is.size() &&
+                 (int)is.size() == rr, "pad arity");
+        for (int i = 0; i < rr; ++i) {
+          need(op.a2[i] >= 0, "negative interior padding");
+          need(rs[i] == op.a0[i] + op.a1[i] + is[i] + std::max<int64_t>(is[i] - 1, 0) * op.a2[i], "pad extent");
+        }
+        break;
+      }
+      case OpKind::Concatenate: {
+        need(op.axis >= 0 && op.axis < rr, "concatenate dim");
+        int64_t sum = 0;
+        for (int o : op.operands) {
+          const auto& is = T(o).shape;
+          need((int)is.size() == rr, "concatenate rank");
+          for (int i = 0; i < rr && (int)is.size() == rr; ++i)
+            if (i != op.axis) need(is[i] == rs[i], "concatenate extent");
+          if ((int)is.size() == rr) sum += is[op.axis];
+        }
+        need(sum == rs[op.axis], "concatenate total extent");
+        break;
+      }
+      case OpKind::Reverse:
+        need(T(op.operands[0]).shape == rs, "reverse shape");
+        for (auto d : op.dims) need(d >= 0 && d < rr, "reverse dim");
+        break;
+      case OpKind::Reduce: {
+        const auto& is = T(op.operands[0]).shape;
+        need(T(op.operands[1]).shape.empty(), "reduce init must be a scalar");
+        std::vector<int64_t> keep;
+        std::vector<int> seen(is.size(), 0);
+        for (auto d : op.dims) need(d >= 0 && d < (int64_t)is.size() && !seen[d]++, "reduce dims");
+        for (size_t i = 0; i < is.size(); ++i)
+          if (!seen[i]) keep.push_back(is[i]);
+        need(keep == rs, "reduce result shape");
+        break;
+      }
+      case OpKind::DotGeneral: {
+        const auto& a = T(op.operands[0]).shape;
+        const auto& b = T(op.operands[1]).shape;
+        need(op.lb.size() == op.rb.size() && op.lc.size() == op.rc.size(), "dot_general dim arity");
+        std::vector<int> ua(a.size(), 0), ub(b.size(), 0);
+        std::vector<int64_t> res;
+        for (size_t i = 0; i < op.lb.size(); ++i) {
+          need(op.lb[i] >= 0 && op.lb[i] < (int64_t)a.size() && op.rb[i] >= 0 && op.rb[i] < (int64_t)b.size(),
+               "dot_general batch dim");
+          need(!ua[op.lb[i]]++ && !ub[op.rb[i]]++, "dot_general repeated dim");
+          need(a[op.lb[i]] == b[op.rb[i]], "dot_general batch extent");
+          res.push_back(a[op.lb[i]]);
+        }
+        for (size_t i = 0; i < op.lc.size(); ++i) {
+          need(op.lc[i] >= 0 && op.lc[i] < (int64_t)a.size() && op.rc[i] >= 0 && op.rc[i] < (int64_t)b.size(),
+               "dot_general contracting dim");
+          need(!ua[op.lc[i]]++ && !ub[op.rc[i]]++, "dot_general repeated dim");
+          need(a[op.lc[i]] == b[op.rc[i]], "dot_general contracting extent");
+        }
+        for (size_t i = 0; i < a.size(); ++i) if (!ua[i]) res.push_back(a[i]);
+        for (size_t i = 0; i < b.size(); ++i) if (!ub[i]) res.push_back(b[i]);
+        need(res == rs, "dot_general result shape");
+        need(T(op.operands[0]).dtype == DType::F32 && T(op.operands[1]).dtype == DType::F32 &&
+                 op.type.dtype == DType::F32, "dot_general supports f32 operands");
+        break;
+      }
+      case OpKind::Gather: {
+        const auto& t = T(op.operands[0]).shape;
+        const auto& ix = T(op.operands[1]).shape;
+        need(op.slice_sizes.size() == t.size(), "gather slice_sizes arity");
+        for (size_t d = 0; d < t.size(); ++d) need(op.slice_sizes[d] >= 0 && op.slice_sizes[d] <= t[d], "gather slice size");
+        for (auto d : op.collapsed) need(d >= 0 && d < (int64_t)t.size() && op.slice_sizes[d] <= 1, "gather collapsed dim");
+        for (auto d : op.start_index_map) need(d >= 0 && d < (int64_t)t.size(), "gather start_index_map");
+        need(op.axis >= 0 && op.axis <= (int64_t)ix.size(), "gather index_vector_dim");
+        int64_t nvec = op.axis < (int64_t)ix.size() ? ix[op.axis] : 1;
+        need(nvec == (int64_t)op.start_index_map.size(), "gather index vector length");
+        int64_t batch_rank = (int64_t)ix.size() - (op.axis < (int64_t)ix.size() ? 1 : 0);
+        need((int64_t)rs.size() == batch_rank + (int64_t)op.offset_dims.size(), "gather result rank");
+        need(op.offset_dims.size() + op.collapsed.size() == t.size(), "gather offset dims");
+        for (auto d : op.offset_dims) need(d >= 0 && d < rr, "gather offset dim");
+        std::vector<int64_t> offs_sizes;
+        for (size_t d = 0; d < t.size(); ++d)
+          if (!std::count(op.collapsed.begin(), op.collapsed.end(), (int64_t)d)) offs_sizes.push_back(op.slice_sizes[d]);
+        for (size_t k = 0; k < op.offset_dims.size() && k < offs_sizes.size(); ++k)
+          if (op.offset_dims[k] >= 0 && op.offset_dims[k] < rr) need(rs[op.offset_dims[k]] == offs_sizes[k], "gather offset extent");
+        break;
+      }
+      default:
+        break;
+    }
+  }
+  for (size_t j = 0; j < f.returns.size(); ++j)
+    if (!(f.value_types[f.returns[j]] == f.results[j]))
+      throw std::runtime_error("return value " + std::to_string(j) + " does not match the declared result type");
+}
+
+// Every address a GEMM operand view touches must lie inside its base buffer.
+void check_view_bounds(const Function& f, const View& v, const char* what) {
+  int64_t lo = v.offset, hi = v.offset;
+  for (size_t i = 0; i < v.shape.size(); ++i) {
+    if (v.shape[i] == 0) return;
+    int64_t span = (v.shape[i] - 1) * v.strides[i];
+    if (span > 0) hi += span;
+    else lo += span;
+  }
+  int64_t n = f.value_types[v.value].numel();
+  if (lo < 0 || hi >= n)
+    throw std::runtime_error(std::string("internal: ") + what + " view exceeds its buffer");
+}
+
+}  // namespace
+
+Plan build_plan(const Function& f, Precision prec) {
+  verify(f);
+  Planner pl(f, prec);
+  pl.liveness();
+  for (int iter = 0;; ++iter) {
+    if (iter > 8) throw std::runtime_error("planner did not converge");
+    pl.clusterize();
+    bool retry = false;
+    for (size_t i = 0; i < f.ops.size(); ++i) {
+      const Op& op = f.ops[i];
+      if (!pl.live[op.result]) continue;
+      if (op.kind == OpKind::DotGeneral) {
+        GemmDesc g;
+        if (!pl.gemm_of(op, &g)) retry = true;
+      } else if (op.kind == OpKind::Gather) {
+        View t;
+        if (!pl.view_of(op.operands[0], &t)) {
+          pl.forced.insert(op.operands[0]);
+          retry = true;
+        }
+      }
+    }
+    if (!retry) break;
+  }
+
+  Plan plan;
+  plan.fn = &f;
+  int NV = pl.NV;
+  plan.value_offset.assign(NV, -1);
+  for (size_t i = 0; i < f.ops.size(); ++i) {
+    const Op& op = f.ops[i];
+    if (pl.live[op.result] && pl.cluster[op.result] == kConst) plan.constants.push_back(op.result);
+  }
+
+  CodeGen cg(f, pl.cluster);
+  std::map<int, int> step_of_value;
+  for (size_t i = 0; i < f.ops.size(); ++i) {
+    const Op& op = f.ops[i];
+    int v = op.result;
+    if (!pl.live[v] || pl.cluster[v] != v) continue;
+    Step st;
+    st.root = v;
+    st.elements = op.type.numel();
+    if (op.kind == OpKind::DotGeneral) {
+      st.kind = StepKind::Gemm;
+      if (!pl.gemm_of(op, &st.gemm)) fail(op, "internal: GEMM operand views changed after planning");
+      check_view_bounds(f, st.gemm.a, "GEMM lhs");
+      check_view_bounds(f, st.gemm.b, "GEMM rhs");
+      st.leaves = {st.gemm.a.value, st.gemm.b.value};
+      st.flops = 2.0 * st.gemm.batch * st.gemm.M * st.gemm.N * st.gemm.K;
+      st.bytes_moved = 4 * (st.gemm.batch * (st.gemm.M * st.gemm.K + st.gemm.K * st.gemm.N + st.gemm.M * st.gemm.N));
+    } else if (op.kind == OpKind::Reduce) {
+      st.kind = StepKind::Reduce;
+      cg.gen_reduce(op, &st);
+    } else {
+      st.kind = StepKind::Loop;
+      cg.gen_loop(op, &st);
+    }
+    step_of_value[v] = (int)plan.steps.size();
+    plan.materialized.push_back(v);
+    plan.steps.push_back(std::move(st));
+  }
+  plan.source = cg.source();
+  plan.snippets = cg.snippets();
+  plan.kernel_names = cg.kernel_names();
+
+  // Output slots: first occurrence of a step root writes the output buffer directly.
+  plan.output_step.assign(f.returns.size(), -1);
+  {
+    std::set<int> seen;
+    for (size_t j = 0; j < f.returns.size(); ++j) {
+      int v = f.returns[j];
+      if (pl.cluster[v] == v && !seen.count(v)) {
+        plan.output_step[j] = step_of_value[v];
+        seen.insert(v);
+      }
+    }
+  }
+
+  // Arena: intermediates that are not outputs, plus split-reduction scratch.
+  struct Interval { int64_t bytes; int start, end; int value; int step_scratch; };
+  std::vector<Interval> iv;
+  std::vector<int> last_use(NV, -1);
+  for (int s = 0; s < (int)plan.steps.size(); ++s)
+    for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], s);
+  for (int s = 0; s < (int)plan.steps.size(); ++s) {
+    int v = plan.steps[s].root;
+    if (pl.returned[v]) continue;
+    int64_t bytes = f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype);
+    iv.push_back({bytes, s, std::max(s, last_use[v]), v, -1});
+    if (plan.steps[s].scratch_elems)
+      iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
+  }
+  for (int s = 0; s < (int)plan.steps.size(); ++s)
+    if (plan.steps[s].scratch_elems && pl.returned[plan.steps[s].root])
+      iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
+  std::vector<int> order(iv.size());
+  for (size_t i = 0; i < iv.size(); ++i) order[i] = (int)i;
+  std::sort(order.begin(), order.end(), [&](int x, int y) { return iv[x].bytes > iv[y].bytes; });
+  std::vector<std::pair<int64_t, int>> placed;  // offset, interval
+  std::vector<int64_t> off(iv.size(), 0);
+  int64_t total = 0;
+  auto align = [](int64_t x) { return (x + 255) & ~int64_t(255); };
+  for (int k : order) {
+    std::vector<std::pair<int64_t, int64_t>> busy;
+    for (auto& [o, j] : placed)
+      if (!(iv[j].end < iv[k].start || iv[k].end < iv[j].start)) busy.push_back({o, o + align(iv[j].bytes)});
+    std::sort(busy.begin(), busy.end());
+    int64_t cand = 0;
+    for (auto& [b, e] : busy) {
+      if (cand + align(iv[k].bytes) <= b) break;
+      cand = std::max(cand, e);
+    }
+    off[k] = cand;
+    placed.push_back({cand, k});
+    total = std::max(total, cand + align(iv[k].bytes));
+  }
+  plan.scratch_offset.assign(plan.steps.size(), -1);
+  for (size_t k = 0; k < iv.size(); ++k) {
+    if (iv[k].value >= 0) plan.value_offset[iv[k].value] = off[k];
+    else plan.scratch_offset[iv[k].step_scratch] = off[k];
+  }
+  plan.arena_bytes = total;
+  return plan;
+}
+
+std::string Plan::summary() const {
+  std::ostringstream os;
+  os.precision(17);
+  int loops = 0, reds = 0, gemms = 0;
+  double flops = 0;
+  for (auto& s : steps) {
+    if (s.kind == StepKind::Loop) ++loops;
+    else if (s.kind == StepKind::Reduce) ++reds;
+    else ++gemms;
+    flops += s.flops;
+  }
+  os << "steps=" << steps.size() << " loop=" << loops << " reduce=" << reds << " gemm=" << gemms
+     << " constants=" << constants.size() << " arena_bytes=" << arena_bytes << " gemm_flops=" << flops;
+  return os.str();
+}
+
+}  // namespace sb

@@ -1,0 +1,72 @@
+// Execution plan for one StableHLO function: fusion clusters, GEMM steps,
+// memory layout of intermediates, and the CUDA source of the fused kernels.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+
+namespace sb {
+
+enum class Precision : int { FP32 = 0, TF32 = 1, BF16 = 2 };
+
+// Affine view of a materialized buffer: element (i0..in) lives at
+// base[offset + sum(i_k * strides[k])].
+struct View {
+  int value = -1;  // materialized value id (param, constant or step root)
+  int64_t offset = 0;
+  std::vector<int64_t> shape, strides;
+};
+
+// Batched GEMM C[b,m,n] = sum_k A[b,m,k] * B[b,k,n]; strides in elements.
+struct GemmDesc {
+  View a, b;
+  int64_t batch = 1, M = 1, N = 1, K = 1;
+  int64_t sab = 0, sam = 0, sak = 0;
+  int64_t sbb = 0, sbk = 0, sbn = 0;
+};
+
+struct GatherDesc {
+  int table = -1;
+};
+
+enum class StepKind : uint8_t { Loop, Reduce, Gemm };
+
+struct Step {
+  StepKind kind = StepKind::Loop;
+  int root = -1;                // value written by this step
+  std::vector<int> leaves;      // materialized values read (kernel argument order)
+  std::string kernel;           // generated kernel name (Loop / Reduce)
+  int64_t grid = 1, block = 256, grid_y = 1;
+  // split reduction: partial results go to scratch, a second kernel finishes
+  std::string finish_kernel;
+  int64_t finish_grid = 1, splits = 1, scratch_elems = 0;
+  GemmDesc gemm;
+  int64_t elements = 0;         // output elements
+  int64_t bytes_moved = 0;      // algorithmic bytes (inputs read once + output)
+  double flops = 0;
+};
+
+struct Plan {
+  const Function* fn = nullptr;
+  std::vector<Step> steps;
+  std::vector<int> materialized;      // values written by steps, in step order
+  std::vector<int> constants;         // dense (non-splat) constants uploaded at load
+  std::vector<int64_t> value_offset;  // arena byte offset per value (-1 if not in arena)
+  std::vector<int64_t> scratch_offset;  // per step, arena offset of split-reduce scratch
+  std::vector<int> output_step;       // per return slot: step that writes it (-1: copy)
+  int64_t arena_bytes = 0;
+  std::string source;                 // CUDA C++ of all generated kernels
+  std::vector<std::string> snippets;  // the same, one independent piece per step
+  std::vector<std::string> kernel_names;
+  std::string summary() const;
+};
+
+// Builds the plan.  Throws std::runtime_error with a diagnostic on failure.
+Plan build_plan(const Function& f, Precision prec);
+
+// Row-major strides of a shape.
+std::vector<int64_t> row_major(const std::vector<int64_t>& shape);
+
+}  // namespace sb

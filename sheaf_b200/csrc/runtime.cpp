@@ -1,0 +1,778 @@
+// Session, buffers, module loading and function execution behind the C ABI.
+// Role model: sheaf/src/runtime/iree_session.rs (IreeSession: session creation
+// :174, load_vmfb :373, call_device :574), buffer_convert.rs and
+// device_buffer.rs.  One CUDA stream per session; all work on a session is
+// stream-ordered, so buffers returned by a call may be consumed by the next
+// call without a host synchronization.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/sheaf_b200.h"
+#include "ir.h"
+#include "jit.h"
+#include "kernels/kernels.h"
+#include "nccl_dl.h"
+#include "plan.h"
+
+struct sb_status {
+  sb_status_code code;
+  std::string message;
+};
+
+namespace sb {
+namespace {
+
+sb_status* make_status(sb_status_code code, const std::string& msg) { return new sb_status{code, msg}; }
+
+sb_status* cuda_status(cudaError_t e, const char* what) {
+  sb_status_code code = e == cudaErrorMemoryAllocation ? SB_STATUS_RESOURCE_EXHAUSTED
+                        : e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? SB_STATUS_UNAVAILABLE
+                                                                                       : SB_STATUS_INTERNAL;
+  return make_status(code, std::string("CUDA error in ") + what + ": " + cudaGetErrorName(e) + " (" +
+                               cudaGetErrorString(e) + ")");
+}
+
+#define SB_CUDA(expr)                                   \
+  do {                                                  \
+    cudaError_t e_ = (expr);                            \
+    if (e_ != cudaSuccess) return cuda_status(e_, #expr); \
+  } while (0)
+
+bool etype_to_dtype(uint32_t et, DType* out) {
+  switch (et) {
+    case SB_ELEMENT_TYPE_FLOAT_32: *out = DType::F32; return true;
+    case SB_ELEMENT_TYPE_BFLOAT_16: *out = DType::BF16; return true;
+    case SB_ELEMENT_TYPE_INT_32: *out = DType::I32; return true;
+  }
+  return false;
+}
+
+uint32_t dtype_to_etype(DType t) {
+  switch (t) {
+    case DType::F32: return SB_ELEMENT_TYPE_FLOAT_32;
+    case DType::BF16: return SB_ELEMENT_TYPE_BFLOAT_16;
+    case DType::I32: return SB_ELEMENT_TYPE_INT_32;
+    default: return 0;
+  }
+}
+
+struct Device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  std::atomic<uint64_t> allocated{0}, freed{0}, live{0}, peak{0};
+  void note_alloc(size_t n) {
+    allocated += n;
+    uint64_t l = (live += n);
+    uint64_t p = peak.load();
+    while (l > p && !peak.compare_exchange_weak(p, l)) {}
+  }
+  void note_free(size_t n) {
+    freed += n;
+    live -= n;
+  }
+  ~Device() {
+    if (stream) {
+      cudaSetDevice(ordinal);
+      cudaStreamSynchronize(stream);
+      cudaStreamDestroy(stream);
+    }
+  }
+};
+
+}  // namespace
+}  // namespace sb
+
+struct sb_buffer {
+  std::atomic<int> refs{1};
+  std::shared_ptr<sb::Device> dev;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  bool owned = false;
+  sb::Type type;
+};
+
+namespace sb {
+namespace {
+
+sb_buffer* new_device_buffer(const std::shared_ptr<Device>& dev, const Type& t, sb_status** st) {
+  auto* b = new sb_buffer();
+  b->dev = dev;
+  b->type = t;
+  b->bytes = (size_t)t.numel() * dtype_bytes(t.dtype);
+  b->owned = true;
+  if (b->bytes) {
+    cudaError_t e = cudaMallocAsync(&b->ptr, b->bytes, dev->stream);
+    if (e != cudaSuccess) {
+      *st = cuda_status(e, "cudaMallocAsync");
+      delete b;
+      return nullptr;
+    }
+    dev->note_alloc(b->bytes);
+  }
+  return b;
+}
+
+struct LoadedFunction {
+  std::string qname;
+  const Function* fn = nullptr;
+  Plan plan;
+  std::vector<double> prof_ms;
+  std::vector<uint64_t> prof_n;
+  std::vector<cudaKernel_t> kern, fin;
+  std::map<int, void*> const_ptr;
+  void* arena = nullptr;
+  size_t arena_cap = 0;
+  void* ws = nullptr;
+  size_t ws_cap = 0;
+  uint64_t calls = 0;
+};
+
+struct LoadedModule {
+  std::unique_ptr<Module> mod;
+  std::vector<cudaLibrary_t> libs;
+  std::vector<std::unique_ptr<LoadedFunction>> fns;
+};
+
+struct Nccl {
+  ncclComm_t comm = nullptr;
+  bool aborted = false;
+};
+
+}  // namespace
+}  // namespace sb
+
+struct sb_session {
+  sb_session_options opts;
+  std::shared_ptr<sb::Device> dev;
+  std::mutex mu;
+  std::vector<std::unique_ptr<sb::LoadedModule>> modules;
+  std::map<std::string, sb::LoadedFunction*> by_name;
+  std::string cache_dir;
+  sb::Nccl nccl;
+  // per-step CUDA-event timing (sb_session_set_profiling)
+  bool profiling = false;
+  struct Pending {
+    sb::LoadedFunction* fn;
+    int step;
+    cudaEvent_t a, b;
+  };
+  std::vector<Pending> pending;
+  std::vector<cudaEvent_t> free_events;
+  cudaEvent_t event() {
+    if (!free_events.empty()) {
+      cudaEvent_t e = free_events.back();
+      free_events.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+
+namespace sb {
+namespace {
+
+int64_t deadline_ms(const sb_session* s) {
+  return s->opts.collective_timeout_ms > 0 ? s->opts.collective_timeout_ms : 600000;
+}
+
+// Waits for all work on the session stream with a host deadline.  When NCCL is
+// active and the deadline passes, the communicator is aborted so the pending
+// collective kernels return, and DEADLINE_EXCEEDED is reported.
+sb_status* wait_stream(sb_session* s, int64_t timeout_ms) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(s->dev->stream);
+    if (e == cudaSuccess) return nullptr;
+    if (e != cudaErrorNotReady) return cuda_status(e, "cudaStreamQuery");
+    if (s->nccl.comm) {
+      ncclResult_t ae = ncclSuccess;
+      nccl_api().async_error(s->nccl.comm, &ae);
+      if (ae != ncclSuccess && ae != ncclInProgress) {
+        nccl_api().comm_abort(s->nccl.comm);
+        s->nccl.comm = nullptr;
+        s->nccl.aborted = true;
+        return make_status(SB_STATUS_INTERNAL, std::string("NCCL error: ") + nccl_api().error_string(ae));
+      }
+    }
+    auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (timeout_ms > 0 && el > timeout_ms) {
+      if (s->nccl.comm) {
+        nccl_api().comm_abort(s->nccl.comm);
+        s->nccl.comm = nullptr;
+        s->nccl.aborted = true;
+      }
+      return make_status(SB_STATUS_DEADLINE_EXCEEDED,
+                         "device work did not finish within " + std::to_string(timeout_ms) + " ms");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+sb_status* load_module(sb_session* s, const std::string& text) {
+  std::string err;
+  auto mod = parse_module(text, &err);
+  if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
+  auto lm = std::make_unique<LoadedModule>();
+  std::vector<std::string> snippets;
+  Precision prec = (Precision)s->opts.precision;
+  for (auto& f : mod->funcs) {
+    auto lf = std::make_unique<LoadedFunction>();
+    lf->fn = &f;
+    lf->qname = mod->name.empty() ? f.name : mod->name + "." + f.name;
+    try {
+      lf->plan = build_plan(f, prec);
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_UNIMPLEMENTED, "planning @" + f.name + ": " + e.what());
+    }
+    for (auto& sn : lf->plan.snippets) snippets.push_back(sn);
+    lm->fns.push_back(std::move(lf));
+  }
+  // Kernel names are per function (k0, k1, ...): prefix them per function.
+  // (build_plan names kernels from 0 for each function, so compile per function.)
+  std::map<std::string, cudaKernel_t> kernels;
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  for (size_t fi = 0; fi < lm->fns.size(); ++fi) {
+    auto& lf = lm->fns[fi];
+    std::vector<CubinChunk> chunks = split_source(lf->plan.snippets, std::string("// function ") + lf->qname + "\n", 16);
+    try {
+      if (!lf->plan.snippets.empty()) compile_chunks(chunks, s->cache_dir);
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_INTERNAL, "kernel compilation for @" + lf->fn->name + " failed: " + e.what());
+    }
+    std::vector<cudaLibrary_t> libs;
+    if (!lf->plan.snippets.empty()) {
+      for (auto& ch : chunks) {
+        cudaLibrary_t lib;
+        SB_CUDA(cudaLibraryLoadData(&lib, ch.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+        libs.push_back(lib);
+        lm->libs.push_back(lib);
+      }
+    }
+    auto find = [&](const std::string& name, cudaKernel_t* k) -> bool {
+      for (auto lib : libs)
+        if (cudaLibraryGetKernel(k, lib, name.c_str()) == cudaSuccess) return true;
+      cudaGetLastError();
+      return false;
+    };
+    for (auto& st : lf->plan.steps) {
+      cudaKernel_t k = nullptr, fk = nullptr;
+      if (!st.kernel.empty() && !find(st.kernel, &k))
+        return make_status(SB_STATUS_INTERNAL, "generated kernel " + st.kernel + " not found");
+      if (!st.finish_kernel.empty() && !find(st.finish_kernel, &fk))
+        return make_status(SB_STATUS_INTERNAL, "generated kernel " + st.finish_kernel + " not found");
+      lf->kern.push_back(k);
+      lf->fin.push_back(fk);
+    }
+    // dense constants
+    for (int v : lf->plan.constants) {
+      const Op& op = lf->fn->ops[lf->fn->producer[v]];
+      size_t n = (size_t)op.type.numel();
+      std::vector<uint8_t> host(n * dtype_bytes(op.type.dtype));
+      for (size_t i = 0; i < n; ++i) {
+        double x = op.values[i];
+        switch (op.type.dtype) {
+          case DType::F32: { float f = (float)x; std::memcpy(&host[i * 4], &f, 4); break; }
+          case DType::I32: { int32_t q = (int32_t)x; std::memcpy(&host[i * 4], &q, 4); break; }
+          case DType::I1: host[i] = x != 0; break;
+          default: return make_status(SB_STATUS_UNIMPLEMENTED, "constant element type");
+        }
+      }
+      void* p = nullptr;
+      SB_CUDA(cudaMalloc(&p, std::max<size_t>(host.size(), 4)));
+      SB_CUDA(cudaMemcpy(p, host.data(), host.size(), cudaMemcpyHostToDevice));
+      lf->const_ptr[v] = p;
+    }
+    if (lf->plan.arena_bytes) {
+      SB_CUDA(cudaMalloc(&lf->arena, (size_t)lf->plan.arena_bytes));
+      lf->arena_cap = (size_t)lf->plan.arena_bytes;
+    }
+  }
+  lm->mod = std::move(mod);
+  for (auto& lf : lm->fns) {
+    s->by_name[lf->qname] = lf.get();
+    if (!s->by_name.count(lf->fn->name)) s->by_name[lf->fn->name] = lf.get();
+  }
+  s->modules.push_back(std::move(lm));
+  return nullptr;
+}
+
+sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs, int64_t gx, int64_t gy,
+                            int64_t block, cudaStream_t stream) {
+  void* args[1] = {(void*)ptrs.data()};
+  dim3 grid((unsigned)gx, (unsigned)gy, 1);
+  SB_CUDA(cudaLaunchKernel((const void*)k, grid, dim3((unsigned)block), args, 0, stream));
+  return nullptr;
+}
+
+sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin,
+                        const int32_t* reduce, sb_buffer** out, size_t cap, size_t* nout) {
+  const Function& f = *lf->fn;
+  if (nin != f.params.size())
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "@" + f.name + " expects " + std::to_string(f.params.size()) +
+                                                       " inputs, got " + std::to_string(nin));
+  for (size_t i = 0; i < nin; ++i) {
+    if (!in[i]) return make_status(SB_STATUS_INVALID_ARGUMENT, "input " + std::to_string(i) + " is NULL");
+    if (!(in[i]->type.shape == f.params[i].shape))
+      return make_status(SB_STATUS_INVALID_ARGUMENT, "shape mismatch for input " + std::to_string(i) + ": got " +
+                                                         in[i]->type.str() + ", expected " + f.params[i].str());
+    if (in[i]->type.dtype != f.params[i].dtype)
+      return make_status(SB_STATUS_INVALID_ARGUMENT, "element type mismatch for input " + std::to_string(i));
+  }
+  if (cap < f.returns.size())
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "output capacity " + std::to_string(cap) + " < " +
+                                                       std::to_string(f.returns.size()));
+  cudaStream_t stream = s->dev->stream;
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  const Plan& plan = lf->plan;
+  // outputs
+  std::vector<sb_buffer*> outs(f.returns.size(), nullptr);
+  auto cleanup = [&]() {
+    for (auto* b : outs) if (b) sb_buffer_release(b);
+  };
+  for (size_t j = 0; j < f.returns.size(); ++j) {
+    sb_status* st = nullptr;
+    outs[j] = new_device_buffer(s->dev, f.value_types[f.returns[j]], &st);
+    if (!outs[j]) { cleanup(); return st; }
+  }
+  std::vector<void*> ptr(f.num_values(), nullptr);
+  for (size_t i = 0; i < nin; ++i) ptr[i] = in[i]->ptr;
+  for (auto& [v, p] : lf->const_ptr) ptr[v] = p;
+  for (size_t j = 0; j < f.returns.size(); ++j)
+    if (plan.output_step[j] >= 0) ptr[f.returns[j]] = outs[j]->ptr;
+  for (int v : plan.materialized)
+    if (!ptr[v] && plan.value_offset[v] >= 0) ptr[v] = (char*)lf->arena + plan.value_offset[v];
+
+  std::vector<const void*> args;
+  for (size_t si = 0; si < plan.steps.size(); ++si) {
+    const Step& st = plan.steps[si];
+    if (!ptr[st.root] && st.elements) { cleanup(); return make_status(SB_STATUS_INTERNAL, "unplaced value"); }
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    if (s->profiling) {
+      ev_a = s->event();
+      ev_b = s->event();
+      cudaEventRecord(ev_a, stream);
+      s->pending.push_back({lf, (int)si, ev_a, ev_b});
+    }
+    struct EndEvent {
+      cudaEvent_t e;
+      cudaStream_t s;
+      ~EndEvent() { if (e) cudaEventRecord(e, s); }
+    } end_event{ev_b, stream};
+    if (st.kind == StepKind::Gemm) {
+      const GemmDesc& g = st.gemm;
+      GemmArgs a;
+      a.a = (const float*)ptr[g.a.value] + g.a.offset;
+      a.b = (const float*)ptr[g.b.value] + g.b.offset;
+      a.c = (float*)ptr[st.root];
+      a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
+      a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
+      a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
+      a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
+      cudaError_t e = cudaErrorNotSupported;
+      if (s->opts.precision != SB_PRECISION_FP32) {
+        bool bf16 = s->opts.precision == SB_PRECISION_BF16;
+        size_t need = gemm_tcgen05_workspace(a, bf16);
+        if (need > lf->ws_cap) {
+          if (lf->ws) cudaFreeAsync(lf->ws, stream);
+          if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+          else lf->ws_cap = need;
+        }
+        e = gemm_tcgen05(a, bf16, lf->ws, lf->ws_cap, stream);
+      }
+      if (e == cudaErrorNotSupported) e = gemm_simt(a, stream);
+      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
+      continue;
+    }
+    args.clear();
+    for (int l : st.leaves) args.push_back(ptr[l]);
+    args.push_back(ptr[st.root]);
+    void* scratch = nullptr;
+    if (st.splits > 1) {
+      scratch = (char*)lf->arena + plan.scratch_offset[si];
+      args.push_back(scratch);
+    }
+    sb_status* e = launch_generated(lf->kern[si], args, st.grid, st.grid_y, st.block, stream);
+    if (e) { cleanup(); return e; }
+    if (st.splits > 1) {
+      e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
+      if (e) { cleanup(); return e; }
+    }
+  }
+  // outputs not written by a step: copies
+  for (size_t j = 0; j < f.returns.size(); ++j) {
+    if (plan.output_step[j] >= 0) continue;
+    int v = f.returns[j];
+    if (outs[j]->bytes && ptr[v])
+      SB_CUDA(cudaMemcpyAsync(outs[j]->ptr, ptr[v], outs[j]->bytes, cudaMemcpyDeviceToDevice, stream));
+  }
+  // data-parallel combine of outputs
+  if (s->opts.world_size > 1 && reduce) {
+    if (!s->nccl.comm) { cleanup(); return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available"); }
+    const NcclApi& api = nccl_api();
+    api.group_start();
+    for (size_t j = 0; j < f.returns.size(); ++j) {
+      if (reduce[j] == SB_REDUCE_NONE) continue;
+      if (outs[j]->type.dtype != DType::F32) { api.group_end(); cleanup(); return make_status(SB_STATUS_UNIMPLEMENTED, "reduce of non-f32 output"); }
+      ncclRedOp_t op = reduce[j] == SB_REDUCE_MEAN ? ncclAvg : ncclSum;
+      ncclResult_t r = api.all_reduce(outs[j]->ptr, outs[j]->ptr, (size_t)outs[j]->type.numel(), ncclFloat32, op,
+                                      s->nccl.comm, stream);
+      if (r != ncclSuccess && r != ncclInProgress) { api.group_end(); cleanup(); return make_status(SB_STATUS_INTERNAL, std::string("ncclAllReduce: ") + api.error_string(r)); }
+    }
+    ncclResult_t r = api.group_end();
+    if (r != ncclSuccess && r != ncclInProgress) { cleanup(); return make_status(SB_STATUS_INTERNAL, std::string("ncclGroupEnd: ") + api.error_string(r)); }
+  }
+  SB_CUDA(cudaGetLastError());
+  for (size_t j = 0; j < f.returns.size(); ++j) out[j] = outs[j];
+  *nout = f.returns.size();
+  lf->calls++;
+  return nullptr;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" {
+
+sb_status_code sb_status_code_of(const sb_status* s) { return s ? s->code : SB_STATUS_OK; }
+const char* sb_status_message(const sb_status* s) { return s ? s->message.c_str() : "OK"; }
+void sb_status_free(sb_status* s) { delete s; }
+const char* sb_version(void) { return "sheaf_b200 0.1 (sm_100a)"; }
+
+void sb_session_options_initialize(sb_session_options* o) {
+  std::memset(o, 0, sizeof *o);
+  o->device_ordinal = 0;
+  o->precision = SB_PRECISION_TF32;
+  o->rank = 0;
+  o->world_size = 1;
+  o->collective_timeout_ms = 600000;
+}
+
+sb_status* sb_session_create(const sb_session_options* o, sb_session** out) {
+  if (!o || !out) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  *out = nullptr;
+  if (o->precision < 0 || o->precision > 2) return make_status(SB_STATUS_INVALID_ARGUMENT, "bad precision");
+  if (o->world_size < 1 || o->rank < 0 || o->rank >= o->world_size)
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "bad rank / world_size");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return make_status(SB_STATUS_UNAVAILABLE, "no CUDA device is available");
+  }
+  if (o->device_ordinal < 0 || o->device_ordinal >= n)
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "device ordinal out of range");
+  cudaDeviceProp prop;
+  SB_CUDA(cudaGetDeviceProperties(&prop, o->device_ordinal));
+  if (prop.major != 10)
+    return make_status(SB_STATUS_UNAVAILABLE, std::string("device ") + prop.name +
+                                                  " is not an sm_100 (B200-class) GPU; this library is built for sm_100a only");
+  auto s = std::make_unique<sb_session>();
+  s->opts = *o;
+  s->cache_dir = o->kernel_cache_dir ? o->kernel_cache_dir : default_cache_dir();
+  s->dev = std::make_shared<Device>();
+  s->dev->ordinal = o->device_ordinal;
+  SB_CUDA(cudaSetDevice(o->device_ordinal));
+  SB_CUDA(cudaStreamCreateWithFlags(&s->dev->stream, cudaStreamNonBlocking));
+  if (o->world_size > 1) {
+    const NcclApi& api = nccl_api();
+    if (!api.ok) return make_status(SB_STATUS_UNAVAILABLE, api.error);
+    ncclUniqueId id;
+    std::memcpy(&id, o->nccl_unique_id, sizeof id);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = api.init_rank_config(&comm, o->world_size, id, o->rank, &cfg);
+    auto t0 = std::chrono::steady_clock::now();
+    int64_t tmo = o->collective_timeout_ms > 0 ? o->collective_timeout_ms : 600000;
+    while (r == ncclInProgress || r == ncclSuccess) {
+      ncclResult_t ae = ncclInProgress;
+      if (comm) api.async_error(comm, &ae);
+      if (ae == ncclSuccess) break;
+      if (ae != ncclInProgress) { r = ae; break; }
+      if (std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count() > tmo) {
+        if (comm) api.comm_abort(comm);
+        return make_status(SB_STATUS_DEADLINE_EXCEEDED, "NCCL communicator initialization timed out");
+      }
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (r != ncclSuccess && r != ncclInProgress) {
+      if (comm) api.comm_abort(comm);
+      return make_status(SB_STATUS_UNAVAILABLE, std::string("ncclCommInitRankConfig: ") + api.error_string(r));
+    }
+    s->nccl.comm = comm;
+  }
+  *out = s.release();
+  return nullptr;
+}
+
+void sb_session_release(sb_session* s) {
+  if (!s) return;
+  cudaSetDevice(s->dev->ordinal);
+  cudaStreamSynchronize(s->dev->stream);
+  if (s->nccl.comm) nccl_api().comm_destroy(s->nccl.comm);
+  for (auto& m : s->modules) {
+    for (auto& lf : m->fns) {
+      for (auto& [v, p] : lf->const_ptr) cudaFree(p);
+      if (lf->arena) cudaFree(lf->arena);
+      if (lf->ws) cudaFree(lf->ws);
+    }
+    for (auto lib : m->libs) cudaLibraryUnload(lib);
+  }
+  delete s;
+}
+
+sb_status* sb_session_synchronize(sb_session* s) {
+  if (!s) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL session");
+  std::lock_guard<std::mutex> g(s->mu);
+  return wait_stream(s, s->opts.world_size > 1 ? deadline_ms(s) : 0);
+}
+
+sb_status* sb_session_allocator_stats(sb_session* s, sb_allocator_stats* o) {
+  if (!s || !o) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  std::memset(o, 0, sizeof *o);
+  o->device_bytes_peak = s->dev->peak;
+  o->device_bytes_allocated = s->dev->allocated;
+  o->device_bytes_freed = s->dev->freed;
+  return nullptr;
+}
+
+void* sb_session_cuda_stream(sb_session* s) { return s ? (void*)s->dev->stream : nullptr; }
+
+sb_status* sb_session_set_profiling(sb_session* s, int enable) {
+  if (!s) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL session");
+  std::lock_guard<std::mutex> g(s->mu);
+  s->profiling = enable != 0;
+  return nullptr;
+}
+
+sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t cap, size_t* out_len) {
+  if (!s) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL session");
+  std::lock_guard<std::mutex> g(s->mu);
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  SB_CUDA(cudaStreamSynchronize(s->dev->stream));
+  for (auto& p : s->pending) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, p.a, p.b);
+    auto* lf = p.fn;
+    if (lf->prof_ms.size() != lf->plan.steps.size()) {
+      lf->prof_ms.assign(lf->plan.steps.size(), 0.0);
+      lf->prof_n.assign(lf->plan.steps.size(), 0);
+    }
+    lf->prof_ms[p.step] += ms;
+    lf->prof_n[p.step] += 1;
+    s->free_events.push_back(p.a);
+    s->free_events.push_back(p.b);
+  }
+  s->pending.clear();
+  std::ostringstream os;
+  os.precision(9);
+  os << "function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call\n";
+  static const char* kinds[] = {"loop", "reduce", "gemm"};
+  for (auto& m : s->modules)
+    for (auto& lf : m->fns) {
+      if (lf->prof_ms.empty()) continue;
+      for (size_t i = 0; i < lf->plan.steps.size(); ++i) {
+        const Step& st = lf->plan.steps[i];
+        if (!lf->prof_n[i]) continue;
+        os << lf->qname << "," << i << "," << kinds[(int)st.kind] << ","
+           << (st.kind == StepKind::Gemm ? "gemm" : st.kernel) << "," << lf->prof_n[i] << "," << lf->prof_ms[i]
+           << "," << st.elements << "," << st.bytes_moved << "," << st.flops << "," << (st.splits > 1 ? 2 : 1)
+           << "\n";
+      }
+      if (reset) {
+        std::fill(lf->prof_ms.begin(), lf->prof_ms.end(), 0.0);
+        std::fill(lf->prof_n.begin(), lf->prof_n.end(), 0);
+      }
+    }
+  std::string r = os.str();
+  if (out_len) *out_len = r.size();
+  if (out && cap) {
+    size_t n = std::min(cap - 1, r.size());
+    std::memcpy(out, r.data(), n);
+    out[n] = 0;
+  }
+  return nullptr;
+}
+
+sb_status* sb_session_load_stablehlo(sb_session* s, const char* text, size_t len) {
+  if (!s || !text) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  std::lock_guard<std::mutex> g(s->mu);
+  return load_module(s, std::string(text, len));
+}
+
+int sb_session_has_function(sb_session* s, const char* name) {
+  if (!s || !name) return 0;
+  std::lock_guard<std::mutex> g(s->mu);
+  return s->by_name.count(name) ? 1 : 0;
+}
+
+sb_status* sb_session_call(sb_session* s, const char* name, sb_buffer* const* inputs, size_t n_in,
+                           const int32_t* reduce, sb_buffer** outputs, size_t cap, size_t* n_out) {
+  if (!s || !name || (n_in && !inputs) || !n_out) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  *n_out = 0;
+  std::lock_guard<std::mutex> g(s->mu);
+  if (s->nccl.aborted) return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator was aborted");
+  auto it = s->by_name.find(name);
+  if (it == s->by_name.end()) return make_status(SB_STATUS_NOT_FOUND, std::string("function not found: ") + name);
+  return run_function(s, it->second, inputs, n_in, reduce, outputs, cap, n_out);
+}
+
+sb_status* sb_buffer_allocate_copy(sb_session* s, size_t rank, const uint64_t* shape, uint32_t et,
+                                   const void* host, size_t bytes, sb_buffer** out) {
+  if (!s || !out || (rank && !shape)) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  Type t;
+  if (!etype_to_dtype(et, &t.dtype)) return make_status(SB_STATUS_INVALID_ARGUMENT, "unsupported element type");
+  for (size_t i = 0; i < rank; ++i) t.shape.push_back((int64_t)shape[i]);
+  size_t need = (size_t)t.numel() * dtype_bytes(t.dtype);
+  if (bytes != need)
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "byte length " + std::to_string(bytes) + " does not match shape (" +
+                                                       std::to_string(need) + ")");
+  if (need && !host) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL host data");
+  std::lock_guard<std::mutex> g(s->mu);
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  sb_status* st = nullptr;
+  sb_buffer* b = new_device_buffer(s->dev, t, &st);
+  if (!b) return st;
+  if (need) {
+    cudaError_t e = cudaMemcpyAsync(b->ptr, host, need, cudaMemcpyHostToDevice, s->dev->stream);
+    if (e != cudaSuccess) {
+      sb_buffer_release(b);
+      return cuda_status(e, "cudaMemcpyAsync(H2D)");
+    }
+  }
+  *out = b;
+  return nullptr;
+}
+
+sb_status* sb_buffer_wrap_device(sb_session* s, size_t rank, const uint64_t* shape, uint32_t et, void* dptr,
+                                 size_t bytes, sb_buffer** out) {
+  if (!s || !out || (rank && !shape)) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  Type t;
+  if (!etype_to_dtype(et, &t.dtype)) return make_status(SB_STATUS_INVALID_ARGUMENT, "unsupported element type");
+  for (size_t i = 0; i < rank; ++i) t.shape.push_back((int64_t)shape[i]);
+  if (bytes != (size_t)t.numel() * dtype_bytes(t.dtype))
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "byte length does not match shape");
+  auto* b = new sb_buffer();
+  b->type = t;
+  b->bytes = bytes;
+  b->ptr = dptr;
+  b->owned = false;
+  *out = b;
+  return nullptr;
+}
+
+sb_status* sb_buffer_d2h(sb_session* s, sb_buffer* b, void* host, size_t bytes, int64_t timeout_ms) {
+  if (!s || !b || (bytes && !host)) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  if (bytes != b->bytes) return make_status(SB_STATUS_INVALID_ARGUMENT, "byte length does not match buffer");
+  std::lock_guard<std::mutex> g(s->mu);
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  if (bytes) SB_CUDA(cudaMemcpyAsync(host, b->ptr, bytes, cudaMemcpyDeviceToHost, s->dev->stream));
+  int64_t tmo = timeout_ms;
+  if (s->opts.world_size > 1 && tmo <= 0) tmo = deadline_ms(s);
+  return wait_stream(s, tmo);
+}
+
+void sb_buffer_retain(sb_buffer* b) {
+  if (b) b->refs.fetch_add(1);
+}
+
+void sb_buffer_release(sb_buffer* b) {
+  if (!b) return;
+  if (b->refs.fetch_sub(1) != 1) return;
+  if (b->owned && b->ptr && b->dev) {
+    cudaSetDevice(b->dev->ordinal);
+    cudaFreeAsync(b->ptr, b->dev->stream);
+    b->dev->note_free(b->bytes);
+  }
+  delete b;
+}
+
+size_t sb_buffer_rank(const sb_buffer* b) { return b ? b->type.shape.size() : 0; }
+uint64_t sb_buffer_dim(const sb_buffer* b, size_t i) {
+  return (b && i < b->type.shape.size()) ? (uint64_t)b->type.shape[i] : 0;
+}
+uint32_t sb_buffer_element_type(const sb_buffer* b) { return b ? dtype_to_etype(b->type.dtype) : 0; }
+size_t sb_buffer_byte_length(const sb_buffer* b) { return b ? b->bytes : 0; }
+void* sb_buffer_device_pointer(const sb_buffer* b) { return b ? b->ptr : nullptr; }
+
+sb_status* sb_nccl_get_unique_id(uint8_t out[128]) {
+  if (!out) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return make_status(SB_STATUS_UNAVAILABLE, api.error);
+  ncclUniqueId id;
+  ncclResult_t r = api.get_unique_id(&id);
+  if (r != ncclSuccess) return make_status(SB_STATUS_UNAVAILABLE, std::string("ncclGetUniqueId: ") + api.error_string(r));
+  std::memcpy(out, &id, 128);
+  return nullptr;
+}
+
+sb_status* sb_module_inspect(const char* text, size_t len, int32_t precision, char* report, size_t cap) {
+  if (!text) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  std::string err;
+  auto mod = parse_module(std::string(text, len), &err);
+  if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
+  std::ostringstream os;
+  for (auto& f : mod->funcs) {
+    Plan p;
+    try {
+      p = build_plan(f, (Precision)precision);
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_UNIMPLEMENTED, "planning @" + f.name + ": " + e.what());
+    }
+    std::vector<CubinChunk> chunks = split_source(p.snippets, "// inspect\n", 16);
+    try {
+      if (!p.snippets.empty()) compile_chunks(chunks, default_cache_dir());
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_INTERNAL, "kernel compilation for @" + f.name + " failed: " + e.what());
+    }
+    size_t cubin = 0;
+    for (auto& c : chunks) cubin += c.cubin.size();
+    os << f.name << ": ops=" << f.ops.size() << " " << p.summary() << " cubin_bytes=" << cubin << "\n";
+  }
+  std::string r = os.str();
+  if (report && cap) {
+    size_t n = std::min(cap - 1, r.size());
+    std::memcpy(report, r.data(), n);
+    report[n] = 0;
+  }
+  return nullptr;
+}
+
+sb_status* sb_module_kernel_source(const char* text, size_t len, const char* fn, char* out, size_t cap,
+                                   size_t* out_len) {
+  if (!text || !fn) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  std::string err;
+  auto mod = parse_module(std::string(text, len), &err);
+  if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
+  const Function* f = mod->find(fn);
+  if (!f) return make_status(SB_STATUS_NOT_FOUND, std::string("function not found: ") + fn);
+  Plan p;
+  try {
+    p = build_plan(*f, Precision::TF32);
+  } catch (const std::exception& e) {
+    return make_status(SB_STATUS_UNIMPLEMENTED, e.what());
+  }
+  if (out_len) *out_len = p.source.size();
+  if (out && cap) {
+    size_t n = std::min(cap - 1, p.source.size());
+    std::memcpy(out, p.source.data(), n);
+    out[n] = 0;
+  }
+  return nullptr;
+}
+
+}  // extern "C"
