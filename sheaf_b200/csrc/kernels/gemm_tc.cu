@@ -1,11 +1,358 @@
-// Placeholder for the tcgen05 path: declines every problem so callers use the
-// CUDA-core kernel.
+// tcgen05 tensor-core GEMM for sm_100a: C[b] = A[b] @ B[b] with f32 operands in
+// global memory read by the tensor cores as TF32 (kind::tf32), f32 accumulation
+// in TMEM.
+//
+// One 128 x BN output tile per CTA, 192 threads:
+//   warp 0      TMA producer (one elected lane): 128B-swizzled tiles of A and B
+//               into a STAGES-deep shared-memory ring, completion via mbarrier
+//               transaction bytes;
+//   warp 1      MMA issuer (one lane): 4 x tcgen05.mma (K = 8 each) per 32-wide
+//               K tile into a 128 x BN f32 accumulator in TMEM; tcgen05.commit
+//               frees ring slots and finally signals the epilogue;
+//   warps 2..5  epilogue: tcgen05.ld 32x32b from the four TMEM lane quadrants,
+//               predicated stores to C.
+// Operands may be K-major or MN-major (the transpose bits of the instruction
+// descriptor), so x @ W^T, G @ W and X^T @ G all run without transposing copies.
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records an
+// error code, stops issuing work, frees its TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "kernels.h"
 
 namespace sb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;                       // f32 elements = 128 bytes: one swizzle row
+constexpr int kThreads = 192;
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false when the CTA is aborting or the wait expired
+// (then the abort flag is raised and the error recorded).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0 = now_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > kTimeoutNs) {
+      *abort_flag = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                         bool is3d) {
+  if (is3d) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+  }
+}
+
+// Shared-memory matrix descriptor, 128B swizzle (sm_100 format, version 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int BYTES = 1024 /*alignment slack*/ + STAGES * STAGE + 256;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
+                      int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
+                      int* err) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(accf + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, bz = blockIdx.z;
+  const int ktiles = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
+        if (kt >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) break;
+        if (*abort_flag) break;
+        mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
+        uint8_t* a = sA + s * S::A_BYTES;
+        uint8_t* b = sB + s * S::B_BYTES;
+        if (!a_mn) {
+          tma_load(a, &tmA, &full[s], kt * BK, m0, bz, a3d);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BM / 32; ++j) tma_load(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, bz, a3d);
+        }
+        if (!b_mn) {
+          tma_load(b, &tmB, &full[s], kt * BK, n0, bz, b3d);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) tma_load(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, bz, b3d);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // kind::tf32 instruction descriptor: D f32, A/B tf32, transpose bits, N>>3, M>>4
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      bool ok = true;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
+        fence_after();
+        const uint32_t a = smem_u32(sA + s * S::A_BYTES);
+        const uint32_t b = smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 1024) : smem_desc(a + kk * 32, 16, 1024);
+          const uint64_t bd = b_mn ? smem_desc(b + kk * 1024, BK * 128, 1024) : smem_desc(b + kk * 32, 16, 1024);
+          mma_tf32(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      if (ok) mma_commit(accf);
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quadrant = warp % 4
+    const int quad = warp & 3;
+    const int row = m0 + quad * 32 + lane;
+    if (mbar_wait(accf, 0, abort_flag, err, 3)) {
+      fence_after();
+      float* crow = C + (long long)bz * scb + (long long)row * ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
+        if (row < M) {
+          const int col0 = n0 + c;
+          if (col0 + 16 <= N && (ldc & 3) == 0 && (((uintptr_t)(crow + col0)) & 15) == 0) {
+            float4* dst = (float4*)(crow + col0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col0 + j < N) crow[col0 + j] = v[j];
+          }
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 2-D or 3-D f32 map: inner (contiguous) extent d0, outer d1, batch d2.
+bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+              uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, is3d ? 3 : 2, (void*)base, dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  const int64_t lda = a_mn ? g.sak : g.sam;
+  const int64_t ldb = b_mn ? g.sbk : g.sbn;
+  const bool a3d = g.batch > 1 && g.sab != 0, b3d = g.batch > 1 && g.sbb != 0;
+  // A: K-major dims {K, M}, box {32, 128}; M-major dims {M, K}, box {32, 32}
+  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d)
+                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d);
+  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d)
+                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d));
+  if (!ok) return cudaErrorNotSupported;
+  using S = Smem<BN, STAGES>;
+  auto kern = gemm_tf32_tcgen05<BN, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM), (unsigned)g.batch);
+  kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, err);
+  return cudaGetLastError();
+}
+
+int* error_word() {
+  static int* p = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) cudaMemset(p, 0, sizeof(int));
+    else p = nullptr;
+  });
+  return p;
+}
+
+}  // namespace
 
 size_t gemm_tcgen05_workspace(const GemmArgs&, bool) { return 0; }
 
-cudaError_t gemm_tcgen05(const GemmArgs&, bool, void*, size_t, cudaStream_t) { return cudaErrorNotSupported; }
+cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void*, size_t, cudaStream_t stream) {
+  if (bf16) return cudaErrorNotSupported;
+  if (g.M < 64 || g.N < 32 || g.K < 32 || g.batch < 1 || g.batch > 65535) return cudaErrorNotSupported;
+  if (g.M > (1ll << 30) || g.N > (1ll << 30) || g.K > (1ll << 30)) return cudaErrorNotSupported;
+  if (g.scn != 1 || g.scm < g.N) return cudaErrorNotSupported;
+  bool a_mn, b_mn;
+  if (g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) a_mn = false;
+  else if (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M) a_mn = true;
+  else return cudaErrorNotSupported;
+  if (g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) b_mn = false;
+  else if (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N) b_mn = true;
+  else return cudaErrorNotSupported;
+  if ((((uintptr_t)g.a) & 15) || (((uintptr_t)g.b) & 15)) return cudaErrorNotSupported;
+  if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return cudaErrorNotSupported;
+  int* err = error_word();
+  if (!err) return cudaErrorNotSupported;
+  if (g.N <= 64) return launch<64, 6>(g, a_mn, b_mn, err, stream);
+  return launch<128, 4>(g, a_mn, b_mn, err, stream);
+}
+
+int gemm_tcgen05_error() {
+  int* p = error_word();
+  int v = 0;
+  if (p) cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost);
+  return v;
+}
 
 }  // namespace sb

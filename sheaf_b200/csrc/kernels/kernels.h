@@ -28,5 +28,8 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void* workspace, size_t w
                          cudaStream_t stream);
 // Workspace the tcgen05 path needs for this problem (bf16 operand copies).
 size_t gemm_tcgen05_workspace(const GemmArgs& g, bool bf16);
+// Non-zero when a tcgen05 GEMM gave up on a bounded wait (1: ring slot,
+// 2: operand tiles, 3: accumulator).  Reads a device word (synchronizing).
+int gemm_tcgen05_error();
 
 }  // namespace sb

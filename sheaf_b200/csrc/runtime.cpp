@@ -159,6 +159,7 @@ struct sb_session {
   std::map<std::string, sb::LoadedFunction*> by_name;
   std::string cache_dir;
   sb::Nccl nccl;
+  bool used_tc = false;  // a tcgen05 GEMM ran on this session
   // per-step CUDA-event timing (sb_session_set_profiling)
   bool profiling = false;
   struct Pending {
@@ -194,7 +195,15 @@ sb_status* wait_stream(sb_session* s, int64_t timeout_ms) {
   auto t0 = std::chrono::steady_clock::now();
   for (;;) {
     cudaError_t e = cudaStreamQuery(s->dev->stream);
-    if (e == cudaSuccess) return nullptr;
+    if (e == cudaSuccess) {
+      if (s->used_tc) {
+        int code = gemm_tcgen05_error();
+        if (code)
+          return make_status(SB_STATUS_INTERNAL, "tensor-core GEMM gave up on a bounded wait (code " +
+                                                     std::to_string(code) + "); results are invalid");
+      }
+      return nullptr;
+    }
     if (e != cudaErrorNotReady) return cuda_status(e, "cudaStreamQuery");
     if (s->nccl.comm) {
       ncclResult_t ae = ncclSuccess;
@@ -261,9 +270,10 @@ sb_status* load_module(sb_session* s, const std::string& text) {
       }
     }
     auto find = [&](const std::string& name, cudaKernel_t* k) -> bool {
-      for (auto lib : libs)
+      for (auto lib : libs) {
         if (cudaLibraryGetKernel(k, lib, name.c_str()) == cudaSuccess) return true;
-      cudaGetLastError();
+        cudaGetLastError();  // a miss in one chunk is expected; do not leave it sticky
+      }
       return false;
     };
     for (auto& st : lf->plan.steps) {
@@ -390,6 +400,7 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
           else lf->ws_cap = need;
         }
         e = gemm_tcgen05(a, bf16, lf->ws, lf->ws_cap, stream);
+        if (e == cudaSuccess) s->used_tc = true;
       }
       if (e == cudaErrorNotSupported) e = gemm_simt(a, stream);
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
