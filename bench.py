@@ -276,6 +276,13 @@ def run_ours(args):
                 o.release()
         rows = sess.profile_report()
         sess.set_profiling(False)
+        dump = os.environ.get("SHEAF_B200_PROFILE_CSV")
+        if dump and rank == 0:
+            with open(dump, "w") as fh:
+                fh.write("step,kind,kernel,calls,total_ms,elements,bytes,flops\n")
+                for r in rows:
+                    fh.write(f"{r['step']},{r['kind']},{r['kernel']},{r['calls']},{r['total_ms']:.6f},"
+                             f"{r['elements']},{r['bytes']},{r['flops']}\n")
         calls = max(1, rows[0]["calls"]) if rows else 1
         launches = sum(r["launches_per_call"] for r in rows if r["function"] == q)
         tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in ("gemm", "loop", "reduce")}

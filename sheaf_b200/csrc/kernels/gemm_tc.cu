@@ -90,14 +90,16 @@ __device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint
   }
 }
 
-// Shared-memory matrix descriptor, 128B swizzle (sm_100 format, version 1).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor (sm_100 format, version 1).  layout 2 =
+// SWIZZLE_128B (K-major tiles); layout 1 = SWIZZLE_128B with 32-byte atoms,
+// the only MN-major layout the tf32 MMA accepts.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);
   d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  d |= (uint64_t)layout << 61;
   return d;
 }
 
@@ -218,8 +220,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 1024) : smem_desc(a + kk * 32, 16, 1024);
-          const uint64_t bd = b_mn ? smem_desc(b + kk * 1024, BK * 128, 1024) : smem_desc(b + kk * 32, 16, 1024);
+          // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
+          // k-th MMA starts 32 B further along the row.  MN-major: 128 B (32 M/N
+          // values) by BK rows per chunk, chunks BK*128 B apart (LBO), 4-row
+          // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
+          const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
+          const uint64_t bd = b_mn ? smem_desc(b + kk * 1024, BK * 128, 512, 1) : smem_desc(b + kk * 32, 16, 1024, 2);
           mma_tf32(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
         }
         mma_commit(&empty[s]);
@@ -275,7 +281,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D or 3-D f32 map: inner (contiguous) extent d0, outer d1, batch d2.
 bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
-              uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d) {
+              uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d, bool mn_major) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {d0, d1, d2};
@@ -283,7 +289,9 @@ bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint6
   cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, is3d ? 3 : 2, (void*)base, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -295,10 +303,10 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   const int64_t ldb = b_mn ? g.sbk : g.sbn;
   const bool a3d = g.batch > 1 && g.sab != 0, b3d = g.batch > 1 && g.sbb != 0;
   // A: K-major dims {K, M}, box {32, 128}; M-major dims {M, K}, box {32, 32}
-  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d)
-                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d);
-  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d)
-                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d));
+  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
+                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false);
+  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
+                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false));
   if (!ok) return cudaErrorNotSupported;
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tf32_tcgen05<BN, STAGES>;

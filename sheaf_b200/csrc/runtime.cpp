@@ -763,6 +763,42 @@ sb_status* sb_module_inspect(const char* text, size_t len, int32_t precision, ch
   return nullptr;
 }
 
+sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, int32_t precision, char* out,
+                                 size_t cap, size_t* out_len) {
+  if (!text || !fn) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  std::string err;
+  auto mod = parse_module(std::string(text, len), &err);
+  if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
+  const Function* f = mod->find(fn);
+  if (!f) return make_status(SB_STATUS_NOT_FOUND, std::string("function not found: ") + fn);
+  Plan p;
+  try {
+    p = build_plan(*f, (Precision)precision);
+  } catch (const std::exception& e) {
+    return make_status(SB_STATUS_UNIMPLEMENTED, e.what());
+  }
+  std::ostringstream os;
+  os.precision(17);
+  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
+  static const char* kinds[] = {"loop", "reduce", "gemm"};
+  for (size_t i = 0; i < p.steps.size(); ++i) {
+    const Step& st = p.steps[i];
+    const GemmDesc& g = st.gemm;
+    os << i << "," << kinds[(int)st.kind] << "," << (st.kind == StepKind::Gemm ? "gemm" : st.kernel) << ","
+       << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
+       << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
+       << g.sbn << "\n";
+  }
+  std::string r = os.str();
+  if (out_len) *out_len = r.size();
+  if (out && cap) {
+    size_t n = std::min(cap - 1, r.size());
+    std::memcpy(out, r.data(), n);
+    out[n] = 0;
+  }
+  return nullptr;
+}
+
 sb_status* sb_module_kernel_source(const char* text, size_t len, const char* fn, char* out, size_t cap,
                                    size_t* out_len) {
   if (!text || !fn) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");

@@ -86,6 +86,8 @@ SIGNATURES = {
     "sb_module_inspect": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_char_p, ctypes.c_size_t]),
     "sb_module_kernel_source": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_char_p,
                                      ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "sb_module_plan_steps": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_int32,
+                                  ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     "sb_version": (ctypes.c_char_p, []),
 }
 
@@ -128,6 +130,27 @@ def inspect_module(text: str, precision: str = "tf32") -> str:
     raw = text.encode()
     _check(library().sb_module_inspect(raw, len(raw), PRECISIONS[precision], out, len(out)))
     return out.value.decode()
+
+
+def plan_steps(text: str, function: str, precision: str = "tf32") -> List[dict]:
+    """The execution plan of one function (host only): one dict per step."""
+    raw = text.encode()
+    n = ctypes.c_size_t(0)
+    _check(library().sb_module_plan_steps(raw, len(raw), function.encode(), PRECISIONS[precision], None, 0,
+                                          ctypes.byref(n)))
+    out = ctypes.create_string_buffer(n.value + 1)
+    _check(library().sb_module_plan_steps(raw, len(raw), function.encode(), PRECISIONS[precision], out, len(out),
+                                          ctypes.byref(n)))
+    lines = out.value.decode().strip().splitlines()
+    keys = lines[0].split(",")
+    rows = []
+    for ln in lines[1:]:
+        r = dict(zip(keys, ln.split(",")))
+        for k in keys:
+            if k not in ("kind", "kernel"):
+                r[k] = float(r[k]) if k == "flops" else int(r[k])
+        rows.append(r)
+    return rows
 
 
 def kernel_source(text: str, function: str) -> str:
