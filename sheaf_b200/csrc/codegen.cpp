@@ -413,7 +413,7 @@ void CodeGen::gen_loop(const Op& root, Step* st) {
   src_ << pre.str();
   c.indent = 2;
   src_ << c.body.str();
-  src_ << "    O[i] = " << v.name << ";\n  }\n}\n\n";
+  src_ << "    O[i] = " << store(root, v.name) << ";\n  }\n}\n\n";
   names_.push_back(name);
   st->kernel = name;
   st->leaves = c.leaves;
@@ -534,7 +534,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
     src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
-    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
   } else if (mode == 1) {
     src_ << "  __shared__ float red_[" << kThreads / 32 << "];\n";
@@ -550,7 +550,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "    if (warp == 0) {\n      acc = lane < " << kThreads / 32 << " ? red_[lane] : " << ident << ";\n";
     src_ << "      for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
-    src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << combine("acc", init.name) << ";\n      }\n    }\n";
+    src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name)) << ";\n      }\n    }\n";
     src_ << "    __syncthreads();\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>(O, kMaxGrid));
   } else {
@@ -566,7 +566,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     if (splits > 1) {
       src_ << "    S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n  }\n}\n\n";
     } else {
-      src_ << "    {\n" << init_code << "    O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
     }
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
     st->grid_y = splits;
@@ -586,7 +586,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
            << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
       src_ << "    float acc = " << ident << ";\n";
       src_ << "    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = " << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
-      src_ << "    {\n" << init_code << "    O[o] = " << combine("acc", init.name) << ";\n    }\n  }\n}\n\n";
+      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
       names_.push_back(fin);
       st->finish_kernel = fin;
       st->finish_grid = st->grid;
@@ -603,7 +603,21 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
   st->bytes_moved = bytes;
 }
 
-std::string CodeGen::prelude() { return "// generated by sheaf_b200 for sm_100a\n"; }
+std::string CodeGen::prelude() {
+  return "// generated by sheaf_b200 for sm_100a\n"
+         "__device__ __forceinline__ float sb_rna_tf32(float x) {\n"
+         "  unsigned u;\n"
+         "  asm(\"cvt.rna.tf32.f32 %0, %1;\" : \"=r\"(u) : \"f\"(x));\n"
+         "  return __uint_as_float(u);\n"
+         "}\n";
+}
+
+std::string CodeGen::store(const Op& root, const std::string& expr) const {
+  if (root.type.dtype == DType::F32 &&
+      std::find(round_roots_.begin(), round_roots_.end(), root.result) != round_roots_.end())
+    return "sb_rna_tf32(" + expr + ")";
+  return expr;
+}
 
 std::string CodeGen::source() const { return prelude() + src_.str(); }
 

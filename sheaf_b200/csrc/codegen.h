@@ -16,6 +16,9 @@ class CodeGen {
   // cluster[v]: root value id for fused/root nodes, negative for duplicable (-2),
   // dense constant (-3) and parameter (-4) values.
   CodeGen(const Function& f, const std::vector<int>& cluster) : f_(f), cluster_(cluster) {}
+  // Roots whose stored values are rounded to nearest TF32 (they feed tf32 GEMMs;
+  // the tensor cores would otherwise truncate them).
+  void set_round_roots(const std::vector<int>& roots) { round_roots_ = roots; }
 
   void gen_loop(const Op& root, Step* st);
   void gen_reduce(const Op& root, Step* st);
@@ -51,8 +54,11 @@ class CodeGen {
   const Function& f_;
   const std::vector<int>& cluster_;
   std::ostringstream src_;
+  std::string store(const Op& root, const std::string& expr) const;
+
   std::vector<std::string> names_;
   std::vector<std::string> snippets_;
+  std::vector<int> round_roots_;
 };
 
 const char* ctype_of(DType t);

@@ -144,7 +144,7 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                       int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
-                      int* err) {
+                      int round_out, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -243,6 +243,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN; c += 16) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
+        if (round_out) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            uint32_t u;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(v[j]));
+            v[j] = __uint_as_float(u);
+          }
+        }
         if (row < M) {
           const int col0 = n0 + c;
           if (col0 + 16 <= N && (ldc & 3) == 0 && (((uintptr_t)(crow + col0)) & 15) == 0) {
@@ -318,7 +326,7 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   }
   dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM), (unsigned)g.batch);
   kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, err);
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, err);
   return cudaGetLastError();
 }
 

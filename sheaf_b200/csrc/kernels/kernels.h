@@ -16,7 +16,11 @@ struct GemmArgs {
   int64_t sab, sam, sak;
   int64_t sbb, sbk, sbn;
   int64_t scb, scm, scn;
+  int round_out = 0;  // tcgen05 path: store C rounded to nearest TF32
 };
+
+// dst[i] = src[i] rounded to nearest TF32 (cvt.rna), n elements.
+cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream);
 
 // f32 FMA on CUDA cores; any strides.
 cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream);

@@ -1,0 +1,41 @@
+// Small hand-written helper kernels.
+#include "kernels.h"
+
+namespace sb {
+namespace {
+
+__device__ __forceinline__ float rna_tf32(float x) {
+  uint32_t u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+  return __uint_as_float(u);
+}
+
+// Streaming copy with rounding: n4 float4 groups (when both pointers are
+// 16-byte aligned), then a scalar tail.
+__global__ void __launch_bounds__(256) round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                         int64_t n, int64_t n4) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = s4[i];
+    d4[i] = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = rna_tf32(src[i]);
+}
+
+}  // namespace
+
+cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const bool aligned = ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0;
+  const int64_t n4 = aligned ? n / 4 : 0;
+  int64_t blocks = ((aligned ? n4 : n) + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  round_tf32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, dst, n, n4);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

@@ -37,6 +37,7 @@ namespace {
 constexpr int kDup = -2;   // duplicable (never materialized)
 constexpr int kConst = -3; // dense constant buffer
 constexpr int kParam = -4;
+constexpr int kAbsorbed = -5;  // batched dot_general folded into the GEMM of its batch reduction
 
 bool is_dup_kind(const Op& op) {
   switch (op.kind) {
@@ -122,6 +123,62 @@ struct Planner {
       if (!live[op.result]) continue;
       for (int s = 0; s < (int)op.operands.size(); ++s) consumers[op.operands[s]].push_back({i, s});
     }
+    find_batch_reduced_dots();
+  }
+
+  // reduce(add, init 0) over a batch dimension of a dot_general that has no
+  // other use: sum_b A_b @ B_b is one GEMM whose contraction also runs over b.
+  // This is how weight gradients of 3-D activations arrive
+  // (transpose(x) @ adj, then sum_to_shape over the batch).
+  std::map<int, int> fused_dot;  // reduce result -> dot op index
+  void find_batch_reduced_dots() {
+    for (int i = 0; i < (int)f.ops.size(); ++i) {
+      const Op& r = f.ops[i];
+      if (!live[r.result] || r.kind != OpKind::Reduce || r.body != ReduceBody::Add || r.dims.size() != 1) continue;
+      int x = r.operands[0];
+      const Op* d = producer(x);
+      if (!d || d->kind != OpKind::DotGeneral || returned[x] || consumers[x].size() != 1) continue;
+      const Op* init = producer(r.operands[1]);
+      if (!init || init->kind != OpKind::Constant || init->values.size() != 1 || init->values[0] != 0.0) continue;
+      if (r.dims[0] >= (int64_t)d->lb.size()) continue;
+      fused_dot[r.result] = f.producer[x];
+    }
+  }
+
+  // The dot_general a GEMM step computes: the op itself, or for a fused batch
+  // reduction the absorbed dot with the reduced batch dim moved into the
+  // contraction (outermost, so it merges with the contracting dims).
+  Op gemm_op(const Op& op) const {
+    auto it = fused_dot.find(op.result);
+    if (it == fused_dot.end()) return op;
+    Op d = f.ops[it->second];
+    size_t bd = (size_t)op.dims[0];
+    int64_t l = d.lb[bd], r = d.rb[bd];
+    d.lb.erase(d.lb.begin() + bd);
+    d.rb.erase(d.rb.begin() + bd);
+    d.lc.insert(d.lc.begin(), l);
+    d.rc.insert(d.rc.begin(), r);
+    d.type = op.type;
+    d.result = op.result;
+    return d;
+  }
+  // True when every use of v (seen through index maps) is a GEMM operand.
+  bool only_gemm_consumers(int v) const {
+    if (returned[v]) return false;
+    for (auto [oi, slot] : consumers[v]) {
+      const Op& c = f.ops[oi];
+      if (c.kind == OpKind::DotGeneral) continue;
+      if (cluster[c.result] == kDup && !returned[c.result]) {
+        if (!only_gemm_consumers(c.result)) return false;
+        continue;
+      }
+      return false;
+    }
+    return !consumers[v].empty();
+  }
+  bool is_gemm_root(const Op& op) const {
+    if (op.kind == OpKind::DotGeneral) return cluster.empty() || cluster[op.result] != kAbsorbed;
+    return op.kind == OpKind::Reduce && fused_dot.count(op.result);
   }
 
   void collect(int v, std::set<int>& cs, bool& blocked, std::set<int>& seen) {
@@ -146,6 +203,9 @@ struct Planner {
       int v = op.result;
       if (!live[v]) continue;
       if (op.kind == OpKind::Constant && op.values.size() != 1) { cluster[v] = kConst; continue; }
+      bool absorbed = false;
+      for (auto& [rv, di] : fused_dot) if (di == i) absorbed = true;
+      if (absorbed) { cluster[v] = kAbsorbed; continue; }
       if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral) {
         cluster[v] = v;
         continue;
@@ -237,11 +297,26 @@ struct Planner {
   }
 
   // Tries to describe a dot_general as a strided batched GEMM.
-  bool gemm_of(const Op& op, GemmDesc* g) {
+  // Materializes the deepest value of an index-map chain that has no strided
+  // view, so the maps above it (e.g. a transpose feeding a GEMM) stay views.
+  void force_for_view(int v) {
+    const Op* op = producer(v);
+    if (op && cluster[v] == kDup && op->kind != OpKind::Iota && op->kind != OpKind::Constant) {
+      View in;
+      if (!view_of(op->operands[0], &in)) {
+        force_for_view(op->operands[0]);
+        return;
+      }
+    }
+    forced.insert(v);
+  }
+
+  bool gemm_of(const Op& root, GemmDesc* g) {
+    const Op op = gemm_op(root);
     View a, b;
     bool ok = true;
-    if (!view_of(op.operands[0], &a)) { forced.insert(op.operands[0]); ok = false; }
-    if (!view_of(op.operands[1], &b)) { forced.insert(op.operands[1]); ok = false; }
+    if (!view_of(op.operands[0], &a)) { force_for_view(op.operands[0]); ok = false; }
+    if (!view_of(op.operands[1], &b)) { force_for_view(op.operands[1]); ok = false; }
     if (!ok) return false;
     int ra = (int)a.shape.size(), rb = (int)b.shape.size();
     std::vector<int64_t> af, bf;
@@ -249,21 +324,22 @@ struct Planner {
       if (!std::count(op.lb.begin(), op.lb.end(), d) && !std::count(op.lc.begin(), op.lc.end(), d)) af.push_back(d);
     for (int d = 0; d < rb; ++d)
       if (!std::count(op.rb.begin(), op.rb.end(), d) && !std::count(op.rc.begin(), op.rc.end(), d)) bf.push_back(d);
-    int64_t e1, e2;
-    bool good = true;
-    good &= merge(a, op.lb, &g->batch, &g->sab) && merge(b, op.rb, &e1, &g->sbb) && e1 == g->batch;
-    good &= merge(a, af, &g->M, &g->sam);
-    good &= merge(a, op.lc, &g->K, &g->sak) && merge(b, op.rc, &e2, &g->sbk) && e2 == g->K;
-    good &= merge(b, bf, &g->N, &g->sbn);
-    if (!good) {
-      // materialize both operands contiguously in their own dim order; if the
-      // dims are still not mergeable the dot needs a canonical transpose.
-      bool changed = false;
-      if (!materialized(op.operands[0])) { changed |= forced.insert(op.operands[0]).second; }
-      if (!materialized(op.operands[1])) { changed |= forced.insert(op.operands[1]).second; }
-      if (!changed) fail(op, "dot_general operand layout is not expressible as a strided batched GEMM");
-      return false;
+    int64_t e1 = 0, e2 = 0;
+    bool a_ok = merge(a, op.lb, &g->batch, &g->sab) && merge(a, af, &g->M, &g->sam) &&
+                merge(a, op.lc, &g->K, &g->sak);
+    bool b_ok = merge(b, op.rb, &e1, &g->sbb) && merge(b, op.rc, &e2, &g->sbk) && merge(b, bf, &g->N, &g->sbn);
+    if (!a_ok || !b_ok) {
+      // Materialize the operand whose dims do not merge (contiguous in its own
+      // dim order).  A batch reduction that still does not merge stays a
+      // batched GEMM followed by a reduction.
+      bool pending = false;  // an operand will be materialized on the next pass
+      if (!a_ok && !materialized(op.operands[0])) { forced.insert(op.operands[0]); pending = true; }
+      if (!b_ok && !materialized(op.operands[1])) { forced.insert(op.operands[1]); pending = true; }
+      if (pending) return false;
+      if (fused_dot.erase(root.result)) return false;
+      fail(op, "dot_general operand layout is not expressible as a strided batched GEMM");
     }
+    if (e1 != g->batch || e2 != g->K) fail(op, "internal: dot_general extents disagree");
     g->a = a;
     g->b = b;
     return true;
@@ -453,7 +529,7 @@ Plan build_plan(const Function& f, Precision prec) {
     for (size_t i = 0; i < f.ops.size(); ++i) {
       const Op& op = f.ops[i];
       if (!pl.live[op.result]) continue;
-      if (op.kind == OpKind::DotGeneral) {
+      if (pl.is_gemm_root(op)) {
         GemmDesc g;
         if (!pl.gemm_of(op, &g)) retry = true;
       } else if (op.kind == OpKind::Gather) {
@@ -476,7 +552,33 @@ Plan build_plan(const Function& f, Precision prec) {
     if (pl.live[op.result] && pl.cluster[op.result] == kConst) plan.constants.push_back(op.result);
   }
 
+  // TF32: operands are rounded to nearest TF32 where they are produced (the
+  // tensor cores would truncate them).  Parameters get rounded copies; step
+  // roots consumed only by GEMMs are stored rounded.
+  std::set<int> round_gemm_outputs;
+  std::vector<int> round_roots;
+  if (prec == Precision::TF32) {
+    std::set<int> bases;
+    for (const Op& op : f.ops) {
+      if (!pl.live[op.result] || !pl.is_gemm_root(op)) continue;
+      GemmDesc g;
+      if (pl.gemm_of(op, &g)) {
+        bases.insert(g.a.value);
+        bases.insert(g.b.value);
+      }
+    }
+    for (int v : bases) {
+      if (pl.cluster[v] == kParam && f.value_types[v].dtype == DType::F32) {
+        plan.rounded_params.push_back(v);
+      } else if (pl.cluster[v] == v && pl.only_gemm_consumers(v)) {
+        const Op* p = pl.producer(v);
+        if (p && pl.is_gemm_root(*p)) round_gemm_outputs.insert(v);
+        else round_roots.push_back(v);
+      }
+    }
+  }
   CodeGen cg(f, pl.cluster);
+  cg.set_round_roots(round_roots);
   std::map<int, int> step_of_value;
   for (size_t i = 0; i < f.ops.size(); ++i) {
     const Op& op = f.ops[i];
@@ -485,9 +587,14 @@ Plan build_plan(const Function& f, Precision prec) {
     Step st;
     st.root = v;
     st.elements = op.type.numel();
-    if (op.kind == OpKind::DotGeneral) {
+    if (pl.is_gemm_root(op)) {
       st.kind = StepKind::Gemm;
       if (!pl.gemm_of(op, &st.gemm)) fail(op, "internal: GEMM operand views changed after planning");
+      st.gemm.round_out = round_gemm_outputs.count(v) > 0;
+      for (int rp : plan.rounded_params) {
+        if (st.gemm.a.value == rp) st.gemm.a_rounded = true;
+        if (st.gemm.b.value == rp) st.gemm.b_rounded = true;
+      }
       check_view_bounds(f, st.gemm.a, "GEMM lhs");
       check_view_bounds(f, st.gemm.b, "GEMM rhs");
       st.leaves = {st.gemm.a.value, st.gemm.b.value};
@@ -506,6 +613,7 @@ Plan build_plan(const Function& f, Precision prec) {
   }
   plan.source = cg.source();
   plan.snippets = cg.snippets();
+  plan.prelude = CodeGen::prelude();
   plan.kernel_names = cg.kernel_names();
 
   // Output slots: first occurrence of a step root writes the output buffer directly.
@@ -538,6 +646,11 @@ Plan build_plan(const Function& f, Precision prec) {
   for (int s = 0; s < (int)plan.steps.size(); ++s)
     if (plan.steps[s].scratch_elems && pl.returned[plan.steps[s].root])
       iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
+  int last_gemm = -1;
+  for (int s2 = 0; s2 < (int)plan.steps.size(); ++s2)
+    if (plan.steps[s2].kind == StepKind::Gemm) last_gemm = s2;
+  for (int rp : plan.rounded_params)
+    iv.push_back({f.value_types[rp].numel() * 4, 0, std::max(last_gemm, 0), -1, -2 - rp});
   std::vector<int> order(iv.size());
   for (size_t i = 0; i < iv.size(); ++i) order[i] = (int)i;
   std::sort(order.begin(), order.end(), [&](int x, int y) { return iv[x].bytes > iv[y].bytes; });
@@ -560,9 +673,15 @@ Plan build_plan(const Function& f, Precision prec) {
     total = std::max(total, cand + align(iv[k].bytes));
   }
   plan.scratch_offset.assign(plan.steps.size(), -1);
+  plan.rounded_offset.assign(plan.rounded_params.size(), -1);
   for (size_t k = 0; k < iv.size(); ++k) {
     if (iv[k].value >= 0) plan.value_offset[iv[k].value] = off[k];
-    else plan.scratch_offset[iv[k].step_scratch] = off[k];
+    else if (iv[k].step_scratch >= 0) plan.scratch_offset[iv[k].step_scratch] = off[k];
+    else {
+      int rp = -2 - iv[k].step_scratch;
+      for (size_t j = 0; j < plan.rounded_params.size(); ++j)
+        if (plan.rounded_params[j] == rp) plan.rounded_offset[j] = off[k];
+    }
   }
   plan.arena_bytes = total;
   return plan;

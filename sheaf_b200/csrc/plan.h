@@ -25,6 +25,8 @@ struct GemmDesc {
   int64_t batch = 1, M = 1, N = 1, K = 1;
   int64_t sab = 0, sam = 0, sak = 0;
   int64_t sbb = 0, sbk = 0, sbn = 0;
+  bool a_rounded = false, b_rounded = false;  // read the TF32-rounded copy of a parameter
+  bool round_out = false;                     // store the result rounded to TF32
 };
 
 struct GatherDesc {
@@ -56,9 +58,12 @@ struct Plan {
   std::vector<int64_t> value_offset;  // arena byte offset per value (-1 if not in arena)
   std::vector<int64_t> scratch_offset;  // per step, arena offset of split-reduce scratch
   std::vector<int> output_step;       // per return slot: step that writes it (-1: copy)
+  std::vector<int> rounded_params;    // parameters read by tf32 GEMMs through a rounded copy
+  std::vector<int64_t> rounded_offset;  // arena offset of each rounded copy
   int64_t arena_bytes = 0;
   std::string source;                 // CUDA C++ of all generated kernels
   std::vector<std::string> snippets;  // the same, one independent piece per step
+  std::string prelude;                // helpers every compilation unit starts with
   std::vector<std::string> kernel_names;
   std::string summary() const;
 };

@@ -254,7 +254,7 @@ sb_status* load_module(sb_session* s, const std::string& text) {
   SB_CUDA(cudaSetDevice(s->dev->ordinal));
   for (size_t fi = 0; fi < lm->fns.size(); ++fi) {
     auto& lf = lm->fns[fi];
-    std::vector<CubinChunk> chunks = split_source(lf->plan.snippets, std::string("// function ") + lf->qname + "\n", 16);
+    std::vector<CubinChunk> chunks = split_source(lf->plan.snippets, lf->plan.prelude, 16);
     try {
       if (!lf->plan.snippets.empty()) compile_chunks(chunks, s->cache_dir);
     } catch (const std::exception& e) {
@@ -364,6 +364,15 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   for (int v : plan.materialized)
     if (!ptr[v] && plan.value_offset[v] >= 0) ptr[v] = (char*)lf->arena + plan.value_offset[v];
 
+  // TF32-rounded copies of parameters read by tensor-core GEMMs
+  std::map<int, const float*> rounded;
+  for (size_t j = 0; j < plan.rounded_params.size(); ++j) {
+    int v = plan.rounded_params[j];
+    float* dst = (float*)((char*)lf->arena + plan.rounded_offset[j]);
+    cudaError_t e = round_tf32_copy((const float*)ptr[v], dst, f.value_types[v].numel(), stream);
+    if (e != cudaSuccess) { cleanup(); return cuda_status(e, "round_tf32_copy"); }
+    rounded[v] = dst;
+  }
   std::vector<const void*> args;
   for (size_t si = 0; si < plan.steps.size(); ++si) {
     const Step& st = plan.steps[si];
@@ -383,9 +392,10 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     if (st.kind == StepKind::Gemm) {
       const GemmDesc& g = st.gemm;
       GemmArgs a;
-      a.a = (const float*)ptr[g.a.value] + g.a.offset;
-      a.b = (const float*)ptr[g.b.value] + g.b.offset;
+      a.a = (g.a_rounded ? rounded[g.a.value] : (const float*)ptr[g.a.value]) + g.a.offset;
+      a.b = (g.b_rounded ? rounded[g.b.value] : (const float*)ptr[g.b.value]) + g.b.offset;
       a.c = (float*)ptr[st.root];
+      a.round_out = g.round_out ? 1 : 0;
       a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
       a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
       a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
@@ -744,7 +754,7 @@ sb_status* sb_module_inspect(const char* text, size_t len, int32_t precision, ch
     } catch (const std::exception& e) {
       return make_status(SB_STATUS_UNIMPLEMENTED, "planning @" + f.name + ": " + e.what());
     }
-    std::vector<CubinChunk> chunks = split_source(p.snippets, "// inspect\n", 16);
+    std::vector<CubinChunk> chunks = split_source(p.snippets, p.prelude, 16);
     try {
       if (!p.snippets.empty()) compile_chunks(chunks, default_cache_dir());
     } catch (const std::exception& e) {
