@@ -21,6 +21,13 @@ __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
   for (int64_t bz = blockIdx.z; bz < p.batch; bz += gridDim.z) {
     const float* A = p.a + bz * p.sab;
     const float* B = p.b + bz * p.sbb;
+    int64_t kbeg = 0, kend = p.K;
+    if (p.k_chunk > 0) {  // split-K: z indexes the K range, operands are shared
+      A = p.a;
+      B = p.b;
+      kbeg = bz * p.k_chunk;
+      kend = kbeg + p.k_chunk < p.K ? kbeg + p.k_chunk : p.K;
+    }
     float acc[8][8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -41,9 +48,9 @@ __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int64_t m = m0 + am[e], k = k0 + ak[e];
-        ra[e] = (m < p.M && k < p.K) ? A[m * p.sam + k * p.sak] : 0.f;
+        ra[e] = (m < p.M && k < kend) ? A[m * p.sam + k * p.sak] : 0.f;
         int64_t kb = k0 + bk[e], n = n0 + bn[e];
-        rb[e] = (kb < p.K && n < p.N) ? B[kb * p.sbk + n * p.sbn] : 0.f;
+        rb[e] = (kb < kend && n < p.N) ? B[kb * p.sbk + n * p.sbn] : 0.f;
       }
     };
     auto store = [&](int buf) {
@@ -53,13 +60,13 @@ __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
         Bs[buf][bk[e]][bn[e]] = rb[e];
       }
     };
-    const int64_t ktiles = (p.K + BK - 1) / BK;
-    load(0);
+    const int64_t ktiles = (kend - kbeg + BK - 1) / BK;
+    load(kbeg);
     store(0);
     __syncthreads();
     for (int64_t t = 0; t < ktiles; ++t) {
       const int cur = t & 1;
-      if (t + 1 < ktiles) load((t + 1) * BK);
+      if (t + 1 < ktiles) load(kbeg + (t + 1) * BK);
 #pragma unroll
       for (int kk = 0; kk < BK; ++kk) {
         float a[8], b[8];

@@ -144,7 +144,7 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                       int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
-                      int round_out, int* err) {
+                      int round_out, int kchunk, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -158,7 +158,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, bz = blockIdx.z;
-  const int ktiles = (K + BK - 1) / BK;
+  const int ktiles_all = (K + BK - 1) / BK;
+  int kt0 = 0, kt1 = ktiles_all, zab = bz;
+  if (kchunk > 0) {  // split-K: z selects a K range; A and B are shared
+    kt0 = bz * kchunk;
+    kt1 = kt0 + kchunk < ktiles_all ? kt0 + kchunk : ktiles_all;
+    zab = 0;
+  }
+  const int ktiles = kt1 - kt0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -183,25 +190,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (kt >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) break;
+      for (int i = 0; i < ktiles; ++i) {
+        const int kt = kt0 + i;
+        const int s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) break;
         if (*abort_flag) break;
         mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
         uint8_t* a = sA + s * S::A_BYTES;
         uint8_t* b = sB + s * S::B_BYTES;
         if (!a_mn) {
-          tma_load(a, &tmA, &full[s], kt * BK, m0, bz, a3d);
+          tma_load(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
         } else {
 #pragma unroll
-          for (int j = 0; j < BM / 32; ++j) tma_load(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, bz, a3d);
+          for (int j = 0; j < BM / 32; ++j) tma_load(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
         }
         if (!b_mn) {
-          tma_load(b, &tmB, &full[s], kt * BK, n0, bz, b3d);
+          tma_load(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, bz, b3d);
+          for (int j = 0; j < BN / 32; ++j) tma_load(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
         }
       }
     }
@@ -211,9 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
                              ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
       bool ok = true;
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
+      for (int i = 0; i < ktiles; ++i) {
+        const int kt = kt0 + i;
+        const int s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
         fence_after();
         const uint32_t a = smem_u32(sA + s * S::A_BYTES);
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
           const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
           const uint64_t bd = b_mn ? smem_desc(b + kk * 1024, BK * 128, 512, 1) : smem_desc(b + kk * 32, 16, 1024, 2);
-          mma_tf32(tmem, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+          mma_tf32(tmem, ad, bd, idesc, (i | kk) != 0 ? 1u : 0u);
         }
         mma_commit(&empty[s]);
       }
@@ -236,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
     const int quad = warp & 3;
     const int row = m0 + quad * 32 + lane;
-    if (mbar_wait(accf, 0, abort_flag, err, 3)) {
+    if (ktiles > 0 && mbar_wait(accf, 0, abort_flag, err, 3)) {
       fence_after();
       float* crow = C + (long long)bz * scb + (long long)row * ldc;
 #pragma unroll 1
@@ -309,7 +318,9 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   CUtensorMap ta, tb;
   const int64_t lda = a_mn ? g.sak : g.sam;
   const int64_t ldb = b_mn ? g.sbk : g.sbn;
-  const bool a3d = g.batch > 1 && g.sab != 0, b3d = g.batch > 1 && g.sbb != 0;
+  const bool split = g.k_chunk > 0;
+  const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
+  const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
   // A: K-major dims {K, M}, box {32, 128}; M-major dims {M, K}, box {32, 32}
   bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
                  : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false);
@@ -326,7 +337,7 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   }
   dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM), (unsigned)g.batch);
   kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, err);
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, kchunk, err);
   return cudaGetLastError();
 }
 

@@ -17,7 +17,21 @@ struct GemmArgs {
   int64_t sbb, sbk, sbn;
   int64_t scb, scm, scn;
   int round_out = 0;  // tcgen05 path: store C rounded to nearest TF32
+  // split-K (batch == 1 only): when > 0, "batch" index s computes the K range
+  // [s*k_chunk, min(K, (s+1)*k_chunk)) into c + s*scb
+  int64_t k_chunk = 0;
 };
+
+// C[i] = sum_s P[s*M*N + i] over `splits` partial products (row-major M x N
+// partials, C with leading dimension ldc), optionally rounded to TF32.
+cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64_t M, int64_t N, int64_t ldc,
+                          int round_tf32, cudaStream_t stream);
+
+// Dispatch: precision 1 (TF32) tries the tcgen05 kernel, anything else or an
+// unsupported layout runs on CUDA cores; split-K through `ws` when the output
+// has few tiles.  *used_tc reports whether the tensor-core kernel ran.
+size_t gemm_workspace(const GemmArgs& g, int precision);
+cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc);
 
 // dst[i] = src[i] rounded to nearest TF32 (cvt.rna), n elements.
 cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream);

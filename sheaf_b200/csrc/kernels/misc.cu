@@ -39,3 +39,32 @@ cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_
 }
 
 }  // namespace sb
+
+namespace sb {
+namespace {
+
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ p, float* __restrict__ c,
+                                                            int64_t splits, int64_t M, int64_t N, int64_t ldc,
+                                                            int round) {
+  const int64_t mn = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int64_t s = 0; s < splits; ++s) acc += p[s * mn + i];
+    if (round) acc = rna_tf32(acc);
+    c[(i / N) * ldc + (i % N)] = acc;
+  }
+}
+
+}  // namespace
+
+cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64_t M, int64_t N, int64_t ldc,
+                          int round_tf32, cudaStream_t stream) {
+  int64_t mn = M * N;
+  if (mn <= 0) return cudaSuccess;
+  int64_t blocks = (mn + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(partials, c, splits, M, N, ldc, round_tf32);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

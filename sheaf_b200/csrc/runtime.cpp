@@ -400,19 +400,15 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
       a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
       a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
-      cudaError_t e = cudaErrorNotSupported;
-      if (s->opts.precision != SB_PRECISION_FP32) {
-        bool bf16 = s->opts.precision == SB_PRECISION_BF16;
-        size_t need = gemm_tcgen05_workspace(a, bf16);
-        if (need > lf->ws_cap) {
-          if (lf->ws) cudaFreeAsync(lf->ws, stream);
-          if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
-          else lf->ws_cap = need;
-        }
-        e = gemm_tcgen05(a, bf16, lf->ws, lf->ws_cap, stream);
-        if (e == cudaSuccess) s->used_tc = true;
+      size_t need = gemm_workspace(a, s->opts.precision);
+      if (need > lf->ws_cap) {
+        if (lf->ws) cudaFreeAsync(lf->ws, stream);
+        if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+        else lf->ws_cap = need;
       }
-      if (e == cudaErrorNotSupported) e = gemm_simt(a, stream);
+      bool tc = false;
+      cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
+      if (tc) s->used_tc = true;
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
       continue;
     }

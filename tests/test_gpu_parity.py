@@ -118,7 +118,8 @@ def test_nanogpt_full_batch_properties(tf32_session):
     ins = [inp[n] for n in low.arg_names]
     outs = _call(tf32_session, low, ins)
     assert all(np.isfinite(o).all() for o in outs)
-    assert abs(float(outs[0]) - np.log(c.vocab_size)) < 0.05
+    # N(0, 0.02) weights give logits of small spread: the loss sits just above ln(V)
+    assert 0 < float(outs[0]) - np.log(c.vocab_size) < 0.15
     parts = []
     for h in range(2):
         hi = [inp[n][h * 32:(h + 1) * 32] if n in ("x", "y") else inp[n] for n in half.arg_names]
