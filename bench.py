@@ -39,7 +39,8 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
                    choices=["fp32", "tf32", "bf16"])
-    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "gpt2"])
+    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "gpt2", "matmul"])
+    p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-profile", action="store_true")
@@ -290,7 +291,7 @@ def run_ours(args):
         breakdown = {k: {"ms_per_step": v, "share": v / allms if allms else 0} for k, v in tot.items()}
         hbm, tc, src = peaks()
         gem = [r for r in rows if r["kind"] == "gemm"]
-        gflops = sum(r["flops"] for r in gem) / calls
+        gflops = sum(r["flops"] for r in gem)  # per step (static per plan step)
         gms = tot["gemm"]
         if gem and gms > 0:
             ach = gflops / (gms / 1e3) / 1e12
@@ -322,10 +323,54 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_matmul(args):
+    """Op-sweep matmul: C = A @ B with M = N = K = --size, f32 in
+    memory, as Sheaf emits `(@ a b)`; contraction per --precision."""
+    import torch
+    from sheaf_b200 import build
+    from sheaf_b200.session import B200Session
+    build.build()
+    n = args.size
+    t = f"tensor<{n}x{n}xf32>"
+    text = (f"module @matmul_{n} {{\n func.func @f(%arg0: {t}, %arg1: {t}) -> {t} {{\n"
+            f"    %0 = stablehlo.dot_general %arg0, %arg1, contracting_dims = [1] x [0] : ({t}, {t}) -> {t}\n"
+            f"    return %0 : {t}\n }}\n}}\n")
+    sess = B200Session(precision=args.precision)
+    sess.load_stablehlo(text)
+    rng = np.random.default_rng(0)
+    a = sess.buffer(rng.standard_normal((n, n), dtype=np.float32))
+    b = sess.buffer(rng.standard_normal((n, n), dtype=np.float32))
+    q = f"matmul_{n}.f"
+    for _ in range(args.warmup):
+        for o in sess.call_device(q, [a, b]):
+            o.release()
+    sess.synchronize()
+    stream = torch.cuda.ExternalStream(sess.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for o in sess.call_device(q, [a, b]):
+            o.release()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    _, tc, src = peaks()
+    tf = 2 * n ** 3 / (ms / 1e3) / 1e12
+    print(json.dumps({"metric": "matmul TFLOP/s", "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+                      "vs_baseline": None, "dtype": "f32", "contraction": args.precision, "data": "synthetic N(0,1)",
+                      "config": {"workload": f"matmul {n}x{n}x{n} (configs[4])"},
+                      "roofline": {"bound": "tensor", "achieved": tf, "peak": tc, "unit": "TFLOP/s",
+                                   "frac": tf / tc, "traffic": None, "peak_source": src}}), flush=True)
+    sess.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "matmul":
+        run_matmul(args)
     else:
         run_ours(args)
 

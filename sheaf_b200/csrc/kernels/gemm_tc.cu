@@ -371,8 +371,10 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void*, size_t, cudaStream
   if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
-  if (g.N <= 64) return launch<64, 6>(g, a_mn, b_mn, err, stream);
-  return launch<128, 4>(g, a_mn, b_mn, err, stream);
+  // ~97 KB of shared memory per CTA: two CTAs per SM, so one CTA's epilogue
+  // overlaps the other's main loop.
+  if (g.N <= 64) return launch<64, 4>(g, a_mn, b_mn, err, stream);
+  return launch<128, 3>(g, a_mn, b_mn, err, stream);
 }
 
 int gemm_tcgen05_error() {
