@@ -147,6 +147,28 @@ SB_API uint32_t sb_buffer_element_type(const sb_buffer* buffer);
 SB_API size_t sb_buffer_byte_length(const sb_buffer* buffer);
 SB_API void* sb_buffer_device_pointer(const sb_buffer* buffer);
 
+/* --- allocation-free GEMM --------------------------------------------------- *
+ * No counterpart in the reference.  For callers that must not allocate device
+ * memory: work recorded in a CUDA stream capture, code running under another
+ * framework's memory manager, or latency paths that may not touch the
+ * allocator.  Computes C = A @ B for row-major f32 device matrices A (m x k),
+ * B (k x n), C (m x n) on the current device with the CUDA-core GEMM, enqueued
+ * on `cuda_stream` (NULL = default stream); it allocates nothing.  When the
+ * output has too few tiles to fill the GPU, K is split and the partial
+ * products go to a static device array of SB_GEMM_SPLITK_NOALLOC_MAX_FLOATS
+ * floats (16 MiB, present on every GPU that loads this library until the
+ * process exits).  Calls whose partials would exceed it return
+ * SB_STATUS_RESOURCE_EXHAUSTED and launch nothing.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls on a device share the array:
+ * calls that overlap on the GPU race on it, so serialize them.  Returns
+ * SB_STATUS_OK, SB_STATUS_INVALID_ARGUMENT, SB_STATUS_RESOURCE_EXHAUSTED,
+ * SB_STATUS_UNAVAILABLE (no device / array not reachable) or
+ * SB_STATUS_INTERNAL (launch failure). */
+#define SB_GEMM_SPLITK_NOALLOC_MAX_FLOATS (4u << 20)
+SB_API sb_status_code sb_gemm_f32_splitk_noalloc(const float* a, const float* b, float* c, int64_t m, int64_t n,
+                                                 int64_t k, void* cuda_stream);
+
 /* --- collectives ---------------------------------------------------------- */
 SB_API sb_status* sb_nccl_get_unique_id(uint8_t out_id[128]);
 

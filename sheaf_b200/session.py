@@ -83,6 +83,7 @@ SIGNATURES = {
     "sb_buffer_byte_length": (ctypes.c_size_t, [_P]),
     "sb_buffer_device_pointer": (_P, [_P]),
     "sb_nccl_get_unique_id": (_P, [ctypes.POINTER(ctypes.c_uint8)]),
+    "sb_gemm_f32_splitk_noalloc": (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P]),
     "sb_module_inspect": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_char_p, ctypes.c_size_t]),
     "sb_module_kernel_source": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_char_p,
                                      ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
