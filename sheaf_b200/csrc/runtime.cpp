@@ -229,6 +229,31 @@ sb_status* wait_stream(sb_session* s, int64_t timeout_ms) {
   }
 }
 
+// The communicator is nonblocking: after ncclGroupEnd returns ncclInProgress the
+// collectives are enqueued onto the stream by NCCL in the background, and the
+// communicator accepts no new call until ncclCommGetAsyncError stops reporting
+// ncclInProgress.  Polls that state with the collective deadline; on error or
+// timeout the communicator is aborted.
+sb_status* nccl_settle(sb_session* s) {
+  const NcclApi& api = nccl_api();
+  auto t0 = std::chrono::steady_clock::now();
+  int64_t tmo = deadline_ms(s);
+  for (;;) {
+    ncclResult_t ae = ncclInProgress;
+    api.async_error(s->nccl.comm, &ae);
+    if (ae == ncclSuccess) return nullptr;
+    bool late = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count() > tmo;
+    if (ae != ncclInProgress || late) {
+      api.comm_abort(s->nccl.comm);
+      s->nccl.comm = nullptr;
+      s->nccl.aborted = true;
+      if (late) return make_status(SB_STATUS_DEADLINE_EXCEEDED, "NCCL collective was not enqueued within the deadline");
+      return make_status(SB_STATUS_INTERNAL, std::string("NCCL error: ") + api.error_string(ae));
+    }
+    std::this_thread::yield();
+  }
+}
+
 sb_status* load_module(sb_session* s, const std::string& text) {
   std::string err;
   auto mod = parse_module(text, &err);
@@ -449,6 +474,7 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     }
     ncclResult_t r = api.group_end();
     if (r != ncclSuccess && r != ncclInProgress) { cleanup(); return make_status(SB_STATUS_INTERNAL, std::string("ncclGroupEnd: ") + api.error_string(r)); }
+    if (sb_status* e = nccl_settle(s)) { cleanup(); return e; }
   }
   SB_CUDA(cudaGetLastError());
   for (size_t j = 0; j < f.returns.size(); ++j) out[j] = outs[j];
