@@ -303,8 +303,8 @@ def run_ours(args):
               "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
               "contraction": args.precision,
               "data": "synthetic: seeded N(0,0.02) weights, uniform tokens",
-              "config": {"workload": f"{args.workload} value-and-grad (configs[2])" if args.workload == "nanogpt"
-                         else "gpt2-small value-and-grad (configs[3])",
+              "config": {"workload": f"{args.workload} value-and-grad 64x256" if args.workload == "nanogpt"
+                         else "gpt2-small value-and-grad 8x1024",
                          "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
                          "global_batch": gb, "seq_len": c.T, "parallelism": f"dp{world}",
                          "l2": "inputs and activations exceed L2; no flush"},
@@ -324,7 +324,7 @@ def run_ours(args):
 
 
 def run_matmul(args):
-    """Op-sweep matmul (configs[4]): C = A @ B with M = N = K = --size, f32 in
+    """Op-sweep matmul: C = A @ B with M = N = K = --size, f32 in
     memory, as Sheaf emits `(@ a b)`; contraction per --precision."""
     import torch
     from sheaf_b200 import build
@@ -359,7 +359,7 @@ def run_matmul(args):
     print(json.dumps({"metric": "matmul TFLOP/s", "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
                       "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
                       "vs_baseline": None, "dtype": "f32", "contraction": args.precision, "data": "synthetic N(0,1)",
-                      "config": {"workload": f"matmul {n}x{n}x{n} (configs[4])"},
+                      "config": {"workload": f"matmul {n}x{n}x{n}"},
                       "roofline": {"bound": "tensor", "achieved": tf, "peak": tc, "unit": "TFLOP/s",
                                    "frac": tf / tc, "traffic": None, "peak_source": src}}), flush=True)
     sess.close()

@@ -43,6 +43,11 @@ enum class OpKind : uint8_t {
   Clamp, Convert, Select, Compare,
   BroadcastInDim, Reshape, Transpose, Iota, Slice, Pad, Concatenate, Reverse,
   Reduce, DotGeneral, Gather,
+  // Fused attention (head dim 64), created by the planner's attention rewrite,
+  // never parsed.  Operands: q, k, v [B,H,T,64] (+ dy, y, lse for AttnBwdQ;
+  // + dy, lse, dsum for AttnBwdKV).  values[0] = score scale, axis = causal.
+  // Results are packed 1-D buffers (see AttnArgs in kernels/kernels.h).
+  AttnFwd, AttnBwdQ, AttnBwdKV,
 };
 const char* opkind_name(OpKind k);
 
@@ -56,6 +61,9 @@ inline bool is_unary_elementwise(OpKind k) {
          k == OpKind::Log || k == OpKind::Abs || k == OpKind::Neg || k == OpKind::Sin ||
          k == OpKind::Cos || k == OpKind::Not || k == OpKind::Sign || k == OpKind::Floor ||
          k == OpKind::Ceil || k == OpKind::Logistic || k == OpKind::Convert;
+}
+inline bool is_attention(OpKind k) {
+  return k == OpKind::AttnFwd || k == OpKind::AttnBwdQ || k == OpKind::AttnBwdKV;
 }
 inline bool is_elementwise(OpKind k) {
   return is_binary_elementwise(k) || is_unary_elementwise(k) || k == OpKind::Clamp ||

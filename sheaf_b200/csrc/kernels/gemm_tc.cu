@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "tc_common.h"
 
 namespace sb {
 namespace {
@@ -28,108 +29,12 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;                       // f32 elements = 128 bytes: one swizzle row
 constexpr int kThreads = 192;
-constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+using namespace tc;
 
-__device__ __forceinline__ unsigned long long now_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false when the CTA is aborting or the wait expired
-// (then the abort flag is raised and the error recorded).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  unsigned long long t0 = now_ns();
-  for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (now_ns() - t0 > kTimeoutNs) {
-      *abort_flag = 1;
-      atomicExch(err, code);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
-                                         bool is3d) {
-  if (is3d) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-        : "memory");
-  } else {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-  }
-}
-
-// Shared-memory matrix descriptor (sm_100 format, version 1).  layout 2 =
-// SWIZZLE_128B (K-major tiles); layout 1 = SWIZZLE_128B with 32-byte atoms,
-// the only MN-major layout the tf32 MMA accepts.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+__device__ __forceinline__ void tma_ld(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z, bool is3d) {
+  if (is3d) tma_load_3d(dst, map, bar, x, y, z);
+  else tma_load_2d(dst, map, bar, x, y);
 }
 
 template <int BN, int STAGES>
@@ -200,27 +105,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* a = sA + s * S::A_BYTES;
         uint8_t* b = sB + s * S::B_BYTES;
         if (!a_mn) {
-          tma_load(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
+          tma_ld(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
         } else {
 #pragma unroll
-          for (int j = 0; j < BM / 32; ++j) tma_load(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
+          for (int j = 0; j < BM / 32; ++j) tma_ld(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
         }
         if (!b_mn) {
-          tma_load(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
+          tma_ld(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
+          for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // kind::tf32 instruction descriptor: D f32, A/B tf32, transpose bits, N>>3, M>>4
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      const uint32_t idesc = idesc_tf32(BM, BN, a_mn, b_mn);
       bool ok = true;
       for (int i = 0; i < ktiles; ++i) {
-        const int kt = kt0 + i;
         const int s = i % STAGES;
         const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
@@ -283,34 +186,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-  });
-  return fn;
-}
-
 // 2-D or 3-D f32 map: inner (contiguous) extent d0, outer d1, batch d2.
 bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
               uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d, bool mn_major) {
-  auto enc = encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
-  cuuint32_t box[3] = {box0, box1, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, is3d ? 3 : 2, (void*)base, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  (void)box0;
+  const uint64_t dims[3] = {d0, d1, d2};
+  const uint64_t strides[2] = {s1_bytes, s2_bytes};
+  return tc_make_map(m, base, is3d ? 3 : 2, dims, strides, box1, mn_major);
 }
 
 template <int BN, int STAGES>
@@ -341,7 +223,43 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   return cudaGetLastError();
 }
 
-int* error_word() {
+int* error_word() { return tc_error_word(); }
+
+}  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+bool tc_make_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                 uint32_t box_rows, bool mn_major) {
+  auto enc = encode_fn();
+  if (!enc || rank < 2 || rank > 5) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t box[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    box[i] = i == 0 ? 32u : (i == 1 ? box_rows : 1u);
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, (void*)base, d, st, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int* tc_error_word() {
   static int* p = nullptr;
   static std::once_flag once;
   std::call_once(once, []() {
@@ -350,8 +268,6 @@ int* error_word() {
   });
   return p;
 }
-
-}  // namespace
 
 size_t gemm_tcgen05_workspace(const GemmArgs&, bool) { return 0; }
 

@@ -46,8 +46,34 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void* workspace, size_t w
                          cudaStream_t stream);
 // Workspace the tcgen05 path needs for this problem (bf16 operand copies).
 size_t gemm_tcgen05_workspace(const GemmArgs& g, bool bf16);
-// Non-zero when a tcgen05 GEMM gave up on a bounded wait (1: ring slot,
-// 2: operand tiles, 3: accumulator).  Reads a device word (synchronizing).
+// Non-zero when a tcgen05 kernel gave up on a bounded wait (GEMM 1: ring slot,
+// 2: operand tiles, 3: accumulator; attention 11..35).  Reads a device word
+// (synchronizing).
 int gemm_tcgen05_error();
+
+// Fused attention, head dim 64 (kernels/attention.cu).  Views are [B,H,T,64]
+// with unit stride on the last dim; strides in elements.
+enum class AttnKind : int { Fwd = 0, BwdQ = 1, BwdKV = 2 };
+struct AttnView {
+  const float* p = nullptr;
+  int64_t sb = 0, sh = 0, st = 0;
+};
+struct AttnArgs {
+  AttnKind kind = AttnKind::Fwd;
+  int64_t B = 0, H = 0, T = 0, hd = 0;
+  float scale = 1.f;      // multiplier of q.k before the softmax
+  bool causal = false;    // key index > query index is masked out
+  bool round_out = false; // store Y / dQ / dK / dV rounded to TF32
+  AttnView q, k, v, dy, y;
+  const float* lse = nullptr;  // [B,H,T] row log2-sum-exp (backward)
+  int64_t l_sb = 0, l_sh = 0, l_st = 0;
+  const float* dsum = nullptr; // [B,H,T] rowsum(dY * Y) (BwdKV)
+  int64_t d_sb = 0, d_sh = 0, d_st = 0;
+  // Fwd:   [Y (B,T,H,64) | L (B,H,T)]
+  // BwdQ:  [dQ (B,T,H,64) | D (B,H,T)]
+  // BwdKV: [dK (B,T,H,64) | dV (B,T,H,64)]
+  float* out = nullptr;
+};
+cudaError_t attention(const AttnArgs& a, cudaStream_t stream);
 
 }  // namespace sb

@@ -39,7 +39,8 @@ const char* opkind_name(OpKind k) {
       "remainder", "and", "or", "tanh", "sqrt", "rsqrt", "exponential", "log", "abs",
       "negate", "sine", "cosine", "not", "sign", "floor", "ceil", "logistic", "clamp",
       "convert", "select", "compare", "broadcast_in_dim", "reshape", "transpose", "iota",
-      "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather"};
+      "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather",
+      "attention_fwd", "attention_bwd_q", "attention_bwd_kv"};
   return names[(int)k];
 }
 

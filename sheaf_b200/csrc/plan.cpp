@@ -167,7 +167,7 @@ struct Planner {
     if (returned[v]) return false;
     for (auto [oi, slot] : consumers[v]) {
       const Op& c = f.ops[oi];
-      if (c.kind == OpKind::DotGeneral) continue;
+      if (c.kind == OpKind::DotGeneral || is_attention(c.kind)) continue;
       if (cluster[c.result] == kDup && !returned[c.result]) {
         if (!only_gemm_consumers(c.result)) return false;
         continue;
@@ -184,7 +184,7 @@ struct Planner {
   void collect(int v, std::set<int>& cs, bool& blocked, std::set<int>& seen) {
     for (auto [oi, slot] : consumers[v]) {
       const Op& c = f.ops[oi];
-      if (c.kind == OpKind::DotGeneral) { blocked = true; continue; }
+      if (c.kind == OpKind::DotGeneral || is_attention(c.kind)) { blocked = true; continue; }
       if (c.kind == OpKind::Gather && slot == 0) { blocked = true; continue; }
       int cv = c.result;
       if (cluster[cv] == kDup) {
@@ -206,7 +206,8 @@ struct Planner {
       bool absorbed = false;
       for (auto& [rv, di] : fused_dot) if (di == i) absorbed = true;
       if (absorbed) { cluster[v] = kAbsorbed; continue; }
-      if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral) {
+      if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral ||
+          is_attention(op.kind)) {
         cluster[v] = v;
         continue;
       }
@@ -343,6 +344,45 @@ struct Planner {
     g->a = a;
     g->b = b;
     return true;
+  }
+
+  // Views of an attention op's operands.  The [B,H,T,64] operands are read by
+  // TMA or 16-byte loads: unit stride on the head dim, the other strides and
+  // the offset multiples of 4 elements.  An operand whose view does not qualify
+  // is materialized (row-major) on the next pass.
+  bool attn_of(const Op& op, AttnDesc* d) {
+    d->kind = op.kind;
+    d->in.clear();
+    const auto& qs = f.value_types[op.operands[0]].shape;
+    d->B = qs[0];
+    d->H = qs[1];
+    d->T = qs[2];
+    d->scale = op.values.empty() ? 1.0 : op.values[0];
+    d->causal = op.axis != 0;
+    bool ok = true;
+    for (int o : op.operands) {
+      View w;
+      if (!view_of(o, &w)) {
+        force_for_view(o);
+        ok = false;
+        continue;
+      }
+      if (w.shape.size() == 4) {
+        bool good = w.strides[3] == 1 && w.offset % 4 == 0;
+        for (int i = 0; i < 3; ++i) {
+          if (w.shape[i] == 1) w.strides[i] = 4;  // any 16-byte multiple: the index is always 0
+          good = good && w.strides[i] > 0 && w.strides[i] % 4 == 0;
+        }
+        if (!good) {
+          if (materialized(o)) fail(op, "internal: attention operand layout");
+          forced.insert(o);
+          ok = false;
+          continue;
+        }
+      }
+      d->in.push_back(w);
+    }
+    return ok;
   }
 };
 
@@ -493,6 +533,23 @@ void verify(const Function& f) {
           if (op.offset_dims[k] >= 0 && op.offset_dims[k] < rr) need(rs[op.offset_dims[k]] == offs_sizes[k], "gather offset extent");
         break;
       }
+      case OpKind::AttnFwd: case OpKind::AttnBwdQ: case OpKind::AttnBwdKV: {
+        const size_t arity = op.kind == OpKind::AttnFwd ? 3 : 6;
+        need(op.operands.size() == arity, "attention arity");
+        if (op.operands.size() != arity) break;
+        const auto& q = T(op.operands[0]).shape;
+        need(q.size() == 4 && q[3] == 64, "attention operand shape");
+        if (q.size() != 4) break;
+        const std::vector<int64_t> rows{q[0], q[1], q[2]};
+        const int n4 = op.kind == OpKind::AttnFwd ? 3 : (op.kind == OpKind::AttnBwdQ ? 5 : 4);
+        for (size_t s = 0; s < op.operands.size(); ++s) {
+          need(T(op.operands[s]).dtype == DType::F32, "attention operands are f32");
+          need(T(op.operands[s]).shape == ((int)s < n4 ? q : rows), "attention operand shape");
+        }
+        const int64_t N = q[0] * q[1] * q[2] * 64, R = q[0] * q[1] * q[2];
+        need(rs == std::vector<int64_t>{op.kind == OpKind::AttnBwdKV ? 2 * N : N + R}, "attention result size");
+        break;
+      }
       default:
         break;
     }
@@ -518,7 +575,9 @@ void check_view_bounds(const Function& f, const View& v, const char* what) {
 
 }  // namespace
 
-Plan build_plan(const Function& f, Precision prec) {
+namespace {
+
+Plan plan_function(const Function& f, Precision prec) {
   verify(f);
   Planner pl(f, prec);
   pl.liveness();
@@ -532,6 +591,9 @@ Plan build_plan(const Function& f, Precision prec) {
       if (pl.is_gemm_root(op)) {
         GemmDesc g;
         if (!pl.gemm_of(op, &g)) retry = true;
+      } else if (is_attention(op.kind)) {
+        AttnDesc d;
+        if (!pl.attn_of(op, &d)) retry = true;
       } else if (op.kind == OpKind::Gather) {
         View t;
         if (!pl.view_of(op.operands[0], &t)) {
@@ -553,26 +615,36 @@ Plan build_plan(const Function& f, Precision prec) {
   }
 
   // TF32: operands are rounded to nearest TF32 where they are produced (the
-  // tensor cores would truncate them).  Parameters get rounded copies; step
-  // roots consumed only by GEMMs are stored rounded.
+  // tensor cores would truncate them).  Parameters read by GEMMs get rounded
+  // copies; step roots consumed only by GEMMs and attention are stored rounded
+  // (GEMM and attention steps in their epilogues, loops as they store).
   std::set<int> round_gemm_outputs;
   std::vector<int> round_roots;
   if (prec == Precision::TF32) {
-    std::set<int> bases;
+    std::set<int> bases, attn_bases;
     for (const Op& op : f.ops) {
-      if (!pl.live[op.result] || !pl.is_gemm_root(op)) continue;
+      if (!pl.live[op.result]) continue;
+      if (is_attention(op.kind)) {
+        AttnDesc d;
+        if (pl.attn_of(op, &d))
+          for (const View& w : d.in)
+            if (w.shape.size() == 4) attn_bases.insert(w.value);
+        continue;
+      }
+      if (!pl.is_gemm_root(op)) continue;
       GemmDesc g;
       if (pl.gemm_of(op, &g)) {
         bases.insert(g.a.value);
         bases.insert(g.b.value);
       }
     }
+    bases.insert(attn_bases.begin(), attn_bases.end());
     for (int v : bases) {
       if (pl.cluster[v] == kParam && f.value_types[v].dtype == DType::F32) {
         plan.rounded_params.push_back(v);
       } else if (pl.cluster[v] == v && pl.only_gemm_consumers(v)) {
         const Op* p = pl.producer(v);
-        if (p && pl.is_gemm_root(*p)) round_gemm_outputs.insert(v);
+        if (p && (pl.is_gemm_root(*p) || is_attention(p->kind))) round_gemm_outputs.insert(v);
         else round_roots.push_back(v);
       }
     }
@@ -600,6 +672,30 @@ Plan build_plan(const Function& f, Precision prec) {
       st.leaves = {st.gemm.a.value, st.gemm.b.value};
       st.flops = 2.0 * st.gemm.batch * st.gemm.M * st.gemm.N * st.gemm.K;
       st.bytes_moved = 4 * (st.gemm.batch * (st.gemm.M * st.gemm.K + st.gemm.K * st.gemm.N + st.gemm.M * st.gemm.N));
+    } else if (is_attention(op.kind)) {
+      st.kind = StepKind::Attn;
+      if (!pl.attn_of(op, &st.attn)) fail(op, "internal: attention operand views changed after planning");
+      st.attn.round_out = round_gemm_outputs.count(v) > 0 || (prec == Precision::TF32 && pl.only_gemm_consumers(v));
+      for (const View& w : st.attn.in) {
+        check_view_bounds(f, w, "attention operand");
+        st.leaves.push_back(w.value);
+        st.attn.rounded.push_back(w.shape.size() == 4 && std::count(plan.rounded_params.begin(),
+                                                                     plan.rounded_params.end(), w.value) > 0);
+      }
+      const AttnDesc& a = st.attn;
+      const double T = (double)a.T, pairs = a.causal ? T * (T + 1) / 2 : T * T;
+      const double prod = 2.0 * a.B * a.H * 64 * pairs;  // one T x T x 64 product
+      const int64_t N = a.B * a.H * a.T * 64, R = a.B * a.H * a.T;
+      if (op.kind == OpKind::AttnFwd) {
+        st.flops = 2 * prod;
+        st.bytes_moved = 4 * (3 * N + N + R);
+      } else if (op.kind == OpKind::AttnBwdQ) {
+        st.flops = 3 * prod;
+        st.bytes_moved = 4 * (5 * N + R + N + R);
+      } else {
+        st.flops = 4 * prod;
+        st.bytes_moved = 4 * (4 * N + 2 * R + 2 * N);
+      }
     } else if (op.kind == OpKind::Reduce) {
       st.kind = StepKind::Reduce;
       cg.gen_reduce(op, &st);
@@ -648,7 +744,7 @@ Plan build_plan(const Function& f, Precision prec) {
       iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
   int last_gemm = -1;
   for (int s2 = 0; s2 < (int)plan.steps.size(); ++s2)
-    if (plan.steps[s2].kind == StepKind::Gemm) last_gemm = s2;
+    if (plan.steps[s2].kind == StepKind::Gemm || plan.steps[s2].kind == StepKind::Attn) last_gemm = s2;
   for (int rp : plan.rounded_params)
     iv.push_back({f.value_types[rp].numel() * 4, 0, std::max(last_gemm, 0), -1, -2 - rp});
   std::vector<int> order(iv.size());
@@ -687,19 +783,38 @@ Plan build_plan(const Function& f, Precision prec) {
   return plan;
 }
 
+}  // namespace
+
+Plan build_plan(const Function& f, Precision prec) {
+  if (prec == Precision::TF32) {
+    std::string log;
+    std::shared_ptr<Function> rf(rewrite_attention(f, &log));
+    if (rf) {
+      Plan p = plan_function(*rf, prec);
+      p.rewritten = rf;
+      p.fn = rf.get();
+      p.rewrite_log = log;
+      return p;
+    }
+  }
+  return plan_function(f, prec);
+}
+
 std::string Plan::summary() const {
   std::ostringstream os;
   os.precision(17);
-  int loops = 0, reds = 0, gemms = 0;
-  double flops = 0;
+  int loops = 0, reds = 0, gemms = 0, attn = 0;
+  double flops = 0, aflops = 0;
   for (auto& s : steps) {
     if (s.kind == StepKind::Loop) ++loops;
     else if (s.kind == StepKind::Reduce) ++reds;
+    else if (s.kind == StepKind::Attn) { ++attn; aflops += s.flops; continue; }
     else ++gemms;
     flops += s.flops;
   }
   os << "steps=" << steps.size() << " loop=" << loops << " reduce=" << reds << " gemm=" << gemms
-     << " constants=" << constants.size() << " arena_bytes=" << arena_bytes << " gemm_flops=" << flops;
+     << " attention=" << attn << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
+     << " gemm_flops=" << flops << " attention_flops=" << aflops;
   return os.str();
 }
 

@@ -2,6 +2,7 @@
 // memory layout of intermediates, and the CUDA source of the fused kernels.
 #pragma once
 #include <cstdint>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -33,7 +34,19 @@ struct GatherDesc {
   int table = -1;
 };
 
-enum class StepKind : uint8_t { Loop, Reduce, Gemm };
+// Fused attention step (OpKind::AttnFwd / AttnBwdQ / AttnBwdKV).  Operand
+// views in the op's operand order; dims B, H, T, head dim 64.
+struct AttnDesc {
+  OpKind kind = OpKind::AttnFwd;
+  std::vector<View> in;
+  std::vector<char> rounded;  // per operand: read the TF32-rounded copy of a parameter
+  int64_t B = 0, H = 0, T = 0;
+  double scale = 1;
+  bool causal = false;
+  bool round_out = false;  // Y / dQ / dK / dV stored rounded to TF32
+};
+
+enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn };
 
 struct Step {
   StepKind kind = StepKind::Loop;
@@ -45,13 +58,16 @@ struct Step {
   std::string finish_kernel;
   int64_t finish_grid = 1, splits = 1, scratch_elems = 0;
   GemmDesc gemm;
+  AttnDesc attn;
   int64_t elements = 0;         // output elements
   int64_t bytes_moved = 0;      // algorithmic bytes (inputs read once + output)
   double flops = 0;
 };
 
 struct Plan {
-  const Function* fn = nullptr;
+  const Function* fn = nullptr;       // the planned function (may be `rewritten`)
+  std::shared_ptr<Function> rewritten;  // set when the attention rewrite applied
+  std::string rewrite_log;
   std::vector<Step> steps;
   std::vector<int> materialized;      // values written by steps, in step order
   std::vector<int> constants;         // dense (non-splat) constants uploaded at load
@@ -69,7 +85,13 @@ struct Plan {
 };
 
 // Builds the plan.  Throws std::runtime_error with a diagnostic on failure.
+// With TF32 the attention rewrite runs first; plan.fn then points at the
+// rewritten function, which has the same parameters and results as `f`.
 Plan build_plan(const Function& f, Precision prec);
+
+// Replaces attention regions (and their reverse-mode gradients) by fused
+// attention ops.  Returns nullptr when nothing matched (attn_rewrite.cpp).
+std::unique_ptr<Function> rewrite_attention(const Function& f, std::string* log);
 
 // Row-major strides of a shape.
 std::vector<int64_t> row_major(const std::vector<int64_t>& shape);

@@ -312,7 +312,7 @@ sb_status* load_module(sb_session* s, const std::string& text) {
     }
     // dense constants
     for (int v : lf->plan.constants) {
-      const Op& op = lf->fn->ops[lf->fn->producer[v]];
+      const Op& op = lf->plan.fn->ops[lf->plan.fn->producer[v]];
       size_t n = (size_t)op.type.numel();
       std::vector<uint8_t> host(n * dtype_bytes(op.type.dtype));
       for (size_t i = 0; i < n; ++i) {
@@ -353,7 +353,7 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
 
 sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin,
                         const int32_t* reduce, sb_buffer** out, size_t cap, size_t* nout) {
-  const Function& f = *lf->fn;
+  const Function& f = *lf->plan.fn;
   if (nin != f.params.size())
     return make_status(SB_STATUS_INVALID_ARGUMENT, "@" + f.name + " expects " + std::to_string(f.params.size()) +
                                                        " inputs, got " + std::to_string(nin));
@@ -435,6 +435,41 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
       if (tc) s->used_tc = true;
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
+      continue;
+    }
+    if (st.kind == StepKind::Attn) {
+      const AttnDesc& d = st.attn;
+      AttnArgs a;
+      a.kind = d.kind == OpKind::AttnFwd ? AttnKind::Fwd : (d.kind == OpKind::AttnBwdQ ? AttnKind::BwdQ : AttnKind::BwdKV);
+      a.B = d.B; a.H = d.H; a.T = d.T; a.hd = 64;
+      a.scale = (float)d.scale;
+      a.causal = d.causal;
+      a.round_out = d.round_out;
+      a.out = (float*)ptr[st.root];
+      auto view = [&](size_t i) {
+        const View& w = d.in[i];
+        AttnView r;
+        r.p = (d.rounded[i] ? rounded[w.value] : (const float*)ptr[w.value]) + w.offset;
+        r.sb = w.strides[0]; r.sh = w.strides[1]; r.st = w.strides[2];
+        return r;
+      };
+      auto rows = [&](size_t i, const float** p, int64_t* sb, int64_t* sh, int64_t* stt) {
+        const View& w = d.in[i];
+        *p = (const float*)ptr[w.value] + w.offset;
+        *sb = w.strides[0]; *sh = w.strides[1]; *stt = w.strides[2];
+      };
+      a.q = view(0); a.k = view(1); a.v = view(2);
+      if (a.kind != AttnKind::Fwd) a.dy = view(3);
+      if (a.kind == AttnKind::BwdQ) {
+        a.y = view(4);
+        rows(5, &a.lse, &a.l_sb, &a.l_sh, &a.l_st);
+      } else if (a.kind == AttnKind::BwdKV) {
+        rows(4, &a.lse, &a.l_sb, &a.l_sh, &a.l_st);
+        rows(5, &a.dsum, &a.d_sb, &a.d_sh, &a.d_st);
+      }
+      cudaError_t e = attention(a, stream);
+      s->used_tc = true;
+      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "attention"); }
       continue;
     }
     args.clear();
@@ -624,7 +659,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
   std::ostringstream os;
   os.precision(9);
   os << "function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention"};
   for (auto& m : s->modules)
     for (auto& lf : m->fns) {
       if (lf->prof_ms.empty()) continue;
@@ -812,7 +847,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   std::ostringstream os;
   os.precision(17);
   os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
     const GemmDesc& g = st.gemm;

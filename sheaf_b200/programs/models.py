@@ -208,7 +208,7 @@ def gpt_inputs(c: GPTConfig, batch: int = None, seed: int = 0) -> Dict[str, np.n
 
 
 # ---------------------------------------------------------------------------
-# MLP value-and-grad (configs[0]): linear -> gelu -> linear, mse-loss
+# MLP value-and-grad: linear -> gelu -> linear, mse-loss
 # ---------------------------------------------------------------------------
 
 MLP_SHAPES = {"x": (256, 784), "W1": (784, 512), "W2": (512, 10), "b1": (512,), "b2": (10,)}

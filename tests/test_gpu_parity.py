@@ -107,7 +107,7 @@ def test_repeated_calls_are_bitwise_identical(fp32_session):
 
 
 def test_nanogpt_full_batch_properties(tf32_session):
-    """Full configs[2] batch (64x256): size-independent properties, since the
+    """Full nanoGPT batch (64x256): size-independent properties, since the
     oracle is too slow at this size: finite outputs, loss near ln(V) for
     N(0, 0.02) weights, and exact data-parallel linearity of the loss
     (mean over two half batches == full-batch loss)."""
