@@ -41,6 +41,11 @@ def parse():
                    choices=["fp32", "tf32", "bf16"])
     p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "gpt2", "matmul"])
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
+    p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
+    p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
+                   help="matmul workload: operands stored transposed (t) or not (n)")
+    p.add_argument("--batch", type=int, default=0,
+                   help="global batch override (profiling captures on a smaller case)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-profile", action="store_true")
@@ -52,11 +57,11 @@ def env_rank():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
-def workload(name, world):
+def workload(name, world, batch=0):
     from sheaf_b200.programs import models as M
     if name == "nanogpt":
         c = M.NANOGPT
-        gb = c.batch
+        gb = batch or c.batch
         if gb % world:
             raise SystemExit(f"global batch {gb} is not divisible by {world} ranks")
         return c, gb, gb // world, "strong"
@@ -185,7 +190,7 @@ def run_ours(args):
     from sheaf_b200.programs import models as M
     from sheaf_b200.session import B200Session, nccl_unique_id
     build.build()
-    c, gb, b, scaling = workload(args.workload, world)
+    c, gb, b, scaling = workload(args.workload, world, args.batch)
     low = M.gpt_vag(c, batch=b)
     inp = M.gpt_inputs(c, batch=gb, seed=0)
     shard = {"x": inp["x"][rank * b:(rank + 1) * b], "y": inp["y"][rank * b:(rank + 1) * b]}
@@ -286,9 +291,13 @@ def run_ours(args):
                              f"{r['elements']},{r['bytes']},{r['flops']}\n")
         calls = max(1, rows[0]["calls"]) if rows else 1
         launches = sum(r["launches_per_call"] for r in rows if r["function"] == q)
-        tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in ("gemm", "loop", "reduce")}
+        kinds = ("gemm", "attention", "loop", "reduce")
+        tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in kinds}
         allms = sum(tot.values())
         breakdown = {k: {"ms_per_step": v, "share": v / allms if allms else 0} for k, v in tot.items()}
+        att = [r for r in rows if r["kind"] == "attention"]
+        if att and tot["attention"] > 0:
+            breakdown["attention"]["tflops"] = sum(r["flops"] for r in att) / (tot["attention"] / 1e3) / 1e12
         hbm, tc, src = peaks()
         gem = [r for r in rows if r["kind"] == "gemm"]
         gflops = sum(r["flops"] for r in gem)  # per step (static per plan step)
@@ -324,23 +333,36 @@ def run_ours(args):
 
 
 def run_matmul(args):
-    """Op-sweep matmul: C = A @ B with M = N = K = --size, f32 in
-    memory, as Sheaf emits `(@ a b)`; contraction per --precision."""
+    """Op-sweep matmul: C = A @ B, M = N = K = --size or --shape M,N,K, f32 in
+    memory, as Sheaf emits `(@ a b)`; --layout picks which operands are stored
+    transposed (t) and read through a transpose view, as in x @ W^T ("nt") and
+    X^T @ G ("tn"); contraction per --precision."""
     import torch
     from sheaf_b200 import build
     from sheaf_b200.session import B200Session
     build.build()
-    n = args.size
-    t = f"tensor<{n}x{n}xf32>"
-    text = (f"module @matmul_{n} {{\n func.func @f(%arg0: {t}, %arg1: {t}) -> {t} {{\n"
-            f"    %0 = stablehlo.dot_general %arg0, %arg1, contracting_dims = [1] x [0] : ({t}, {t}) -> {t}\n"
-            f"    return %0 : {t}\n }}\n}}\n")
+    m, n, k = (int(x) for x in args.shape.split(",")) if args.shape else (args.size,) * 3
+    at, bt = args.layout[0] == "t", args.layout[1] == "t"
+    ty = lambda r, c: f"tensor<{r}x{c}xf32>"
+    sa, sb = (ty(k, m) if at else ty(m, k)), (ty(n, k) if bt else ty(k, n))
+    body, lhs, rhs = [], "%arg0", "%arg1"
+    if at:
+        body.append(f"    %ta = stablehlo.transpose %arg0, dims = [1, 0] : ({sa}) -> {ty(m, k)}")
+        lhs = "%ta"
+    if bt:
+        body.append(f"    %tb = stablehlo.transpose %arg1, dims = [1, 0] : ({sb}) -> {ty(k, n)}")
+        rhs = "%tb"
+    body.append(f"    %0 = stablehlo.dot_general {lhs}, {rhs}, contracting_dims = [1] x [0] : "
+                f"({ty(m, k)}, {ty(k, n)}) -> {ty(m, n)}")
+    name = f"matmul_{m}_{n}_{k}_{args.layout}"
+    text = (f"module @{name} {{\n func.func @f(%arg0: {sa}, %arg1: {sb}) -> {ty(m, n)} {{\n" +
+            "\n".join(body) + f"\n    return %0 : {ty(m, n)}\n }}\n}}\n")
     sess = B200Session(precision=args.precision)
     sess.load_stablehlo(text)
     rng = np.random.default_rng(0)
-    a = sess.buffer(rng.standard_normal((n, n), dtype=np.float32))
-    b = sess.buffer(rng.standard_normal((n, n), dtype=np.float32))
-    q = f"matmul_{n}.f"
+    a = sess.buffer(rng.standard_normal((k, m) if at else (m, k), dtype=np.float32))
+    b = sess.buffer(rng.standard_normal((n, k) if bt else (k, n), dtype=np.float32))
+    q = f"{name}.f"
     for _ in range(args.warmup):
         for o in sess.call_device(q, [a, b]):
             o.release()
@@ -355,11 +377,12 @@ def run_matmul(args):
     e1.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     _, tc, src = peaks()
-    tf = 2 * n ** 3 / (ms / 1e3) / 1e12
+    tf = 2 * m * n * k / (ms / 1e3) / 1e12
     print(json.dumps({"metric": "matmul TFLOP/s", "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
                       "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
                       "vs_baseline": None, "dtype": "f32", "contraction": args.precision, "data": "synthetic N(0,1)",
-                      "config": {"workload": f"matmul {n}x{n}x{n}"},
+                      "config": {"workload": f"matmul {m}x{n}x{k} {args.layout}",
+                                 "l2": "operands L2-resident below ~40 MB; no flush (op sweep, not a bench line)"},
                       "roofline": {"bound": "tensor", "achieved": tf, "peak": tc, "unit": "TFLOP/s",
                                    "frac": tf / tc, "traffic": None, "peak_source": src}}), flush=True)
     sess.close()

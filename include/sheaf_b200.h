@@ -131,7 +131,8 @@ SB_API sb_status* sb_session_call(sb_session* session, const char* qualified_nam
 SB_API sb_status* sb_buffer_allocate_copy(sb_session* session, size_t rank, const uint64_t* shape,
                                           uint32_t element_type, const void* host_data,
                                           size_t byte_length, sb_buffer** out_buffer);
-/* Wraps caller-owned device memory without copying; the caller keeps it alive. */
+/* Wraps caller-owned device memory without copying; the caller keeps it alive.
+ * The pointer must be 16-byte aligned (vector loads and TMA read it directly). */
 SB_API sb_status* sb_buffer_wrap_device(sb_session* session, size_t rank, const uint64_t* shape,
                                         uint32_t element_type, void* device_ptr, size_t byte_length,
                                         sb_buffer** out_buffer);

@@ -71,6 +71,21 @@ std::string c_add(const std::string& a, const std::string& b) {
   return a + "+" + b;
 }
 
+// Raised while generating a 4-wide loop when some access uses the lane
+// coordinate other than as the innermost index of a contiguous f32 read; the
+// loop is then generated one element per thread.
+struct VecFail {};
+
+const char* const kLane[4] = {"cL", "(cL+1)", "(cL+2)", "(cL+3)"};
+
+int lane_of(const std::string& s) {
+  for (int j = 0; j < 4; ++j)
+    if (s == kLane[j]) return j;
+  return -1;
+}
+
+bool uses_lane(const std::string& s) { return s.find("cL") != std::string::npos; }
+
 }  // namespace
 
 bool CodeGen::is_materialized_for(const Ctx& c, int v) const {
@@ -97,10 +112,37 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
   }
   const Type& t = f_.value_types[v];
   auto st = row_major(t.shape);
+  if (t.dtype == DType::BF16) throw std::runtime_error("bf16 buffers are not supported in fused kernels");
+  if (c.vec) {
+    int lane = -1;
+    for (size_t i = 0; i < coords.size(); ++i) {
+      if (!uses_lane(coords[i])) continue;
+      if (i + 1 != coords.size() || (lane = lane_of(coords[i])) < 0) throw VecFail{};
+    }
+    if (lane >= 0) {
+      // innermost index is the lane coordinate itself: lanes 0..3 read 4
+      // consecutive floats starting at a multiple of 4 (row-major leaf whose
+      // innermost extent is a multiple of 4, lane 0 coordinate cL % 4 == 0)
+      if (t.dtype != DType::F32 || t.shape.back() % 4 || c.memo.size() > 1) throw VecFail{};
+      std::string off0 = "0";
+      for (size_t i = 0; i + 1 < coords.size(); ++i) off0 = c_add(off0, c_mul(coords[i], st[i]));
+      off0 = c_add(off0, "cL");
+      const std::string key = std::to_string(li) + ":" + off0;
+      auto vit = c.vloads.find(key);
+      std::string var;
+      if (vit == c.vloads.end()) {
+        var = fresh(c, "v");
+        c.body << c.pad() << "const float4 " << var << " = *(const float4*)(L" << li << " + " << off0 << ");\n";
+        c.vloads[key] = var;
+      } else {
+        var = vit->second;
+      }
+      return Val{var + "." + "xyzw"[lane], "float"};
+    }
+  }
   std::string off = "0";
   for (size_t i = 0; i < coords.size(); ++i) off = c_add(off, c_mul(coords[i], st[i]));
   Val r{fresh(c), ctype_of(t.dtype)};
-  if (t.dtype == DType::BF16) throw std::runtime_error("bf16 buffers are not supported in fused kernels");
   c.body << c.pad() << "const " << r.ctype << " " << r.name << " = L" << li << "[" << off << "];\n";
   return r;
 }
@@ -161,6 +203,9 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
         size_t k = 0;
         for (size_t i = 0; i < ish.size(); ++i) if (ish[i] != 1) ic[i] = coords[outpos[k++]];
       } else {
+        if (c.vec)
+          for (auto& x : coords)
+            if (uses_lane(x)) throw VecFail{};
         auto so = row_major(osh);
         std::string lin = "0";
         for (size_t i = 0; i < osh.size(); ++i) lin = c_add(lin, c_mul(coords[i], so[i]));
@@ -242,6 +287,9 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
       break;
     }
     case OpKind::Gather: {
+      if (c.vec)
+        for (auto& x : coords)
+          if (uses_lane(x)) throw VecFail{};
       const auto& tsh = f_.value_types[op.operands[0]].shape;
       const auto& ish = f_.value_types[op.operands[1]].shape;
       int ivd = (int)op.axis;
@@ -370,6 +418,12 @@ std::string CodeGen::header(const std::string& name, const Ctx& c, int extra_ptr
 }
 
 void CodeGen::gen_loop(const Op& root, Step* st) {
+  {
+    const auto& sh = root.type.shape;
+    if (!sh.empty() && sh.back() % 4 == 0 && root.type.numel() > 0 && root.type.dtype == DType::F32 &&
+        gen_loop_vec4(root, st))
+      return;
+  }
   const std::string start_text = src_.str();
   struct Snip {
     CodeGen* g; size_t start;
@@ -384,12 +438,12 @@ void CodeGen::gen_loop(const Op& root, Step* st) {
     st->block = 32;
     return;
   }
+  const auto& sh = root.type.shape;
+  int r = (int)sh.size();
   Ctx c;
   c.root = root.result;
   c.idx = index_type(root, 0);
   c.memo.emplace_back();
-  const auto& sh = root.type.shape;
-  int r = (int)sh.size();
   std::vector<std::string> coords(r);
   c.indent = 2;
   std::ostringstream pre;
@@ -422,6 +476,65 @@ void CodeGen::gen_loop(const Op& root, Step* st) {
   int64_t bytes = n * dtype_bytes(root.type.dtype);
   for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
   st->bytes_moved = bytes;
+}
+
+// Loop kernel computing 4 consecutive outputs per thread (innermost extent a
+// multiple of 4, f32 output): float4 loads of contiguous leaves, uniform values
+// computed once per lane group, one float4 store.  Returns false (nothing
+// emitted) when an access pattern does not vectorize.
+bool CodeGen::gen_loop_vec4(const Op& root, Step* st) {
+  const auto& sh = root.type.shape;
+  const int r = (int)sh.size();
+  const int64_t n = root.type.numel();
+  const int64_t q = sh[r - 1] / 4;
+  Ctx c;
+  c.root = root.result;
+  c.idx = index_type(root, 0);
+  c.memo.emplace_back();
+  c.vec = true;
+  c.indent = 2;
+  std::vector<std::string> coords(r);
+  std::ostringstream pre;
+  pre << "    " << c.idx << " r_ = i;\n";
+  pre << "    const " << c.idx << " cL = (r_ % " << q << ") * 4; r_ /= " << q << ";\n";
+  for (int d = r - 2; d >= 0; --d) {
+    coords[d] = "c" + std::to_string(d);
+    if (d == 0) pre << "    const " << c.idx << " c0 = r_;\n";
+    else pre << "    const " << c.idx << " c" << d << " = r_ % " << sh[d] << "; r_ /= " << sh[d] << ";\n";
+  }
+  std::string lanes[4];
+  try {
+    for (int j = 0; j < 4; ++j) {
+      coords[r - 1] = kLane[j];
+      lanes[j] = store(root, eval(c, root.result, coords).name);
+    }
+  } catch (const VecFail&) {
+    return false;
+  }
+  const std::string start_text = src_.str();
+  struct Snip {
+    CodeGen* g; size_t start;
+    ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
+  } snip{this, start_text.size()};
+  std::string name = "k" + std::to_string(names_.size());
+  const int64_t nv = n / 4;
+  src_ << header(name, c, 0);
+  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  src_ << "  for (" << c.idx << " i = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; i < ("
+       << c.idx << ")" << nv << "; i += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+  src_ << pre.str();
+  src_ << c.body.str();
+  src_ << "    *(float4*)(O + i * 4) = make_float4(" << lanes[0] << ", " << lanes[1] << ", " << lanes[2] << ", "
+       << lanes[3] << ");\n  }\n}\n\n";
+  names_.push_back(name);
+  st->kernel = name;
+  st->leaves = c.leaves;
+  st->block = kThreads;
+  st->grid = std::max<int64_t>(1, std::min<int64_t>((nv + kThreads - 1) / kThreads, kMaxGrid));
+  int64_t bytes = n * 4;
+  for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
+  st->bytes_moved = bytes;
+  return true;
 }
 
 void CodeGen::gen_reduce(const Op& root, Step* st) {

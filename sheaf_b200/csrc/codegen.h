@@ -41,9 +41,14 @@ class CodeGen {
     int indent = 2;
     std::string idx;  // index C type
     std::vector<std::map<std::string, Val>> memo;
+    // 4-wide mode: the innermost output coordinate of lane j is "cL" (j = 0)
+    // or "(cL+j)"; contiguous f32 leaf reads become one float4 load per lane group
+    bool vec = false;
+    std::map<std::string, std::string> vloads;  // leaf:offset -> float4 variable
     std::string pad() const { return std::string(indent * 2, ' '); }
   };
 
+  bool gen_loop_vec4(const Op& root, Step* st);
   Val eval(Ctx& c, int v, const std::vector<std::string>& coords);
   Val leaf_load(Ctx& c, int v, const std::vector<std::string>& coords);
   std::string fresh(Ctx& c, const char* p = "t") { return p + std::to_string(c.tmp++); }

@@ -1,16 +1,21 @@
-// tcgen05 tensor-core GEMM for sm_100a: C[b] = A[b] @ B[b] with f32 operands in
+// tcgen05 tensor-core GEMM for sm_100a: C[z] = A[z] @ B[z] with f32 operands in
 // global memory read by the tensor cores as TF32 (kind::tf32), f32 accumulation
-// in TMEM.
+// in TMEM.  z is a batch index or, for split-K, a K range.
 //
-// One 128 x BN output tile per CTA, 192 threads:
-//   warp 0      TMA producer (one elected lane): 128B-swizzled tiles of A and B
-//               into a STAGES-deep shared-memory ring, completion via mbarrier
-//               transaction bytes;
+// Persistent: PER_SM CTAs per SM walk the 128 x BN output tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (grouped order, see Tiles, so CTAs that run
+// together share A and B tiles in L2).  192 threads, warp-specialized:
+//   warp 0      TMA producer (one lane): 128B-swizzled K slices of A and B into
+//               a STAGES-deep shared-memory ring that runs across tiles,
+//               completion via mbarrier transaction bytes;
 //   warp 1      MMA issuer (one lane): 4 x tcgen05.mma (K = 8 each) per 32-wide
-//               K tile into a 128 x BN f32 accumulator in TMEM; tcgen05.commit
-//               frees ring slots and finally signals the epilogue;
+//               K slice into one of two 128 x BN TMEM accumulators;
+//               tcgen05.commit frees ring slots and hands a finished
+//               accumulator to the epilogue;
 //   warps 2..5  epilogue: tcgen05.ld 32x32b from the four TMEM lane quadrants,
-//               predicated stores to C.
+//               optional TF32 rounding, predicated stores to C, then release
+//               the accumulator.  With two accumulators the epilogue of tile i
+//               overlaps the main loop of tile i + 1.
 // Operands may be K-major or MN-major (the transpose bits of the instruction
 // descriptor), so x @ W^T, G @ W and X^T @ G all run without transposing copies.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records an
@@ -18,6 +23,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kernels.h"
@@ -45,11 +51,29 @@ struct Smem {
   static constexpr int BYTES = 1024 /*alignment slack*/ + STAGES * STAGE + 256;
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+// Tile t -> (z, m, n).  Within a slice z, tiles run in groups of kGroupM
+// M-tiles, column by column, so the ~148 tiles in flight cover a kGroupM x ~18
+// block of C and re-read A and B from L2 rather than HBM.
+constexpr int kGroupM = 8;
+struct Tiles {
+  int m_tiles, n_tiles, per_z, total;
+  __device__ void at(int t, int* z, int* m0, int* n0, int bn) const {
+    *z = t / per_z;
+    const int r = t - *z * per_z;
+    const int gsz = kGroupM * n_tiles;
+    const int g = r / gsz, rr = r - g * gsz;
+    const int mf = g * kGroupM;
+    const int gm = min(kGroupM, m_tiles - mf);
+    *m0 = (mf + rr % gm) * BM;
+    *n0 = (rr / gm) * bn;
+  }
+};
+
+template <int BN, int STAGES, int PER_SM>
+__global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                       int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
-                      int round_out, int kchunk, int* err) {
+                      int round_out, int kchunk, Tiles tl, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -57,111 +81,137 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(accf + 1);
+  uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (128 arrivals)
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, bz = blockIdx.z;
   const int ktiles_all = (K + BK - 1) / BK;
-  int kt0 = 0, kt1 = ktiles_all, zab = bz;
-  if (kchunk > 0) {  // split-K: z selects a K range; A and B are shared
-    kt0 = bz * kchunk;
-    kt1 = kt0 + kchunk < ktiles_all ? kt0 + kchunk : ktiles_all;
-    zab = 0;
-  }
-  const int ktiles = kt1 - kt0;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    fence_proxy_async();
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"((uint32_t)BN)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // K range of output slice z
+  auto krange = [&](int z, int* kt0, int* kt1, int* zab) {
+    *kt0 = 0;
+    *kt1 = ktiles_all;
+    *zab = z;
+    if (kchunk > 0) {
+      *kt0 = z * kchunk;
+      *kt1 = min(*kt0 + kchunk, ktiles_all);
+      *zab = 0;
+    }
+  };
+
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < ktiles; ++i) {
-        const int kt = kt0 + i;
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) break;
-        if (*abort_flag) break;
-        mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
-        uint8_t* a = sA + s * S::A_BYTES;
-        uint8_t* b = sB + s * S::B_BYTES;
-        if (!a_mn) {
-          tma_ld(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
-        } else {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x) {
+        int z, m0, n0, kt0, kt1, zab;
+        tl.at(t, &z, &m0, &n0, BN);
+        krange(z, &kt0, &kt1, &zab);
+        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
+          mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
+          uint8_t* a = sA + s * S::A_BYTES;
+          uint8_t* b = sB + s * S::B_BYTES;
+          if (!a_mn) {
+            tma_ld(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BM / 32; ++j) tma_ld(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
-        }
-        if (!b_mn) {
-          tma_ld(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
-        } else {
+            for (int j = 0; j < BM / 32; ++j) tma_ld(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
+          }
+          if (!b_mn) {
+            tma_ld(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
+            for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // kind::tf32 instruction descriptor: D f32, A/B tf32, transpose bits, N>>3, M>>4
       const uint32_t idesc = idesc_tf32(BM, BN, a_mn, b_mn);
+      int it = 0, j = 0;
       bool ok = true;
-      for (int i = 0; i < ktiles; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
+      for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x, ++j) {
+        int z, m0, n0, kt0, kt1, zab;
+        tl.at(t, &z, &m0, &n0, BN);
+        krange(z, &kt0, &kt1, &zab);
+        const int b = j & 1, use = j >> 1;
+        if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
         fence_after();
-        const uint32_t a = smem_u32(sA + s * S::A_BYTES);
-        const uint32_t b = smem_u32(sB + s * S::B_BYTES);
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
+          fence_after();
+          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
+          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 8; ++kk) {
-          // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
-          // k-th MMA starts 32 B further along the row.  MN-major: 128 B (32 M/N
-          // values) by BK rows per chunk, chunks BK*128 B apart (LBO), 4-row
-          // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
-          const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
-          const uint64_t bd = b_mn ? smem_desc(b + kk * 1024, BK * 128, 512, 1) : smem_desc(b + kk * 32, 16, 1024, 2);
-          mma_tf32(tmem, ad, bd, idesc, (i | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
+            // k-th MMA starts 32 B further along the row.  MN-major: 128 B (32 M/N
+            // values) by BK rows per chunk, chunks BK*128 B apart (LBO), 4-row
+            // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
+            const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
+            const uint64_t bd = b_mn ? smem_desc(bb + kk * 1024, BK * 128, 512, 1) : smem_desc(bb + kk * 32, 16, 1024, 2);
+            mma_tf32(acc, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        if (!ok) break;
+        mma_commit(&acc_full[b]);
       }
-      if (ok) mma_commit(accf);
     }
   } else {
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
     const int quad = warp & 3;
-    const int row = m0 + quad * 32 + lane;
-    if (ktiles > 0 && mbar_wait(accf, 0, abort_flag, err, 3)) {
+    int j = 0;
+    for (int t = blockIdx.x; t < tl.total; t += gridDim.x, ++j) {
+      int z, m0, n0, kt0, kt1, zab;
+      tl.at(t, &z, &m0, &n0, BN);
+      krange(z, &kt0, &kt1, &zab);
+      const int b = j & 1, use = j >> 1;
+      if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
       fence_after();
-      float* crow = C + (long long)bz * scb + (long long)row * ldc;
+      const int row = m0 + quad * 32 + lane;
+      float* crow = C + (long long)z * scb + (long long)row * ldc;
+      const uint32_t acc = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
+        tmem_ld16(acc + (uint32_t)c, v);
+        if (kt1 <= kt0) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = 0.f;
+        }
         if (round_out) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            uint32_t u;
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(v[j]));
-            v[j] = __uint_as_float(u);
-          }
+          for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
         }
         if (row < M) {
           const int col0 = n0 + c;
@@ -171,18 +221,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (col0 + j < N) crow[col0 + j] = v[j];
+            for (int q = 0; q < 16; ++q)
+              if (col0 + q < N) crow[col0 + q] = v[q];
           }
         }
       }
+      fence_before();
+      mbar_arrive(&acc_empty[b]);
     }
   }
   fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -195,7 +247,17 @@ bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint6
   return tc_make_map(m, base, is3d ? 3 : 2, dims, strides, box1, mn_major);
 }
 
-template <int BN, int STAGES>
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int PER_SM>
 cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
   CUtensorMap ta, tb;
   const int64_t lda = a_mn ? g.sak : g.sam;
@@ -210,16 +272,23 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
                    : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false));
   if (!ok) return cudaErrorNotSupported;
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tf32_tcgen05<BN, STAGES>;
+  auto kern = gemm_tf32_tcgen05<BN, STAGES, PER_SM>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM), (unsigned)g.batch);
+  Tiles tl;
+  tl.m_tiles = (int)((g.M + BM - 1) / BM);
+  tl.n_tiles = (int)((g.N + BN - 1) / BN);
+  tl.per_z = tl.m_tiles * tl.n_tiles;
+  const int64_t total = (int64_t)tl.per_z * g.batch;
+  if (total > (1ll << 30)) return cudaErrorNotSupported;
+  tl.total = (int)total;
+  const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
   kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, kchunk, err);
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, kchunk, tl, err);
   return cudaGetLastError();
 }
 
@@ -287,10 +356,12 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void*, size_t, cudaStream
   if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
-  // ~97 KB of shared memory per CTA: two CTAs per SM, so one CTA's epilogue
-  // overlaps the other's main loop.
-  if (g.N <= 64) return launch<64, 4>(g, a_mn, b_mn, err, stream);
-  return launch<128, 3>(g, a_mn, b_mn, err, stream);
+  // Two persistent CTAs per SM (~97 KB of shared memory and 2 x BN TMEM
+  // columns each): two independent TMA/MMA streams hide the ring refill
+  // latency better than one deeper ring (measured on 2048..8192 matmuls and
+  // the nanoGPT shapes, against BN = 128 / 256 with one CTA per SM).
+  if (g.N <= 64) return launch<64, 4, 2>(g, a_mn, b_mn, err, stream);
+  return launch<128, 3, 2>(g, a_mn, b_mn, err, stream);
 }
 
 int gemm_tcgen05_error() {

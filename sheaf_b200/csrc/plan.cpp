@@ -195,6 +195,54 @@ struct Planner {
     }
   }
 
+  // Rematerialization.  An element-wise value used by several clusters is
+  // recomputed inside each of them instead of being written and re-read, when
+  // the recomputation is cheap: at most kRematOps element-wise ops (at most
+  // two transcendental) down to at most three values that are materialized
+  // anyway, and every consumer reads it at its own shape (no broadcast that
+  // would repeat the work).  Typical cases: the tanh term of GELU and the
+  // normalized input of layer norm, which the reverse pass would otherwise
+  // read back from HBM.
+  static constexpr int kRematOps = 16;
+  static bool transcendental(OpKind k) {
+    return k == OpKind::Tanh || k == OpKind::Exp || k == OpKind::Log || k == OpKind::Sin || k == OpKind::Cos ||
+           k == OpKind::Logistic || k == OpKind::Pow || k == OpKind::Sqrt || k == OpKind::Rsqrt;
+  }
+  bool remat_cone(int u, int& ops, int& trans, std::set<int>& leaves, std::set<int>& seen) const {
+    if (!seen.insert(u).second) return true;
+    const Op* p = producer(u);
+    if (!p || returned[u] || forced.count(u) || p->kind == OpKind::Reduce || p->kind == OpKind::DotGeneral ||
+        is_attention(p->kind) || (p->kind == OpKind::Constant && p->values.size() != 1)) {
+      leaves.insert(u);
+      return leaves.size() <= 3;
+    }
+    if (p->kind == OpKind::Constant || p->kind == OpKind::Iota) return true;
+    if (is_dup_kind(*p)) return remat_cone(p->operands[0], ops, trans, leaves, seen);
+    if (!is_elementwise(p->kind)) return false;
+    if (++ops > kRematOps || (transcendental(p->kind) && ++trans > 2)) return false;
+    for (int o : p->operands)
+      if (!remat_cone(o, ops, trans, leaves, seen)) return false;
+    return true;
+  }
+  bool same_shape_uses(int v, int depth = 0) const {
+    if (depth > 8) return false;
+    for (auto [oi, slot] : consumers[v]) {
+      const Op& c = f.ops[oi];
+      if (!is_dup_kind(c)) continue;
+      if (c.kind != OpKind::Reshape && c.kind != OpKind::Transpose && c.kind != OpKind::Slice) return false;
+      if (!same_shape_uses(c.result, depth + 1)) return false;
+    }
+    return true;
+  }
+  bool rematerializable(int v) const {
+    const Op* p = producer(v);
+    if (!p || !is_elementwise(p->kind) || returned[v] || f.value_types[v].numel() < (1 << 16)) return false;
+    if (!same_shape_uses(v)) return false;
+    int ops = 0, trans = 0;
+    std::set<int> leaves, seen;
+    return remat_cone(v, ops, trans, leaves, seen);
+  }
+
   void clusterize() {
     cluster.assign(NV, -1);
     for (int p = 0; p < P; ++p) cluster[p] = kParam;
@@ -215,7 +263,9 @@ struct Planner {
       std::set<int> cs, seen;
       bool blocked = false;
       collect(v, cs, blocked, seen);
-      cluster[v] = (!blocked && cs.size() == 1) ? *cs.begin() : v;
+      if (!blocked && cs.size() == 1) cluster[v] = *cs.begin();
+      else if (!blocked && cs.size() > 1 && rematerializable(v)) cluster[v] = kDup;
+      else cluster[v] = v;
     }
   }
 

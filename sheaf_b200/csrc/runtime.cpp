@@ -199,7 +199,7 @@ sb_status* wait_stream(sb_session* s, int64_t timeout_ms) {
       if (s->used_tc) {
         int code = gemm_tcgen05_error();
         if (code)
-          return make_status(SB_STATUS_INTERNAL, "tensor-core GEMM gave up on a bounded wait (code " +
+          return make_status(SB_STATUS_INTERNAL, "tensor-core kernel gave up on a bounded wait (code " +
                                                      std::to_string(code) + "); results are invalid");
       }
       return nullptr;
@@ -341,6 +341,14 @@ sb_status* load_module(sb_session* s, const std::string& text) {
   }
   s->modules.push_back(std::move(lm));
   return nullptr;
+}
+
+// Kernel name of a step as the profile report and plan listing show it.
+std::string step_name(const Step& st) {
+  if (st.kind == StepKind::Gemm) return "gemm";
+  if (st.kind == StepKind::Attn)
+    return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : (st.attn.kind == OpKind::AttnBwdQ ? "attn_bwd_q" : "attn_bwd_kv");
+  return st.kernel;
 }
 
 sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs, int64_t gx, int64_t gy,
@@ -667,7 +675,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
         const Step& st = lf->plan.steps[i];
         if (!lf->prof_n[i]) continue;
         os << lf->qname << "," << i << "," << kinds[(int)st.kind] << ","
-           << (st.kind == StepKind::Gemm ? "gemm" : st.kernel) << "," << lf->prof_n[i] << "," << lf->prof_ms[i]
+           << step_name(st) << "," << lf->prof_n[i] << "," << lf->prof_ms[i]
            << "," << st.elements << "," << st.bytes_moved << "," << st.flops << "," << (st.splits > 1 ? 2 : 1)
            << "\n";
       }
@@ -744,6 +752,8 @@ sb_status* sb_buffer_wrap_device(sb_session* s, size_t rank, const uint64_t* sha
   for (size_t i = 0; i < rank; ++i) t.shape.push_back((int64_t)shape[i]);
   if (bytes != (size_t)t.numel() * dtype_bytes(t.dtype))
     return make_status(SB_STATUS_INVALID_ARGUMENT, "byte length does not match shape");
+  if (((uintptr_t)dptr) & 15)
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "device pointer must be 16-byte aligned");
   auto* b = new sb_buffer();
   b->type = t;
   b->bytes = bytes;
@@ -851,7 +861,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
     const GemmDesc& g = st.gemm;
-    os << i << "," << kinds[(int)st.kind] << "," << (st.kind == StepKind::Gemm ? "gemm" : st.kernel) << ","
+    os << i << "," << kinds[(int)st.kind] << "," << step_name(st) << ","
        << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
        << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
        << g.sbn << "\n";

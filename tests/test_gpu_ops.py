@@ -199,6 +199,44 @@ def test_large_gemm_shapes_match_oracle(tf32_session):
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
 
 
+@pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1)])
+@pytest.mark.parametrize("at,bt", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_tiles_and_layouts(tf32_session, shape, at, bt):
+    """Every tile width of the tcgen05 GEMM (N <= 64, 128, 256-wide tiles for
+    N % 256 == 0 or N >= 1024) with ragged M/N/K edges, K-major and MN-major
+    operands, batched."""
+    M_, N_, K_, B_ = shape
+    lead = [B_] if B_ > 1 else []
+    sa = lead + ([K_, M_] if at else [M_, K_])
+    sb = lead + ([N_, K_] if bt else [K_, N_])
+    ty = lambda s: "tensor<" + "x".join(map(str, s)) + "xf32>"
+    nb = len(lead)
+    perm = "[" + ", ".join(map(str, list(range(nb)) + [nb + 1, nb])) + "]"
+    body, a, b = [], "%arg0", "%arg1"
+    if at:
+        body.append(f"%ta = stablehlo.transpose %arg0, dims = {perm} : ({ty(sa)}) -> {ty(lead + [M_, K_])}")
+        a = "%ta"
+    if bt:
+        body.append(f"%tb = stablehlo.transpose %arg1, dims = {perm} : ({ty(sb)}) -> {ty(lead + [K_, N_])}")
+        b = "%tb"
+    batch = "batching_dims = [0] x [0], " if nb else ""
+    rt = ty(lead + [M_, N_])
+    body.append(f"%0 = stablehlo.dot_general {a}, {b}, {batch}contracting_dims = [{nb + 1}] x [{nb}] : "
+                f"({ty(lead + [M_, K_])}, {ty(lead + [K_, N_])}) -> {rt}")
+    name, text = module([ty(sa), ty(sb)], body, [("%0", rt)])
+    ins = [rnd(*sa), rnd(*sb)]
+    tf32_session.load_stablehlo(text)
+    out = tf32_session.call(name, ins)[0]
+    A = ins[0].astype(np.float64)
+    Bm = ins[1].astype(np.float64)
+    if at:
+        A = np.swapaxes(A, -1, -2)
+    if bt:
+        Bm = np.swapaxes(Bm, -1, -2)
+    ref = np.matmul(A, Bm)
+    assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
+
+
 def test_input_validation_errors(fp32_session):
     from sheaf_b200.session import B200Error
     name, text = module(["tensor<4xf32>"], ["%0 = stablehlo.exponential %arg0 : tensor<4xf32>"], [("%0", "tensor<4xf32>")])
