@@ -77,6 +77,9 @@ typedef struct sb_session_options {
 } sb_session_options;
 
 #define SB_SESSION_FLAG_NO_CUDA_GRAPH 1u /* launch kernels one by one instead of replaying a graph */
+/* TF32: keep the attention region on the generic fused-loop + GEMM path instead
+ * of the fused tcgen05 attention kernels (for A/B parity checks). */
+#define SB_SESSION_FLAG_NO_ATTENTION_FUSION 2u
 
 typedef struct sb_allocator_stats {
   /* field meaning follows iree_hal_allocator_statistics_t as read by

@@ -537,7 +537,198 @@ bool CodeGen::gen_loop_vec4(const Op& root, Step* st) {
   return true;
 }
 
+// 4-wide reductions (f32).  Row mode (reduced dims trailing, R <= 4096): a
+// warp per output, each lane consuming 4 consecutive elements of the innermost
+// reduced dim per step.  Column mode (innermost dim kept): a thread per 4
+// adjacent outputs with 4 accumulators, optionally split over the reduced
+// range like the scalar column kernel.  Partial sums are combined in a fixed
+// order, so results are deterministic.  Returns false (nothing emitted) when an
+// access does not vectorize or the shape does not qualify.
+bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
+  const Type& in = f_.value_types[root.operands[0]];
+  const auto& ish = in.shape;
+  const int r = (int)ish.size();
+  if (r == 0 || ish[r - 1] % 4 || root.type.dtype != DType::F32 || in.dtype != DType::F32) return false;
+  std::vector<int64_t> rd(root.dims.begin(), root.dims.end());
+  std::sort(rd.begin(), rd.end());
+  std::vector<int64_t> kd;
+  for (int d = 0; d < r; ++d) if (!std::count(rd.begin(), rd.end(), d)) kd.push_back(d);
+  int64_t R = 1, O = 1;
+  for (auto d : rd) R *= ish[d];
+  for (auto d : kd) O *= ish[d];
+  bool trailing = true;
+  for (size_t i = 0; i < rd.size(); ++i) if (rd[rd.size() - 1 - i] != r - 1 - (int64_t)i) trailing = false;
+  const bool inner_reduced = !rd.empty() && rd.back() == r - 1;
+  int mode;
+  if (trailing && R <= 4096 && inner_reduced) mode = 0;
+  else if (!trailing && !inner_reduced && !kd.empty() && kd.back() == r - 1) mode = 2;
+  else return false;
+  if (R == 0 || O == 0) return false;
+  const char* ident = root.body == ReduceBody::Add ? "0.f"
+                      : root.body == ReduceBody::Max ? "__int_as_float(0xff800000)"
+                      : root.body == ReduceBody::Min ? "__int_as_float(0x7f800000)" : "1.f";
+  auto combine = [&](const std::string& a, const std::string& b) {
+    switch (root.body) {
+      case ReduceBody::Add: return a + " + " + b;
+      case ReduceBody::Max: return "fmaxf(" + a + ", " + b + ")";
+      case ReduceBody::Min: return "fminf(" + a + ", " + b + ")";
+      case ReduceBody::Mul: return a + " * " + b;
+    }
+    return a;
+  };
+  Ctx c;
+  c.root = root.result;
+  c.idx = index_type(root, 0);
+  c.memo.emplace_back();
+  c.vec = true;
+  // coordinates: the lane coordinate "cL" is the innermost input coordinate
+  // (a reduced one in row mode, a kept one in column mode)
+  std::ostringstream pre, loopb;
+  std::vector<std::string> oc(kd.size(), "0"), kc(rd.size(), "0");
+  int64_t splits = 1, chunk = R;
+  if (mode == 0) {
+    if (!kd.empty()) {
+      pre << "    " << c.idx << " ro_ = o;\n";
+      for (int j = (int)kd.size() - 1; j >= 0; --j) {
+        oc[j] = "o" + std::to_string(j);
+        if (j == 0) pre << "    const " << c.idx << " o0 = ro_;\n";
+        else pre << "    const " << c.idx << " o" << j << " = ro_ % " << ish[kd[j]] << "; ro_ /= " << ish[kd[j]] << ";\n";
+      }
+    }
+    const int64_t e = ish[rd.back()];
+    loopb << "      " << c.idx << " rk_ = k4 * 4;\n";
+    loopb << "      const " << c.idx << " cL = rk_ % " << e << "; rk_ /= " << e << ";\n";
+    for (int j = (int)rd.size() - 2; j >= 0; --j) {
+      kc[j] = "q" + std::to_string(j);
+      if (j == 0) loopb << "      const " << c.idx << " q0 = rk_;\n";
+      else loopb << "      const " << c.idx << " q" << j << " = rk_ % " << ish[rd[j]] << "; rk_ /= " << ish[rd[j]] << ";\n";
+    }
+  } else {
+    const int64_t e = ish[kd.back()];
+    pre << "    " << c.idx << " ro_ = o4 * 4;\n";
+    pre << "    const " << c.idx << " cL = ro_ % " << e << "; ro_ /= " << e << ";\n";
+    for (int j = (int)kd.size() - 2; j >= 0; --j) {
+      oc[j] = "o" + std::to_string(j);
+      if (j == 0) pre << "    const " << c.idx << " o0 = ro_;\n";
+      else pre << "    const " << c.idx << " o" << j << " = ro_ % " << ish[kd[j]] << "; ro_ /= " << ish[kd[j]] << ";\n";
+    }
+    loopb << "      " << c.idx << " rk_ = k;\n";
+    for (int j = (int)rd.size() - 1; j >= 0; --j) {
+      kc[j] = "q" + std::to_string(j);
+      if (j == 0) loopb << "      const " << c.idx << " q0 = rk_;\n";
+      else loopb << "      const " << c.idx << " q" << j << " = rk_ % " << ish[rd[j]] << "; rk_ /= " << ish[rd[j]] << ";\n";
+    }
+    const int64_t target = 148 * 2048;
+    const int64_t O4 = O / 4;
+    if (O4 < target && R >= 64) {
+      splits = std::max<int64_t>(1, std::min<int64_t>((target + O4 - 1) / O4, R / 32));
+      chunk = (R + splits - 1) / splits;
+      splits = (R + chunk - 1) / chunk;
+    }
+  }
+  std::string lanes[4];
+  c.indent = 3;
+  try {
+    for (int j = 0; j < 4; ++j) {
+      std::vector<std::string> ic(r);
+      for (size_t q = 0; q < kd.size(); ++q) ic[kd[q]] = oc[q];
+      for (size_t q = 0; q < rd.size(); ++q) ic[rd[q]] = kc[q];
+      ic[r - 1] = kLane[j];
+      lanes[j] = eval(c, root.operands[0], ic).name;
+    }
+  } catch (const VecFail&) {
+    return false;
+  }
+  const std::string loop_code = loopb.str() + c.body.str();
+  c.body.str("");
+  c.vec = false;
+  auto saved_memo = std::move(c.memo);
+  c.memo.assign(1, {});
+  c.indent = 3;
+  Val init = eval(c, root.operands[1], {});
+  const std::string init_code = c.body.str();
+  c.memo = std::move(saved_memo);
+
+  const std::string start_text = src_.str();
+  struct Snip {
+    CodeGen* g; size_t start;
+    ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
+  } snip{this, start_text.size()};
+  std::string name = "k" + std::to_string(names_.size());
+  src_ << header(name, c, mode == 2 && splits > 1 ? 1 : 0);
+  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  if (mode == 0) {
+    src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+    src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; o < " << O
+         << "; o += (" << c.idx << ")gridDim.x * " << kThreads / 32 << ") {\n";
+    src_ << pre.str();
+    src_ << "    float acc = " << ident << ";\n";
+    src_ << "    for (" << c.idx << " k4 = lane; k4 < " << R / 4 << "; k4 += 32) {\n" << loop_code;
+    for (int j = 0; j < 4; ++j) src_ << "      acc = " << combine("acc", lanes[j]) << ";\n";
+    src_ << "    }\n";
+    src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+         << combine("acc", "y_") << "; }\n";
+    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
+         << ";\n    }\n  }\n}\n\n";
+    st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
+  } else {
+    const int64_t O4 = O / 4;
+    if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
+    src_ << "  for (" << c.idx << " o4 = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o4 < " << O4
+         << "; o4 += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+    src_ << pre.str();
+    src_ << "    float a0 = " << ident << ", a1 = " << ident << ", a2 = " << ident << ", a3 = " << ident << ";\n";
+    src_ << "    const " << c.idx << " k0 = (" << c.idx << ")blockIdx.y * " << chunk << ";\n";
+    src_ << "    const " << c.idx << " k1 = min((" << c.idx << ")" << R << ", k0 + (" << c.idx << ")" << chunk << ");\n";
+    src_ << "    for (" << c.idx << " k = k0; k < k1; ++k) {\n" << loop_code;
+    for (int j = 0; j < 4; ++j) src_ << "      a" << j << " = " << combine("a" + std::to_string(j), lanes[j]) << ";\n";
+    src_ << "    }\n";
+    if (splits > 1) {
+      src_ << "    *(float4*)(S + (" << c.idx << ")blockIdx.y * " << O << " + o4 * 4) = make_float4(a0, a1, a2, a3);\n  }\n}\n\n";
+    } else {
+      src_ << "    {\n" << init_code << "    *(float4*)(O + o4 * 4) = make_float4(" << store(root, combine("a0", init.name))
+           << ", " << store(root, combine("a1", init.name)) << ", " << store(root, combine("a2", init.name)) << ", "
+           << store(root, combine("a3", init.name)) << ");\n    }\n  }\n}\n\n";
+    }
+    st->grid = std::max<int64_t>(1, std::min<int64_t>((O4 + kThreads - 1) / kThreads, kMaxGrid));
+    st->grid_y = splits;
+    if (splits > 1) {
+      std::string fin = name + "f";
+      src_ << "struct __align__(8) A_" << fin << " { const void* p[" << c.leaves.size() + 2 << "]; };\n";
+      src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
+           << " a) {\n";
+      for (size_t i = 0; i < c.leaves.size(); ++i) {
+        const Type& t = f_.value_types[c.leaves[i]];
+        src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+             << "*)a.p[" << i << "];\n";
+      }
+      src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+      src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
+      src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
+           << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+      src_ << "    float acc = " << ident << ";\n";
+      src_ << "    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = "
+           << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
+      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+      names_.push_back(fin);
+      st->finish_kernel = fin;
+      st->finish_grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
+      st->splits = splits;
+      st->scratch_elems = splits * O;
+    }
+  }
+  names_.push_back(name);
+  st->kernel = name;
+  st->leaves = c.leaves;
+  st->block = kThreads;
+  int64_t bytes = O * 4;
+  for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
+  st->bytes_moved = bytes;
+  return true;
+}
+
 void CodeGen::gen_reduce(const Op& root, Step* st) {
+  if (gen_reduce_vec4(root, st)) return;
   const std::string start_text = src_.str();
   struct Snip {
     CodeGen* g; size_t start;

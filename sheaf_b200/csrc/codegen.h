@@ -49,6 +49,7 @@ class CodeGen {
   };
 
   bool gen_loop_vec4(const Op& root, Step* st);
+  bool gen_reduce_vec4(const Op& root, Step* st);
   Val eval(Ctx& c, int v, const std::vector<std::string>& coords);
   Val leaf_load(Ctx& c, int v, const std::vector<std::string>& coords);
   std::string fresh(Ctx& c, const char* p = "t") { return p + std::to_string(c.tmp++); }

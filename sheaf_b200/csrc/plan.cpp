@@ -835,8 +835,8 @@ Plan plan_function(const Function& f, Precision prec) {
 
 }  // namespace
 
-Plan build_plan(const Function& f, Precision prec) {
-  if (prec == Precision::TF32) {
+Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
+  if (prec == Precision::TF32 && fuse_attention) {
     std::string log;
     std::shared_ptr<Function> rf(rewrite_attention(f, &log));
     if (rf) {

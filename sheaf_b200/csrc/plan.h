@@ -87,7 +87,7 @@ struct Plan {
 // Builds the plan.  Throws std::runtime_error with a diagnostic on failure.
 // With TF32 the attention rewrite runs first; plan.fn then points at the
 // rewritten function, which has the same parameters and results as `f`.
-Plan build_plan(const Function& f, Precision prec);
+Plan build_plan(const Function& f, Precision prec, bool fuse_attention = true);
 
 // Replaces attention regions (and their reverse-mode gradients) by fused
 // attention ops.  Returns nullptr when nothing matched (attn_rewrite.cpp).

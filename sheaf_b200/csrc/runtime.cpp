@@ -266,7 +266,7 @@ sb_status* load_module(sb_session* s, const std::string& text) {
     lf->fn = &f;
     lf->qname = mod->name.empty() ? f.name : mod->name + "." + f.name;
     try {
-      lf->plan = build_plan(f, prec);
+      lf->plan = build_plan(f, prec, !(s->opts.flags & SB_SESSION_FLAG_NO_ATTENTION_FUSION));
     } catch (const std::exception& e) {
       return make_status(SB_STATUS_UNIMPLEMENTED, "planning @" + f.name + ": " + e.what());
     }

@@ -205,15 +205,21 @@ class DeviceBuffer:
             pass
 
 
+FLAG_NO_ATTENTION_FUSION = 2  # SB_SESSION_FLAG_NO_ATTENTION_FUSION
+
+
 class B200Session:
     """One GPU, one stream.  `world_size > 1` makes `call_device(..., reduce=...)`
     combine outputs across data-parallel ranks with NCCL."""
 
     def __init__(self, device: int = 0, precision: str = "tf32", rank: int = 0, world_size: int = 1,
-                 nccl_id: Optional[bytes] = None, timeout_ms: int = 600000, cache_dir: Optional[str] = None):
+                 nccl_id: Optional[bytes] = None, timeout_ms: int = 600000, cache_dir: Optional[str] = None,
+                 fuse_attention: bool = True):
         lib = library()
         o = _Options()
         lib.sb_session_options_initialize(ctypes.byref(o))
+        if not fuse_attention:
+            o.flags |= FLAG_NO_ATTENTION_FUSION
         o.device_ordinal = device
         o.precision = PRECISIONS[precision]
         o.rank = rank

@@ -112,14 +112,33 @@ def test_gpt_layer_with_fused_attention(tf32_session):
     _check(outs, run(low.text, low.qualified, ins))
 
 
+def _errs(outs, ref):
+    e = [abs(float(outs[0]) - float(ref[0])) / abs(float(ref[0]))]
+    for o, r in zip(outs[1:], ref[1:]):
+        e.append(float(np.linalg.norm(o.astype(np.float64) - r) / np.linalg.norm(r)))
+    return e
+
+
 def test_nanogpt_full_batch_fused_matches_fp32(tf32_session, fp32_session):
-    """Full nanoGPT batch (64 x 256): the fused TF32 step against the unfused
-    exact-f32 step of the same graph (the oracle is too slow at this size)."""
+    """Full nanoGPT batch (64 x 256), the oracle being too slow at this size:
+    the fused TF32 step and the unfused TF32 step of the same graph, both
+    against the exact-f32 step.  TF32 operand rounding alone puts the deepest
+    (layer 0) gradients near 2e-3 here, so the fused path is held to the 2e-3
+    bound or, if the unfused TF32 graph is already there, to within 10% of it:
+    fusing attention must not cost accuracy."""
+    from sheaf_b200.session import B200Session
     low = M.gpt_vag(M.NANOGPT)
     inp = M.gpt_inputs(M.NANOGPT, seed=1)
     ins = [inp[n] for n in low.arg_names]
     tf32_session.load_stablehlo(low.text)
     fp32_session.load_stablehlo(low.text)
     fused = tf32_session.call(low.qualified, ins)
-    exact = fp32_session.call(low.qualified, ins)
-    _check(fused, [x.astype(np.float64) for x in exact])
+    exact = [x.astype(np.float64) for x in fp32_session.call(low.qualified, ins)]
+    unfused_sess = B200Session(precision="tf32", fuse_attention=False)
+    try:
+        unfused_sess.load_stablehlo(low.text)
+        unfused = unfused_sess.call(low.qualified, ins)
+    finally:
+        unfused_sess.close()
+    ef, eu = _errs(fused, exact), _errs(unfused, exact)
+    assert max(ef) <= max(2e-3, 1.1 * max(eu)), (max(ef), max(eu))
