@@ -57,6 +57,7 @@ struct Smem {
 constexpr int kGroupM = 8;
 struct Tiles {
   int m_tiles, n_tiles, per_z, total;
+  int bm;  // tile height: 128 (one CTA) or 256 (CTA pair)
   __device__ void at(int t, int* z, int* m0, int* n0, int bn) const {
     *z = t / per_z;
     const int r = t - *z * per_z;
@@ -64,7 +65,7 @@ struct Tiles {
     const int g = r / gsz, rr = r - g * gsz;
     const int mf = g * kGroupM;
     const int gm = min(kGroupM, m_tiles - mf);
-    *m0 = (mf + rr % gm) * BM;
+    *m0 = (mf + rr % gm) * bm;
     *n0 = (rr / gm) * bn;
   }
 };
@@ -238,6 +239,192 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   }
 }
 
+// CTA-pair variant: a cluster of two CTAs computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2.  Each CTA loads its 128 rows of A and BN/2 columns
+// of B into its own shared memory (pair TMA loads count their bytes on the
+// leader's full barrier); the leader's MMA thread issues the pair MMA, which
+// reads both CTAs' tiles and accumulates rows 0..127 into the leader's TMEM and
+// rows 128..255 into the peer's.  Per SM this moves 25% (BN = 128) or 50%
+// (BN = 256) fewer operand bytes per FLOP than the 128 x 128 single-CTA tile.
+// Completion is signalled to both CTAs with one non-multicast commit each; the
+// peer's epilogue releases an accumulator with a remote mbarrier arrive.
+template <int BN, int STAGES, int PER_SM>
+__global__ void __launch_bounds__(kThreads, PER_SM)
+    gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
+                   int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
+                   int round_out, int kchunk, Tiles tl, int* err) {
+  constexpr int BNH = BN / 2;
+  using S = Smem<BNH, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);  // leader: both CTAs' bytes
+  uint64_t* empty = full + STAGES;                            // each CTA: slot free
+  uint64_t* acc_full = empty + STAGES;                        // each CTA: accumulator ready
+  uint64_t* acc_empty = acc_full + 2;                         // leader: 256 arrivals
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+  const int ktiles_all = (K + BK - 1) / BK;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 256);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_proxy_async();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  fence_before();
+  __syncthreads();
+  cluster_sync();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto krange = [&](int z, int* kt0, int* kt1, int* zab) {
+    *kt0 = 0;
+    *kt1 = ktiles_all;
+    *zab = z;
+    if (kchunk > 0) {
+      *kt0 = z * kchunk;
+      *kt1 = min(*kt0 + kchunk, ktiles_all);
+      *zab = 0;
+    }
+  };
+  auto ld = [&](void* dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z, bool is3d) {
+    if (is3d) tma_load_3d_pair(dst, map, bar, x, y, z);
+    else tma_load_2d_pair(dst, map, bar, x, y);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < tl.total && ok; t += npairs) {
+        int z, m0, n0, kt0, kt1, zab;
+        tl.at(t, &z, &m0, &n0, BN);
+        krange(z, &kt0, &kt1, &zab);
+        const int ma = m0 + (int)rank * BM, nb = n0 + (int)rank * BNH;
+        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
+          if (leader) mbar_expect_tx(&full[s], 2u * (uint32_t)S::STAGE);
+          const uint32_t bar = cluster_addr(&full[s], 0);
+          uint8_t* a = sA + s * S::A_BYTES;
+          uint8_t* b = sB + s * S::B_BYTES;
+          if (!a_mn) {
+            ld(a, &tmA, bar, kt * BK, ma, zab, a3d);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j) ld(a + j * BK * 128, &tmA, bar, ma + 32 * j, kt * BK, zab, a3d);
+          }
+          if (!b_mn) {
+            ld(b, &tmB, bar, kt * BK, nb, zab, b3d);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 32; ++j) ld(b + j * BK * 128, &tmB, bar, nb + 32 * j, kt * BK, zab, b3d);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_tf32(2 * BM, BN, a_mn, b_mn);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = pair; t < tl.total && ok; t += npairs, ++j) {
+        int z, m0, n0, kt0, kt1, zab;
+        tl.at(t, &z, &m0, &n0, BN);
+        krange(z, &kt0, &kt1, &zab);
+        const int b = j & 1, use = j >> 1;
+        if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
+        fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
+          fence_after();
+          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
+          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
+            const uint64_t bd = b_mn ? smem_desc(bb + kk * 1024, BK * 128, 512, 1) : smem_desc(bb + kk * 32, 16, 1024, 2);
+            mma_tf32_pair(acc, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit_pair(cluster_addr(&empty[s], 0));
+          mma_commit_pair(cluster_addr(&empty[s], 1));
+        }
+        if (!ok) break;
+        mma_commit_pair(cluster_addr(&acc_full[b], 0));
+        mma_commit_pair(cluster_addr(&acc_full[b], 1));
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    int j = 0;
+    for (int t = pair; t < tl.total; t += npairs, ++j) {
+      int z, m0, n0, kt0, kt1, zab;
+      tl.at(t, &z, &m0, &n0, BN);
+      krange(z, &kt0, &kt1, &zab);
+      const int b = j & 1, use = j >> 1;
+      if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
+      fence_after();
+      const int row = m0 + (int)rank * BM + quad * 32 + lane;
+      float* crow = C + (long long)z * scb + (long long)row * ldc;
+      const uint32_t accp = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(accp + (uint32_t)c, v);
+        if (kt1 <= kt0) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = 0.f;
+        }
+        if (round_out) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
+        }
+        if (row < M) {
+          const int col0 = n0 + c;
+          if (col0 + 16 <= N && (ldc & 3) == 0 && (((uintptr_t)(crow + col0)) & 15) == 0) {
+            float4* dst = (float4*)(crow + col0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (col0 + q < N) crow[col0 + q] = v[q];
+          }
+        }
+      }
+      fence_before();
+      mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 // 2-D or 3-D f32 map: inner (contiguous) extent d0, outer d1, batch d2.
 bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
               uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d, bool mn_major) {
@@ -280,6 +467,7 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
     attr_set = true;
   }
   Tiles tl;
+  tl.bm = BM;
   tl.m_tiles = (int)((g.M + BM - 1) / BM);
   tl.n_tiles = (int)((g.N + BN - 1) / BN);
   tl.per_z = tl.m_tiles * tl.n_tiles;
@@ -290,6 +478,53 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
                                              (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, kchunk, tl, err);
   return cudaGetLastError();
+}
+
+template <int BN, int STAGES, int PER_SM>
+cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
+  constexpr int BNH = BN / 2;
+  CUtensorMap ta, tb;
+  const int64_t lda = a_mn ? g.sak : g.sam;
+  const int64_t ldb = b_mn ? g.sbk : g.sbn;
+  const bool split = g.k_chunk > 0;
+  const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
+  const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
+  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
+                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false);
+  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
+                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false));
+  if (!ok) return cudaErrorNotSupported;
+  using S = Smem<BNH, STAGES>;
+  auto kern = gemm_tf32_pair<BN, STAGES, PER_SM>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  Tiles tl;
+  tl.bm = 2 * BM;
+  tl.m_tiles = (int)((g.M + 2 * BM - 1) / (2 * BM));
+  tl.n_tiles = (int)((g.N + BN - 1) / BN);
+  tl.per_z = tl.m_tiles * tl.n_tiles;
+  const int64_t total = (int64_t)tl.per_z * g.batch;
+  if (total > (1ll << 30)) return cudaErrorNotSupported;
+  tl.total = (int)total;
+  const int pairs = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
+                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, g.round_out, kchunk, tl, err);
 }
 
 int* error_word() { return tc_error_word(); }
@@ -360,6 +595,11 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void*, size_t, cudaStream
   // columns each): two independent TMA/MMA streams hide the ring refill
   // latency better than one deeper ring (measured on 2048..8192 matmuls and
   // the nanoGPT shapes, against BN = 128 / 256 with one CTA per SM).
+  // CTA pairs where the contraction is long enough for their halved operand
+  // traffic per SM to pay (measured: 4096^3 and 8192^3 +11-13%; K = 384 and
+  // the short split-K ranges gain nothing, so they keep single-CTA tiles).
+  const int64_t k_run = g.k_chunk > 0 ? g.k_chunk : g.K;
+  if (g.M >= 512 && g.N >= 256 && k_run >= 768) return launch_pair<128, 4, 2>(g, a_mn, b_mn, err, stream);
   if (g.N <= 64) return launch<64, 4, 2>(g, a_mn, b_mn, err, stream);
   return launch<128, 3, 2>(g, a_mn, b_mn, err, stream);
 }

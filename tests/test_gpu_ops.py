@@ -184,6 +184,11 @@ def test_dot_general_layouts(request, case, prec):
     ref = run(text, name, ins)[0]
     if prec == "fp32":
         np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-4)
+    elif case == "dot":
+        # a single 72-term dot product can cancel: bound the error by the sum
+        # of |a_k b_k|, the scale TF32 operand rounding errors accumulate on
+        scale = float(np.sum(np.abs(ins[0].astype(np.float64) * ins[1])))
+        assert abs(float(out) - float(ref)) <= (2e-3 if prec == "tf32" else 6e-3) * scale
     else:
         err = np.linalg.norm(out - ref) / np.linalg.norm(ref)
         assert err <= (2e-3 if prec == "tf32" else 6e-3), err
@@ -203,12 +208,13 @@ def test_large_gemm_shapes_match_oracle(tf32_session):
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
 
 
-@pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1)])
+@pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1),
+                                   (1000, 300, 800, 1), (520, 272, 1000, 2)])
 @pytest.mark.parametrize("at,bt", [(False, False), (False, True), (True, False), (True, True)])
 def test_gemm_tiles_and_layouts(tf32_session, shape, at, bt):
-    """Every tile width of the tcgen05 GEMM (N <= 64, 128, 256-wide tiles for
-    N % 256 == 0 or N >= 1024) with ragged M/N/K edges, K-major and MN-major
-    operands, batched."""
+    """Both tcgen05 GEMM kernels with ragged M/N/K edges, K-major and MN-major
+    operands, batched: single-CTA 128 x 64 / 128 x 128 tiles, and CTA-pair
+    256 x 128 tiles (M >= 512, N >= 256, K >= 768)."""
     M_, N_, K_, B_ = shape
     lead = [B_] if B_ > 1 else []
     sa = lead + ([K_, M_] if at else [M_, K_])
