@@ -5,10 +5,12 @@ Workload (default): the nanoGPT-style model of examples/nanoGPT/model.shf
 (6 layers, d_model 384, 6 heads, ctx 256, vocab 65), value-and-grad of the
 cross-entropy loss on shifted tokens, global batch 64 x 256 split over the
 ranks (strong scaling); lowered to StableHLO as Sheaf's JIT lowers it and run
-through libsheafb200's C ABI.  `--workload gpt2` selects the GPT-2-small
-shape (12 layers, d768, ctx 1024, vocab 50304, batch 8 per GPU, weak scaling).
+through libsheafb200's C ABI.  Other workloads: `gpt2` (GPT-2-small value-and-
+grad: 12 layers, d768, ctx 1024, vocab 50304, batch 8 per GPU, weak scaling),
+`nanogpt-fwd` (the forward alone), `mlp` (the 784-512-10 MLP value-and-grad,
+samples/s), `matmul` (op sweep, --size / --shape / --layout).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload W]
 
 Prints one JSON line (rank 0).  Device time: CUDA events on the session's
 stream around K steps, max over ranks.  Inputs (weights, activations) are far
@@ -39,7 +41,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
                    choices=["fp32", "tf32", "bf16"])
-    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "gpt2", "matmul"])
+    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "nanogpt-fwd", "gpt2", "mlp", "matmul"])
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
     p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
@@ -58,15 +60,50 @@ def env_rank():
 
 
 def workload(name, world, batch=0):
+    """(config, global batch, per-rank batch, scaling) of a GPT workload."""
     from sheaf_b200.programs import models as M
-    if name == "nanogpt":
+    if name in ("nanogpt", "nanogpt-fwd"):
         c = M.NANOGPT
         gb = batch or c.batch
         if gb % world:
             raise SystemExit(f"global batch {gb} is not divisible by {world} ranks")
         return c, gb, gb // world, "strong"
     c = M.GPT2_SMALL
-    return c, c.batch * world, c.batch, "weak"
+    b = batch or c.batch
+    return c, b * world, b, "weak"
+
+
+def program(args, world, rank):
+    """The timed program: lowered module, host inputs of this rank, the names of
+    the per-step data inputs, work units per step (all ranks), unit, scaling,
+    config, and whether the outputs are data-parallel means (value-and-grad)."""
+    from sheaf_b200.programs import models as M
+    if args.workload == "mlp":
+        gb = args.batch or 256
+        if gb % world:
+            raise SystemExit(f"global batch {gb} is not divisible by {world} ranks")
+        b = gb // world
+        low = M.mlp_vag(batch=b)
+        full = M.mlp_inputs(batch=gb, seed=0)
+        inp = dict(full)
+        inp["x"], inp["y"] = full["x"][rank * b:(rank + 1) * b], full["y"][rank * b:(rank + 1) * b]
+        cfg = {"workload": f"mlp value-and-grad {gb}x784", "model": "784-512-10 gelu, mse",
+               "global_batch": gb, "parallelism": f"dp{world}",
+               "l2": "operands fit in L2 (3.4 MB), no flush: launch-latency bound by design"}
+        return low, inp, ["x", "y"], gb, "samples/s", "strong", cfg, True
+    c, gb, b, scaling = workload(args.workload, world, args.batch)
+    inp = M.gpt_inputs(c, batch=gb, seed=0)
+    for n in ("x", "y", "idx"):
+        inp[n] = inp[n][rank * b:(rank + 1) * b]
+    fwd = args.workload == "nanogpt-fwd"
+    low = M.gpt_fwd(c, batch=b) if fwd else M.gpt_vag(c, batch=b)
+    kind = "forward" if fwd else "value-and-grad"
+    name = "gpt2-small" if args.workload == "gpt2" else "nanogpt"
+    cfg = {"workload": f"{name} {kind} {gb}x{c.T}",
+           "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
+           "global_batch": gb, "seq_len": c.T, "parallelism": f"dp{world}",
+           "l2": "inputs and activations exceed L2; no flush"}
+    return low, inp, (["idx"] if fwd else ["x", "y"]), gb * c.T, "tokens/s", scaling, cfg, not fwd
 
 
 class Clocks:
@@ -129,46 +166,46 @@ def peaks():
         return 6650.0, 1400.0, "fallback"
 
 
-def cpu_baseline(c, steps=2):
-    """The oracle port (numpy f32) on a bounded sample: 2 sequences of the same model."""
+def cpu_baseline(args, steps=2):
+    """The oracle port (numpy f32) timed on a bounded sample of the same workload:
+    the full MLP batch, or 2 sequences of the GPT model (GPT-2: 1 sequence of
+    256 tokens), same graph (value-and-grad or forward) as the device run."""
     from oracle.stablehlo_ref import evaluate, parse_module
     from sheaf_b200.programs import models as M
-    b = 2
-    low = M.gpt_vag(c, batch=b) if c.T <= 256 else M.gpt_vag(M.GPTConfig(c.n_layer, c.n_head, c.n_embd, c.block_size,
-                                                                         c.vocab_size, 1, 256), batch=1)
-    f = parse_module(low.text)[low.qualified]
-    inp = M.gpt_inputs(c, batch=b) if c.T <= 256 else None
-    if inp is None:
-        cc = M.GPTConfig(c.n_layer, c.n_head, c.n_embd, c.block_size, c.vocab_size, 1, 256)
-        inp = M.gpt_inputs(cc, batch=1)
-        b, T = 1, 256
+    if args.workload == "mlp":
+        low, inp, units, unit = M.mlp_vag(batch=256), M.mlp_inputs(batch=256), 256, "samples/s"
+        sample = "the full 256-sample batch"
     else:
-        T = c.T
+        c = workload(args.workload, 1)[0]
+        b, T = (2, c.T) if c.T <= 256 else (1, 256)
+        if T != c.T:
+            c = M.GPTConfig(c.n_layer, c.n_head, c.n_embd, c.block_size, c.vocab_size, 1, T)
+        low = M.gpt_fwd(c, batch=b) if args.workload == "nanogpt-fwd" else M.gpt_vag(c, batch=b)
+        inp, units, unit = M.gpt_inputs(c, batch=b), b * T, "tokens/s"
+        sample = f"{b} sequence(s) x {T} tokens of the same model"
+    f = parse_module(low.text)[low.qualified]
     ins = [inp[n] for n in low.arg_names]
     evaluate(f, ins, dtype=np.float32)
     t0 = time.time()
     for _ in range(steps):
         evaluate(f, ins, dtype=np.float32)
     dt = (time.time() - t0) / steps
-    return {"value": b * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{b} sequence(s) x {T} tokens of the same model per step, numpy float32 "
-                      f"interpretation of the same StableHLO (oracle/stablehlo_ref.py), mean of {steps} steps"}
+    return {"value": units / dt, "unit": unit, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample} per step, numpy float32 interpretation of the same StableHLO "
+                      f"(oracle/stablehlo_ref.py), mean of {steps} steps"}
 
 
 def run_reference(args):
     rank, _, world = env_rank()
     if rank != 0:
         return
-    from sheaf_b200.programs import models as M
-    c, gb, _, scaling = workload(args.workload, world)
-    res = cpu_baseline(c, steps=max(1, min(args.steps, 3)))
-    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
+    _, _, _, _, unit, scaling, cfg, _ = program(args, world, 0)
+    res = cpu_baseline(args, steps=max(1, min(args.steps, 3)))
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.workload} value-and-grad", "global_batch": gb, "seq_len": c.T,
-                       "parallelism": f"dp{world}"},
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
             "cpu_baseline": res,
-            "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "e2e": {"value": res["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's IREE llvm-cpu path cannot be built here (no Rust toolchain, no IREE); "
                     "this times the CPU restatement of the same graphs on the host cores"}
     print(json.dumps(line), flush=True)
@@ -190,10 +227,7 @@ def run_ours(args):
     from sheaf_b200.programs import models as M
     from sheaf_b200.session import B200Session, nccl_unique_id
     build.build()
-    c, gb, b, scaling = workload(args.workload, world, args.batch)
-    low = M.gpt_vag(c, batch=b)
-    inp = M.gpt_inputs(c, batch=gb, seed=0)
-    shard = {"x": inp["x"][rank * b:(rank + 1) * b], "y": inp["y"][rank * b:(rank + 1) * b]}
+    low, inp, data_names, units, unit, scaling, cfg, vag = program(args, world, rank)
     nid = None
     if world > 1:
         obj = [nccl_unique_id() if rank == 0 else None]
@@ -205,9 +239,9 @@ def run_ours(args):
     sess.load_stablehlo(low.text)
     load_s = time.time() - t0
     names = low.arg_names
-    bufs = [sess.buffer(shard[n] if n in shard else inp[n]) for n in names]
+    bufs = [sess.buffer(inp[n]) for n in names]
     q = low.qualified
-    reduce = ["mean"] * len(low.result_types) if world > 1 else None
+    reduce = ["mean"] * len(low.result_types) if (world > 1 and vag) else None
 
     def step(buffers):
         outs = sess.call_device(q, buffers, reduce)
@@ -238,30 +272,31 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    tokens = gb * c.T
-    value = tokens / (ms_step / 1e3)
+    value = units / (ms_step / 1e3)
 
-    # end to end: per step, H2D of the step's tokens from pinned host memory,
-    # the call, and the loss read back to the host (as Sheaf's VAG dispatch does)
+    # end to end: per step, H2D of the step's data inputs from pinned host
+    # memory, the call, and the first output (the loss; the logits of a
+    # forward) read back to the host (as Sheaf's VAG dispatch does for the loss)
     e2e = None
     if not args.no_e2e:
-        px = torch.from_numpy(shard["x"]).pin_memory().numpy()
-        py = torch.from_numpy(shard["y"]).pin_memory().numpy()
-        ix, iy = names.index("x"), names.index("y")
+        pinned = [torch.from_numpy(inp[n]).pin_memory().numpy() for n in data_names]
+        idx = [names.index(n) for n in data_names]
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        w0 = time.time()
         e0.record(stream)
+        d2h = 0
         for _ in range(args.steps):
-            bx, by = sess.buffer(px), sess.buffer(py)
+            staged = [sess.buffer(p) for p in pinned]
             bb = list(bufs)
-            bb[ix], bb[iy] = bx, by
+            for i, bx in zip(idx, staged):
+                bb[i] = bx
             outs = step(bb)
-            loss = outs[0].to_host()
+            first = outs[0].to_host()
+            d2h = int(np.asarray(first).nbytes)
             for o in outs:
                 o.release()
-            bx.release()
-            by.release()
+            for bx in staged:
+                bx.release()
         e1.record(stream)
         e1.synchronize()
         ems = e0.elapsed_time(e1)
@@ -269,9 +304,11 @@ def run_ours(args):
             t = torch.tensor([ems], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = float(t.item())
-        e2e = {"value": tokens / (ems / args.steps / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(px.nbytes + py.nbytes) * world, "d2h_bytes_per_step": 4 * world,
-               "steps_per_s": 1e3 / (ems / args.steps), "loss": float(loss)}
+        e2e = {"value": units / (ems / args.steps / 1e3), "unit": unit,
+               "h2d_bytes_per_step": int(sum(p.nbytes for p in pinned)) * world, "d2h_bytes_per_step": d2h * world,
+               "steps_per_s": 1e3 / (ems / args.steps)}
+        if vag:
+            e2e["loss"] = float(np.asarray(first))
 
     # per-kernel device time (separate pass of the same steps, CUDA events per launch)
     roof, launches, breakdown = None, None, None
@@ -307,21 +344,17 @@ def run_ours(args):
             roof = {"bound": "tensor", "kernel": "gemm (all dot_general launches)", "achieved": ach, "peak": tc,
                     "unit": "TFLOP/s", "frac": ach / tc, "traffic": None, "peak_source": src,
                     "flops_per_step": gflops, "launches_per_step": len(gem), "share_of_step": gms / allms}
-    result = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+    data = ("synthetic: seeded N(0,1) inputs, Xavier-uniform weights, one-hot labels" if args.workload == "mlp"
+            else "synthetic: seeded N(0,0.02) weights, uniform tokens")
+    result = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
               "warmup": args.warmup, "ms_per_step": ms_step, "steps_per_s": 1e3 / ms_step,
               "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-              "contraction": args.precision,
-              "data": "synthetic: seeded N(0,0.02) weights, uniform tokens",
-              "config": {"workload": f"{args.workload} value-and-grad 64x256" if args.workload == "nanogpt"
-                         else "gpt2-small value-and-grad 8x1024",
-                         "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
-                         "global_batch": gb, "seq_len": c.T, "parallelism": f"dp{world}",
-                         "l2": "inputs and activations exceed L2; no flush"},
+              "contraction": args.precision, "data": data, "config": cfg,
               "clocks": clk.summary(), "e2e": e2e, "gpu_launches": (launches or 0) * args.steps,
               "roofline": roof, "breakdown": breakdown, "module_load_s": load_s}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            result["cpu_baseline"] = cpu_baseline(c)
+            result["cpu_baseline"] = cpu_baseline(args)
         except Exception as ex:  # reported, not fatal
             result["cpu_baseline"] = {"error": str(ex)[:200]}
     if rank == 0:
