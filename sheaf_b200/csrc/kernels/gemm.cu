@@ -27,44 +27,55 @@ Split choose_split(const GemmArgs& g, int64_t tile_m, int64_t tile_n, int64_t gr
   return s;
 }
 
-bool tc_candidate(const GemmArgs& g, int precision) {
-  return precision == 1 && g.M >= 64 && g.N >= 32 && g.K >= 32 &&
-         ((g.sak == 1 && g.sam % 4 == 0) || (g.sam == 1 && g.sak % 4 == 0)) &&
-         ((g.sbk == 1 && g.sbn % 4 == 0) || (g.sbn == 1 && g.sbk % 4 == 0));
+}  // namespace
+
+size_t gemm_workspace(const GemmArgs& g, int precision) {
+  if (precision == 1) {
+    TcPlan p;
+    if (tc_plan(g, &p)) return p.splits > 1 ? (size_t)(p.splits * g.M * g.N) * sizeof(float) : 0;
+  }
+  Split s = choose_split(g, 128, 128, 8);
+  return s.splits > 1 ? (size_t)(s.splits * g.M * g.N) * sizeof(float) : 0;
+}
+
+namespace {
+
+// g split along K into `splits` partial products written to ws.
+GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws) {
+  GemmArgs run = g;
+  run.c = (float*)ws;
+  run.batch = splits;
+  run.k_chunk = k_chunk;
+  run.scb = g.M * g.N;
+  run.scm = g.N;
+  run.scn = 1;
+  run.round_out = 0;
+  return run;
 }
 
 }  // namespace
 
-size_t gemm_workspace(const GemmArgs& g, int precision) {
-  bool tc = tc_candidate(g, precision);
-  Split s = choose_split(g, 128, tc ? (g.N <= 64 ? 64 : 128) : 128, tc ? 32 : 8);
-  return s.splits > 1 ? (size_t)(s.splits * g.M * g.N) * sizeof(float) : 0;
-}
-
 cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
   *used_tc = false;
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
-  bool tc = tc_candidate(g, precision);
-  Split s = choose_split(g, 128, tc ? (g.N <= 64 ? 64 : 128) : 128, tc ? 32 : 8);
-  GemmArgs run = g;
-  bool split = s.splits > 1 && ws && ws_bytes >= (size_t)(s.splits * g.M * g.N) * sizeof(float);
-  if (split) {
-    run.c = (float*)ws;
-    run.batch = s.splits;
-    run.k_chunk = s.k_chunk;
-    run.scb = g.M * g.N;
-    run.scm = g.N;
-    run.scn = 1;
-    run.round_out = 0;
+  if (precision == 1) {
+    TcPlan p;
+    if (tc_plan(g, &p)) {
+      const bool split = p.splits > 1 && ws && ws_bytes >= (size_t)(p.splits * g.M * g.N) * sizeof(float);
+      cudaError_t e = gemm_tcgen05(split ? split_args(g, p.splits, p.k_chunk, ws) : g, p.cfg, stream);
+      if (e == cudaSuccess) {
+        *used_tc = true;
+        if (!split) return cudaSuccess;
+        return splitk_reduce((const float*)ws, g.c, p.splits, g.M, g.N, g.scm, g.round_out, stream);
+      }
+      if (e != cudaErrorNotSupported) return e;
+    }
   }
-  cudaError_t e = cudaErrorNotSupported;
-  if (tc) {
-    e = gemm_tcgen05(run, false, nullptr, 0, stream);
-    if (e == cudaSuccess) *used_tc = true;
-  }
-  if (e == cudaErrorNotSupported) e = gemm_simt(run, stream);
+  Split s = choose_split(g, 128, 128, 8);
+  const bool split = s.splits > 1 && ws && ws_bytes >= (size_t)(s.splits * g.M * g.N) * sizeof(float);
+  cudaError_t e = gemm_simt(split ? split_args(g, s.splits, s.k_chunk, ws) : g, stream);
   if (e != cudaSuccess || !split) return e;
-  return splitk_reduce((const float*)ws, g.c, s.splits, g.M, g.N, g.scm, g.round_out && *used_tc, stream);
+  return splitk_reduce((const float*)ws, g.c, s.splits, g.M, g.N, g.scm, 0, stream);
 }
 
 }  // namespace sb

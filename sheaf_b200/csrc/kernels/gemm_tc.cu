@@ -24,6 +24,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels.h"
@@ -48,7 +50,8 @@ struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int BYTES = 1024 /*alignment slack*/ + STAGES * STAGE + 256;
+  static constexpr int EPI_BYTES = 4 * 32 * 16 * 4;  // one 32 x 16 f32 staging slot per epilogue warp
+  static constexpr int BYTES = 1024 /*alignment slack*/ + STAGES * STAGE + EPI_BYTES + 256;
 };
 
 // Tile t -> (z, m, n).  Within a slice z, tiles run in groups of kGroupM
@@ -70,7 +73,42 @@ struct Tiles {
   }
 };
 
-template <int BN, int STAGES, int PER_SM>
+// Epilogue store of a 32-row x 16-column chunk held one row per lane (v =
+// columns col0..col0+15 of row row0 + lane).  The warp passes it through its
+// 2 KB shared-memory slot so that each store instruction writes 8 rows x 64
+// contiguous bytes instead of 32 rows x 16 bytes (the row-per-lane stores ran
+// at ~1.5 TB/s).  16-byte units are XOR-swizzled by (row >> 1) & 3: both the
+// row-wise writes and the column-wise reads are bank-conflict free.
+__device__ __forceinline__ void store_chunk(float* slot, const float* v, int lane, float* C, int row0, int col0, int M,
+                                            int N, long long ldc, bool vec) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    ((float4*)(slot + lane * 16))[u ^ ((lane >> 1) & 3)] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  __syncwarp();
+  const int sub = lane >> 2, u = lane & 3, col = col0 + 4 * u;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + sub, row = row0 + r;
+    const float4 x = ((const float4*)(slot + r * 16))[u ^ ((r >> 1) & 3)];
+    if (row < M) {
+      float* dst = C + (long long)row * ldc + col;
+      if (vec && col + 4 <= N) {
+        *(float4*)dst = x;
+      } else {
+        if (col < N) dst[0] = x.x;
+        if (col + 1 < N) dst[1] = x.y;
+        if (col + 2 < N) dst[2] = x.z;
+        if (col + 3 < N) dst[3] = x.w;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// TMEM allocations are powers of two of at least 32 columns.
+__host__ __device__ constexpr uint32_t tmem_cols(int n) { return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u; }
+
+template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                       int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
@@ -80,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);
+  float* epi = (float*)(smem + STAGES * S::STAGE);
+  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE + S::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;    // [2]: epilogue -> MMA (128 arrivals)
@@ -89,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ktiles_all = (K + BK - 1) / BK;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -161,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
         int z, m0, n0, kt0, kt1, zab;
         tl.at(t, &z, &m0, &n0, BN);
         krange(z, &kt0, &kt1, &zab);
-        const int b = j & 1, use = j >> 1;
+        const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
         if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
@@ -196,11 +235,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       int z, m0, n0, kt0, kt1, zab;
       tl.at(t, &z, &m0, &n0, BN);
       krange(z, &kt0, &kt1, &zab);
-      const int b = j & 1, use = j >> 1;
+      const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
       fence_after();
-      const int row = m0 + quad * 32 + lane;
-      float* crow = C + (long long)z * scb + (long long)row * ldc;
+      const int row0 = m0 + quad * 32;
+      float* cz = C + (long long)z * scb;
+      const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
+      float* slot = epi + (warp - 2) * 512;
       const uint32_t acc = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
@@ -214,18 +255,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
         }
-        if (row < M) {
-          const int col0 = n0 + c;
-          if (col0 + 16 <= N && (ldc & 3) == 0 && (((uintptr_t)(crow + col0)) & 15) == 0) {
-            float4* dst = (float4*)(crow + col0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-              if (col0 + q < N) crow[col0 + q] = v[q];
-          }
-        }
+        store_chunk(slot, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
       }
       fence_before();
       mbar_arrive(&acc_empty[b]);
@@ -248,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 // (BN = 256) fewer operand bytes per FLOP than the 128 x 128 single-CTA tile.
 // Completion is signalled to both CTAs with one non-multicast commit each; the
 // peer's epilogue releases an accumulator with a remote mbarrier arrive.
-template <int BN, int STAGES, int PER_SM>
+template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                    int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
@@ -259,7 +289,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);  // leader: both CTAs' bytes
+  float* epi = (float*)(smem + STAGES * S::STAGE);
+  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE + S::EPI_BYTES);  // leader: both CTAs' bytes
   uint64_t* empty = full + STAGES;                            // each CTA: slot free
   uint64_t* acc_full = empty + STAGES;                        // each CTA: accumulator ready
   uint64_t* acc_empty = acc_full + 2;                         // leader: 256 arrivals
@@ -271,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   const bool leader = rank == 0;
   const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
   const int ktiles_all = (K + BK - 1) / BK;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -349,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
         int z, m0, n0, kt0, kt1, zab;
         tl.at(t, &z, &m0, &n0, BN);
         krange(z, &kt0, &kt1, &zab);
-        const int b = j & 1, use = j >> 1;
+        const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
         if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
@@ -381,11 +412,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       int z, m0, n0, kt0, kt1, zab;
       tl.at(t, &z, &m0, &n0, BN);
       krange(z, &kt0, &kt1, &zab);
-      const int b = j & 1, use = j >> 1;
+      const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
       fence_after();
-      const int row = m0 + (int)rank * BM + quad * 32 + lane;
-      float* crow = C + (long long)z * scb + (long long)row * ldc;
+      const int row0 = m0 + (int)rank * BM + quad * 32;
+      float* cz = C + (long long)z * scb;
+      const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
+      float* slot = epi + (warp - 2) * 512;
       const uint32_t accp = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
@@ -399,18 +432,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
         }
-        if (row < M) {
-          const int col0 = n0 + c;
-          if (col0 + 16 <= N && (ldc & 3) == 0 && (((uintptr_t)(crow + col0)) & 15) == 0) {
-            float4* dst = (float4*)(crow + col0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-              if (col0 + q < N) crow[col0 + q] = v[q];
-          }
-        }
+        store_chunk(slot, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
       }
       fence_before();
       mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
@@ -444,7 +466,7 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int STAGES, int PER_SM>
+template <int BN, int STAGES, int PER_SM, int ACC>
 cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
   CUtensorMap ta, tb;
   const int64_t lda = a_mn ? g.sak : g.sam;
@@ -459,7 +481,7 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
                    : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false));
   if (!ok) return cudaErrorNotSupported;
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tf32_tcgen05<BN, STAGES, PER_SM>;
+  auto kern = gemm_tf32_tcgen05<BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -480,7 +502,7 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   return cudaGetLastError();
 }
 
-template <int BN, int STAGES, int PER_SM>
+template <int BN, int STAGES, int PER_SM, int ACC>
 cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
   constexpr int BNH = BN / 2;
   CUtensorMap ta, tb;
@@ -495,7 +517,7 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
                    : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false));
   if (!ok) return cudaErrorNotSupported;
   using S = Smem<BNH, STAGES>;
-  auto kern = gemm_tf32_pair<BN, STAGES, PER_SM>;
+  auto kern = gemm_tf32_pair<BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -573,35 +595,115 @@ int* tc_error_word() {
   return p;
 }
 
-size_t gemm_tcgen05_workspace(const GemmArgs&, bool) { return 0; }
 
-cudaError_t gemm_tcgen05(const GemmArgs& g, bool bf16, void*, size_t, cudaStream_t stream) {
-  if (bf16) return cudaErrorNotSupported;
-  if (g.M < 64 || g.N < 32 || g.K < 32 || g.batch < 1 || g.batch > 65535) return cudaErrorNotSupported;
-  if (g.M > (1ll << 30) || g.N > (1ll << 30) || g.K > (1ll << 30)) return cudaErrorNotSupported;
-  if (g.scn != 1 || g.scm < g.N) return cudaErrorNotSupported;
+namespace {
+
+// Kernel configurations: single-CTA 128 x BN tiles or CTA-pair 256 x BN
+// tiles; ACC TMEM accumulators per CTA; PER_SM resident CTAs per SM (shared
+// memory and TMEM are sized so that PER_SM CTAs fit: <= 512 TMEM columns).
+struct TcCfg {
+  bool pair;
+  int bn, acc, per_sm, stages;
+};
+constexpr TcCfg kCfgs[] = {
+    {false, 64, 2, 2, 4},   // 0
+    {false, 128, 2, 2, 3},  // 1
+    {true, 128, 2, 2, 4},   // 2
+    {true, 192, 1, 2, 3},   // 3
+    {true, 256, 1, 2, 3},   // 4
+};
+constexpr int kNumCfgs = (int)(sizeof(kCfgs) / sizeof(kCfgs[0]));
+
+// Cost model (microseconds) of one launch: waves of tile-units times the time
+// of one unit, whose K steps are bound by the operand bytes an SM receives
+// from L2 (~110 GB/s per SM, shared by the CTAs on it) or by the TF32 tensor
+// rate (~5.5 TFLOP/s per SM), plus pipeline fill and, with one accumulator, the
+// epilogue.  Split-K adds the partial-sum reduction.  The constants are from
+// measurements on B200 (matmul 2048..8192, the nanoGPT and GPT-2 shapes).
+constexpr double kSmBytesPerUs = 110e3, kSmFlopsPerUs = 5.5e6, kFillUs = 2.0, kEpiBytesPerUs = 50e3;
+constexpr double kHbmBytesPerUs = 5e6, kReduceLaunchUs = 4.0;
+
+double est_us(const TcCfg& c, int64_t M, int64_t N, int64_t K, int64_t units_z, int sms) {
+  const int tm = c.pair ? 256 : 128;
+  const double tiles = (double)((M + tm - 1) / tm) * (double)((N + c.bn - 1) / c.bn) * (double)units_z;
+  const double slots = c.pair ? c.per_sm * sms / 2.0 : (double)c.per_sm * sms;
+  const double waves = std::ceil(tiles / slots);
+  const double ksteps = std::ceil((double)K / BK);
+  const int bcols = c.pair ? c.bn / 2 : c.bn;
+  const double t_mem = (128.0 + bcols) * 128.0 / (kSmBytesPerUs / c.per_sm);
+  const double t_mma = 2.0 * 128 * c.bn * BK / (kSmFlopsPerUs / c.per_sm);
+  const double t_epi = 128.0 * c.bn * 4 / kEpiBytesPerUs;
+  const double unit = kFillUs + ksteps * std::max(t_mem, t_mma) + (c.acc == 1 ? t_epi : 0.0);
+  return waves * unit + (c.acc == 2 ? t_epi : 0.0);
+}
+
+bool tc_layout(const GemmArgs& g, bool* a_mn, bool* b_mn) {
+  if (g.M < 64 || g.N < 32 || g.K < 32 || g.batch < 1 || g.batch > 65535) return false;
+  if (g.M > (1ll << 30) || g.N > (1ll << 30) || g.K > (1ll << 30)) return false;
+  if (g.scn != 1 || g.scm < g.N) return false;
+  if (g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) *a_mn = false;
+  else if (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M) *a_mn = true;
+  else return false;
+  if (g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) *b_mn = false;
+  else if (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N) *b_mn = true;
+  else return false;
+  if ((((uintptr_t)g.a) & 15) || (((uintptr_t)g.b) & 15)) return false;
+  if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return false;
+  return true;
+}
+
+}  // namespace
+
+bool tc_plan(const GemmArgs& g, TcPlan* p) {
   bool a_mn, b_mn;
-  if (g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) a_mn = false;
-  else if (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M) a_mn = true;
-  else return cudaErrorNotSupported;
-  if (g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) b_mn = false;
-  else if (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N) b_mn = true;
-  else return cudaErrorNotSupported;
-  if ((((uintptr_t)g.a) & 15) || (((uintptr_t)g.b) & 15)) return cudaErrorNotSupported;
-  if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return cudaErrorNotSupported;
+  if (!tc_layout(g, &a_mn, &b_mn)) return false;
+  const int sms = sm_count();
+  // SHEAF_B200_GEMM_CONFIG=n forces configuration n (0..kNumCfgs-1) for every
+  // tensor-core GEMM (the split factor is still chosen for it): used by the
+  // tests to run every kernel variant on the same shapes.
+  int forced = -1;
+  if (const char* e = std::getenv("SHEAF_B200_GEMM_CONFIG")) {
+    forced = std::atoi(e);
+    if (forced < 0 || forced >= kNumCfgs) forced = -1;
+  }
+  double best = 1e300;
+  for (int ci = 0; ci < kNumCfgs; ++ci) {
+    const TcCfg& c = kCfgs[ci];
+    if (forced >= 0 && ci != forced) continue;
+    if (forced < 0 && c.pair && g.M <= 128) continue;
+    if (forced < 0 && c.bn > 64 && g.N <= 32) continue;
+    // split-K candidates: single GEMMs only, at least 256 of K per split
+    const int64_t max_s = g.batch == 1 ? std::max<int64_t>(1, g.K / 256) : 1;
+    for (int64_t s = 1; s <= std::min<int64_t>(max_s, 64); s = s < 4 ? s + 1 : s * 3 / 2) {
+      int64_t chunk = (g.K + s - 1) / s;
+      chunk = (chunk + BK - 1) / BK * BK;
+      const int64_t splits = (g.K + chunk - 1) / chunk;
+      double t = est_us(c, g.M, g.N, chunk, splits * g.batch, sms);
+      if (splits > 1) t += kReduceLaunchUs + (double)splits * g.M * g.N * 8.0 / kHbmBytesPerUs;
+      if (t < best * 0.97 || (t < best && splits <= p->splits)) {  // prefer fewer splits on near-ties
+        best = t;
+        p->cfg = ci;
+        p->splits = splits;
+        p->k_chunk = splits > 1 ? chunk : 0;
+      }
+    }
+  }
+  return p->cfg >= 0;
+}
+
+cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) {
+  bool a_mn, b_mn;
+  if (!tc_layout(g, &a_mn, &b_mn)) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
-  // Two persistent CTAs per SM (~97 KB of shared memory and 2 x BN TMEM
-  // columns each): two independent TMA/MMA streams hide the ring refill
-  // latency better than one deeper ring (measured on 2048..8192 matmuls and
-  // the nanoGPT shapes, against BN = 128 / 256 with one CTA per SM).
-  // CTA pairs where the contraction is long enough for their halved operand
-  // traffic per SM to pay (measured: 4096^3 and 8192^3 +11-13%; K = 384 and
-  // the short split-K ranges gain nothing, so they keep single-CTA tiles).
-  const int64_t k_run = g.k_chunk > 0 ? g.k_chunk : g.K;
-  if (g.M >= 512 && g.N >= 256 && k_run >= 768) return launch_pair<128, 4, 2>(g, a_mn, b_mn, err, stream);
-  if (g.N <= 64) return launch<64, 4, 2>(g, a_mn, b_mn, err, stream);
-  return launch<128, 3, 2>(g, a_mn, b_mn, err, stream);
+  switch (cfg) {
+    case 0: return launch<64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 1: return launch<128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 2: return launch_pair<128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 3: return launch_pair<192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+    case 4: return launch_pair<256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+  }
+  return cudaErrorNotSupported;
 }
 
 int gemm_tcgen05_error() {

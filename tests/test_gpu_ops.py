@@ -208,13 +208,17 @@ def test_large_gemm_shapes_match_oracle(tf32_session):
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
 
 
+@pytest.mark.parametrize("config", [None, 0, 1, 2, 3, 4])
 @pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1),
-                                   (1000, 300, 800, 1), (520, 272, 1000, 2)])
+                                   (1000, 300, 800, 1), (520, 272, 1000, 2), (384, 384, 4096, 1)])
 @pytest.mark.parametrize("at,bt", [(False, False), (False, True), (True, False), (True, True)])
-def test_gemm_tiles_and_layouts(tf32_session, shape, at, bt):
-    """Both tcgen05 GEMM kernels with ragged M/N/K edges, K-major and MN-major
-    operands, batched: single-CTA 128 x 64 / 128 x 128 tiles, and CTA-pair
-    256 x 128 tiles (M >= 512, N >= 256, K >= 768)."""
+def test_gemm_tiles_and_layouts(tf32_session, monkeypatch, config, shape, at, bt):
+    """Every tcgen05 GEMM configuration (SHEAF_B200_GEMM_CONFIG: single-CTA
+    128 x 64 / 128 x 128 tiles with two TMEM accumulators, CTA-pair 256 x 128 /
+    256 x 192 / 256 x 256 tiles) and the cost-model choice (None), with ragged
+    M/N/K edges, K-major and MN-major operands, batched, and split-K."""
+    if config is not None:
+        monkeypatch.setenv("SHEAF_B200_GEMM_CONFIG", str(config))
     M_, N_, K_, B_ = shape
     lead = [B_] if B_ > 1 else []
     sa = lead + ([K_, M_] if at else [M_, K_])
