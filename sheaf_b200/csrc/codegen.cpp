@@ -618,13 +618,14 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
       if (j == 0) loopb << "      const " << c.idx << " q0 = rk_;\n";
       else loopb << "      const " << c.idx << " q" << j << " = rk_ % " << ish[rd[j]] << "; rk_ /= " << ish[rd[j]] << ";\n";
     }
-    const int64_t target = 148 * 2048;
+    // a block covers 32 float4 column groups x 8 row lanes; enough splits of
+    // the reduced range for ~148 x 1536 threads, at least 32 rows per split
     const int64_t O4 = O / 4;
-    if (O4 < target && R >= 64) {
-      splits = std::max<int64_t>(1, std::min<int64_t>((target + O4 - 1) / O4, R / 32));
-      chunk = (R + splits - 1) / splits;
-      splits = (R + chunk - 1) / chunk;
-    }
+    const int64_t blocks_x = (O4 + 31) / 32;
+    const int64_t want = (148 * 6 + blocks_x - 1) / blocks_x;
+    splits = std::max<int64_t>(1, std::min<int64_t>(want, R / 32));
+    chunk = (R + splits - 1) / splits;
+    splits = (R + chunk - 1) / chunk;
   }
   std::string lanes[4];
   c.indent = 3;
@@ -674,23 +675,30 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
   } else {
     const int64_t O4 = O / 4;
     if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
-    src_ << "  for (" << c.idx << " o4 = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o4 < " << O4
-         << "; o4 += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+    src_ << "  __shared__ float4 part_[8][32];\n";
+    src_ << "  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;\n";
+    src_ << "  const " << c.idx << " o4 = (" << c.idx << ")blockIdx.x * 32 + cx;\n";
+    src_ << "  float a0 = " << ident << ", a1 = " << ident << ", a2 = " << ident << ", a3 = " << ident << ";\n";
+    src_ << "  if (o4 < " << O4 << ") {\n";
     src_ << pre.str();
-    src_ << "    float a0 = " << ident << ", a1 = " << ident << ", a2 = " << ident << ", a3 = " << ident << ";\n";
     src_ << "    const " << c.idx << " k0 = (" << c.idx << ")blockIdx.y * " << chunk << ";\n";
     src_ << "    const " << c.idx << " k1 = min((" << c.idx << ")" << R << ", k0 + (" << c.idx << ")" << chunk << ");\n";
-    src_ << "    for (" << c.idx << " k = k0; k < k1; ++k) {\n" << loop_code;
+    src_ << "#pragma unroll 4\n    for (" << c.idx << " k = k0 + ry; k < k1; k += 8) {\n" << loop_code;
     for (int j = 0; j < 4; ++j) src_ << "      a" << j << " = " << combine("a" + std::to_string(j), lanes[j]) << ";\n";
-    src_ << "    }\n";
+    src_ << "    }\n  }\n";
+    src_ << "  part_[ry][cx] = make_float4(a0, a1, a2, a3);\n  __syncthreads();\n";
+    src_ << "  if (ry == 0 && o4 < " << O4 << ") {\n";
+    src_ << "    for (int j = 1; j < 8; ++j) {\n      const float4 q = part_[j][cx];\n";
+    src_ << "      a0 = " << combine("a0", "q.x") << "; a1 = " << combine("a1", "q.y") << "; a2 = " << combine("a2", "q.z")
+         << "; a3 = " << combine("a3", "q.w") << ";\n    }\n";
     if (splits > 1) {
       src_ << "    *(float4*)(S + (" << c.idx << ")blockIdx.y * " << O << " + o4 * 4) = make_float4(a0, a1, a2, a3);\n  }\n}\n\n";
     } else {
-      src_ << "    {\n" << init_code << "    *(float4*)(O + o4 * 4) = make_float4(" << store(root, combine("a0", init.name))
-           << ", " << store(root, combine("a1", init.name)) << ", " << store(root, combine("a2", init.name)) << ", "
-           << store(root, combine("a3", init.name)) << ");\n    }\n  }\n}\n\n";
+      src_ << init_code << "    *(float4*)(O + o4 * 4) = make_float4(" << store(root, combine("a0", init.name)) << ", "
+           << store(root, combine("a1", init.name)) << ", " << store(root, combine("a2", init.name)) << ", "
+           << store(root, combine("a3", init.name)) << ");\n  }\n}\n\n";
     }
-    st->grid = std::max<int64_t>(1, std::min<int64_t>((O4 + kThreads - 1) / kThreads, kMaxGrid));
+    st->grid = (O4 + 31) / 32;
     st->grid_y = splits;
     if (splits > 1) {
       std::string fin = name + "f";
@@ -704,15 +712,27 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
       }
       src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
       src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
-      src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
-           << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
-      src_ << "    float acc = " << ident << ";\n";
-      src_ << "    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = "
-           << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
-      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+      // same block shape as the main kernel: 8 row lanes take every 8th split
+      src_ << "  __shared__ float4 part_[8][32];\n";
+      src_ << "  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;\n";
+      src_ << "  const " << c.idx << " o4 = (" << c.idx << ")blockIdx.x * 32 + cx;\n";
+      src_ << "  float a0 = " << ident << ", a1 = " << ident << ", a2 = " << ident << ", a3 = " << ident << ";\n";
+      src_ << "  if (o4 < " << O4 << ") {\n";
+      src_ << "#pragma unroll 4\n    for (" << c.idx << " s = ry; s < " << splits << "; s += 8) {\n";
+      src_ << "      const float4 q = *(const float4*)(S + s * " << O << " + o4 * 4);\n";
+      src_ << "      a0 = " << combine("a0", "q.x") << "; a1 = " << combine("a1", "q.y") << "; a2 = "
+           << combine("a2", "q.z") << "; a3 = " << combine("a3", "q.w") << ";\n    }\n  }\n";
+      src_ << "  part_[ry][cx] = make_float4(a0, a1, a2, a3);\n  __syncthreads();\n";
+      src_ << "  if (ry == 0 && o4 < " << O4 << ") {\n";
+      src_ << "    for (int j = 1; j < 8; ++j) {\n      const float4 q = part_[j][cx];\n";
+      src_ << "      a0 = " << combine("a0", "q.x") << "; a1 = " << combine("a1", "q.y") << "; a2 = "
+           << combine("a2", "q.z") << "; a3 = " << combine("a3", "q.w") << ";\n    }\n";
+      src_ << init_code << "    *(float4*)(O + o4 * 4) = make_float4(" << store(root, combine("a0", init.name)) << ", "
+           << store(root, combine("a1", init.name)) << ", " << store(root, combine("a2", init.name)) << ", "
+           << store(root, combine("a3", init.name)) << ");\n  }\n}\n\n";
       names_.push_back(fin);
       st->finish_kernel = fin;
-      st->finish_grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
+      st->finish_grid = (O4 + 31) / 32;
       st->splits = splits;
       st->scratch_elems = splits * O;
     }
@@ -801,10 +821,18 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
   if (trailing && R <= 4096) mode = 0;
   else if (trailing) mode = 1;
   else mode = 2;
+  if (mode == 1 && O < 2 * 148 && R >= 2 * 8192) {
+    // few long rows (a merged full reduction): blocks split each row, a
+    // finish kernel combines the partials in split order
+    splits = std::min<int64_t>((148 * 4 + O - 1) / O, R / 4096);
+    splits = std::max<int64_t>(splits, 1);
+    chunk = (R + splits - 1) / splits;
+    splits = (R + chunk - 1) / chunk;
+  }
   if (mode == 2) {
     int64_t target = 148 * 2048;
     if (O < target && R >= 64) {
-      splits = std::min<int64_t>((target + O - 1) / O, R / 32);
+      splits = std::min<int64_t>((target + O - 1) / O, R / 8);
       splits = std::max<int64_t>(splits, 1);
       chunk = (R + splits - 1) / splits;
       splits = (R + chunk - 1) / chunk;
@@ -826,7 +854,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
   std::string init_code = c.body.str();
   c.memo = std::move(saved_memo);
 
-  src_ << header(name, c, mode == 2 && splits > 1 ? 1 : 0);
+  src_ << header(name, c, splits > 1 ? 1 : 0);
   src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
   if (mode == 0) {
     src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
@@ -841,12 +869,15 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
   } else if (mode == 1) {
+    if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
     src_ << "  __shared__ float red_[" << kThreads / 32 << "];\n";
     src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+    src_ << "  const " << c.idx << " k0 = (" << c.idx << ")blockIdx.y * " << chunk << ";\n";
+    src_ << "  const " << c.idx << " k1 = min((" << c.idx << ")" << R << ", k0 + (" << c.idx << ")" << chunk << ");\n";
     src_ << "  for (" << c.idx << " o = blockIdx.x; o < " << O << "; o += gridDim.x) {\n";
     src_ << pre.str();
     src_ << "    float acc = " << ident << ";\n";
-    src_ << "    for (" << c.idx << " k = threadIdx.x; k < " << R << "; k += " << kThreads << ") {\n" << loop_code;
+    src_ << "#pragma unroll 4\n    for (" << c.idx << " k = k0 + threadIdx.x; k < k1; k += " << kThreads << ") {\n" << loop_code;
     src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
     src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
@@ -854,9 +885,14 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "    if (warp == 0) {\n      acc = lane < " << kThreads / 32 << " ? red_[lane] : " << ident << ";\n";
     src_ << "      for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
-    src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name)) << ";\n      }\n    }\n";
+    if (splits > 1)
+      src_ << "      if (lane == 0) S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n    }\n";
+    else
+      src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
+           << ";\n      }\n    }\n";
     src_ << "    __syncthreads();\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>(O, kMaxGrid));
+    st->grid_y = splits;
   } else {
     if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
     src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
@@ -865,7 +901,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "    float acc = " << ident << ";\n";
     src_ << "    const " << c.idx << " k0 = (" << c.idx << ")blockIdx.y * " << chunk << ";\n";
     src_ << "    const " << c.idx << " k1 = min((" << c.idx << ")" << R << ", k0 + (" << c.idx << ")" << chunk << ");\n";
-    src_ << "    for (" << c.idx << " k = k0; k < k1; ++k) {\n" << loop_code;
+    src_ << "#pragma unroll 4\n    for (" << c.idx << " k = k0; k < k1; ++k) {\n" << loop_code;
     src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
     if (splits > 1) {
       src_ << "    S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n  }\n}\n\n";
@@ -874,7 +910,9 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     }
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
     st->grid_y = splits;
-    if (splits > 1) {
+  }
+  if (splits > 1) {
+    {
       std::string fin = name + "f";
       src_ << "struct __align__(8) A_" << fin << " { const void* p[" << c.leaves.size() + 2 << "]; };\n";
       src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
@@ -886,14 +924,35 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
       }
       src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
       src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
-      src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
-           << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
-      src_ << "    float acc = " << ident << ";\n";
-      src_ << "    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = " << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
-      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+      const bool block_per_output = O <= 2 * 148;
+      if (block_per_output) {
+        // one block per output: threads take the partials of a strided
+        // subset of splits, then a fixed shuffle/shared-memory tree
+        src_ << "  __shared__ float red_[" << kThreads / 32 << "];\n";
+        src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+        src_ << "  for (" << c.idx << " o = blockIdx.x; o < " << O << "; o += gridDim.x) {\n";
+        src_ << "    float acc = " << ident << ";\n";
+        src_ << "#pragma unroll 4\n    for (" << c.idx << " s = threadIdx.x; s < " << splits << "; s += " << kThreads
+             << ") acc = " << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
+        src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+             << combine("acc", "y_") << "; }\n";
+        src_ << "    if (lane == 0) red_[warp] = acc;\n    __syncthreads();\n";
+        src_ << "    if (warp == 0) {\n      acc = lane < " << kThreads / 32 << " ? red_[lane] : " << ident << ";\n";
+        src_ << "      for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+             << combine("acc", "y_") << "; }\n";
+        src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
+             << ";\n      }\n    }\n    __syncthreads();\n  }\n}\n\n";
+      } else {
+        src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
+             << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+        src_ << "    float acc = " << ident << ";\n";
+        src_ << "#pragma unroll 4\n    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = "
+             << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
+        src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+      }
       names_.push_back(fin);
       st->finish_kernel = fin;
-      st->finish_grid = st->grid;
+      st->finish_grid = block_per_output ? O : std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
       st->splits = splits;
       st->scratch_elems = splits * O;
     }

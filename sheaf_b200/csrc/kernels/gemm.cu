@@ -2,6 +2,8 @@
 // layouts allow it, CUDA-core path otherwise; split-K for problems whose output
 // has too few tiles to fill 148 SMs (e.g. weight gradients of shape D x D with
 // the whole token count as the contraction).
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace sb {
@@ -27,12 +29,110 @@ Split choose_split(const GemmArgs& g, int64_t tile_m, int64_t tile_n, int64_t gr
   return s;
 }
 
+// An operand whose unit-stride (inner) dimension is fine but whose row stride
+// or base address is not 16-byte aligned (e.g. a vocabulary of 65 as the
+// inner extent) is copied to a dense buffer with the row stride rounded up to
+// 4 floats, keeping its major-ness; the tensor maps use the logical extents,
+// so the padding columns are never read.
+struct PadOp {
+  bool on = false;
+  int64_t rows = 0, inner = 0, s_row = 0, s_batch = 0, ld = 0;
+  size_t elems = 0;
+};
+
+struct Padding {
+  PadOp a, b;
+  TcPlan plan;
+  size_t a_off = 0, b_off = 0, split_bytes = 0, total = 0;
+};
+
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Describes operand (rows x inner per batch) with strides (s_row, 1) and
+// batch stride s_batch as a padded dense copy; the padded view has row stride
+// ld and batch stride rows * ld.
+PadOp pad_op(int64_t batch, int64_t rows, int64_t inner, int64_t s_row, int64_t s_batch) {
+  PadOp o;
+  o.on = true;
+  o.rows = rows;
+  o.inner = inner;
+  o.s_row = s_row;
+  o.s_batch = s_batch;
+  o.ld = (inner + 3) / 4 * 4;
+  o.elems = (size_t)(batch * rows * o.ld);
+  return o;
+}
+
+// The tensor-core plan of g, padding A and/or B when only their row strides or
+// base addresses keep g off the tensor cores.  *view is g with the padded
+// operands at (fake, aligned) workspace offsets; false when no padding helps.
+bool pad_plan(const GemmArgs& g, Padding* pd, GemmArgs* view) {
+  if (g.batch > 1 && (g.sab < 0 || g.sbb < 0)) return false;
+  GemmArgs v = g;
+  // A: K-major (sak == 1, rows M) or M-major (sam == 1, rows K)
+  const bool a_ok = ((uintptr_t)g.a & 15) == 0 &&
+                    ((g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) || (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M)) &&
+                    (g.batch == 1 || g.sab % 4 == 0);
+  if (!a_ok) {
+    if (g.sak == 1 && g.sam >= g.K) pd->a = pad_op(g.batch, g.M, g.K, g.sam, g.sab);
+    else if (g.sam == 1 && g.sak >= g.M) pd->a = pad_op(g.batch, g.K, g.M, g.sak, g.sab);
+    else return false;
+    if (g.sak == 1) { v.sam = pd->a.ld; v.sak = 1; }
+    else { v.sak = pd->a.ld; v.sam = 1; }
+    v.sab = pd->a.rows * pd->a.ld;
+  }
+  const bool b_ok = ((uintptr_t)g.b & 15) == 0 &&
+                    ((g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) || (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N)) &&
+                    (g.batch == 1 || g.sbb % 4 == 0);
+  if (!b_ok) {
+    if (g.sbk == 1 && g.sbn >= g.K) pd->b = pad_op(g.batch, g.N, g.K, g.sbn, g.sbb);
+    else if (g.sbn == 1 && g.sbk >= g.N) pd->b = pad_op(g.batch, g.K, g.N, g.sbk, g.sbb);
+    else return false;
+    if (g.sbk == 1) { v.sbn = pd->b.ld; v.sbk = 1; }
+    else { v.sbk = pd->b.ld; v.sbn = 1; }
+    v.sbb = pd->b.rows * pd->b.ld;
+  }
+  if (!pd->a.on && !pd->b.on) return false;
+  // plan with aligned stand-in addresses; the real ones are set at run time
+  if (pd->a.on) v.a = reinterpret_cast<const float*>(uintptr_t(1) << 12);
+  if (pd->b.on) v.b = reinterpret_cast<const float*>(uintptr_t(1) << 12);
+  if (!tc_plan(v, &pd->plan)) return false;
+  pd->split_bytes = pd->plan.splits > 1 ? align256((size_t)(pd->plan.splits * g.M * g.N) * sizeof(float)) : 0;
+  pd->a_off = pd->split_bytes;
+  pd->b_off = pd->a_off + (pd->a.on ? align256(pd->a.elems * sizeof(float)) : 0);
+  pd->total = pd->b_off + (pd->b.on ? align256(pd->b.elems * sizeof(float)) : 0);
+  *view = v;
+  return true;
+}
+
+__global__ void pad_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t batch, int64_t rows,
+                                int64_t inner, int64_t s_row, int64_t s_batch, int64_t ld) {
+  const int64_t n = batch * rows * inner;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % inner;
+    const int64_t r = (i / inner) % rows;
+    const int64_t b = i / (inner * rows);
+    dst[(b * rows + r) * ld + c] = src[b * s_batch + r * s_row + c];
+  }
+}
+
+cudaError_t pad_copy(const float* src, float* dst, int64_t batch, const PadOp& o, cudaStream_t stream) {
+  const int64_t n = batch * o.rows * o.inner;
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
+  pad_copy_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, dst, batch, o.rows, o.inner, o.s_row, o.s_batch, o.ld);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t gemm_workspace(const GemmArgs& g, int precision) {
   if (precision == 1) {
     TcPlan p;
     if (tc_plan(g, &p)) return p.splits > 1 ? (size_t)(p.splits * g.M * g.N) * sizeof(float) : 0;
+    Padding pd;
+    GemmArgs v;
+    if (pad_plan(g, &pd, &v)) return pd.total;
   }
   Split s = choose_split(g, 128, 128, 8);
   return s.splits > 1 ? (size_t)(s.splits * g.M * g.N) * sizeof(float) : 0;
@@ -69,6 +169,28 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
         return splitk_reduce((const float*)ws, g.c, p.splits, g.M, g.N, g.scm, g.round_out, stream);
       }
       if (e != cudaErrorNotSupported) return e;
+    } else {
+      Padding pd;
+      GemmArgs v;
+      if (pad_plan(g, &pd, &v) && ws && ws_bytes >= pd.total) {
+        char* base = (char*)ws;
+        if (pd.a.on) {
+          v.a = (const float*)(base + pd.a_off);
+          cudaError_t e = pad_copy(g.a, (float*)v.a, g.batch, pd.a, stream);
+          if (e != cudaSuccess) return e;
+        }
+        if (pd.b.on) {
+          v.b = (const float*)(base + pd.b_off);
+          cudaError_t e = pad_copy(g.b, (float*)v.b, g.batch, pd.b, stream);
+          if (e != cudaSuccess) return e;
+        }
+        const bool split = pd.plan.splits > 1;
+        cudaError_t e = gemm_tcgen05(split ? split_args(v, pd.plan.splits, pd.plan.k_chunk, ws) : v, pd.plan.cfg, stream);
+        if (e != cudaSuccess) return e;
+        *used_tc = true;
+        if (!split) return cudaSuccess;
+        return splitk_reduce((const float*)ws, g.c, pd.plan.splits, g.M, g.N, g.scm, g.round_out, stream);
+      }
     }
   }
   Split s = choose_split(g, 128, 128, 8);

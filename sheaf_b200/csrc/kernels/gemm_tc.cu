@@ -32,6 +32,9 @@
 #include "tc_common.h"
 
 namespace sb {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
+
 namespace {
 
 constexpr int BM = 128;
@@ -50,8 +53,11 @@ struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int EPI_BYTES = 4 * 32 * 16 * 4;  // one 32 x 16 f32 staging slot per epilogue warp
-  static constexpr int BYTES = 1024 /*alignment slack*/ + STAGES * STAGE + EPI_BYTES + 256;
+  // two 32 x 16 f32 staging buffers per epilogue warp
+  static constexpr int EPI_BYTES = 4 * 2 * 32 * 16 * 4;
+  // the dynamic shared memory window is 1024-byte aligned (checked at entry),
+  // so two CTAs of every configuration fit in an SM's 228 KB
+  static constexpr int BYTES = STAGES * STAGE + EPI_BYTES + 256;
 };
 
 // Tile t -> (z, m, n).  Within a slice z, tiles run in groups of kGroupM
@@ -105,17 +111,69 @@ __device__ __forceinline__ void store_chunk(float* slot, const float* v, int lan
   __syncwarp();
 }
 
+// Epilogue of one warp's 32 accumulator rows (TMEM lane quadrant at `acc`) to
+// rows row0..row0+31, columns n0..n0+BN-1 of output slice z.  With a C tensor
+// map (c_tma) each 32 x 16 chunk is staged in one of the warp's two 2 KB
+// buffers (64-byte swizzle) and lane 0 issues a TMA store for it, so the
+// stores drain asynchronously while the next chunk is read from TMEM; a buffer
+// is rewritten only after the store issued from it two chunks earlier has read
+// it.  Without a map (row stride or base not 16-byte aligned) store_chunk
+// writes through the first buffer.
+template <int BN>
+__device__ __forceinline__ void epilogue_warp(uint32_t acc, float* bufs, int lane, int* sb, const CUtensorMap* tmC,
+                                              bool c_tma, bool c3d, int z, float* cz, int row0, int n0, int M, int N,
+                                              long long ldc, bool vec, bool zero, int round_out) {
+  if (row0 >= M) return;
+#pragma unroll 1
+  for (int c = 0; c < BN && n0 + c < N; c += 16) {
+    float v[16];
+    tmem_ld16(acc + (uint32_t)c, v);
+    if (zero) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = 0.f;
+    }
+    if (round_out) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
+    }
+    if (c_tma) {
+      float* buf = bufs + *sb * 512;
+      if (lane == 0) bulk_wait_read1();
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        ((float4*)(buf + lane * 16))[u ^ ((lane >> 1) & 3)] =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        if (c3d) tma_store_3d(tmC, buf, n0 + c, row0, z);
+        else tma_store_2d(tmC, buf, n0 + c, row0);
+        bulk_commit();
+      }
+      *sb ^= 1;
+    } else {
+      store_chunk(bufs, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
+    }
+  }
+}
+
 // TMEM allocations are powers of two of at least 32 columns.
 __host__ __device__ constexpr uint32_t tmem_cols(int n) { return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u; }
 
 template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
-                      int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
-                      int round_out, int kchunk, Tiles tl, int* err) {
+    gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
+                      long long ldc, int a_mn, int b_mn, int a3d, int b3d, int c_tma, int c3d, int round_out,
+                      int kchunk, Tiles tl, int* err) {
   using S = Smem<BN, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // uniform: every thread leaves before any barrier
+    if (threadIdx.x == 0) atomicExch(err, 9);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   float* epi = (float*)(smem + STAGES * S::STAGE);
@@ -163,15 +221,15 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 
   if (warp == 0) {
     if (lane == 0) {
-      int it = 0;
+      // ring position: slot s, phase ph (advanced after each K step)
+      int it = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x) {
         int z, m0, n0, kt0, kt1, zab;
         tl.at(t, &z, &m0, &n0, BN);
         krange(z, &kt0, &kt1, &zab);
         for (int kt = kt0; kt < kt1; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
           mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
           uint8_t* a = sA + s * S::A_BYTES;
@@ -188,13 +246,19 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
           }
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(BM, BN, a_mn, b_mn);
-      int it = 0, j = 0;
+      // descriptors of slot 0, K slice 0 (see the CTA-pair kernel)
+      const uint64_t a_d0 = a_mn ? smem_desc(smem_u32(sA), BK * 128, 512, 1) : smem_desc(smem_u32(sA), 16, 1024, 2);
+      const uint64_t b_d0 = b_mn ? smem_desc(smem_u32(sB), BK * 128, 512, 1) : smem_desc(smem_u32(sB), 16, 1024, 2);
+      const uint64_t a_kk = a_mn ? 1024 >> 4 : 32 >> 4, b_kk = b_mn ? 1024 >> 4 : 32 >> 4;
+      int it = 0, j = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x, ++j) {
         int z, m0, n0, kt0, kt1, zab;
@@ -205,23 +269,19 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
         for (int kt = kt0; kt < kt1; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
           fence_after();
-          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
-          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
+          // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
+          // k-th MMA starts 32 B further along the row.  MN-major: 128 B (32 M/N
+          // values) by BK rows per chunk, chunks BK*128 B apart (LBO), 4-row
+          // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
+          const uint64_t ad = a_d0 + (uint64_t)((s * S::A_BYTES) >> 4);
+          const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
-            // k-th MMA starts 32 B further along the row.  MN-major: 128 B (32 M/N
-            // values) by BK rows per chunk, chunks BK*128 B apart (LBO), 4-row
-            // atoms 512 B apart (SBO); the k-th MMA starts 8 rows (1024 B) down.
-            const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
-            const uint64_t bd = b_mn ? smem_desc(bb + kk * 1024, BK * 128, 512, 1) : smem_desc(bb + kk * 32, 16, 1024, 2);
-            mma_tf32(acc, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < BK / 8; ++kk)
+            mma_tf32(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
           mma_commit(&empty[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
         if (!ok) break;
         mma_commit(&acc_full[b]);
@@ -230,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   } else {
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
     const int quad = warp & 3;
-    int j = 0;
+    int j = 0, sb = 0;
     for (int t = blockIdx.x; t < tl.total; t += gridDim.x, ++j) {
       int z, m0, n0, kt0, kt1, zab;
       tl.at(t, &z, &m0, &n0, BN);
@@ -241,25 +301,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       const int row0 = m0 + quad * 32;
       float* cz = C + (long long)z * scb;
       const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
-      float* slot = epi + (warp - 2) * 512;
       const uint32_t acc = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(acc + (uint32_t)c, v);
-        if (kt1 <= kt0) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = 0.f;
-        }
-        if (round_out) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
-        }
-        store_chunk(slot, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
-      }
+      epilogue_warp<BN>(acc, epi + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc, vec,
+                        kt1 <= kt0, round_out);
       fence_before();
       mbar_arrive(&acc_empty[b]);
     }
+    if (c_tma && lane == 0) bulk_wait_all();
   }
   fence_before();
   __syncthreads();
@@ -280,13 +328,19 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 // peer's epilogue releases an accumulator with a remote mbarrier arrive.
 template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
-                   int M, int N, int K, long long scb, long long ldc, int a_mn, int b_mn, int a3d, int b3d,
-                   int round_out, int kchunk, Tiles tl, int* err) {
+    gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
+                   long long ldc, int a_mn, int b_mn, int a3d, int b3d, int c_tma, int c3d, int round_out,
+                   int kchunk, Tiles tl, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // both CTAs of a pair have the same layout, so both leave here or neither
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) atomicExch(err, 9);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   float* epi = (float*)(smem + STAGES * S::STAGE);
@@ -341,7 +395,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 
   if (warp == 0) {
     if (lane == 0) {
-      int it = 0;
+      // ring position: slot s, phase ph (advanced after each K step)
+      int it = 0, s = 0;
+      uint32_t ph = 0;
+      const uint32_t full_leader = cluster_addr(&full[0], 0);
       bool ok = true;
       for (int t = pair; t < tl.total && ok; t += npairs) {
         int z, m0, n0, kt0, kt1, zab;
@@ -349,11 +406,9 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
         krange(z, &kt0, &kt1, &zab);
         const int ma = m0 + (int)rank * BM, nb = n0 + (int)rank * BNH;
         for (int kt = kt0; kt < kt1; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
           if (leader) mbar_expect_tx(&full[s], 2u * (uint32_t)S::STAGE);
-          const uint32_t bar = cluster_addr(&full[s], 0);
+          const uint32_t bar = full_leader + (uint32_t)(s * 8);
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
           if (!a_mn) {
@@ -368,13 +423,22 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 #pragma unroll
             for (int j = 0; j < BNH / 32; ++j) ld(b + j * BK * 128, &tmB, bar, nb + 32 * j, kt * BK, zab, b3d);
           }
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       const uint32_t idesc = idesc_tf32(2 * BM, BN, a_mn, b_mn);
-      int it = 0, j = 0;
+      // descriptors of slot 0, K slice 0; a slot adds its byte offset and a
+      // K slice 32 B (K-major) or 1024 B (MN-major), in 16-byte units, to the
+      // start-address field (shared addresses stay below 2^18, no carry)
+      const uint64_t a_d0 = a_mn ? smem_desc(smem_u32(sA), BK * 128, 512, 1) : smem_desc(smem_u32(sA), 16, 1024, 2);
+      const uint64_t b_d0 = b_mn ? smem_desc(smem_u32(sB), BK * 128, 512, 1) : smem_desc(smem_u32(sB), 16, 1024, 2);
+      const uint64_t a_kk = a_mn ? 1024 >> 4 : 32 >> 4, b_kk = b_mn ? 1024 >> 4 : 32 >> 4;
+      const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
+      int it = 0, j = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int t = pair; t < tl.total && ok; t += npairs, ++j) {
         int z, m0, n0, kt0, kt1, zab;
@@ -385,20 +449,16 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
         for (int kt = kt0; kt < kt1; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
           fence_after();
-          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
-          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
+          const uint64_t ad = a_d0 + (uint64_t)((s * S::A_BYTES) >> 4);
+          const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t ad = a_mn ? smem_desc(a + kk * 1024, BK * 128, 512, 1) : smem_desc(a + kk * 32, 16, 1024, 2);
-            const uint64_t bd = b_mn ? smem_desc(bb + kk * 1024, BK * 128, 512, 1) : smem_desc(bb + kk * 32, 16, 1024, 2);
-            mma_tf32_pair(acc, ad, bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit_pair(cluster_addr(&empty[s], 0));
-          mma_commit_pair(cluster_addr(&empty[s], 1));
+          for (int kk = 0; kk < BK / 8; ++kk)
+            mma_tf32_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          mma_commit_pair(empty0 + (uint32_t)(s * 8));
+          mma_commit_pair(empty1 + (uint32_t)(s * 8));
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
         if (!ok) break;
         mma_commit_pair(cluster_addr(&acc_full[b], 0));
@@ -407,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     }
   } else {
     const int quad = warp & 3;
-    int j = 0;
+    int j = 0, sb = 0;
     for (int t = pair; t < tl.total; t += npairs, ++j) {
       int z, m0, n0, kt0, kt1, zab;
       tl.at(t, &z, &m0, &n0, BN);
@@ -418,25 +478,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       const int row0 = m0 + (int)rank * BM + quad * 32;
       float* cz = C + (long long)z * scb;
       const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
-      float* slot = epi + (warp - 2) * 512;
       const uint32_t accp = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(accp + (uint32_t)c, v);
-        if (kt1 <= kt0) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = 0.f;
-        }
-        if (round_out) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
-        }
-        store_chunk(slot, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
-      }
+      epilogue_warp<BN>(accp, epi + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc, vec,
+                        kt1 <= kt0, round_out);
       fence_before();
       mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
     }
+    if (c_tma && lane == 0) bulk_wait_all();
   }
   fence_before();
   __syncthreads();
@@ -454,6 +502,23 @@ bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint6
   const uint64_t dims[3] = {d0, d1, d2};
   const uint64_t strides[2] = {s1_bytes, s2_bytes};
   return tc_make_map(m, base, is3d ? 3 : 2, dims, strides, box1, mn_major);
+}
+
+// Store map of C (f32, inner extent N, rows M, slices `batch`): 32-row x
+// 16-column boxes, 64-byte swizzle.  False when the row stride, the slice
+// stride or the base is not 16-byte aligned (the epilogue then stores through
+// store_chunk).
+bool make_store_map(CUtensorMap* m, const GemmArgs& g) {
+  if ((g.scm & 3) || (((uintptr_t)g.c) & 15) || (g.batch > 1 && (g.scb & 3))) return false;
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const bool is3d = g.batch > 1;
+  cuuint64_t d[3] = {(cuuint64_t)g.N, (cuuint64_t)g.M, (cuuint64_t)g.batch};
+  cuuint64_t st[2] = {(cuuint64_t)g.scm * 4, (cuuint64_t)g.scb * 4};
+  cuuint32_t box[3] = {16, 32, 1}, es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, is3d ? 3u : 2u, (void*)g.c, d, st, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int sm_count() {
@@ -480,6 +545,9 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
                    : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false));
   if (!ok) return cudaErrorNotSupported;
+  CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
+  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
+  const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tf32_tcgen05<BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
@@ -497,8 +565,9 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   if (total > (1ll << 30)) return cudaErrorNotSupported;
   tl.total = (int)total;
   const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
-  kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, g.round_out, kchunk, tl, err);
+  kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, c_tma, c3d, g.round_out, kchunk,
+                                             tl, err);
   return cudaGetLastError();
 }
 
@@ -516,6 +585,9 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
                    : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false));
   if (!ok) return cudaErrorNotSupported;
+  CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
+  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
+  const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BNH, STAGES>;
   auto kern = gemm_tf32_pair<BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
@@ -545,8 +617,9 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, g.round_out, kchunk, tl, err);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
+                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, c_tma, c3d, g.round_out,
+                            kchunk, tl, err);
 }
 
 int* error_word() { return tc_error_word(); }

@@ -16,6 +16,7 @@
 #include "plan.h"
 
 #include <algorithm>
+#include <cmath>
 #include <functional>
 #include <map>
 #include <set>
@@ -835,17 +836,83 @@ Plan plan_function(const Function& f, Precision prec) {
 
 }  // namespace
 
-Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
-  if (prec == Precision::TF32 && fuse_attention) {
-    std::string log;
-    std::shared_ptr<Function> rf(rewrite_attention(f, &log));
-    if (rf) {
-      Plan p = plan_function(*rf, prec);
-      p.rewritten = rf;
-      p.fn = rf.get();
-      p.rewrite_log = log;
-      return p;
+namespace {
+
+bool is_identity_init(const Function& f, int v, ReduceBody body) {
+  const int pi = f.producer[v];
+  if (pi < 0) return false;
+  const Op& op = f.ops[pi];
+  if (op.kind != OpKind::Constant || op.values.size() != 1) return false;
+  const double x = op.values[0];
+  switch (body) {
+    case ReduceBody::Add: return x == 0.0;
+    case ReduceBody::Mul: return x == 1.0;
+    case ReduceBody::Max: return std::isinf(x) && x < 0;
+    case ReduceBody::Min: return std::isinf(x) && x > 0;
+  }
+  return false;
+}
+
+// reduce(reduce(x, D1), D2) with one body, identity inits and a single-use
+// inner value -> reduce(x, D1 + D2 mapped to x's dims).  Sheaf's sum_to_shape
+// emits such chains (one single-axis reduce per broadcast axis, e.g. the
+// [B,T,D] -> [D] gradient of a layer-norm gain); merged, the sum is one pass.
+// Reductions of a dot_general are left alone (they fold into the GEMM).
+std::unique_ptr<Function> merge_reduce_chains(const Function& f) {
+  std::vector<int> uses(f.num_values(), 0);
+  std::vector<char> returned(f.num_values(), 0);
+  for (int r : f.returns) returned[r] = 1;
+  for (const Op& op : f.ops)
+    for (int o : op.operands) ++uses[o];
+  std::unique_ptr<Function> g;
+  for (size_t i = 0; i < f.ops.size(); ++i) {
+    const Function& cur = g ? *g : f;
+    const Op& r2 = cur.ops[i];
+    if (r2.kind != OpKind::Reduce) continue;
+    const int v = r2.operands[0];
+    const int pi = cur.producer[v];
+    if (pi < 0 || returned[v] || uses[v] != 1) continue;
+    const Op& r1 = cur.ops[pi];
+    if (r1.kind != OpKind::Reduce || r1.body != r2.body) continue;
+    const int x = r1.operands[0];
+    if (cur.producer[x] >= 0 && cur.ops[cur.producer[x]].kind == OpKind::DotGeneral) continue;
+    if (!is_identity_init(cur, r1.operands[1], r1.body) || !is_identity_init(cur, r2.operands[1], r2.body)) continue;
+    const int rx = (int)cur.value_types[x].shape.size();
+    std::vector<int64_t> kept;
+    for (int d = 0; d < rx; ++d)
+      if (!std::count(r1.dims.begin(), r1.dims.end(), (int64_t)d)) kept.push_back(d);
+    std::vector<int64_t> dims(r1.dims.begin(), r1.dims.end());
+    bool ok = true;
+    for (int64_t d : r2.dims) {
+      if (d < 0 || d >= (int64_t)kept.size()) { ok = false; break; }
+      dims.push_back(kept[d]);
     }
+    if (!ok) continue;
+    std::sort(dims.begin(), dims.end());
+    if (!g) g = std::make_unique<Function>(f);
+    Op merged = g->ops[i];
+    merged.operands = {x, r2.operands[1]};
+    merged.dims = dims;
+    g->ops[i] = merged;
+    --uses[v];
+    ++uses[x];
+  }
+  return g;
+}
+
+}  // namespace
+
+Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
+  std::shared_ptr<Function> cur;
+  std::string log;
+  if (prec == Precision::TF32 && fuse_attention) cur.reset(rewrite_attention(f, &log).release());
+  if (auto m = merge_reduce_chains(cur ? *cur : f)) cur.reset(m.release());
+  if (cur) {
+    Plan p = plan_function(*cur, prec);
+    p.rewritten = cur;
+    p.fn = cur.get();
+    p.rewrite_log = log;
+    return p;
   }
   return plan_function(f, prec);
 }

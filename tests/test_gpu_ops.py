@@ -6,6 +6,7 @@ import numpy as np
 import pytest
 
 from oracle.stablehlo_ref import run
+from sheaf_b200.session import plan_steps
 
 pytestmark = pytest.mark.gpu
 
@@ -41,22 +42,42 @@ def rnd(*s):
 
 
 @pytest.mark.parametrize("shape,dim", [((4096, 64), 0), ((64, 4096), 1), ((3, 8192), 1), ((7, 5, 300), 1),
-                                       ((16384, 1536), 0), ((6, 70000), 1), ((2, 3, 4), 0)])
+                                       ((16384, 1536), 0), ((6, 70000), 1), ((2, 3, 4), 0),
+                                       # full and few-output reductions of long rows (split rows)
+                                       ((1024, 2048), (0, 1)), ((3, 40000), 1),
+                                       # many rows onto few columns (split columns, 4-wide and scalar)
+                                       ((16, 512, 384), (0, 1)), ((40000, 65), 0), ((9000, 12), 0)])
 @pytest.mark.parametrize("body", ["add", "maximum", "minimum"])
 def test_reduce(fp32_session, shape, dim, body):
+    dims = (dim,) if isinstance(dim, int) else tuple(dim)
     t = "tensor<" + "x".join(map(str, shape)) + "xf32>"
-    out = [d for i, d in enumerate(shape) if i != dim]
-    ot = "tensor<" + "x".join(map(str, out)) + "xf32>"
+    out = [d for i, d in enumerate(shape) if i not in dims]
+    ot = "tensor<" + "".join(f"{d}x" for d in out) + "f32>"
     init = {"add": "0.0", "maximum": "0xFF800000", "minimum": "0x7F800000"}[body]
+    dl = ", ".join(map(str, dims))
     name, text = module([t], [f"%0 = stablehlo.constant dense<{init}> : tensor<f32>",
-                              f"%1 = stablehlo.reduce(%arg0 init: %0) applies stablehlo.{body} across dimensions = [{dim}] : ({t}, tensor<f32>) -> {ot}"],
+                              f"%1 = stablehlo.reduce(%arg0 init: %0) applies stablehlo.{body} across dimensions = [{dl}] : ({t}, tensor<f32>) -> {ot}"],
                         [("%1", ot)])
     # f32 sums of R unit normals: rounding error grows like sqrt(R) (blocked
     # summation), ~2e-4 at R = 16384; max/min are exact.
-    R = shape[dim]
+    R = int(np.prod([shape[d] for d in dims]))
     rtol = 2e-5 if body == "add" else 0
     atol = 2e-4 * max(1.0, (R / 4096) ** 0.5) if body == "add" else 0
     check(fp32_session, name, text, [rnd(*shape)], rtol=rtol, atol=atol)
+
+
+def test_reduce_chain_merged(fp32_session):
+    # reduce(reduce(x*x, [2]), [0, 1]): the planner merges the chain into one
+    # full reduction of the squared input
+    t = "tensor<64x96x400xf32>"
+    name, text = module([t], ["%0 = stablehlo.constant dense<0.0> : tensor<f32>",
+                              f"%1 = stablehlo.multiply %arg0, %arg0 : {t}",
+                              f"%2 = stablehlo.reduce(%1 init: %0) applies stablehlo.add across dimensions = [2] : ({t}, tensor<f32>) -> tensor<64x96xf32>",
+                              "%3 = stablehlo.reduce(%2 init: %0) applies stablehlo.add across dimensions = [0, 1] : (tensor<64x96xf32>, tensor<f32>) -> tensor<f32>"],
+                        [("%3", "tensor<f32>")])
+    check(fp32_session, name, text, [rnd(64, 96, 400)], rtol=2e-5, atol=0)
+    steps = plan_steps(text, name, "fp32")
+    assert [st["kind"] for st in steps] == ["reduce"], steps
 
 
 def test_elementwise_chain_with_broadcasts(fp32_session):
@@ -210,13 +231,16 @@ def test_large_gemm_shapes_match_oracle(tf32_session):
 
 @pytest.mark.parametrize("config", [None, 0, 1, 2, 3, 4])
 @pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1),
-                                   (1000, 300, 800, 1), (520, 272, 1000, 2), (384, 384, 4096, 1)])
+                                   (1000, 300, 800, 1), (520, 272, 1000, 2), (384, 384, 4096, 1),
+                                   # row strides that are not a multiple of 4 floats (padded operand copies)
+                                   (1000, 65, 384, 1), (65, 384, 4000, 1), (700, 384, 65, 1), (130, 70, 333, 2)])
 @pytest.mark.parametrize("at,bt", [(False, False), (False, True), (True, False), (True, True)])
 def test_gemm_tiles_and_layouts(tf32_session, monkeypatch, config, shape, at, bt):
     """Every tcgen05 GEMM configuration (SHEAF_B200_GEMM_CONFIG: single-CTA
     128 x 64 / 128 x 128 tiles with two TMEM accumulators, CTA-pair 256 x 128 /
     256 x 192 / 256 x 256 tiles) and the cost-model choice (None), with ragged
-    M/N/K edges, K-major and MN-major operands, batched, and split-K."""
+    M/N/K edges, K-major and MN-major operands, batched, split-K, and operands
+    whose row stride is not 16-byte aligned (copied to padded buffers)."""
     if config is not None:
         monkeypatch.setenv("SHEAF_B200_GEMM_CONFIG", str(config))
     M_, N_, K_, B_ = shape
