@@ -3,6 +3,9 @@
 // has too few tiles to fill 148 SMs (e.g. weight gradients of shape D x D with
 // the whole token count as the contraction).
 #include <algorithm>
+#include <array>
+#include <map>
+#include <mutex>
 
 #include "kernels.h"
 
@@ -153,6 +156,52 @@ GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws
   return run;
 }
 
+// Measured choice of the tensor-core configuration, once per problem
+// signature (shapes, strides, split, 16-byte alignment of the pointers): each
+// configuration runs once to warm up and twice timed on the real operands
+// (the output is rewritten by the call that follows, with the same values:
+// configurations differ only in tiling, not in summation order), and the
+// fastest is kept.  The cost model's proposal stands while the stream is being
+// captured into a graph, or when the environment forces a configuration.
+using TuneKey = std::array<int64_t, 19>;
+std::mutex tune_mu;
+std::map<TuneKey, int> tune_cache;
+
+int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
+  if (tc_forced_config() >= 0) return proposed;
+  const TuneKey key = {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
+                       run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
+                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), 0};
+  std::lock_guard<std::mutex> lock(tune_mu);
+  auto it = tune_cache.find(key);
+  if (it != tune_cache.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return proposed;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+    if (e0) cudaEventDestroy(e0);
+    return proposed;
+  }
+  int best = proposed;
+  float best_ms = 1e30f;
+  for (int c = 0; c < tc_num_configs(); ++c) {
+    if (gemm_tcgen05(run, c, stream) != cudaSuccess) continue;
+    cudaEventRecord(e0, stream);
+    bool ok = gemm_tcgen05(run, c, stream) == cudaSuccess && gemm_tcgen05(run, c, stream) == cudaSuccess;
+    cudaEventRecord(e1, stream);
+    float ms = 0.f;
+    if (!ok || cudaEventSynchronize(e1) != cudaSuccess || cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) continue;
+    if (ms < best_ms) {
+      best_ms = ms;
+      best = c;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  tune_cache[key] = best;
+  return best;
+}
+
 }  // namespace
 
 cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
@@ -162,7 +211,8 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
     TcPlan p;
     if (tc_plan(g, &p)) {
       const bool split = p.splits > 1 && ws && ws_bytes >= (size_t)(p.splits * g.M * g.N) * sizeof(float);
-      cudaError_t e = gemm_tcgen05(split ? split_args(g, p.splits, p.k_chunk, ws) : g, p.cfg, stream);
+      const GemmArgs run = split ? split_args(g, p.splits, p.k_chunk, ws) : g;
+      cudaError_t e = gemm_tcgen05(run, tuned_config(run, p.cfg, stream), stream);
       if (e == cudaSuccess) {
         *used_tc = true;
         if (!split) return cudaSuccess;
@@ -185,7 +235,8 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
           if (e != cudaSuccess) return e;
         }
         const bool split = pd.plan.splits > 1;
-        cudaError_t e = gemm_tcgen05(split ? split_args(v, pd.plan.splits, pd.plan.k_chunk, ws) : v, pd.plan.cfg, stream);
+        const GemmArgs run = split ? split_args(v, pd.plan.splits, pd.plan.k_chunk, ws) : v;
+        cudaError_t e = gemm_tcgen05(run, tuned_config(run, pd.plan.cfg, stream), stream);
         if (e != cudaSuccess) return e;
         *used_tc = true;
         if (!split) return cudaSuccess;

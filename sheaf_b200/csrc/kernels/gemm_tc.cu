@@ -48,6 +48,14 @@ __device__ __forceinline__ void tma_ld(void* dst, const CUtensorMap* map, uint64
   else tma_load_2d(dst, map, bar, x, y);
 }
 
+// MN-major operand through a chunked map (dims {32, K, MN/32[, batch]}): one
+// load brings all 32-wide chunks of a stage, laid out BK * 128 B apart.
+__device__ __forceinline__ void tma_ld_chunks(void* dst, const CUtensorMap* map, uint64_t* bar, int k, int chunk0,
+                                              int z, bool batched) {
+  if (batched) tma_load_4d(dst, map, bar, 0, k, chunk0, z);
+  else tma_load_3d(dst, map, bar, 0, k, chunk0);
+}
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -165,8 +173,8 @@ template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
-                      long long ldc, int a_mn, int b_mn, int a3d, int b3d, int c_tma, int c3d, int round_out,
-                      int kchunk, Tiles tl, int* err) {
+                      long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
+                      int c3d, int round_out, int kchunk, Tiles tl, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {  // uniform: every thread leaves before any barrier
@@ -236,12 +244,16 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           uint8_t* b = sB + s * S::B_BYTES;
           if (!a_mn) {
             tma_ld(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
+          } else if (a_chunks) {
+            tma_ld_chunks(a, &tmA, &full[s], kt * BK, m0 / 32, zab, a3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j) tma_ld(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
           }
           if (!b_mn) {
             tma_ld(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
+          } else if (b_chunks) {
+            tma_ld_chunks(b, &tmB, &full[s], kt * BK, n0 / 32, zab, b3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
@@ -330,8 +342,8 @@ template <int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
-                   long long ldc, int a_mn, int b_mn, int a3d, int b3d, int c_tma, int c3d, int round_out,
-                   int kchunk, Tiles tl, int* err) {
+                   long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
+                   int c3d, int round_out, int kchunk, Tiles tl, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -392,6 +404,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     if (is3d) tma_load_3d_pair(dst, map, bar, x, y, z);
     else tma_load_2d_pair(dst, map, bar, x, y);
   };
+  auto ld_chunks = [&](void* dst, const CUtensorMap* map, uint32_t bar, int k, int chunk0, int z, bool batched) {
+    if (batched) tma_load_4d_pair(dst, map, bar, 0, k, chunk0, z);
+    else tma_load_3d_pair(dst, map, bar, 0, k, chunk0);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -413,12 +429,16 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           uint8_t* b = sB + s * S::B_BYTES;
           if (!a_mn) {
             ld(a, &tmA, bar, kt * BK, ma, zab, a3d);
+          } else if (a_chunks) {
+            ld_chunks(a, &tmA, bar, kt * BK, ma / 32, zab, a3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j) ld(a + j * BK * 128, &tmA, bar, ma + 32 * j, kt * BK, zab, a3d);
           }
           if (!b_mn) {
             ld(b, &tmB, bar, kt * BK, nb, zab, b3d);
+          } else if (b_chunks) {
+            ld_chunks(b, &tmB, bar, kt * BK, nb / 32, zab, b3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BNH / 32; ++j) ld(b + j * BK * 128, &tmB, bar, nb + 32 * j, kt * BK, zab, b3d);
@@ -504,6 +524,23 @@ bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint6
   return tc_make_map(m, base, is3d ? 3 : 2, dims, strides, box1, mn_major);
 }
 
+// Chunked map of an MN-major operand (MN values contiguous, rows of K):
+// dims {32, K, MN / 32[, batch]} with the 32-value chunks 128 B apart, box
+// {32, BK, chunks}, so one load fills a stage's chunks BK * 128 B apart.
+// Only when MN is a multiple of 32 (the last chunk ends inside the row).
+bool make_chunk_map(CUtensorMap* m, const float* base, uint64_t mn, uint64_t k, uint64_t batch, uint64_t ld_bytes,
+                    uint64_t batch_bytes, uint32_t chunks, bool batched) {
+  if (mn % 32) return false;
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t d[4] = {32, (cuuint64_t)k, (cuuint64_t)(mn / 32), (cuuint64_t)batch};
+  cuuint64_t st[3] = {(cuuint64_t)ld_bytes, 128, (cuuint64_t)batch_bytes};
+  cuuint32_t box[4] = {32, (cuuint32_t)BK, chunks, 1}, es[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, batched ? 4u : 3u, (void*)base, d, st, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Store map of C (f32, inner extent N, rows M, slices `batch`): 32-row x
 // 16-column boxes, 64-byte swizzle.  False when the row stride, the slice
 // stride or the base is not 16-byte aligned (the epilogue then stores through
@@ -540,10 +577,12 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
   const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
   // A: K-major dims {K, M}, box {32, 128}; M-major dims {M, K}, box {32, 32}
-  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
-                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false);
-  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
-                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false));
+  const int a_chunks = a_mn && make_chunk_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, BM / 32, a3d);
+  const int b_chunks = b_mn && make_chunk_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, BN / 32, b3d);
+  bool ok = a_chunks || (a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
+                              : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false));
+  ok = ok && (b_chunks || (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
+                                : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false)));
   if (!ok) return cudaErrorNotSupported;
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
   const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
@@ -566,7 +605,8 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   tl.total = (int)total;
   const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
   kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, c_tma, c3d, g.round_out, kchunk,
+                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, a_chunks, b_chunks, c_tma, c3d,
+                                             g.round_out, kchunk,
                                              tl, err);
   return cudaGetLastError();
 }
@@ -580,10 +620,12 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   const bool split = g.k_chunk > 0;
   const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
   const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
-  bool ok = a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
-                 : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false);
-  ok = ok && (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
-                   : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false));
+  const int a_chunks = a_mn && make_chunk_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, BM / 32, a3d);
+  const int b_chunks = b_mn && make_chunk_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, BNH / 32, b3d);
+  bool ok = a_chunks || (a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
+                              : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false));
+  ok = ok && (b_chunks || (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
+                                : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false)));
   if (!ok) return cudaErrorNotSupported;
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
   const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
@@ -618,7 +660,8 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, c_tma, c3d, g.round_out,
+                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
+                            g.round_out,
                             kchunk, tl, err);
 }
 
@@ -691,10 +734,9 @@ constexpr int kNumCfgs = (int)(sizeof(kCfgs) / sizeof(kCfgs[0]));
 // of one unit, whose K steps are bound by the operand bytes an SM receives
 // from L2 (~110 GB/s per SM, shared by the CTAs on it) or by the TF32 tensor
 // rate (~5.5 TFLOP/s per SM), plus pipeline fill and, with one accumulator, the
-// epilogue.  Split-K adds the partial-sum reduction.  The constants are from
-// measurements on B200 (matmul 2048..8192, the nanoGPT and GPT-2 shapes).
+// epilogue.  The constants are from measurements on B200 (matmul 2048..8192,
+// the nanoGPT and GPT-2 shapes).
 constexpr double kSmBytesPerUs = 110e3, kSmFlopsPerUs = 5.5e6, kFillUs = 2.0, kEpiBytesPerUs = 50e3;
-constexpr double kHbmBytesPerUs = 5e6, kReduceLaunchUs = 4.0;
 
 double est_us(const TcCfg& c, int64_t M, int64_t N, int64_t K, int64_t units_z, int sms) {
   const int tm = c.pair ? 256 : 128;
@@ -727,38 +769,56 @@ bool tc_layout(const GemmArgs& g, bool* a_mn, bool* b_mn) {
 
 }  // namespace
 
+int tc_forced_config() {
+  // SHEAF_B200_GEMM_CONFIG=n forces configuration n (0..kNumCfgs-1) for every
+  // tensor-core GEMM: used by the tests to run every kernel variant on the
+  // same shapes.
+  if (const char* e = std::getenv("SHEAF_B200_GEMM_CONFIG")) {
+    const int f = std::atoi(e);
+    if (f >= 0 && f < kNumCfgs) return f;
+  }
+  return -1;
+}
+
+int tc_num_configs() { return kNumCfgs; }
+
 bool tc_plan(const GemmArgs& g, TcPlan* p) {
   bool a_mn, b_mn;
   if (!tc_layout(g, &a_mn, &b_mn)) return false;
   const int sms = sm_count();
-  // SHEAF_B200_GEMM_CONFIG=n forces configuration n (0..kNumCfgs-1) for every
-  // tensor-core GEMM (the split factor is still chosen for it): used by the
-  // tests to run every kernel variant on the same shapes.
-  int forced = -1;
-  if (const char* e = std::getenv("SHEAF_B200_GEMM_CONFIG")) {
-    forced = std::atoi(e);
-    if (forced < 0 || forced >= kNumCfgs) forced = -1;
+  // Split-K, by a fixed rule so that the summation order (the only part of
+  // the result that depends on the plan) does not depend on the kernel
+  // configuration: a single GEMM whose 128 x 128 tiles do not cover the SMs
+  // is split into enough K ranges for ~2 CTAs per SM, at least 512 of K each.
+  p->splits = 1;
+  p->k_chunk = 0;
+  const int64_t tiles = ((g.M + 127) / 128) * ((g.N + 127) / 128);
+  if (g.batch == 1 && tiles < sms) {
+    const int64_t s = std::min<int64_t>((2 * sms + tiles - 1) / tiles, g.K / 512);
+    if (s >= 2) {
+      int64_t chunk = (g.K + s - 1) / s;
+      chunk = (chunk + BK - 1) / BK * BK;
+      p->splits = (g.K + chunk - 1) / chunk;
+      p->k_chunk = p->splits > 1 ? chunk : 0;
+    }
   }
+  const int forced = tc_forced_config();
+  if (forced >= 0) {
+    p->cfg = forced;
+    return true;
+  }
+  // configuration by the cost model (the measured choice replaces it where
+  // the caller can time the candidates)
+  const int64_t kc = p->splits > 1 ? p->k_chunk : g.K;
   double best = 1e300;
   for (int ci = 0; ci < kNumCfgs; ++ci) {
     const TcCfg& c = kCfgs[ci];
-    if (forced >= 0 && ci != forced) continue;
-    if (forced < 0 && c.pair && g.M <= 128) continue;
-    if (forced < 0 && c.bn > 64 && g.N <= 32) continue;
-    // split-K candidates: single GEMMs only, at least 256 of K per split
-    const int64_t max_s = g.batch == 1 ? std::max<int64_t>(1, g.K / 256) : 1;
-    for (int64_t s = 1; s <= std::min<int64_t>(max_s, 64); s = s < 4 ? s + 1 : s * 3 / 2) {
-      int64_t chunk = (g.K + s - 1) / s;
-      chunk = (chunk + BK - 1) / BK * BK;
-      const int64_t splits = (g.K + chunk - 1) / chunk;
-      double t = est_us(c, g.M, g.N, chunk, splits * g.batch, sms);
-      if (splits > 1) t += kReduceLaunchUs + (double)splits * g.M * g.N * 8.0 / kHbmBytesPerUs;
-      if (t < best * 0.97 || (t < best && splits <= p->splits)) {  // prefer fewer splits on near-ties
-        best = t;
-        p->cfg = ci;
-        p->splits = splits;
-        p->k_chunk = splits > 1 ? chunk : 0;
-      }
+    if (c.pair && g.M <= 128) continue;
+    if (c.bn > 64 && g.N <= 32) continue;
+    const double t = est_us(c, g.M, g.N, kc, p->splits * g.batch, sms);
+    if (t < best) {
+      best = t;
+      p->cfg = ci;
     }
   }
   return p->cfg >= 0;

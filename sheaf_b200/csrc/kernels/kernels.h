@@ -39,17 +39,22 @@ cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_
 // f32 FMA on CUDA cores; any strides.
 cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream);
 
-// tcgen05 tensor-core GEMM (kind::tf32 on f32 operands).  tc_plan picks the
-// kernel configuration (single-CTA or CTA-pair tiles, tile width, TMEM
-// accumulators) and the split-K factor for a problem by a cost model; false when
-// the operand layout is outside what the tensor-core kernels handle (the caller
-// then uses gemm_simt).  gemm_tcgen05 runs configuration `cfg` on g, where g is
-// already split (batch = splits, k_chunk) when the plan split K.
+// tcgen05 tensor-core GEMM (kind::tf32 on f32 operands).  tc_plan fixes the
+// split-K factor of a problem by a rule on its shape and proposes a kernel
+// configuration (single-CTA or CTA-pair tiles, tile width, TMEM accumulators)
+// by a cost model; false when the operand layout is outside what the
+// tensor-core kernels handle (the caller then uses gemm_simt).  gemm_tcgen05
+// runs configuration `cfg` (0 .. tc_num_configs() - 1) on g, where g is
+// already split (batch = splits, k_chunk) when the plan split K.  Every
+// configuration gives bit-identical results for the same split.
+// tc_forced_config() is the configuration forced by the environment, or -1.
 struct TcPlan {
   int cfg = -1;
   int64_t splits = 1, k_chunk = 0;
 };
 bool tc_plan(const GemmArgs& g, TcPlan* plan);
+int tc_num_configs();
+int tc_forced_config();
 cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream);
 // Non-zero when a tcgen05 kernel gave up on a bounded wait (GEMM 1: ring slot,
 // 2: operand tiles, 3: accumulator; attention 11..35) or found its shared

@@ -281,6 +281,14 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc,
                                               uint32_t acc) {
   asm volatile(

@@ -878,6 +878,11 @@ std::unique_ptr<Function> merge_reduce_chains(const Function& f) {
     if (cur.producer[x] >= 0 && cur.ops[cur.producer[x]].kind == OpKind::DotGeneral) continue;
     if (!is_identity_init(cur, r1.operands[1], r1.body) || !is_identity_init(cur, r2.operands[1], r2.body)) continue;
     const int rx = (int)cur.value_types[x].shape.size();
+    // only chains whose first step keeps the innermost dimension (column
+    // reductions: the intermediate is large); a row reduction followed by a
+    // small second step is better left as two kernels, which keep per-row
+    // terms out of the inner loop
+    if (std::count(r1.dims.begin(), r1.dims.end(), (int64_t)(rx - 1))) continue;
     std::vector<int64_t> kept;
     for (int d = 0; d < rx; ++d)
       if (!std::count(r1.dims.begin(), r1.dims.end(), (int64_t)d)) kept.push_back(d);

@@ -66,18 +66,28 @@ def test_reduce(fp32_session, shape, dim, body):
     check(fp32_session, name, text, [rnd(*shape)], rtol=rtol, atol=atol)
 
 
+def chain_module(shape, d1, d2, out1, out2):
+    t = "tensor<" + "x".join(map(str, shape)) + "xf32>"
+    return module([t], ["%0 = stablehlo.constant dense<0.0> : tensor<f32>",
+                        f"%1 = stablehlo.multiply %arg0, %arg0 : {t}",
+                        f"%2 = stablehlo.reduce(%1 init: %0) applies stablehlo.add across dimensions = [{d1}] : ({t}, tensor<f32>) -> {out1}",
+                        f"%3 = stablehlo.reduce(%2 init: %0) applies stablehlo.add across dimensions = [{d2}] : ({out1}, tensor<f32>) -> {out2}"],
+                  [("%3", out2)])
+
+
 def test_reduce_chain_merged(fp32_session):
-    # reduce(reduce(x*x, [2]), [0, 1]): the planner merges the chain into one
-    # full reduction of the squared input
-    t = "tensor<64x96x400xf32>"
-    name, text = module([t], ["%0 = stablehlo.constant dense<0.0> : tensor<f32>",
-                              f"%1 = stablehlo.multiply %arg0, %arg0 : {t}",
-                              f"%2 = stablehlo.reduce(%1 init: %0) applies stablehlo.add across dimensions = [2] : ({t}, tensor<f32>) -> tensor<64x96xf32>",
-                              "%3 = stablehlo.reduce(%2 init: %0) applies stablehlo.add across dimensions = [0, 1] : (tensor<64x96xf32>, tensor<f32>) -> tensor<f32>"],
-                        [("%3", "tensor<f32>")])
+    # reduce(reduce(x*x, [0]), [0]): the planner merges the column chain into
+    # one reduction over dims [0, 1]
+    name, text = chain_module((64, 96, 400), "0", "0", "tensor<96x400xf32>", "tensor<400xf32>")
+    check(fp32_session, name, text, [rnd(64, 96, 400)], rtol=2e-5, atol=1e-4)
+    assert [st["kind"] for st in plan_steps(text, name, "fp32")] == ["reduce"]
+
+
+def test_reduce_chain_rows_then_all(fp32_session):
+    # reduce(reduce(x*x, [2]), [0, 1]) stays two kernels (row sums, then a small sum)
+    name, text = chain_module((64, 96, 400), "2", "0, 1", "tensor<64x96xf32>", "tensor<f32>")
     check(fp32_session, name, text, [rnd(64, 96, 400)], rtol=2e-5, atol=0)
-    steps = plan_steps(text, name, "fp32")
-    assert [st["kind"] for st in steps] == ["reduce"], steps
+    assert [st["kind"] for st in plan_steps(text, name, "fp32")] == ["reduce", "reduce"]
 
 
 def test_elementwise_chain_with_broadcasts(fp32_session):
@@ -273,6 +283,35 @@ def test_gemm_tiles_and_layouts(tf32_session, monkeypatch, config, shape, at, bt
         Bm = np.swapaxes(Bm, -1, -2)
     ref = np.matmul(A, Bm)
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
+
+
+@pytest.mark.parametrize("shape,layout", [((1000, 300, 800), "nt"), ((384, 384, 16384), "tn"), ((2048, 256, 512), "nn")])
+def test_gemm_configs_bit_identical(tf32_session, monkeypatch, shape, layout):
+    """Every tensor-core configuration gives the same bits (tiling changes, the
+    K summation order does not), so the measured configuration choice cannot
+    change results between runs."""
+    M_, N_, K_ = shape
+    at, bt = layout[0] == "t", layout[1] == "t"
+    ty = lambda r, c: f"tensor<{r}x{c}xf32>"
+    sa, sb = (ty(K_, M_) if at else ty(M_, K_)), (ty(N_, K_) if bt else ty(K_, N_))
+    body, a, b = [], "%arg0", "%arg1"
+    if at:
+        body.append(f"%ta = stablehlo.transpose %arg0, dims = [1, 0] : ({sa}) -> {ty(M_, K_)}")
+        a = "%ta"
+    if bt:
+        body.append(f"%tb = stablehlo.transpose %arg1, dims = [1, 0] : ({sb}) -> {ty(K_, N_)}")
+        b = "%tb"
+    body.append(f"%0 = stablehlo.dot_general {a}, {b}, contracting_dims = [1] x [0] : "
+                f"({ty(M_, K_)}, {ty(K_, N_)}) -> {ty(M_, N_)}")
+    name, text = module([sa, sb], body, [("%0", ty(M_, N_))])
+    ins = [rnd(K_, M_) if at else rnd(M_, K_), rnd(N_, K_) if bt else rnd(K_, N_)]
+    outs = []
+    for cfg in range(5):
+        monkeypatch.setenv("SHEAF_B200_GEMM_CONFIG", str(cfg))
+        tf32_session.load_stablehlo(text)
+        outs.append(tf32_session.call(name, ins)[0])
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
 
 
 def test_input_validation_errors(fp32_session):
