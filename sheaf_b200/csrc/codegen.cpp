@@ -544,7 +544,43 @@ bool CodeGen::gen_loop_vec4(const Op& root, Step* st) {
 // range like the scalar column kernel.  Partial sums are combined in a fixed
 // order, so results are deterministic.  Returns false (nothing emitted) when an
 // access does not vectorize or the shape does not qualify.
-bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
+std::string CodeGen::epilogue_code(Ctx& c, const Op& red, const Op& epi, const std::vector<std::string>& oc,
+                                   int indent, std::string* val) {
+  auto saved_memo = std::move(c.memo);
+  const int saved_root = c.root, saved_indent = c.indent;
+  const bool saved_vec = c.vec;
+  std::string saved_body = c.body.str();
+  c.body.str("");
+  c.memo.assign(1, {});
+  // the reduced value at its coordinates (unit dims read as "0", as the unit
+  // reshapes between it and the epilogue root produce them) and the root's
+  // coordinates: the non-unit output coordinates in order, "0" elsewhere
+  const auto& xs = red.type.shape;
+  std::vector<std::string> xc(xs.size()), nu;
+  for (size_t d = 0; d < xs.size(); ++d) {
+    xc[d] = xs[d] == 1 ? "0" : oc[d];
+    if (xs[d] != 1) nu.push_back(oc[d]);
+  }
+  std::vector<std::string> rc;
+  size_t k = 0;
+  for (int64_t e : epi.type.shape) rc.push_back(e == 1 ? "0" : nu[k++]);
+  c.memo[0][std::to_string(red.result) + "@" + join(xc, ",")] = Val{"rv_", "float"};
+  c.root = epi.result;
+  c.indent = indent;
+  c.vec = false;
+  Val v = eval(c, epi.result, rc);
+  std::string code = c.body.str();
+  *val = v.name;
+  c.body.str(saved_body);
+  c.body.seekp(0, std::ios_base::end);
+  c.memo = std::move(saved_memo);
+  c.root = saved_root;
+  c.indent = saved_indent;
+  c.vec = saved_vec;
+  return code;
+}
+
+bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
   const Type& in = f_.value_types[root.operands[0]];
   const auto& ish = in.shape;
   const int r = (int)ish.size();
@@ -561,7 +597,7 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
   const bool inner_reduced = !rd.empty() && rd.back() == r - 1;
   int mode;
   if (trailing && R <= 4096 && inner_reduced) mode = 0;
-  else if (!trailing && !inner_reduced && !kd.empty() && kd.back() == r - 1) mode = 2;
+  else if (!epi && !trailing && !inner_reduced && !kd.empty() && kd.back() == r - 1) mode = 2;
   else return false;
   if (R == 0 || O == 0) return false;
   const char* ident = root.body == ReduceBody::Add ? "0.f"
@@ -649,6 +685,14 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
   Val init = eval(c, root.operands[1], {});
   const std::string init_code = c.body.str();
   c.memo = std::move(saved_memo);
+  // final write of output o from the reduced value `acc`
+  std::string epi_val, epi_code;
+  if (epi) epi_code = epilogue_code(c, root, *epi, oc, 3, &epi_val);
+  auto final_store = [&](const std::string& acc) {
+    if (!epi) return init_code + "      O[o] = " + store(root, combine(acc, init.name)) + ";\n";
+    return init_code + "      const float rv_ = " + combine(acc, init.name) + ";\n" + epi_code + "      O[o] = " +
+           store(*epi, epi_val) + ";\n";
+  };
 
   const std::string start_text = src_.str();
   struct Snip {
@@ -669,8 +713,7 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
     src_ << "    }\n";
     src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
-    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
-         << ";\n    }\n  }\n}\n\n";
+    src_ << "    if (lane == 0) {\n" << final_store("acc") << "    }\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
   } else {
     const int64_t O4 = O / 4;
@@ -747,8 +790,8 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st) {
   return true;
 }
 
-void CodeGen::gen_reduce(const Op& root, Step* st) {
-  if (gen_reduce_vec4(root, st)) return;
+void CodeGen::gen_reduce(const Op& root, Step* st, const Op* epi) {
+  if (gen_reduce_vec4(root, st, epi)) return;
   const std::string start_text = src_.str();
   struct Snip {
     CodeGen* g; size_t start;
@@ -853,6 +896,14 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
   Val init = eval(c, root.operands[1], {});
   std::string init_code = c.body.str();
   c.memo = std::move(saved_memo);
+  // final write of output o from the reduced value `acc`
+  std::string epi_val, epi_code;
+  if (epi) epi_code = epilogue_code(c, root, *epi, oc, 3, &epi_val);
+  auto final_store = [&](const std::string& acc) {
+    if (!epi) return init_code + "      O[o] = " + store(root, combine(acc, init.name)) + ";\n";
+    return init_code + "      const float rv_ = " + combine(acc, init.name) + ";\n" + epi_code + "      O[o] = " +
+           store(*epi, epi_val) + ";\n";
+  };
 
   src_ << header(name, c, splits > 1 ? 1 : 0);
   src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
@@ -866,7 +917,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     src_ << "      acc = " << combine("acc", v.name) << ";\n    }\n";
     src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
-    src_ << "    if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+    src_ << "    if (lane == 0) {\n" << final_store("acc") << "    }\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + 7) / 8, kMaxGrid));
   } else if (mode == 1) {
     if (splits > 1) src_ << "  float* __restrict__ S = (float*)a.p[" << c.leaves.size() + 1 << "];\n";
@@ -888,8 +939,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     if (splits > 1)
       src_ << "      if (lane == 0) S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n    }\n";
     else
-      src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
-           << ";\n      }\n    }\n";
+      src_ << "      if (lane == 0) {\n" << final_store("acc") << "      }\n    }\n";
     src_ << "    __syncthreads();\n  }\n}\n\n";
     st->grid = std::max<int64_t>(1, std::min<int64_t>(O, kMaxGrid));
     st->grid_y = splits;
@@ -906,7 +956,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
     if (splits > 1) {
       src_ << "    S[(" << c.idx << ")blockIdx.y * " << O << " + o] = acc;\n  }\n}\n\n";
     } else {
-      src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+      src_ << "    {\n" << final_store("acc") << "    }\n  }\n}\n\n";
     }
     st->grid = std::max<int64_t>(1, std::min<int64_t>((O + kThreads - 1) / kThreads, kMaxGrid));
     st->grid_y = splits;
@@ -931,6 +981,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
         src_ << "  __shared__ float red_[" << kThreads / 32 << "];\n";
         src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
         src_ << "  for (" << c.idx << " o = blockIdx.x; o < " << O << "; o += gridDim.x) {\n";
+        if (epi) src_ << pre.str();
         src_ << "    float acc = " << ident << ";\n";
         src_ << "#pragma unroll 4\n    for (" << c.idx << " s = threadIdx.x; s < " << splits << "; s += " << kThreads
              << ") acc = " << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
@@ -940,15 +991,15 @@ void CodeGen::gen_reduce(const Op& root, Step* st) {
         src_ << "    if (warp == 0) {\n      acc = lane < " << kThreads / 32 << " ? red_[lane] : " << ident << ";\n";
         src_ << "      for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
              << combine("acc", "y_") << "; }\n";
-        src_ << "      if (lane == 0) {\n" << init_code << "      O[o] = " << store(root, combine("acc", init.name))
-             << ";\n      }\n    }\n    __syncthreads();\n  }\n}\n\n";
+        src_ << "      if (lane == 0) {\n" << final_store("acc") << "      }\n    }\n    __syncthreads();\n  }\n}\n\n";
       } else {
         src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; o < " << O
              << "; o += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
+        if (epi) src_ << pre.str();
         src_ << "    float acc = " << ident << ";\n";
         src_ << "#pragma unroll 4\n    for (" << c.idx << " s = 0; s < " << splits << "; ++s) acc = "
              << combine("acc", "S[s * " + std::to_string(O) + " + o]") << ";\n";
-        src_ << "    {\n" << init_code << "    O[o] = " << store(root, combine("acc", init.name)) << ";\n    }\n  }\n}\n\n";
+        src_ << "    {\n" << final_store("acc") << "    }\n  }\n}\n\n";
       }
       names_.push_back(fin);
       st->finish_kernel = fin;

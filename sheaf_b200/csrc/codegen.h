@@ -21,7 +21,10 @@ class CodeGen {
   void set_round_roots(const std::vector<int>& roots) { round_roots_ = roots; }
 
   void gen_loop(const Op& root, Step* st);
-  void gen_reduce(const Op& root, Step* st);
+  // Reduction `root`; with `epi`, the element-wise cluster rooted at epi (of
+  // root's shape, reading root at the output coordinates) is evaluated on each
+  // reduced value and stored instead.
+  void gen_reduce(const Op& root, Step* st, const Op* epi = nullptr);
   std::string source() const;
   static std::string prelude();
   std::vector<std::string> kernel_names() const { return names_; }
@@ -49,7 +52,11 @@ class CodeGen {
   };
 
   bool gen_loop_vec4(const Op& root, Step* st);
-  bool gen_reduce_vec4(const Op& root, Step* st);
+  bool gen_reduce_vec4(const Op& root, Step* st, const Op* epi);
+  // Code of the epilogue expression at output coordinates oc, with the
+  // reduced value in the variable r_; *val receives its name.
+  std::string epilogue_code(Ctx& c, const Op& red, const Op& epi, const std::vector<std::string>& oc, int indent,
+                            std::string* val);
   Val eval(Ctx& c, int v, const std::vector<std::string>& coords);
   Val leaf_load(Ctx& c, int v, const std::vector<std::string>& coords);
   std::string fresh(Ctx& c, const char* p = "t") { return p + std::to_string(c.tmp++); }

@@ -270,6 +270,136 @@ struct Planner {
     }
   }
 
+  // Reduction epilogues.  A row reduction X (trailing dims) whose every use
+  // is an element-wise op of one loop cluster R (directly or through reshapes
+  // that only add or drop unit dims), with R of X's shape up to unit dims and
+  // X reached from R through element-wise ops and such reshapes only, is
+  // computed inside R's kernel: the reduction runs per output element of R
+  // and R's expression is evaluated on the result (layer-norm statistics
+  // followed by their scalar arithmetic become one kernel).  cluster[X]
+  // becomes R; epilogue_of[R] = X.
+  std::map<int, int> epilogue_of;
+  static std::vector<int64_t> nonunit(const std::vector<int64_t>& sh) {
+    std::vector<int64_t> r;
+    for (int64_t d : sh)
+      if (d != 1) r.push_back(d);
+    return r;
+  }
+  // reshape / broadcast_in_dim that only inserts or removes unit dims
+  bool unit_map(int v) const {
+    const Op* p = producer(v);
+    if (!p || cluster[v] != kDup) return false;
+    if (p->kind != OpKind::Reshape && p->kind != OpKind::BroadcastInDim) return false;
+    const auto& in = f.value_types[p->operands[0]].shape;
+    if (nonunit(in) != nonunit(p->type.shape)) return false;
+    if (p->kind == OpKind::BroadcastInDim)
+      for (size_t i = 1; i < p->dims.size(); ++i)
+        if (p->dims[i] <= p->dims[i - 1]) return false;
+    return true;
+  }
+  // every use of v is an element-wise op of one cluster (*R), possibly through unit maps
+  bool uses_in_one_cluster(int v, int* R, int depth = 0) const {
+    if (depth > 8 || returned[v] || consumers[v].empty()) return false;
+    for (auto [oi, slot] : consumers[v]) {
+      const Op& c = f.ops[oi];
+      if (unit_map(c.result)) {
+        if (!uses_in_one_cluster(c.result, R, depth + 1)) return false;
+        continue;
+      }
+      const int cr = cluster[c.result];
+      if (!is_elementwise(c.kind) || cr < 0 || (*R >= 0 && cr != *R)) return false;
+      *R = cr;
+    }
+    return true;
+  }
+  bool reaches_elementwise_only(int u, int R, int X, std::set<int>& seen, bool& hit) const {
+    if (!seen.insert(u).second) return true;
+    const Op* p = producer(u);
+    if (!p) return true;
+    for (int o : p->operands) {
+      if (o == X) { hit = true; continue; }
+      if (cluster[o] == R) {
+        const Op* q = producer(o);
+        if (!q || !is_elementwise(q->kind)) return false;
+        if (!reaches_elementwise_only(o, R, X, seen, hit)) return false;
+      } else if (unit_map(o)) {
+        if (!reaches_elementwise_only(o, R, X, seen, hit)) return false;
+      } else if (cluster[o] == kDup) {
+        // X must not be read through any other index map
+        std::set<int> seen2;
+        if (reads_value(o, R, X, seen2)) return false;
+      }
+    }
+    return true;
+  }
+  // True when evaluating u inside cluster R reads X.
+  bool reads_value(int u, int R, int X, std::set<int>& seen) const {
+    if (u == X) return true;
+    if (!seen.insert(u).second || (cluster[u] != kDup && cluster[u] != R)) return false;
+    const Op* p = producer(u);
+    if (!p) return false;
+    for (int o : p->operands)
+      if (reads_value(o, R, X, seen)) return true;
+    return false;
+  }
+  // The single element-wise use of v (seen through unit maps), or -1.
+  int single_elementwise_use(int v) const {
+    int u = v, depth = 0;
+    for (;;) {
+      if (returned[u] || consumers[u].size() != 1 || ++depth > 8) return -1;
+      const Op& c = f.ops[consumers[u][0].first];
+      if (unit_map(c.result)) { u = c.result; continue; }
+      return is_elementwise(c.kind) ? c.result : -1;
+    }
+  }
+  // Returns true when it made a value a root (the clustering must be redone):
+  // the top T of a row reduction's per-row element-wise chain (same shape up
+  // to unit dims, one use per step), when T's cluster is wider (T is read
+  // through a broadcast), so that the per-row arithmetic runs once per row in
+  // the reduction's epilogue instead of once per element of the consumer.
+  bool absorb_reduce_epilogues() {
+    bool changed = false;
+    epilogue_of.clear();
+    for (const Op& x : f.ops) {
+      const int X = x.result;
+      if (!live[X] || x.kind != OpKind::Reduce || cluster[X] != X || returned[X] || forced.count(X) ||
+          fused_dot.count(X))
+        continue;
+      const int r = (int)f.value_types[x.operands[0]].shape.size();
+      std::vector<int64_t> rd(x.dims.begin(), x.dims.end());
+      std::sort(rd.begin(), rd.end());
+      bool trailing = !rd.empty();
+      for (size_t i = 0; i < rd.size(); ++i)
+        if (rd[rd.size() - 1 - i] != r - 1 - (int64_t)i) trailing = false;
+      if (!trailing) continue;
+      int R = -1;
+      if (!uses_in_one_cluster(X, &R) || R < 0 || epilogue_of.count(R)) continue;
+      const Op* ro = producer(R);
+      if (ro && is_elementwise(ro->kind) && nonunit(f.value_types[R].shape) != nonunit(f.value_types[X].shape)) {
+        const auto xs = nonunit(f.value_types[X].shape);
+        int t = X;
+        for (int u = single_elementwise_use(X); u >= 0 && cluster[u] == R && nonunit(f.value_types[u].shape) == xs &&
+                                                f.value_types[u].dtype == DType::F32;
+             u = single_elementwise_use(u))
+          t = u;
+        if (t != X && !forced.count(t)) {
+          forced.insert(t);
+          changed = true;
+        }
+        continue;
+      }
+      if (!ro || !is_elementwise(ro->kind) || nonunit(f.value_types[R].shape) != nonunit(f.value_types[X].shape) ||
+          f.value_types[R].dtype != DType::F32 || f.value_types[X].dtype != DType::F32)
+        continue;
+      std::set<int> seen;
+      bool hit = false;
+      if (!reaches_elementwise_only(R, R, X, seen, hit) || !hit) continue;
+      epilogue_of[R] = X;
+      cluster[X] = R;
+    }
+    return changed;
+  }
+
   bool materialized(int v) const { return cluster[v] == kParam || cluster[v] == kConst || cluster[v] == v; }
 
   // View of v over a materialized buffer, through duplicable index maps.
@@ -635,7 +765,7 @@ Plan plan_function(const Function& f, Precision prec) {
   for (int iter = 0;; ++iter) {
     if (iter > 8) throw std::runtime_error("planner did not converge");
     pl.clusterize();
-    bool retry = false;
+    bool retry = pl.absorb_reduce_epilogues();
     for (size_t i = 0; i < f.ops.size(); ++i) {
       const Op& op = f.ops[i];
       if (!pl.live[op.result]) continue;
@@ -750,6 +880,9 @@ Plan plan_function(const Function& f, Precision prec) {
     } else if (op.kind == OpKind::Reduce) {
       st.kind = StepKind::Reduce;
       cg.gen_reduce(op, &st);
+    } else if (pl.epilogue_of.count(v)) {
+      st.kind = StepKind::Reduce;
+      cg.gen_reduce(f.ops[f.producer[pl.epilogue_of[v]]], &st, &op);
     } else {
       st.kind = StepKind::Loop;
       cg.gen_loop(op, &st);

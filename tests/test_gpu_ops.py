@@ -90,6 +90,11 @@ def test_reduce_chain_rows_then_all(fp32_session):
     assert [st["kind"] for st in plan_steps(text, name, "fp32")] == ["reduce", "reduce"]
 
 
+def test_layernorm_reduce_epilogues(fp32_session):
+    from test_abi import LAYERNORM
+    check(fp32_session, "ln.f", LAYERNORM, [rnd(64, 32, 64)], rtol=2e-5, atol=2e-5)
+
+
 def test_elementwise_chain_with_broadcasts(fp32_session):
     name, text = module(["tensor<37x129xf32>", "tensor<129xf32>", "tensor<37x1xf32>"], [
         "%0 = stablehlo.broadcast_in_dim %arg1, dims = [1] : (tensor<129xf32>) -> tensor<37x129xf32>",
