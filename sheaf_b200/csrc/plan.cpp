@@ -1038,6 +1038,86 @@ std::unique_ptr<Function> merge_reduce_chains(const Function& f) {
   return g;
 }
 
+// transpose(dot(L, R)) -> dot(R, L), and transpose(reduce_add over the
+// leading batch dim of dot(L, R)) -> reduce_add(dot(R, L)), when the dot (and
+// the reduction) have no other use and each operand has one free dim: the
+// GEMM writes the transposed layout itself.  Sheaf's weight gradients arrive
+// this way (dW = tr(sum_b x_b^T @ g_b)); without the rewrite the GEMM output
+// is copied through a transposing loop.
+std::unique_ptr<Function> transpose_dot_outputs(const Function& f) {
+  std::vector<int> uses(f.num_values(), 0);
+  std::vector<char> returned(f.num_values(), 0);
+  for (int r : f.returns) returned[r] = 1;
+  for (const Op& op : f.ops)
+    for (int o : op.operands) ++uses[o];
+  auto single = [&](int v) { return v >= 0 && uses[v] == 1 && !returned[v] && f.producer[v] >= 0; };
+  // dot with batch dims 0..nb-1 on both sides and one free dim per operand
+  auto simple_dot = [&](const Op& d) {
+    if (d.kind != OpKind::DotGeneral || d.lb.size() != d.rb.size()) return false;
+    const size_t nb = d.lb.size();
+    for (size_t i = 0; i < nb; ++i)
+      if (d.lb[i] != (int64_t)i || d.rb[i] != (int64_t)i) return false;
+    const size_t lr = f.value_types[d.operands[0]].shape.size(), rr = f.value_types[d.operands[1]].shape.size();
+    return lr == nb + 1 + d.lc.size() && rr == nb + 1 + d.rc.size() && d.type.shape.size() == nb + 2;
+  };
+  auto swapped = [](Op d) {
+    std::swap(d.operands[0], d.operands[1]);
+    std::swap(d.lb, d.rb);
+    std::swap(d.lc, d.rc);
+    return d;
+  };
+  std::unique_ptr<Function> g;
+  std::vector<char> erase(f.ops.size(), 0);
+  for (size_t i = 0; i < f.ops.size(); ++i) {
+    const Op& t = f.ops[i];
+    if (t.kind != OpKind::Transpose || !single(t.operands[0])) continue;
+    const int v = t.operands[0];
+    const int pv = f.producer[v];
+    const Op& pop = f.ops[pv];
+    const size_t r = t.dims.size();
+    if (r < 2 || t.dims[r - 1] != (int64_t)r - 2 || t.dims[r - 2] != (int64_t)r - 1) continue;
+    bool lead_ident = true;
+    for (size_t k = 0; k + 2 < r; ++k) lead_ident = lead_ident && t.dims[k] == (int64_t)k;
+    if (!lead_ident) continue;
+    if (simple_dot(pop) && pop.lb.size() + 2 == r) {
+      if (!g) g = std::make_unique<Function>(f);
+      Op d = swapped(pop);
+      d.result = t.result;
+      d.type = t.type;
+      g->ops[pv] = d;
+      erase[i] = 1;
+      continue;
+    }
+    // reduce_add over dim 0 of a batched simple dot, 2-D result
+    if (pop.kind != OpKind::Reduce || pop.body != ReduceBody::Add || pop.dims.size() != 1 || pop.dims[0] != 0 ||
+        r != 2 || !single(pop.operands[0]) || !is_identity_init(f, pop.operands[1], pop.body))
+      continue;
+    const int dv = pop.operands[0];
+    const int pd = f.producer[dv];
+    const Op& dop = f.ops[pd];
+    if (!simple_dot(dop) || dop.lb.size() != 1) continue;
+    if (!g) g = std::make_unique<Function>(f);
+    Op d = swapped(dop);
+    const auto& ds = f.value_types[dv].shape;
+    d.type.shape = {ds[0], ds[2], ds[1]};
+    g->value_types[dv] = d.type;
+    g->ops[pd] = d;
+    Op red = pop;
+    red.result = t.result;
+    red.type = t.type;
+    g->ops[pv] = red;
+    erase[i] = 1;
+  }
+  if (!g) return g;
+  std::vector<Op> kept;
+  for (size_t i = 0; i < g->ops.size(); ++i)
+    if (!erase[i]) kept.push_back(std::move(g->ops[i]));
+  g->ops = std::move(kept);
+  g->producer.assign(g->num_values(), -1);
+  for (size_t i = 0; i < g->ops.size(); ++i) g->producer[g->ops[i].result] = (int)i;
+  return g;
+}
+
 }  // namespace
 
 Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
@@ -1045,6 +1125,7 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
   std::string log;
   if (prec == Precision::TF32 && fuse_attention) cur.reset(rewrite_attention(f, &log).release());
   if (auto m = merge_reduce_chains(cur ? *cur : f)) cur.reset(m.release());
+  if (auto m = transpose_dot_outputs(cur ? *cur : f)) cur.reset(m.release());
   if (cur) {
     Plan p = plan_function(*cur, prec);
     p.rewritten = cur;

@@ -95,6 +95,20 @@ def test_layernorm_reduce_epilogues(fp32_session):
     check(fp32_session, "ln.f", LAYERNORM, [rnd(64, 32, 64)], rtol=2e-5, atol=2e-5)
 
 
+@pytest.mark.parametrize("fixture", ["fp32_session", "tf32_session"])
+def test_transposed_gemm_outputs(request, fixture):
+    from test_abi import TRANSPOSED_WGRAD
+    sess = request.getfixturevalue(fixture)
+    ins = [rnd(4, 64, 96), rnd(4, 64, 160), rnd(96, 64), rnd(64, 160)]
+    if fixture == "fp32_session":
+        check(sess, "tw.f", TRANSPOSED_WGRAD, ins, rtol=1e-4, atol=1e-4)
+    else:
+        sess.load_stablehlo(TRANSPOSED_WGRAD)
+        outs = sess.call("tw.f", ins)
+        for o, r in zip(outs, run(TRANSPOSED_WGRAD, "tw.f", ins)):
+            assert np.linalg.norm(o - r) / np.linalg.norm(r) <= 2e-3
+
+
 def test_elementwise_chain_with_broadcasts(fp32_session):
     name, text = module(["tensor<37x129xf32>", "tensor<129xf32>", "tensor<37x1xf32>"], [
         "%0 = stablehlo.broadcast_in_dim %arg1, dims = [1] : (tensor<129xf32>) -> tensor<37x129xf32>",
