@@ -212,7 +212,10 @@ struct Planner {
   bool remat_cone(int u, int& ops, int& trans, std::set<int>& leaves, std::set<int>& seen) const {
     if (!seen.insert(u).second) return true;
     const Op* p = producer(u);
-    if (!p || returned[u] || forced.count(u) || p->kind == OpKind::Reduce || p->kind == OpKind::DotGeneral ||
+    // a value already made a root, or (not yet decided: it comes earlier in
+    // the program) one with several uses, is read, not recomputed
+    const bool shared = p && (cluster[u] == u || (cluster[u] == -1 && consumers[u].size() > 1 && !is_dup_kind(*p)));
+    if (!p || returned[u] || forced.count(u) || shared || p->kind == OpKind::Reduce || p->kind == OpKind::DotGeneral ||
         is_attention(p->kind) || (p->kind == OpKind::Constant && p->values.size() != 1)) {
       leaves.insert(u);
       return leaves.size() <= 3;
@@ -242,6 +245,40 @@ struct Planner {
     int ops = 0, trans = 0;
     std::set<int> leaves, seen;
     return remat_cone(v, ops, trans, leaves, seen);
+  }
+
+  // The cone a rematerialized value really has once every value is decided:
+  // kDup nodes are recomputed (followed), everything else is read.  A value
+  // whose cone grew past the limits (its producers were assumed to be read
+  // but were themselves rematerialized) becomes a root; true if any did.
+  bool real_cone(int u, int& ops, int& trans, std::set<int>& leaves, std::set<int>& seen) const {
+    if (!seen.insert(u).second) return true;
+    const Op* p = producer(u);
+    if (!p || cluster[u] != kDup) {
+      leaves.insert(u);
+      return leaves.size() <= 3;
+    }
+    if (p->kind == OpKind::Constant || p->kind == OpKind::Iota) return true;
+    if (is_elementwise(p->kind)) {
+      if (++ops > kRematOps || (transcendental(p->kind) && ++trans > 2)) return false;
+    }
+    for (int o : p->operands)
+      if (!real_cone(o, ops, trans, leaves, seen)) return false;
+    return true;
+  }
+  bool validate_remat() {
+    bool changed = false;
+    for (const Op& op : f.ops) {
+      const int v = op.result;
+      if (!live[v] || cluster[v] != kDup || !is_elementwise(op.kind)) continue;
+      int ops = 0, trans = 0;
+      std::set<int> leaves, seen;
+      if (!real_cone(v, ops, trans, leaves, seen)) {
+        forced.insert(v);
+        changed = true;
+      }
+    }
+    return changed;
   }
 
   void clusterize() {
@@ -763,8 +800,9 @@ Plan plan_function(const Function& f, Precision prec) {
   Planner pl(f, prec);
   pl.liveness();
   for (int iter = 0;; ++iter) {
-    if (iter > 8) throw std::runtime_error("planner did not converge");
+    if (iter > 64) throw std::runtime_error("planner did not converge");
     pl.clusterize();
+    if (pl.validate_remat()) continue;
     bool retry = pl.absorb_reduce_epilogues();
     for (size_t i = 0; i < f.ops.size(); ++i) {
       const Op& op = f.ops[i];
