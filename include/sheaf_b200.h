@@ -151,6 +151,33 @@ SB_API uint32_t sb_buffer_element_type(const sb_buffer* buffer);
 SB_API size_t sb_buffer_byte_length(const sb_buffer* buffer);
 SB_API void* sb_buffer_device_pointer(const sb_buffer* buffer);
 
+/* --- fused optimizer step -------------------------------------------------- *
+ * Replaces lib/optim.shf:72-83 (global-norm, clip-by-global-norm) followed by
+ * lib/optim.shf:36-58 (adamw-step), as examples/nanoGPT/train.shf:26-33 calls
+ * them after every value-and-grad.  For each leaf i (params[i], grads[i],
+ * m[i], v[i]: f32 buffers of one element count, on this session's device),
+ * in place on the session stream:
+ *   norm = sqrt(sum over all leaves of sum(g^2))        (before clipping)
+ *   g'   = g * min(1, max_grad_norm / (norm + 1e-8))     (if max_grad_norm > 0)
+ *   m    = beta1 m + (1 - beta1) g'
+ *   v    = beta2 v + (1 - beta2) g'^2
+ *   p    = p - lr (weight_decay p + (m bc_m) / (sqrt(v bc_v) + epsilon)),
+ *          bc_m = 1 / (1 - beta1^(step+1)), bc_v = 1 / (1 - beta2^(step+1)).
+ * `step` is the t passed to adamw-step (the update uses t + 1; the caller
+ * keeps t).  Gradients are read only.  The norm is a fixed-order sum:
+ * results are deterministic.  When out_global_norm is non-NULL the call waits
+ * for the step and stores the pre-clip norm there; otherwise it returns once
+ * the work is enqueued. */
+typedef struct sb_adamw_options {
+  float learning_rate, beta1, beta2, epsilon, weight_decay;
+  float max_grad_norm; /* > 0: clip by global norm first; <= 0: no clipping */
+  int64_t step;
+} sb_adamw_options;
+SB_API void sb_adamw_options_initialize(sb_adamw_options* options);
+SB_API sb_status* sb_optimizer_adamw_step(sb_session* session, size_t leaf_count, sb_buffer* const* params,
+                                          sb_buffer* const* grads, sb_buffer* const* m, sb_buffer* const* v,
+                                          const sb_adamw_options* options, float* out_global_norm);
+
 /* --- allocation-free GEMM --------------------------------------------------- *
  * No counterpart in the reference.  For callers that must not allocate device
  * memory: work recorded in a CUDA stream capture, code running under another

@@ -789,12 +789,13 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
   // Split-K, by a fixed rule so that the summation order (the only part of
   // the result that depends on the plan) does not depend on the kernel
   // configuration: a single GEMM whose 128 x 128 tiles do not cover the SMs
-  // is split into enough K ranges for ~2 CTAs per SM, at least 512 of K each.
+  // is split into as many K ranges as fit one wave of 2 CTAs per SM (a partial
+  // second wave costs more than it saves), at least 512 of K each.
   p->splits = 1;
   p->k_chunk = 0;
   const int64_t tiles = ((g.M + 127) / 128) * ((g.N + 127) / 128);
   if (g.batch == 1 && tiles < sms) {
-    const int64_t s = std::min<int64_t>((2 * sms + tiles - 1) / tiles, g.K / 512);
+    const int64_t s = std::min<int64_t>(2 * sms / tiles, g.K / 512);
     if (s >= 2) {
       int64_t chunk = (g.K + s - 1) / s;
       chunk = (chunk + BK - 1) / BK * BK;

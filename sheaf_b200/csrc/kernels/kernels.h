@@ -86,4 +86,25 @@ struct AttnArgs {
 };
 cudaError_t attention(const AttnArgs& a, cudaStream_t stream);
 
+// Fused clip-by-global-norm + AdamW (kernels/optim.cu).  Leaves and chunks
+// live in device memory; partials holds one float per chunk.  norm_out (device,
+// may be null) receives the global L2 norm of the gradients before clipping.
+struct OptLeaf {
+  float* p;
+  const float* g;
+  float* m;
+  float* v;
+  int64_t n;
+};
+struct OptChunk {
+  int leaf;
+  int64_t off, len;
+};
+struct AdamwScalars {
+  float lr, b1, b2, one_minus_b1, one_minus_b2, eps, wd, bc_m, bc_v, max_norm;
+  int clip;
+};
+cudaError_t adamw_step(const OptLeaf* leaves, const OptChunk* chunks, int n_chunks, float* partials,
+                       float* norm_out, const AdamwScalars& a, cudaStream_t stream);
+
 }  // namespace sb

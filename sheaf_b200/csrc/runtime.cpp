@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -760,6 +761,89 @@ sb_status* sb_buffer_wrap_device(sb_session* s, size_t rank, const uint64_t* sha
   b->ptr = dptr;
   b->owned = false;
   *out = b;
+  return nullptr;
+}
+
+void sb_adamw_options_initialize(sb_adamw_options* o) {
+  if (!o) return;
+  o->learning_rate = 1e-3f;
+  o->beta1 = 0.9f;
+  o->beta2 = 0.999f;
+  o->epsilon = 1e-8f;
+  o->weight_decay = 0.f;
+  o->max_grad_norm = 0.f;
+  o->step = 0;
+}
+
+sb_status* sb_optimizer_adamw_step(sb_session* s, size_t n, sb_buffer* const* params, sb_buffer* const* grads,
+                                   sb_buffer* const* m, sb_buffer* const* v, const sb_adamw_options* o,
+                                   float* out_global_norm) {
+  using namespace sb;
+  if (!s || !o || (n && (!params || !grads || !m || !v)))
+    return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  if (n > (size_t)INT32_MAX) return make_status(SB_STATUS_INVALID_ARGUMENT, "too many leaves");
+  if (o->step < 0) return make_status(SB_STATUS_INVALID_ARGUMENT, "negative step");
+  // fixed partition of every leaf into chunks of at most 16384 elements
+  constexpr int64_t kChunk = 16384;
+  std::vector<OptLeaf> leaves(n);
+  std::vector<OptChunk> chunks;
+  for (size_t i = 0; i < n; ++i) {
+    sb_buffer* bs[4] = {params[i], grads[i], m[i], v[i]};
+    for (int k = 0; k < 4; ++k) {
+      if (!bs[k]) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL buffer in leaf " + std::to_string(i));
+      if (bs[k]->type.dtype != DType::F32)
+        return make_status(SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": buffers must be f32");
+      if (bs[k]->dev.get() != s->dev.get())
+        return make_status(SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": buffer of another session");
+      if (bs[k]->bytes != params[i]->bytes)
+        return make_status(SB_STATUS_INVALID_ARGUMENT,
+                           "leaf " + std::to_string(i) + ": parameter, gradient and moment sizes differ");
+    }
+    const int64_t count = (int64_t)(params[i]->bytes / 4);
+    leaves[i] = OptLeaf{(float*)params[i]->ptr, (const float*)grads[i]->ptr, (float*)m[i]->ptr, (float*)v[i]->ptr,
+                        count};
+    for (int64_t off = 0; off < count; off += kChunk)
+      chunks.push_back(OptChunk{(int)i, off, std::min(kChunk, count - off)});
+  }
+  if (chunks.size() > (size_t)INT32_MAX) return make_status(SB_STATUS_INVALID_ARGUMENT, "too many elements");
+  std::lock_guard<std::mutex> g(s->mu);
+  SB_CUDA(cudaSetDevice(s->dev->ordinal));
+  if (chunks.empty()) {
+    if (out_global_norm) *out_global_norm = 0.f;
+    return nullptr;
+  }
+  // scalar terms in double, as Sheaf evaluates scalars before they meet tensors
+  const double t1 = (double)o->step + 1.0;
+  AdamwScalars a;
+  a.lr = o->learning_rate;
+  a.b1 = o->beta1;
+  a.b2 = o->beta2;
+  a.one_minus_b1 = (float)(1.0 - (double)o->beta1);
+  a.one_minus_b2 = (float)(1.0 - (double)o->beta2);
+  a.eps = o->epsilon;
+  a.wd = o->weight_decay;
+  a.bc_m = (float)(1.0 / (1.0 - std::pow((double)o->beta1, t1)));
+  a.bc_v = (float)(1.0 / (1.0 - std::pow((double)o->beta2, t1)));
+  a.max_norm = o->max_grad_norm;
+  a.clip = o->max_grad_norm > 0.f ? 1 : 0;
+  const size_t lb = n * sizeof(OptLeaf), cb = chunks.size() * sizeof(OptChunk);
+  const size_t pb = chunks.size() * sizeof(float);
+  const size_t off_c = (lb + 255) & ~(size_t)255, off_p = (off_c + cb + 255) & ~(size_t)255;
+  const size_t off_n = (off_p + pb + 255) & ~(size_t)255, total = off_n + 256;
+  void* ws = nullptr;
+  SB_CUDA(cudaMallocAsync(&ws, total, s->dev->stream));
+  char* base = (char*)ws;
+  // pageable sources: the copies are staged before cudaMemcpyAsync returns
+  cudaError_t e = cudaMemcpyAsync(base, leaves.data(), lb, cudaMemcpyHostToDevice, s->dev->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(base + off_c, chunks.data(), cb, cudaMemcpyHostToDevice, s->dev->stream);
+  if (e == cudaSuccess)
+    e = adamw_step((const OptLeaf*)base, (const OptChunk*)(base + off_c), (int)chunks.size(), (float*)(base + off_p),
+                   out_global_norm ? (float*)(base + off_n) : nullptr, a, s->dev->stream);
+  if (e == cudaSuccess && out_global_norm)
+    e = cudaMemcpyAsync(out_global_norm, base + off_n, sizeof(float), cudaMemcpyDeviceToHost, s->dev->stream);
+  cudaFreeAsync(ws, s->dev->stream);
+  if (e != cudaSuccess) return cuda_status(e, "sb_optimizer_adamw_step");
+  if (out_global_norm) return wait_stream(s, s->opts.world_size > 1 ? deadline_ms(s) : 0);
   return nullptr;
 }
 

@@ -45,6 +45,12 @@ class _Options(ctypes.Structure):
                 ("kernel_cache_dir", ctypes.c_char_p), ("flags", ctypes.c_uint32)]
 
 
+class _AdamwOptions(ctypes.Structure):
+    _fields_ = [("learning_rate", ctypes.c_float), ("beta1", ctypes.c_float), ("beta2", ctypes.c_float),
+                ("epsilon", ctypes.c_float), ("weight_decay", ctypes.c_float), ("max_grad_norm", ctypes.c_float),
+                ("step", ctypes.c_int64)]
+
+
 class _Stats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("host_bytes_peak", "host_bytes_allocated", "host_bytes_freed",
                                                 "device_bytes_peak", "device_bytes_allocated", "device_bytes_freed")]
@@ -83,6 +89,9 @@ SIGNATURES = {
     "sb_buffer_byte_length": (ctypes.c_size_t, [_P]),
     "sb_buffer_device_pointer": (_P, [_P]),
     "sb_nccl_get_unique_id": (_P, [ctypes.POINTER(ctypes.c_uint8)]),
+    "sb_adamw_options_initialize": (None, [ctypes.POINTER(_AdamwOptions)]),
+    "sb_optimizer_adamw_step": (_P, [_P, ctypes.c_size_t, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P),
+                                     ctypes.POINTER(_P), ctypes.POINTER(_AdamwOptions), ctypes.POINTER(ctypes.c_float)]),
     "sb_gemm_f32_splitk_noalloc": (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P]),
     "sb_module_inspect": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_char_p, ctypes.c_size_t]),
     "sb_module_kernel_source": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_char_p,
@@ -326,6 +335,27 @@ class B200Session:
             red = (ctypes.c_int32 * len(reduce))(*[REDUCE[r] for r in reduce])
         _check(library().sb_session_call(self._h, name.encode(), arr, len(bufs), red, outs, cap, ctypes.byref(n)))
         return [DeviceBuffer(self, ctypes.c_void_p(outs[i])) for i in range(n.value)]
+
+    # optimizer ---------------------------------------------------------------
+    def adamw_step(self, params: Sequence[DeviceBuffer], grads: Sequence[DeviceBuffer], m: Sequence[DeviceBuffer],
+                   v: Sequence[DeviceBuffer], t: int, lr: float, b1: float, b2: float, eps: float, wd: float,
+                   max_grad_norm: float = 0.0, return_norm: bool = False):
+        """`(clip-by-global-norm g max_grad_norm)` then `(adamw-step params g m v t lr b1 b2 eps wd)`
+        (sheaf/lib/optim.shf:77-83, :36-58) over the leaf lists, in place on
+        the device buffers.  Returns the new t (t + 1), and with return_norm
+        the gradients' global norm before clipping (waits for the step)."""
+        n = len(params)
+        if not (len(grads) == len(m) == len(v) == n):
+            raise B200Error(3, "params, grads, m and v must have the same number of leaves")
+        arr = lambda bs: (ctypes.c_void_p * max(n, 1))(*[b.handle for b in bs])
+        o = _AdamwOptions()
+        library().sb_adamw_options_initialize(ctypes.byref(o))
+        o.learning_rate, o.beta1, o.beta2, o.epsilon, o.weight_decay = lr, b1, b2, eps, wd
+        o.max_grad_norm, o.step = max_grad_norm, t
+        norm = ctypes.c_float(0.0)
+        _check(library().sb_optimizer_adamw_step(self._h, n, arr(params), arr(grads), arr(m), arr(v), ctypes.byref(o),
+                                                 ctypes.byref(norm) if return_norm else None))
+        return (t + 1, norm.value) if return_norm else t + 1
 
     def call(self, name: str, args: Sequence) -> List[np.ndarray]:
         outs = self.call_device(name, args)

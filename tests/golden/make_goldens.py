@@ -1,10 +1,12 @@
-"""Extract the reference's known-answer vectors into tests/golden/vag_goldens.json.
+"""Extract the reference's known-answer vectors into tests/golden/vag_goldens.json
+and tests/golden/optim_goldens.json.
 
 Reads the reference's own test files as text (they are YAML / Markdown, no
 reference code is executed):
   sheaf/tests/vag_tests.yaml:5-169         finite-difference value-and-grad goldens
   sheaf/tests/interpreter_tests.yaml:753-762  MLP value-and-grad loss with splitmix inputs
   README.md:33-43                          mse-loss value-and-grad example
+  sheaf/tests/interpreter_tests.yaml:623-628  adamw-step with and without decay
 
 Run from the repo root:  python tests/golden/make_goldens.py [reference_root]
 """
@@ -15,6 +17,7 @@ import sys
 
 REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "vag_goldens.json")
+OUT_OPTIM = os.path.join(os.path.dirname(os.path.abspath(__file__)), "optim_goldens.json")
 
 NUM = r"[-+]?(?:\d+\.?\d*|\.\d+)(?:[eE][-+]?\d+)?"
 
@@ -84,6 +87,20 @@ def main():
     with open(OUT, "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
     print(f"wrote {len(out['cases'])} cases to {OUT}")
+    # (adamw-step p g m v t lr b1 b2 eps wd) on one-leaf trees {:w x}
+    optim = {"source": "sheaf/tests/interpreter_tests.yaml", "cases": {}}
+    for c in yaml_cases(it):
+        if not c["name"].startswith("adamw-step"):
+            continue
+        leaves = [float(x) for x in re.findall(r"\{:w (" + NUM + r")\}", c["test"])]
+        m = re.search(r"\(adamw-step p g m v ((?:" + NUM + r"\s*)+)\)", c["test"])
+        args = [float(x) for x in m.group(1).split()]
+        optim["cases"][c["name"]] = {"test": c["test"], "p": leaves[0], "g": leaves[1], "m": leaves[2],
+                                     "v": leaves[3], "t": int(args[0]), "lr": args[1], "b1": args[2], "b2": args[3],
+                                     "eps": args[4], "wd": args[5], "expected_p": float(c["expected"].strip('"'))}
+    with open(OUT_OPTIM, "w") as f:
+        json.dump(optim, f, indent=1, sort_keys=True)
+    print(f"wrote {len(optim['cases'])} cases to {OUT_OPTIM}")
 
 
 if __name__ == "__main__":
