@@ -7,8 +7,10 @@ cross-entropy loss on shifted tokens, global batch 64 x 256 split over the
 ranks (strong scaling); lowered to StableHLO as Sheaf's JIT lowers it and run
 through libsheafb200's C ABI.  Other workloads: `gpt2` (GPT-2-small value-and-
 grad: 12 layers, d768, ctx 1024, vocab 50304, batch 8 per GPU, weak scaling),
-`nanogpt-fwd` (the forward alone), `mlp` (the 784-512-10 MLP value-and-grad,
-samples/s), `matmul` (op sweep, --size / --shape / --layout).
+`nanogpt-fwd` (the forward alone), `nanogpt-train` (value-and-grad followed by
+the fused clip-by-global-norm + AdamW step of examples/nanoGPT/train.shf),
+`mlp` (the 784-512-10 MLP value-and-grad, samples/s), `matmul` (op sweep,
+--size / --shape / --layout).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload W]
 
@@ -41,7 +43,8 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
                    choices=["fp32", "tf32", "bf16"])
-    p.add_argument("--workload", default="nanogpt", choices=["nanogpt", "nanogpt-fwd", "gpt2", "mlp", "matmul"])
+    p.add_argument("--workload", default="nanogpt",
+                   choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "gpt2", "mlp", "matmul"])
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
     p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
@@ -62,7 +65,7 @@ def env_rank():
 def workload(name, world, batch=0):
     """(config, global batch, per-rank batch, scaling) of a GPT workload."""
     from sheaf_b200.programs import models as M
-    if name in ("nanogpt", "nanogpt-fwd"):
+    if name in ("nanogpt", "nanogpt-fwd", "nanogpt-train"):
         c = M.NANOGPT
         gb = batch or c.batch
         if gb % world:
@@ -97,7 +100,8 @@ def program(args, world, rank):
         inp[n] = inp[n][rank * b:(rank + 1) * b]
     fwd = args.workload == "nanogpt-fwd"
     low = M.gpt_fwd(c, batch=b) if fwd else M.gpt_vag(c, batch=b)
-    kind = "forward" if fwd else "value-and-grad"
+    kind = "forward" if fwd else ("train step (value-and-grad, clip-by-global-norm 1.0, adamw)"
+                                  if args.workload == "nanogpt-train" else "value-and-grad")
     name = "gpt2-small" if args.workload == "gpt2" else "nanogpt"
     cfg = {"workload": f"{name} {kind} {gb}x{c.T}",
            "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
@@ -185,14 +189,30 @@ def cpu_baseline(args, steps=2):
         sample = f"{b} sequence(s) x {T} tokens of the same model"
     f = parse_module(low.text)[low.qualified]
     ins = [inp[n] for n in low.arg_names]
-    evaluate(f, ins, dtype=np.float32)
+    train = args.workload == "nanogpt-train"
+    params = [inp[n] for n in low.arg_names if n not in ("x", "y")]
+    moments = [np.zeros_like(p) for p in params]
+
+    def one():
+        outs = evaluate(f, ins, dtype=np.float32)
+        if train:
+            from oracle.optim_ref import train_update
+            train_update(params, outs[1:], moments, moments, 0, *TRAIN_HP)
+    one()
     t0 = time.time()
     for _ in range(steps):
-        evaluate(f, ins, dtype=np.float32)
+        one()
     dt = (time.time() - t0) / steps
+    if train:
+        sample = sample + " plus clip-by-global-norm + AdamW over all parameters (oracle/optim_ref.py)"
     return {"value": units / dt, "unit": unit, "cores": os.cpu_count(), "kind": "port",
             "sample": f"{sample} per step, numpy float32 interpretation of the same StableHLO "
                       f"(oracle/stablehlo_ref.py), mean of {steps} steps"}
+
+
+# train.shf:29-32: clip-by-global-norm 1.0, adamw-step lr b1 b2 eps wd (lr as
+# nanoGPT's shakespeare-char config, before any schedule)
+TRAIN_HP = (1e-3, 0.9, 0.95, 1e-8, 0.1, 1.0)
 
 
 def run_reference(args):
@@ -243,8 +263,20 @@ def run_ours(args):
     q = low.qualified
     reduce = ["mean"] * len(low.result_types) if (world > 1 and vag) else None
 
+    # training step: the fused optimizer applies the (all-reduced) gradients to
+    # the resident parameters, as train.shf's train-step does after value-and-grad
+    train = args.workload == "nanogpt-train"
+    pidx = [i for i, n in enumerate(names) if n not in data_names]
+    if train:
+        moments = [[sess.buffer(np.zeros_like(inp[names[i]])) for i in pidx] for _ in range(2)]
+        tstate = [0]
+        lr, b1, b2, eps, wd, clip = TRAIN_HP
+
     def step(buffers):
         outs = sess.call_device(q, buffers, reduce)
+        if train:
+            tstate[0] = sess.adamw_step([buffers[i] for i in pidx], outs[1:], moments[0], moments[1], tstate[0],
+                                        lr, b1, b2, eps, wd, max_grad_norm=clip)
         return outs
 
     def barrier():
@@ -328,6 +360,8 @@ def run_ours(args):
                              f"{r['elements']},{r['bytes']},{r['flops']}\n")
         calls = max(1, rows[0]["calls"]) if rows else 1
         launches = sum(r["launches_per_call"] for r in rows if r["function"] == q)
+        if train:
+            launches += 2  # optimizer: gradient norm pass + fused clip/AdamW pass
         kinds = ("gemm", "attention", "loop", "reduce")
         tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in kinds}
         allms = sum(tot.values())
