@@ -213,7 +213,7 @@ def _parse_op(st: str) -> Op:
         mm = re.match(r"(.*),\s*dim = (\d+)\s*:\s*\((.*)\)\s*->\s*(.*)$", rest)
         ops = [o.strip() for o in mm.group(1).split(",")]
         return Op(results, kind, ops, {"dim": int(mm.group(2))}, [parse_type(mm.group(4))])
-    if kind in ("reshape", "convert"):
+    if kind in ("reshape", "convert", "bitcast_convert"):
         mm = re.match(r"(%\w+)\s*:\s*\((.*)\)\s*->\s*(.*)$", rest)
         return Op(results, kind, [mm.group(1)], {}, [parse_type(mm.group(3))])
     if kind == "select":
@@ -230,6 +230,12 @@ def _parse_op(st: str) -> Op:
         mm = re.match(r"(%\w+)\s*:\s*(.*)$", rest)
         return Op(results, kind, [mm.group(1)], {}, [parse_type(mm.group(2))])
     raise NotImplementedError(f"oracle: unsupported op {kind}")
+
+
+def _wrap32(x):
+    """Two's-complement wraparound of integers to 32 bits (StableHLO i32)."""
+    x = np.asarray(x, dtype=np.int64)
+    return ((x + (1 << 31)) & 0xFFFFFFFF) - (1 << 31)
 
 
 def _as(x, dt, dtype):
@@ -294,10 +300,23 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
             r = np.cos(v[0])
         elif k == "sign":
             r = np.sign(v[0])
+        elif k == "floor":
+            r = np.floor(v[0])
+        elif k == "ceil":
+            r = np.ceil(v[0])
         elif k == "not":
             r = np.logical_not(v[0]) if v[0].dtype == np.bool_ else ~v[0]
         elif k == "clamp":
             r = np.minimum(np.maximum(v[1], v[0]), v[2])
+        elif k == "bitcast_convert":
+            # 32-bit reinterpretation (f32 <-> i32); f32 values are rounded to
+            # f32 first (the f64 evaluation mode carries them wider)
+            if odt == "i32" and v[0].dtype.kind == "f":
+                r = np.asarray(v[0], np.float32).view(np.int32).astype(np.int64)
+            elif odt in ("f32",) and v[0].dtype.kind != "f":
+                r = _wrap32(v[0]).astype(np.int32).view(np.float32).astype(dtype)
+            else:
+                r = v[0]
         elif k == "convert":
             if odt in ("f32", "bf16", "f64"):
                 r = v[0].astype(dtype)
@@ -384,6 +403,8 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
         r = np.asarray(r)
         if odt in ("f32", "bf16", "f64"):
             r = r.astype(dtype)
+        elif odt == "i32":
+            r = _wrap32(r)
         if tuple(r.shape) != tuple(oshape):
             raise ValueError(f"{op.results[0]} ({k}): shape {r.shape} != {oshape}")
         for name in op.results:

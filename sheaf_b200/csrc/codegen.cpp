@@ -51,6 +51,8 @@ std::string f32_literal(double x) {
 std::string literal(double x, const std::string& ctype) {
   if (ctype == "float") return f32_literal(x);
   if (ctype == "bool") return x != 0 ? "true" : "false";
+  // i32 constants wrap modulo 2^32 (a seed's 32-bit halves arrive as 0..2^32-1)
+  if (ctype == "int") return "(int)" + std::to_string((uint32_t)(uint64_t)(int64_t)x) + "u";
   if (ctype == "double") {
     char buf[48];
     std::snprintf(buf, sizeof buf, "%.17g", x);
@@ -169,6 +171,13 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
     Val r{fresh(c), ct};
     c.body << c.pad() << "const " << ct << " " << r.name << " = " << expr << ";\n";
     return r;
+  };
+  // integer a OP b modulo 2^width, computed unsigned (no signed overflow)
+  auto wrap = [&](const std::string& a, const char* o, const std::string& b) {
+    if (ct == "int") return "(int)((unsigned)(" + a + ") " + o + " (unsigned)(" + b + "))";
+    if (ct == "long long")
+      return "(long long)((unsigned long long)(" + a + ") " + o + " (unsigned long long)(" + b + "))";
+    return a + " " + o + " " + b;
   };
   const auto& osh = op.type.shape;
   switch (op.kind) {
@@ -344,6 +353,13 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
       out = emit("(" + a.name + " " + ops[(int)op.cmp] + " " + b.name + ")");
       break;
     }
+    case OpKind::Bitcast: {
+      Val a = eval(c, op.operands[0], coords);
+      if (a.ctype == ct) out = a;
+      else if (ct == "int") out = emit("__float_as_int(" + a.name + ")");
+      else out = emit("__int_as_float(" + a.name + ")");
+      break;
+    }
     case OpKind::Convert: {
       Val a = eval(c, op.operands[0], coords);
       if (ct == "bool") out = emit("(" + a.name + " != 0)");
@@ -359,9 +375,10 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
         const std::string& y = b.name;
         bool fl = ct == "float" || ct == "double";
         switch (op.kind) {
-          case OpKind::Add: out = emit(x + " + " + y); break;
-          case OpKind::Sub: out = emit(x + " - " + y); break;
-          case OpKind::Mul: out = emit(x + " * " + y); break;
+          // integers wrap modulo 2^width (two's complement), as StableHLO defines
+          case OpKind::Add: out = emit(fl ? x + " + " + y : wrap(x, "+", y)); break;
+          case OpKind::Sub: out = emit(fl ? x + " - " + y : wrap(x, "-", y)); break;
+          case OpKind::Mul: out = emit(fl ? x + " * " + y : wrap(x, "*", y)); break;
           case OpKind::Div: out = emit(fl ? x + " / " + y : "(" + y + " != 0 ? " + x + " / " + y + " : 0)"); break;
           case OpKind::Pow: out = emit(fl ? "powf(" + x + ", " + y + ")" : "(" + ct + ")powf((float)" + x + ", (float)" + y + ")"); break;
           case OpKind::Max: out = emit(fl ? "fmaxf(" + x + ", " + y + ")" : "max(" + x + ", " + y + ")"); break;
@@ -380,8 +397,10 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
           case OpKind::Rsqrt: out = emit("rsqrtf(" + x + ")"); break;
           case OpKind::Exp: out = emit("expf(" + x + ")"); break;
           case OpKind::Log: out = emit("logf(" + x + ")"); break;
-          case OpKind::Abs: out = emit(ct == "float" ? "fabsf(" + x + ")" : "abs(" + x + ")"); break;
-          case OpKind::Neg: out = emit("-" + x); break;
+          case OpKind::Abs:
+            out = emit(ct == "float" ? "fabsf(" + x + ")" : "(" + x + " < 0 ? " + wrap("0", "-", x) + " : " + x + ")");
+            break;
+          case OpKind::Neg: out = emit(ct == "float" || ct == "double" ? "-" + x : wrap("0", "-", x)); break;
           case OpKind::Sin: out = emit("sinf(" + x + ")"); break;
           case OpKind::Cos: out = emit("cosf(" + x + ")"); break;
           case OpKind::Not: out = emit(ct == "bool" ? "!" + x : "~" + x); break;

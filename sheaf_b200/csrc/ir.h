@@ -48,6 +48,8 @@ enum class OpKind : uint8_t {
   // + dy, lse, dsum for AttnBwdKV).  values[0] = score scale, axis = causal.
   // Results are packed 1-D buffers (see AttnArgs in kernels/kernels.h).
   AttnFwd, AttnBwdQ, AttnBwdKV,
+  // stablehlo.bitcast_convert between 32-bit element types (f32 <-> i32)
+  Bitcast,
 };
 const char* opkind_name(OpKind k);
 
@@ -60,7 +62,7 @@ inline bool is_unary_elementwise(OpKind k) {
   return k == OpKind::Tanh || k == OpKind::Sqrt || k == OpKind::Rsqrt || k == OpKind::Exp ||
          k == OpKind::Log || k == OpKind::Abs || k == OpKind::Neg || k == OpKind::Sin ||
          k == OpKind::Cos || k == OpKind::Not || k == OpKind::Sign || k == OpKind::Floor ||
-         k == OpKind::Ceil || k == OpKind::Logistic || k == OpKind::Convert;
+         k == OpKind::Ceil || k == OpKind::Logistic || k == OpKind::Convert || k == OpKind::Bitcast;
 }
 inline bool is_attention(OpKind k) {
   return k == OpKind::AttnFwd || k == OpKind::AttnBwdQ || k == OpKind::AttnBwdKV;

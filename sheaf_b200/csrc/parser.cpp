@@ -40,7 +40,7 @@ const char* opkind_name(OpKind k) {
       "negate", "sine", "cosine", "not", "sign", "floor", "ceil", "logistic", "clamp",
       "convert", "select", "compare", "broadcast_in_dim", "reshape", "transpose", "iota",
       "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather",
-      "attention_fwd", "attention_bwd_q", "attention_bwd_kv"};
+      "attention_fwd", "attention_bwd_q", "attention_bwd_kv", "bitcast_convert"};
   return names[(int)k];
 }
 
@@ -348,8 +348,8 @@ void parse_statement(FuncBuilder& fb, Cursor& c) {
       }
       c.expect(":");
       op.type = c.type();
-    } else if (k == "convert" || k == "reshape") {
-      op.kind = k == "convert" ? OpKind::Convert : OpKind::Reshape;
+    } else if (k == "convert" || k == "reshape" || k == "bitcast_convert") {
+      op.kind = k == "convert" ? OpKind::Convert : k == "reshape" ? OpKind::Reshape : OpKind::Bitcast;
       op.operands.push_back(fb.use_next());
       c.expect(":");
       c.expect("(");

@@ -622,6 +622,12 @@ void verify(const Function& f) {
       case OpKind::Constant:
         need(op.values.size() == 1 || (int64_t)op.values.size() == op.type.numel(), "constant payload size");
         break;
+      case OpKind::Bitcast: {
+        const DType a = T(op.operands[0]).dtype, b = op.type.dtype;
+        auto w32 = [](DType t) { return t == DType::F32 || t == DType::I32; };
+        need(a == b || (w32(a) && w32(b)), "bitcast_convert between f32 and i32 only");
+        break;
+      }
       case OpKind::Select:
         need(T(op.operands[0]).shape == rs || T(op.operands[0]).shape.empty(), "select predicate shape");
         need(T(op.operands[1]).shape == rs && T(op.operands[2]).shape == rs, "select operand shapes");
