@@ -151,6 +151,21 @@ SB_API uint32_t sb_buffer_element_type(const sb_buffer* buffer);
 SB_API size_t sb_buffer_byte_length(const sb_buffer* buffer);
 SB_API void* sb_buffer_device_pointer(const sb_buffer* buffer);
 
+/* --- ahead-of-time bundles (the `sheaf build` .vmfb path) ------------------ *
+ * Replaces compiling a module to a .vmfb ahead of time and loading it
+ * (runtime/vmfb_loader.rs:24; the __sheaf__/ manifest cache, jit/support.rs:
+ * 131-164).  sb_module_build_bundle plans `text` and compiles every fused
+ * kernel for sm_100a on the host (no GPU needed) into one self-contained
+ * buffer: call with out = NULL to get the size in *out_length, then with a
+ * buffer of at least that size.  sb_session_load_bundle loads it without
+ * compiling anything (the plan is rebuilt from the embedded text, the cubins
+ * come from the bundle); the session's precision and planning flags must be
+ * the ones the bundle was built with, and a bundle from another library
+ * version whose kernels differ is rejected. */
+SB_API sb_status* sb_module_build_bundle(const char* text, size_t length, int32_t precision, uint32_t flags,
+                                         uint8_t* out, size_t capacity, size_t* out_length);
+SB_API sb_status* sb_session_load_bundle(sb_session* session, const uint8_t* data, size_t length);
+
 /* --- fused optimizer step -------------------------------------------------- *
  * Replaces lib/optim.shf:72-83 (global-norm, clip-by-global-norm) followed by
  * lib/optim.shf:36-58 (adamw-step), as examples/nanoGPT/train.shf:26-33 calls

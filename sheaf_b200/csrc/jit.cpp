@@ -100,6 +100,8 @@ void compile_one(CubinChunk& ch, const std::string& cache_dir, std::string* err)
 
 }  // namespace
 
+std::string chunk_key(const std::string& source) { return cache_key(source); }
+
 std::string default_cache_dir() {
   if (const char* e = std::getenv("SHEAF_B200_CACHE")) return e;
   Dl_info info;
@@ -132,7 +134,17 @@ std::vector<CubinChunk> split_source(const std::vector<std::string>& snippets, c
   return out;
 }
 
-void compile_chunks(std::vector<CubinChunk>& chunks, const std::string& cache_dir) {
+void compile_chunks(std::vector<CubinChunk>& chunks, const std::string& cache_dir, const Prebuilt* prebuilt) {
+  if (prebuilt) {
+    for (auto& ch : chunks) {
+      auto it = prebuilt->find(cache_key(ch.source));
+      if (it == prebuilt->end())
+        throw std::runtime_error("the bundle has no cubin for a generated kernel chunk (built by another "
+                                 "library version or for other options)");
+      ch.cubin = it->second;
+    }
+    return;
+  }
   std::vector<std::string> errs(chunks.size());
   unsigned hw = std::max(1u, std::thread::hardware_concurrency());
   size_t next = 0;

@@ -255,7 +255,7 @@ sb_status* nccl_settle(sb_session* s) {
   }
 }
 
-sb_status* load_module(sb_session* s, const std::string& text) {
+sb_status* load_module(sb_session* s, const std::string& text, const Prebuilt* prebuilt = nullptr) {
   std::string err;
   auto mod = parse_module(text, &err);
   if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
@@ -282,7 +282,7 @@ sb_status* load_module(sb_session* s, const std::string& text) {
     auto& lf = lm->fns[fi];
     std::vector<CubinChunk> chunks = split_source(lf->plan.snippets, lf->plan.prelude, 16);
     try {
-      if (!lf->plan.snippets.empty()) compile_chunks(chunks, s->cache_dir);
+      if (!lf->plan.snippets.empty()) compile_chunks(chunks, s->cache_dir, prebuilt);
     } catch (const std::exception& e) {
       return make_status(SB_STATUS_INTERNAL, "kernel compilation for @" + lf->fn->name + " failed: " + e.what());
     }
@@ -693,6 +693,107 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
     out[n] = 0;
   }
   return nullptr;
+}
+
+// Ahead-of-time bundle: "SB200BND", u32 version 1, i32 precision, u32 flags,
+// u64 text length + StableHLO text, u32 chunk count, then per chunk a
+// 32-character key, u64 size and the cubin.  Little-endian.
+extern "C++" {
+namespace sb {
+namespace {
+constexpr char kBundleMagic[8] = {'S', 'B', '2', '0', '0', 'B', 'N', 'D'};
+template <typename T>
+void put(std::string& o, T v) {
+  o.append((const char*)&v, sizeof v);
+}
+template <typename T>
+bool get(const uint8_t*& p, const uint8_t* e, T* v) {
+  if ((size_t)(e - p) < sizeof(T)) return false;
+  std::memcpy(v, p, sizeof(T));
+  p += sizeof(T);
+  return true;
+}
+}  // namespace
+}  // namespace sb
+}
+
+sb_status* sb_module_build_bundle(const char* text, size_t len, int32_t precision, uint32_t flags, uint8_t* out,
+                                  size_t cap, size_t* out_len) {
+  using namespace sb;
+  if (!text || !out_len) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  if (precision < 0 || precision > 2) return make_status(SB_STATUS_INVALID_ARGUMENT, "unknown precision");
+  std::string err;
+  const std::string src(text, len);
+  auto mod = parse_module(src, &err);
+  if (!mod) return make_status(SB_STATUS_INVALID_ARGUMENT, err);
+  std::vector<CubinChunk> all;
+  for (auto& f : mod->funcs) {
+    Plan p;
+    try {
+      p = build_plan(f, (Precision)precision, !(flags & SB_SESSION_FLAG_NO_ATTENTION_FUSION));
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_UNIMPLEMENTED, "planning @" + f.name + ": " + e.what());
+    }
+    std::vector<CubinChunk> chunks = split_source(p.snippets, p.prelude, 16);
+    try {
+      if (!p.snippets.empty()) compile_chunks(chunks, default_cache_dir());
+    } catch (const std::exception& e) {
+      return make_status(SB_STATUS_INTERNAL, "kernel compilation for @" + f.name + " failed: " + e.what());
+    }
+    if (!p.snippets.empty())
+      for (auto& c : chunks) all.push_back(std::move(c));
+  }
+  std::string o(kBundleMagic, 8);
+  put<uint32_t>(o, 1);
+  put<int32_t>(o, precision);
+  put<uint32_t>(o, flags);
+  put<uint64_t>(o, src.size());
+  o += src;
+  put<uint32_t>(o, (uint32_t)all.size());
+  for (auto& c : all) {
+    const std::string key = chunk_key(c.source);
+    o += key;
+    put<uint64_t>(o, c.cubin.size());
+    o.append((const char*)c.cubin.data(), c.cubin.size());
+  }
+  *out_len = o.size();
+  if (!out) return nullptr;
+  if (cap < o.size()) return make_status(SB_STATUS_RESOURCE_EXHAUSTED, "bundle buffer too small");
+  std::memcpy(out, o.data(), o.size());
+  return nullptr;
+}
+
+sb_status* sb_session_load_bundle(sb_session* s, const uint8_t* data, size_t len) {
+  using namespace sb;
+  if (!s || !data) return make_status(SB_STATUS_INVALID_ARGUMENT, "NULL argument");
+  const uint8_t *p = data, *e = data + len;
+  auto bad = [](const char* what) { return make_status(SB_STATUS_INVALID_ARGUMENT, std::string("bundle: ") + what); };
+  if (len < 8 || std::memcmp(p, kBundleMagic, 8) != 0) return bad("not a sheaf_b200 bundle");
+  p += 8;
+  uint32_t version = 0, flags = 0, n = 0;
+  int32_t precision = 0;
+  uint64_t tlen = 0;
+  if (!get(p, e, &version) || version != 1) return bad("unsupported version");
+  if (!get(p, e, &precision) || !get(p, e, &flags) || !get(p, e, &tlen) || (uint64_t)(e - p) < tlen)
+    return bad("truncated header");
+  if (precision != s->opts.precision) return bad("built for another precision than this session's");
+  if ((flags & SB_SESSION_FLAG_NO_ATTENTION_FUSION) != (s->opts.flags & SB_SESSION_FLAG_NO_ATTENTION_FUSION))
+    return bad("built with other planning flags than this session's");
+  std::string text((const char*)p, (size_t)tlen);
+  p += tlen;
+  if (!get(p, e, &n)) return bad("truncated chunk table");
+  Prebuilt pre;
+  for (uint32_t i = 0; i < n; ++i) {
+    uint64_t sz = 0;
+    if ((size_t)(e - p) < 32) return bad("truncated chunk key");
+    std::string key((const char*)p, 32);
+    p += 32;
+    if (!get(p, e, &sz) || (uint64_t)(e - p) < sz) return bad("truncated cubin");
+    pre[key].assign(p, p + sz);
+    p += sz;
+  }
+  std::lock_guard<std::mutex> g(s->mu);
+  return load_module(s, text, &pre);
 }
 
 sb_status* sb_session_load_stablehlo(sb_session* s, const char* text, size_t len) {

@@ -89,6 +89,9 @@ SIGNATURES = {
     "sb_buffer_byte_length": (ctypes.c_size_t, [_P]),
     "sb_buffer_device_pointer": (_P, [_P]),
     "sb_nccl_get_unique_id": (_P, [ctypes.POINTER(ctypes.c_uint8)]),
+    "sb_module_build_bundle": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_uint32, _P,
+                                    ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "sb_session_load_bundle": (_P, [_P, _P, ctypes.c_size_t]),
     "sb_adamw_options_initialize": (None, [ctypes.POINTER(_AdamwOptions)]),
     "sb_optimizer_adamw_step": (_P, [_P, ctypes.c_size_t, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P),
                                      ctypes.POINTER(_P), ctypes.POINTER(_AdamwOptions), ctypes.POINTER(ctypes.c_float)]),
@@ -161,6 +164,20 @@ def plan_steps(text: str, function: str, precision: str = "tf32") -> List[dict]:
                 r[k] = float(r[k]) if k == "flops" else int(r[k])
         rows.append(r)
     return rows
+
+
+def build_bundle(text: str, precision: str = "tf32", fuse_attention: bool = True) -> bytes:
+    """Ahead-of-time artifact of a module (host only, like `sheaf build`): the
+    text plus every fused kernel compiled for sm_100a; B200Session.load_bundle
+    loads it without compiling."""
+    raw = text.encode()
+    flags = 0 if fuse_attention else FLAG_NO_ATTENTION_FUSION
+    n = ctypes.c_size_t(0)
+    _check(library().sb_module_build_bundle(raw, len(raw), PRECISIONS[precision], flags, None, 0, ctypes.byref(n)))
+    buf = (ctypes.c_uint8 * n.value)()
+    _check(library().sb_module_build_bundle(raw, len(raw), PRECISIONS[precision], flags, buf, n.value,
+                                            ctypes.byref(n)))
+    return bytes(buf)
 
 
 def kernel_source(text: str, function: str) -> str:
@@ -259,6 +276,11 @@ class B200Session:
     def load_stablehlo(self, text: str):
         raw = text.encode()
         _check(library().sb_session_load_stablehlo(self._h, raw, len(raw)))
+
+    def load_bundle(self, bundle: bytes):
+        """Loads an ahead-of-time bundle (`build_bundle`): no kernel compilation."""
+        buf = (ctypes.c_uint8 * len(bundle)).from_buffer_copy(bundle)
+        _check(library().sb_session_load_bundle(self._h, buf, len(bundle)))
 
     def has_function(self, name: str) -> bool:
         return bool(library().sb_session_has_function(self._h, name.encode()))
