@@ -9,6 +9,8 @@ through libsheafb200's C ABI.  Other workloads: `gpt2` (GPT-2-small value-and-
 grad: 12 layers, d768, ctx 1024, vocab 50304, batch 8 per GPU, weak scaling),
 `nanogpt-fwd` (the forward alone), `nanogpt-train` (value-and-grad followed by
 the fused clip-by-global-norm + AdamW step of examples/nanoGPT/train.shf),
+`nanogpt-generate` (one generate-token step of sample.shf on the 256-token
+window: forward, top-k sort, softmax, split, choice; tokens/s),
 `mlp` (the 784-512-10 MLP value-and-grad, samples/s), `matmul` (op sweep,
 --size / --shape / --layout).
 
@@ -44,7 +46,7 @@ def parse():
     p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
                    choices=["fp32", "tf32", "bf16"])
     p.add_argument("--workload", default="nanogpt",
-                   choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "gpt2", "mlp", "matmul"])
+                   choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "nanogpt-generate", "gpt2", "mlp", "matmul"])
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
     p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
@@ -94,6 +96,18 @@ def program(args, world, rank):
                "global_batch": gb, "parallelism": f"dp{world}",
                "l2": "operands fit in L2 (3.4 MB), no flush: launch-latency bound by design"}
         return low, inp, ["x", "y"], gb, "samples/s", "strong", cfg, True
+    if args.workload == "nanogpt-generate":
+        from sheaf_b200.programs import generate as G
+        from sheaf_b200.programs import random as RG
+        c = M.NANOGPT
+        low = G.gpt_generate_program(c, 200, 0.8)
+        inp = M.gpt_inputs(c, batch=1, seed=0)
+        inp = {n: inp[n] for n in low.arg_names[:-2]} | {"idx": inp["idx"], "key": RG.key_of_seed(1337)}
+        cfg = {"workload": f"nanogpt generate-token (top-k 200, temperature 0.8) 1x{c.T}",
+               "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}", "global_batch": world,
+               "seq_len": c.T, "parallelism": f"replicas{world}",
+               "l2": "weights (43 MB) fit in L2: one token per step, latency-bound by design"}
+        return low, inp, ["idx", "key"], world, "tokens/s", "weak", cfg, False
     c, gb, b, scaling = workload(args.workload, world, args.batch)
     inp = M.gpt_inputs(c, batch=gb, seed=0)
     for n in ("x", "y", "idx"):
@@ -179,6 +193,9 @@ def cpu_baseline(args, steps=2):
     if args.workload == "mlp":
         low, inp, units, unit = M.mlp_vag(batch=256), M.mlp_inputs(batch=256), 256, "samples/s"
         sample = "the full 256-sample batch"
+    elif args.workload == "nanogpt-generate":
+        low, inp, _, units, unit, _, _, _ = program(args, 1, 0)
+        sample = "one generate-token step (1 token on the 256-token window)"
     else:
         c = workload(args.workload, 1)[0]
         b, T = (2, c.T) if c.T <= 256 else (1, 256)

@@ -172,6 +172,15 @@ def _parse_op(st: str) -> Op:
             "slice_sizes": _ints(re.search(r"slice_sizes = array<i64: ([^>]*)>", attrs_s).group(1)),
         }
         return Op(results, "gather", [m.group(1), m.group(2)], attrs, [parse_type(m.group(5))])
+    if rhs.startswith('"stablehlo.sort"'):
+        # keys, payload sorted along `dimension` by a GT / LT comparator on the keys
+        # (the top_k form, lowering/stablehlo/indexing_ops.rs:476-540)
+        m = re.match(r'"stablehlo\.sort"\((%\w+),\s*(%\w+)\)', rhs)
+        d = re.search(r"comparison_direction (\w+)>", rhs).group(1)
+        dim = int(re.search(r"dimension = (\d+)", rhs).group(1))
+        tys = _split_types(rhs.rsplit("->", 1)[1].strip().strip("()"))
+        return Op(results, "sort", [m.group(1), m.group(2)], {"dir": d, "dim": dim},
+                  [parse_type(t) for t in tys])
     m = re.match(r"stablehlo\.(\w+)\s*(.*)$", rhs)
     kind, rest = m.group(1), m.group(2)
     if kind == "constant":
@@ -259,6 +268,12 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
         v = [env[o] for o in op.operands]
         (oshape, odt), = op.out_types[:1]
         k = op.kind
+        if k == "sort":
+            keys = np.asarray(v[0], np.float32 if dtype == np.float32 else np.float64)
+            order = np.argsort(-keys if op.attrs["dir"] == "GT" else keys, axis=op.attrs["dim"], kind="stable")
+            env[op.results[0]] = np.take_along_axis(np.asarray(v[0]), order, axis=op.attrs["dim"])
+            env[op.results[1]] = np.take_along_axis(np.asarray(v[1]), order, axis=op.attrs["dim"])
+            continue
         if k == "constant":
             r = op.attrs["value"]
         elif k == "add":

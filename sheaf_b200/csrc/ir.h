@@ -50,6 +50,12 @@ enum class OpKind : uint8_t {
   AttnFwd, AttnBwdQ, AttnBwdKV,
   // stablehlo.bitcast_convert between 32-bit element types (f32 <-> i32)
   Bitcast,
+  // stablehlo.sort of (f32 keys, i32 payload) along the last dim with a
+  // GT / LT comparator on the keys, stable.  Created by the parser: the op
+  // writes one packed f32 buffer [.., 2N] (sorted keys | payload bits) and
+  // the two results are a slice and a bitcast slice of it.  axis = 1 for
+  // descending (GT).
+  SortPairs,
 };
 const char* opkind_name(OpKind k);
 

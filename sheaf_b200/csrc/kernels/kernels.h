@@ -86,6 +86,11 @@ struct AttnArgs {
 };
 cudaError_t attention(const AttnArgs& a, cudaStream_t stream);
 
+// Stable sort of rows of (f32 key, i32 payload) (kernels/sort.cu): out row =
+// [sorted keys | payload bits as f32], descending or ascending by key.
+cudaError_t sort_pairs(const float* keys, const int* payload, float* out, int64_t rows, int64_t n, bool descending,
+                       cudaStream_t stream);
+
 // Fused clip-by-global-norm + AdamW (kernels/optim.cu).  Leaves and chunks
 // live in device memory; partials holds one float per chunk.  norm_out (device,
 // may be null) receives the global L2 norm of the gradients before clipping.

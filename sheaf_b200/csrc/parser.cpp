@@ -40,7 +40,7 @@ const char* opkind_name(OpKind k) {
       "negate", "sine", "cosine", "not", "sign", "floor", "ceil", "logistic", "clamp",
       "convert", "select", "compare", "broadcast_in_dim", "reshape", "transpose", "iota",
       "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather",
-      "attention_fwd", "attention_bwd_q", "attention_bwd_kv", "bitcast_convert"};
+      "attention_fwd", "attention_bwd_q", "attention_bwd_kv", "bitcast_convert", "sort"};
   return names[(int)k];
 }
 
@@ -260,12 +260,148 @@ OpKind elementwise_kind(const std::string& n, bool* ok) {
   return *ok ? it->second : OpKind::Add;
 }
 
+// %v, %i = "stablehlo.sort"(%keys, %payload) ({ ^bb0(...): compare GT|LT of
+// the first two block arguments; return }) {dimension = last, is_stable} as
+// emitted for top_k (lowering/stablehlo/indexing_ops.rs:476-540).
+void parse_sort(FuncBuilder& fb, Cursor& c, const std::vector<std::string>& results, int line) {
+  c.expect("\"stablehlo.sort\"");
+  c.expect("(");
+  const int x = fb.use_next();
+  c.expect(",");
+  const int pay = fb.use_next();
+  c.expect(")");
+  c.expect("(");
+  c.expect("{");
+  c.expect("^bb0(");
+  std::vector<std::string> args;
+  do {
+    args.push_back(c.value_name());
+    c.expect(":");
+    c.type();
+  } while (c.accept(","));
+  c.expect(")");
+  c.expect(":");
+  const std::string p = c.value_name();
+  c.expect("=");
+  c.expect("\"stablehlo.compare\"");
+  c.expect("(");
+  const std::string l = c.value_name();
+  c.expect(",");
+  const std::string r = c.value_name();
+  c.expect(")");
+  c.expect("{");
+  c.expect("comparison_direction");
+  c.expect("=");
+  c.expect("#stablehlo<comparison_direction");
+  const std::string dir = c.ident();
+  c.expect(">");
+  if (c.accept(",")) {  // compare_type = #stablehlo<comparison_type FLOAT>
+    c.ident();
+    c.expect("=");
+    c.expect("#stablehlo<comparison_type");
+    c.ident();
+    c.expect(">");
+  }
+  c.expect("}");
+  c.expect(":");
+  c.expect("(");
+  c.type();
+  c.expect(",");
+  c.type();
+  c.expect(")");
+  c.expect("->");
+  c.type();
+  c.expect("\"stablehlo.return\"");
+  c.expect("(");
+  const std::string rv = c.value_name();
+  c.expect(")");
+  c.expect(":");
+  c.expect("(");
+  c.type();
+  c.expect(")");
+  c.expect("->");
+  c.expect("(");
+  c.expect(")");
+  c.expect("}");
+  c.expect(")");
+  c.expect("{");
+  c.expect("dimension");
+  c.expect("=");
+  const int64_t dim = c.integer();
+  c.expect(":");
+  c.ident();
+  if (c.accept(",")) {
+    c.expect("is_stable");
+    c.expect("=");
+    c.ident();  // the kernel is stable either way
+  }
+  c.expect("}");
+  c.expect(":");
+  c.expect("(");
+  const Type tx = c.type();
+  c.expect(",");
+  const Type tp = c.type();
+  c.expect(")");
+  c.expect("->");
+  c.expect("(");
+  const Type ta = c.type();
+  c.expect(",");
+  const Type tb = c.type();
+  c.expect(")");
+  if (args.size() != 4 || l != args[0] || r != args[1] || rv != p || (dir != "GT" && dir != "LT"))
+    c.fail("sort: only a GT / LT comparator on the first operand is supported");
+  if (tx.dtype != DType::F32 || tp.dtype != DType::I32 || ta.shape != tx.shape || tb.shape != tp.shape ||
+      tp.shape != tx.shape || ta.dtype != DType::F32 || tb.dtype != DType::I32)
+    c.fail("sort: operands must be (f32 keys, i32 payload) of one shape");
+  if (tx.shape.empty() || dim != (int64_t)tx.shape.size() - 1) c.fail("sort: only the last dimension is supported");
+  const int64_t n = tx.shape.back();
+  Op s;
+  s.kind = OpKind::SortPairs;
+  s.line = line;
+  s.operands = {x, pay};
+  s.axis = dir == "GT" ? 1 : 0;
+  s.type = tx;
+  s.type.shape.back() = 2 * n;
+  s.result = fb.define(results[0] + "$packed", s.type);
+  const int packed = s.result;
+  fb.f.ops.push_back(s);
+  auto half = [&](int64_t lo, const std::string& name) {
+    Op h;
+    h.kind = OpKind::Slice;
+    h.line = line;
+    h.operands = {packed};
+    for (size_t d = 0; d < tx.shape.size(); ++d) {
+      const bool last = d + 1 == tx.shape.size();
+      h.a0.push_back(last ? lo : 0);
+      h.a1.push_back(last ? lo + n : tx.shape[d]);
+      h.a2.push_back(1);
+    }
+    h.type = tx;
+    h.result = fb.define(name, tx);
+    fb.f.ops.push_back(h);
+    return h.result;
+  };
+  half(0, results[0]);
+  const int bits = half(n, results[1] + "$bits");
+  Op b;
+  b.kind = OpKind::Bitcast;
+  b.line = line;
+  b.operands = {bits};
+  b.type = tp;
+  b.result = fb.define(results[1], tp);
+  fb.f.ops.push_back(b);
+}
+
 void parse_statement(FuncBuilder& fb, Cursor& c) {
   int line = c.line();
   std::vector<std::string> results;
   results.push_back(c.value_name());
   while (c.accept(",")) results.push_back(c.value_name());
   c.expect("=");
+  if (results.size() == 2 && c.peek("\"stablehlo.sort\"")) {
+    parse_sort(fb, c, results, line);
+    return;
+  }
   Op op;
   op.line = line;
   if (results.size() != 1) c.fail("multi-result ops are not supported");

@@ -123,6 +123,9 @@ struct Planner {
       const Op& op = f.ops[i];
       if (!live[op.result]) continue;
       for (int s = 0; s < (int)op.operands.size(); ++s) consumers[op.operands[s]].push_back({i, s});
+      // the sort kernel reads dense buffers: its operands are materialized
+      if (op.kind == OpKind::SortPairs)
+        for (int o : op.operands) forced.insert(o);
     }
     find_batch_reduced_dots();
   }
@@ -185,7 +188,10 @@ struct Planner {
   void collect(int v, std::set<int>& cs, bool& blocked, std::set<int>& seen) {
     for (auto [oi, slot] : consumers[v]) {
       const Op& c = f.ops[oi];
-      if (c.kind == OpKind::DotGeneral || is_attention(c.kind)) { blocked = true; continue; }
+      if (c.kind == OpKind::DotGeneral || is_attention(c.kind) || c.kind == OpKind::SortPairs) {
+        blocked = true;
+        continue;
+      }
       if (c.kind == OpKind::Gather && slot == 0) { blocked = true; continue; }
       int cv = c.result;
       if (cluster[cv] == kDup) {
@@ -293,7 +299,7 @@ struct Planner {
       for (auto& [rv, di] : fused_dot) if (di == i) absorbed = true;
       if (absorbed) { cluster[v] = kAbsorbed; continue; }
       if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral ||
-          is_attention(op.kind)) {
+          is_attention(op.kind) || op.kind == OpKind::SortPairs) {
         cluster[v] = v;
         continue;
       }
@@ -622,6 +628,11 @@ void verify(const Function& f) {
       case OpKind::Constant:
         need(op.values.size() == 1 || (int64_t)op.values.size() == op.type.numel(), "constant payload size");
         break;
+      case OpKind::SortPairs:
+        need(op.operands.size() == 2 && T(op.operands[0]).shape == T(op.operands[1]).shape && !rs.empty() &&
+                 rs.back() == 2 * T(op.operands[0]).shape.back(),
+             "sort operand / packed result shapes");
+        break;
       case OpKind::Bitcast: {
         const DType a = T(op.operands[0]).dtype, b = op.type.dtype;
         auto w32 = [](DType t) { return t == DType::F32 || t == DType::I32; };
@@ -921,6 +932,17 @@ Plan plan_function(const Function& f, Precision prec) {
         st.flops = 4 * prod;
         st.bytes_moved = 4 * (4 * N + 2 * R + 2 * N);
       }
+    } else if (op.kind == OpKind::SortPairs) {
+      // operands are materialized dense buffers (a sort consumer blocks fusion)
+      st.kind = StepKind::Sort;
+      for (int o : op.operands)
+        if (!pl.materialized(o)) fail(op, "internal: sort operand is not materialized");
+      st.leaves = {op.operands[0], op.operands[1]};
+      const int64_t n = f.value_types[op.operands[0]].shape.back();
+      st.gemm.M = f.value_types[op.operands[0]].numel() / std::max<int64_t>(n, 1);  // rows
+      st.gemm.N = n;
+      st.gemm.K = op.axis;  // 1: descending
+      st.bytes_moved = 16 * f.value_types[op.operands[0]].numel();
     } else if (op.kind == OpKind::Reduce) {
       st.kind = StepKind::Reduce;
       cg.gen_reduce(op, &st);
@@ -1183,17 +1205,18 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
 std::string Plan::summary() const {
   std::ostringstream os;
   os.precision(17);
-  int loops = 0, reds = 0, gemms = 0, attn = 0;
+  int loops = 0, reds = 0, gemms = 0, attn = 0, sorts = 0;
   double flops = 0, aflops = 0;
   for (auto& s : steps) {
     if (s.kind == StepKind::Loop) ++loops;
     else if (s.kind == StepKind::Reduce) ++reds;
     else if (s.kind == StepKind::Attn) { ++attn; aflops += s.flops; continue; }
+    else if (s.kind == StepKind::Sort) { ++sorts; continue; }
     else ++gemms;
     flops += s.flops;
   }
   os << "steps=" << steps.size() << " loop=" << loops << " reduce=" << reds << " gemm=" << gemms
-     << " attention=" << attn << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
+     << " attention=" << attn << (sorts ? " sort=" + std::to_string(sorts) : std::string()) << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
      << " gemm_flops=" << flops << " attention_flops=" << aflops;
   return os.str();
 }

@@ -46,7 +46,7 @@ struct AttnDesc {
   bool round_out = false;  // Y / dQ / dK / dV stored rounded to TF32
 };
 
-enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn };
+enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort };
 
 struct Step {
   StepKind kind = StepKind::Loop;

@@ -347,6 +347,7 @@ sb_status* load_module(sb_session* s, const std::string& text, const Prebuilt* p
 // Kernel name of a step as the profile report and plan listing show it.
 std::string step_name(const Step& st) {
   if (st.kind == StepKind::Gemm) return "gemm";
+  if (st.kind == StepKind::Sort) return "sort";
   if (st.kind == StepKind::Attn)
     return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : (st.attn.kind == OpKind::AttnBwdQ ? "attn_bwd_q" : "attn_bwd_kv");
   return st.kernel;
@@ -444,6 +445,12 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
       if (tc) s->used_tc = true;
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
+      continue;
+    }
+    if (st.kind == StepKind::Sort) {
+      cudaError_t e = sort_pairs((const float*)ptr[st.leaves[0]], (const int*)ptr[st.leaves[1]], (float*)ptr[st.root],
+                                 st.gemm.M, st.gemm.N, st.gemm.K != 0, stream);
+      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "sort"); }
       continue;
     }
     if (st.kind == StepKind::Attn) {
@@ -668,7 +675,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
   std::ostringstream os;
   os.precision(9);
   os << "function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort"};
   for (auto& m : s->modules)
     for (auto& lf : m->fns) {
       if (lf->prof_ms.empty()) continue;
@@ -1042,7 +1049,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   std::ostringstream os;
   os.precision(17);
   os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
     const GemmDesc& g = st.gemm;
