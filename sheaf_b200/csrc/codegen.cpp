@@ -80,6 +80,13 @@ struct VecFail {};
 
 const char* const kLane[4] = {"cL", "(cL+1)", "(cL+2)", "(cL+3)"};
 
+// Programmatic dependent launch: every generated kernel is launched so that it
+// may start while the previous kernel in the stream finishes; it first waits
+// for that kernel's results, then lets the next kernel start launching.
+const char* const kPdlPrologue =
+    "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+    "  asm volatile(\"griddepcontrol.launch_dependents;\");\n";
+
 int lane_of(const std::string& s) {
   for (int j = 0; j < 4; ++j)
     if (s == kLane[j]) return j;
@@ -427,7 +434,7 @@ std::string CodeGen::header(const std::string& name, const Ctx& c, int extra_ptr
   int np = (int)c.leaves.size() + 1 + extra_ptrs;
   h << "struct __align__(8) A_" << name << " { const void* p[" << np << "]; };\n";
   h << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << name << "(const A_" << name
-    << " a) {\n";
+    << " a) {\n" << kPdlPrologue;
   for (size_t i = 0; i < c.leaves.size(); ++i) {
     const Type& t = f_.value_types[c.leaves[i]];
     h << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
@@ -766,7 +773,7 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
       std::string fin = name + "f";
       src_ << "struct __align__(8) A_" << fin << " { const void* p[" << c.leaves.size() + 2 << "]; };\n";
       src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
-           << " a) {\n";
+           << " a) {\n" << kPdlPrologue;
       for (size_t i = 0; i < c.leaves.size(); ++i) {
         const Type& t = f_.value_types[c.leaves[i]];
         src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
@@ -985,7 +992,7 @@ void CodeGen::gen_reduce(const Op& root, Step* st, const Op* epi) {
       std::string fin = name + "f";
       src_ << "struct __align__(8) A_" << fin << " { const void* p[" << c.leaves.size() + 2 << "]; };\n";
       src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
-           << " a) {\n";
+           << " a) {\n" << kPdlPrologue;
       for (size_t i = 0; i < c.leaves.size(); ++i) {
         const Type& t = f_.value_types[c.leaves[i]];
         src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)

@@ -356,8 +356,18 @@ std::string step_name(const Step& st) {
 sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs, int64_t gx, int64_t gy,
                             int64_t block, cudaStream_t stream) {
   void* args[1] = {(void*)ptrs.data()};
-  dim3 grid((unsigned)gx, (unsigned)gy, 1);
-  SB_CUDA(cudaLaunchKernel((const void*)k, grid, dim3((unsigned)block), args, 0, stream));
+  // generated kernels start with griddepcontrol.wait: they may be launched
+  // while the previous kernel drains (programmatic dependent launch)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gx, (unsigned)gy, 1);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  SB_CUDA(cudaLaunchKernelExC(&cfg, (const void*)k, args));
   return nullptr;
 }
 
