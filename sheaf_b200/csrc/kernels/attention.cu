@@ -27,6 +27,7 @@
 #include <cmath>
 
 #include "kernels.h"
+#include "pdl.h"
 #include "tc_common.h"
 
 namespace sb {
@@ -115,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mK,
              const __grid_constant__ CUtensorMap mV, const __grid_constant__ CUtensorMap mY, const Params p,
              int* err) {
+  pdl_prologue();
   using namespace fwd;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {  // uniform: every thread leaves before any barrier
@@ -297,6 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mKm,
                const __grid_constant__ CUtensorMap mV, const __grid_constant__ CUtensorMap mDQ, const Params p,
                int* err) {
+  pdl_prologue();
   using namespace bq;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {
@@ -456,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const __grid_constant__ CUtensorMap mQm, const __grid_constant__ CUtensorMap mDOm,
                 const __grid_constant__ CUtensorMap mDK, const __grid_constant__ CUtensorMap mDV, const Params p,
                 int* err) {
+  pdl_prologue();
   using namespace bkv;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {
@@ -667,8 +671,7 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
       return cudaErrorNotSupported;
     static cudaError_t attr = set_smem(attn_fwd, fwd::SMEM);
     if (attr != cudaSuccess) return attr;
-    attn_fwd<<<grid, kThreads, fwd::SMEM, stream>>>(mq, mk, mv, my, p, err);
-    return cudaGetLastError();
+    return launch_pdl(attn_fwd, grid, dim3(kThreads), fwd::SMEM, stream, mq, mk, mv, my, p, err);
   }
   if (!view_ok(a.dy, a) || !a.lse) return cudaErrorNotSupported;
   p.dy = a.dy.p; p.dy_sb = a.dy.sb; p.dy_sh = a.dy.sh; p.dy_st = a.dy.st;
@@ -683,8 +686,7 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
       return cudaErrorNotSupported;
     static cudaError_t attr = set_smem(attn_bwd_q, bq::SMEM);
     if (attr != cudaSuccess) return attr;
-    attn_bwd_q<<<grid, kThreads, bq::SMEM, stream>>>(mq, mdo, mk, mkm, mv, mdq, p, err);
-    return cudaGetLastError();
+    return launch_pdl(attn_bwd_q, grid, dim3(kThreads), bq::SMEM, stream, mq, mdo, mk, mkm, mv, mdq, p, err);
   }
   if (a.kind != AttnKind::BwdKV || !a.dsum) return cudaErrorNotSupported;
   p.dsum = a.dsum; p.d_sb = a.d_sb; p.d_sh = a.d_sh; p.d_st = a.d_st;
@@ -697,8 +699,8 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
     return cudaErrorNotSupported;
   static cudaError_t attr = set_smem(attn_bwd_kv, bkv::SMEM);
   if (attr != cudaSuccess) return attr;
-  attn_bwd_kv<<<grid, kThreads, bkv::SMEM, stream>>>(mk, mv, mq, mdo, mqm, mdom, mdk, mdv, p, err);
-  return cudaGetLastError();
+  return launch_pdl(attn_bwd_kv, grid, dim3(kThreads), bkv::SMEM, stream, mk, mv, mq, mdo, mqm, mdom, mdk, mdv, p,
+                    err);
 }
 
 }  // namespace sb

@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "pdl.h"
 
 namespace sb {
 namespace {
@@ -110,6 +111,7 @@ bool pad_plan(const GemmArgs& g, Padding* pd, GemmArgs* view) {
 
 __global__ void pad_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t batch, int64_t rows,
                                 int64_t inner, int64_t s_row, int64_t s_batch, int64_t ld) {
+  pdl_prologue();
   const int64_t n = batch * rows * inner;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t c = i % inner;
@@ -123,8 +125,8 @@ cudaError_t pad_copy(const float* src, float* dst, int64_t batch, const PadOp& o
   const int64_t n = batch * o.rows * o.inner;
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
-  pad_copy_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, dst, batch, o.rows, o.inner, o.s_row, o.s_batch, o.ld);
-  return cudaGetLastError();
+  return launch_pdl(pad_copy_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, batch, o.rows, o.inner,
+                    o.s_row, o.s_batch, o.ld);
 }
 
 }  // namespace

@@ -3,6 +3,7 @@
 // 128x128x8 block tile, 256 threads, 8x8 outputs per thread, register-staged
 // double buffering of the shared-memory tiles.
 #include "kernels.h"
+#include "pdl.h"
 
 namespace sb {
 namespace {
@@ -10,6 +11,7 @@ namespace {
 constexpr int BM = 128, BN = 128, BK = 8;
 
 __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
+  pdl_prologue();
   __shared__ float As[2][BK][BM + 4];
   __shared__ float Bs[2][BK][BN + 4];
   const int tid = threadIdx.x;
@@ -109,8 +111,7 @@ cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream) {
   dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM),
             (unsigned)(g.batch < 65535 ? g.batch : 65535));
   if (grid.y > 65535) return cudaErrorInvalidConfiguration;
-  sgemm_strided<<<grid, 256, 0, stream>>>(g);
-  return cudaGetLastError();
+  return launch_pdl(sgemm_strided, grid, dim3(256), 0, stream, g);
 }
 
 }  // namespace sb

@@ -29,6 +29,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "pdl.h"
 #include "tc_common.h"
 
 namespace sb {
@@ -177,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
                       int c3d, int round_out, int kchunk, Tiles tl, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  pdl_prologue();
   if (smem_u32(smem_raw) & 1023u) {  // uniform: every thread leaves before any barrier
     if (threadIdx.x == 0) atomicExch(err, 9);
     return;
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  pdl_prologue();
   // both CTAs of a pair have the same layout, so both leave here or neither
   if (smem_u32(smem_raw) & 1023u) {
     if (threadIdx.x == 0) atomicExch(err, 9);
@@ -604,11 +607,9 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   if (total > (1ll << 30)) return cudaErrorNotSupported;
   tl.total = (int)total;
   const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
-  kern<<<grid, kThreads, S::BYTES, stream>>>(ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                                             (long long)g.scm, a_mn, b_mn, a3d, b3d, a_chunks, b_chunks, c_tma, c3d,
-                                             g.round_out, kchunk,
-                                             tl, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, ta, tb, tc_map, g.c, (int)g.M,
+                    (int)g.N, (int)g.K, (long long)g.scb, (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d,
+                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, err);
 }
 
 template <int BN, int STAGES, int PER_SM, int ACC>
@@ -652,13 +653,14 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = S::BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  pdl_attribute(&attr[1]);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
                             (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
                             g.round_out,

@@ -1,5 +1,6 @@
 // Small hand-written helper kernels.
 #include "kernels.h"
+#include "pdl.h"
 
 namespace sb {
 namespace {
@@ -14,6 +15,7 @@ __device__ __forceinline__ float rna_tf32(float x) {
 // 16-byte aligned), then a scalar tail.
 __global__ void __launch_bounds__(256) round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                                          int64_t n, int64_t n4) {
+  pdl_prologue();
   const float4* s4 = reinterpret_cast<const float4*>(src);
   float4* d4 = reinterpret_cast<float4*>(dst);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
@@ -34,8 +36,7 @@ cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_
   int64_t blocks = ((aligned ? n4 : n) + 255) / 256;
   if (blocks < 1) blocks = 1;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  round_tf32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, dst, n, n4);
-  return cudaGetLastError();
+  return launch_pdl(round_tf32_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, n, n4);
 }
 
 }  // namespace sb
@@ -46,6 +47,7 @@ namespace {
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ p, float* __restrict__ c,
                                                             int64_t splits, int64_t M, int64_t N, int64_t ldc,
                                                             int round) {
+  pdl_prologue();
   const int64_t mn = M * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
     float acc = 0.f;
@@ -60,6 +62,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 // flight; same summation order (splits ascending) as the scalar kernel.
 __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float4* __restrict__ p, float* __restrict__ c,
                                                              int splits, int mn4, int n4, int ldc, int round) {
+  pdl_prologue();
   const int i4 = blockIdx.x * blockDim.x + threadIdx.x;
   if (i4 >= mn4) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -85,14 +88,13 @@ cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64
   if (N % 4 == 0 && ldc % 4 == 0 && ((uintptr_t)partials & 15) == 0 && ((uintptr_t)c & 15) == 0 &&
       mn / 4 < (1ll << 31) && splits < (1ll << 31)) {
     const int64_t mn4 = mn / 4;
-    splitk_reduce4_kernel<<<(unsigned)((mn4 + 255) / 256), 256, 0, stream>>>(
+    return launch_pdl(splitk_reduce4_kernel, dim3((unsigned)((mn4 + 255) / 256)), dim3(256), 0, stream,
         (const float4*)partials, c, (int)splits, (int)mn4, (int)(N / 4), (int)ldc, round_tf32);
-    return cudaGetLastError();
   }
   int64_t blocks = (mn + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(partials, c, splits, M, N, ldc, round_tf32);
-  return cudaGetLastError();
+  return launch_pdl(splitk_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, partials, c, splits, M, N, ldc,
+                    round_tf32);
 }
 
 }  // namespace sb

@@ -12,6 +12,7 @@
 // v = b2 v + (1 - b2) g'^2; p = p - lr (wd p + (m bc_m) / (sqrt(v bc_v) + eps)),
 // in f32 in the reference's operation order.
 #include "kernels.h"
+#include "pdl.h"
 
 namespace sb {
 namespace {
@@ -37,6 +38,7 @@ __device__ __forceinline__ float block_sum(float x, float* red) {
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(const OptLeaf* __restrict__ leaves,
                                                          const OptChunk* __restrict__ chunks,
                                                          float* __restrict__ partials) {
+  pdl_prologue();
   __shared__ float red[kThreads / 32];
   const OptChunk c = chunks[blockIdx.x];
   const float* g = leaves[c.leaf].g + c.off;
@@ -50,6 +52,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const OptLeaf* __restri
                                                          const OptChunk* __restrict__ chunks, int n_chunks,
                                                          const float* __restrict__ partials,
                                                          float* __restrict__ norm_out, AdamwScalars a) {
+  pdl_prologue();
   __shared__ float red[kThreads / 32];
   float clip = 1.f;
   if (a.clip || norm_out) {
@@ -78,12 +81,11 @@ cudaError_t adamw_step(const OptLeaf* leaves, const OptChunk* chunks, int n_chun
                        float* norm_out, const AdamwScalars& a, cudaStream_t stream) {
   if (n_chunks <= 0) return cudaSuccess;
   if (a.clip || norm_out) {
-    sumsq_kernel<<<n_chunks, kThreads, 0, stream>>>(leaves, chunks, partials);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(sumsq_kernel, dim3(n_chunks), dim3(kThreads), 0, stream, leaves, chunks, partials);
     if (e != cudaSuccess) return e;
   }
-  adamw_kernel<<<n_chunks, kThreads, 0, stream>>>(leaves, chunks, n_chunks, partials, norm_out, a);
-  return cudaGetLastError();
+  return launch_pdl(adamw_kernel, dim3(n_chunks), dim3(kThreads), 0, stream, leaves, chunks, n_chunks, partials,
+                    norm_out, a);
 }
 
 }  // namespace sb

@@ -11,6 +11,7 @@
 // total order, so the ranks are a permutation.  Output row: [sorted keys |
 // payload bits], the packed layout of OpKind::SortPairs.
 #include "kernels.h"
+#include "pdl.h"
 
 namespace sb {
 namespace {
@@ -26,6 +27,7 @@ __device__ __forceinline__ int order_key(float x) {
 __global__ void __launch_bounds__(kThreads) sort_rank_kernel(const float* __restrict__ keys,
                                                              const int* __restrict__ payload,
                                                              float* __restrict__ out, int n, int desc) {
+  pdl_prologue();
   __shared__ int tile[kTile];
   const size_t row = blockIdx.y;
   const float* k = keys + row * n;
@@ -65,8 +67,8 @@ cudaError_t sort_pairs(const float* keys, const int* payload, float* out, int64_
   if (rows <= 0 || n <= 0) return cudaSuccess;
   if (n > (1ll << 30) || rows > 65535) return cudaErrorNotSupported;
   const dim3 grid((unsigned)((n + kThreads - 1) / kThreads), (unsigned)rows);
-  sort_rank_kernel<<<grid, kThreads, 0, stream>>>(keys, payload, out, (int)n, descending ? 1 : 0);
-  return cudaGetLastError();
+  return launch_pdl(sort_rank_kernel, grid, dim3(kThreads), 0, stream, keys, payload, out, (int)n,
+                    descending ? 1 : 0);
 }
 
 }  // namespace sb
