@@ -1,6 +1,6 @@
 // Attention rewrite: finds scaled-dot-product attention in a StableHLO function
 // and its reverse-mode gradient, and replaces them by the fused attention ops
-// (OpKind::AttnFwd / AttnBwdQ / AttnBwdKV, kernels/attention.cu).
+// (OpKind::AttnFwd / AttnBwd, kernels/attention.cu).
 //
 // What Sheaf emits for `causal_self_attention` (sheaf/lib/nn.shf; the softmax
 // of sheaf/lib/nn.shf and the tril mask of the builtins, lowered by
@@ -742,20 +742,27 @@ std::unique_ptr<Function> rewrite_attention(const Function& f, std::string* log)
     std::vector<Op>& pre = bld.before[ip];
     int q2 = bld.canonical(&pre, m.q, "bhqd"), k2 = bld.canonical(&pre, m.k, "bhkd"),
         v2 = bld.canonical(&pre, m.v, "bhkd"), dyc = bld.canonical(&pre, bm.dy, "bhqd");
-    int pq = bld.new_value(bld.f32({N + R}));
-    Op aq = Builder::mk(OpKind::AttnBwdQ, pq, {q2, k2, v2, dyc, m.y, lse}, bld.f32({N + R}));
-    aq.values = {m.scale};
-    aq.axis = af.axis;
-    pre.push_back(aq);
-    int dsum = bld.part(&pre, pq, N, N + R, {B, H, T});
-    int pkv = bld.new_value(bld.f32({2 * N}));
-    Op akv = Builder::mk(OpKind::AttnBwdKV, pkv, {q2, k2, v2, dyc, lse, dsum}, bld.f32({2 * N}));
-    akv.values = {m.scale};
-    akv.axis = af.axis;
-    pre.push_back(akv);
-    int dqb = bld.part(&pre, pq, 0, N, {B, T, H, HD});
-    int dkb = bld.part(&pre, pkv, 0, N, {B, T, H, HD});
-    int dvb = bld.part(&pre, pkv, N, 2 * N, {B, T, H, HD});
+    // dQ, dK, dV interleaved per token: (B,T,3,H,64), so the three gradients
+    // are adjacent column blocks of one [B*T, 3*H*64] matrix (the layout of
+    // the fused projection whose slices produced q, k, v)
+    int pb = bld.new_value(bld.f32({3 * N + R}));
+    Op ab = Builder::mk(OpKind::AttnBwd, pb, {q2, k2, v2, dyc, m.y, lse}, bld.f32({3 * N + R}));
+    ab.values = {m.scale};
+    ab.axis = af.axis;
+    pre.push_back(ab);
+    int g5 = bld.part(&pre, pb, 0, 3 * N, {B, T, 3, H, HD});
+    auto channel = [&](int c) {
+      int s = bld.new_value(bld.f32({B, T, 1, H, HD}));
+      Op sl = Builder::mk(OpKind::Slice, s, {g5}, bld.f32({B, T, 1, H, HD}));
+      sl.a0 = {0, 0, c, 0, 0};
+      sl.a1 = {B, T, c + 1, H, HD};
+      sl.a2 = {1, 1, 1, 1, 1};
+      pre.push_back(sl);
+      int r = bld.new_value(bld.f32({B, T, H, HD}));
+      pre.push_back(Builder::mk(OpKind::Reshape, r, {s}, bld.f32({B, T, H, HD})));
+      return r;
+    };
+    int dqb = channel(0), dkb = channel(1), dvb = channel(2);
     std::vector<Op> rq, rk, rv;
     bld.from_bthd(&rq, dqb, 'q', bm.dq_lab, bm.dq);
     bld.from_bthd(&rk, dkb, 'k', bm.dk_lab, bm.dk);

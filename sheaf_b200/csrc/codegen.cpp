@@ -247,6 +247,29 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
       out = eval(c, op.operands[0], ic);
       break;
     }
+    case OpKind::StridedView: {
+      // flat position in the operand's row-major layout, split into its coords
+      if (c.vec)
+        for (auto& x : coords)
+          if (uses_lane(x)) throw VecFail{};
+      const auto& ish = f_.value_types[op.operands[0]].shape;
+      std::string lin = std::to_string(op.a0[0]);
+      for (size_t i = 0; i < osh.size(); ++i) lin = c_add(lin, c_mul(coords[i], op.a2[i]));
+      std::string ln = fresh(c, "lin");
+      c.body << c.pad() << "const " << c.idx << " " << ln << " = " << lin << ";\n";
+      const auto si = row_major(ish);
+      std::vector<std::string> ic(ish.size(), "0");
+      bool first = true;
+      for (size_t i = 0; i < ish.size(); ++i) {
+        if (ish[i] == 1) continue;
+        std::string e = si[i] == 1 ? ln : "(" + ln + "/" + std::to_string(si[i]) + ")";
+        if (!first) e = "(" + e + "%" + std::to_string(ish[i]) + ")";
+        first = false;
+        ic[i] = e;
+      }
+      out = eval(c, op.operands[0], ic);
+      break;
+    }
     case OpKind::Reverse: {
       std::vector<std::string> ic = coords;
       for (auto d : op.dims) ic[d] = "(" + std::to_string(osh[d] - 1) + "-(" + coords[d] + "))";

@@ -44,10 +44,11 @@ enum class OpKind : uint8_t {
   BroadcastInDim, Reshape, Transpose, Iota, Slice, Pad, Concatenate, Reverse,
   Reduce, DotGeneral, Gather,
   // Fused attention (head dim 64), created by the planner's attention rewrite,
-  // never parsed.  Operands: q, k, v [B,H,T,64] (+ dy, y, lse for AttnBwdQ;
-  // + dy, lse, dsum for AttnBwdKV).  values[0] = score scale, axis = causal.
-  // Results are packed 1-D buffers (see AttnArgs in kernels/kernels.h).
-  AttnFwd, AttnBwdQ, AttnBwdKV,
+  // never parsed.  Operands: q, k, v [B,H,T,64] (+ dy, y [B,H,T,64] and
+  // lse [B,H,T] for AttnBwd).  values[0] = score scale, axis = causal.
+  // Results are packed 1-D buffers: AttnFwd [Y (B,T,H,64) | L (B,H,T)],
+  // AttnBwd [dQ, dK, dV interleaved as (B,T,3,H,64) | D (B,H,T)].
+  AttnFwd, AttnBwd,
   // stablehlo.bitcast_convert between 32-bit element types (f32 <-> i32)
   Bitcast,
   // stablehlo.sort of (f32 keys, i32 payload) along the last dim with a
@@ -56,6 +57,10 @@ enum class OpKind : uint8_t {
   // the two results are a slice and a bitcast slice of it.  axis = 1 for
   // descending (GT).
   SortPairs,
+  // As-strided view of the row-major flattening of its operand, created by
+  // the planner's sibling-GEMM merge, never parsed: element i of the result
+  // is operand_flat[a0[0] + sum_d i_d * a2[d]].  A pure index map.
+  StridedView,
 };
 const char* opkind_name(OpKind k);
 
@@ -71,7 +76,7 @@ inline bool is_unary_elementwise(OpKind k) {
          k == OpKind::Ceil || k == OpKind::Logistic || k == OpKind::Convert || k == OpKind::Bitcast;
 }
 inline bool is_attention(OpKind k) {
-  return k == OpKind::AttnFwd || k == OpKind::AttnBwdQ || k == OpKind::AttnBwdKV;
+  return k == OpKind::AttnFwd || k == OpKind::AttnBwd;
 }
 inline bool is_elementwise(OpKind k) {
   return is_binary_elementwise(k) || is_unary_elementwise(k) || k == OpKind::Clamp ||

@@ -93,7 +93,7 @@ struct Params {
   const float* dy; long long dy_sb, dy_sh, dy_st;
   const float* lse; long long l_sb, l_sh, l_st;
   const float* dsum; long long d_sb, d_sh, d_st;
-  float* out;
+  float* stats;  // [B,H,T] row statistics written by the pass (L forward, D in the dQ pass)
 };
 
 // ---------------------------------------------------------------- forward
@@ -265,8 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // every S MMA has completed: Q's buffer stages the Y block for two TMA stores
     st_row_kmajor(sQ, BM, tid, o);
     fence_proxy_async();
-    const size_t n = (size_t)p.B * p.T * p.H * HD;
-    p.out[n + ((size_t)b * p.H + h) * p.T + row] = m + log2f(l);
+    p.stats[((size_t)b * p.H + h) * p.T + row] = m + log2f(l);
   }
   fence_before();
   __syncthreads();
@@ -420,8 +419,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // every S MMA has completed: Q's buffer stages the dQ block
     st_row_kmajor(sQ, BM, tid, dq);
     fence_proxy_async();
-    const size_t n = (size_t)p.B * p.T * p.H * HD;
-    p.out[n + ((size_t)b * p.H + h) * p.T + row] = D;
+    p.stats[((size_t)b * p.H + h) * p.T + row] = D;
   }
   fence_before();
   __syncthreads();
@@ -631,12 +629,12 @@ bool map_of(CUtensorMap* m, const AttnView& v, const AttnArgs& a, int rows, bool
   return tc_make_map(m, v.p, 4, dims, str, (uint32_t)rows, mn);
 }
 
-// Store map of a [B,T,H,64] output block (dims {64, T, H, B}): boxes of 32
-// columns x `rows` rows of one head, 128-byte swizzle (the layout
-// st_row_kmajor writes).
-bool out_map(CUtensorMap* m, float* out, const AttnArgs& a, int rows) {
+// Store map of a [B,T,H,64] output block (dims {64, T, H, B}) whose tokens
+// are `ld` elements apart: boxes of 32 columns x `rows` rows of one head,
+// 128-byte swizzle (the layout st_row_kmajor writes).
+bool out_map(CUtensorMap* m, float* out, int64_t ld, const AttnArgs& a, int rows) {
   const uint64_t dims[4] = {(uint64_t)HD, (uint64_t)a.T, (uint64_t)a.H, (uint64_t)a.B};
-  const uint64_t str[3] = {(uint64_t)a.H * HD * 4, (uint64_t)HD * 4, (uint64_t)a.T * a.H * HD * 4};
+  const uint64_t str[3] = {(uint64_t)ld * 4, (uint64_t)HD * 4, (uint64_t)a.T * ld * 4};
   return tc_make_map(m, out, 4, dims, str, (uint32_t)rows, false);
 }
 
@@ -653,6 +651,12 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
     return cudaErrorNotSupported;
   if ((int64_t)a.B * a.H * a.T * HD > (1ll << 40)) return cudaErrorNotSupported;
   if (!view_ok(a.q, a) || !view_ok(a.k, a) || !view_ok(a.v, a)) return cudaErrorNotSupported;
+  const int64_t n = a.B * a.T * a.H * HD;
+  const int64_t ld = a.out_ld ? a.out_ld : a.H * HD;
+  if (ld < a.H * HD || ld % 4) return cudaErrorNotSupported;
+  float* stats = a.stats ? a.stats : a.out + n;
+  float* out_v = a.out_v ? a.out_v : a.out + n;
+  if (!aligned16(out_v)) return cudaErrorNotSupported;
   int* err = tc_error_word();
   if (!err) return cudaErrorNotSupported;
   Params p{};
@@ -662,12 +666,12 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
   p.scale = a.scale;
   p.causal = a.causal ? 1 : 0;
   p.round_out = a.round_out ? 1 : 0;
-  p.out = a.out;
+  p.stats = stats;
   const dim3 grid((unsigned)(a.T / 128), (unsigned)a.H, (unsigned)a.B);
   if (a.kind == AttnKind::Fwd) {
     CUtensorMap mq, mk, mv, my;
     if (!map_of(&mq, a.q, a, fwd::BM, false) || !map_of(&mk, a.k, a, fwd::BN, false) ||
-        !map_of(&mv, a.v, a, fwd::BN, true) || !out_map(&my, a.out, a, fwd::BM))
+        !map_of(&mv, a.v, a, fwd::BN, true) || !out_map(&my, a.out, ld, a, fwd::BM))
       return cudaErrorNotSupported;
     static cudaError_t attr = set_smem(attn_fwd, fwd::SMEM);
     if (attr != cudaSuccess) return attr;
@@ -682,7 +686,7 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
     CUtensorMap mq, mdo, mk, mkm, mv, mdq;
     if (!map_of(&mq, a.q, a, bq::BM, false) || !map_of(&mdo, a.dy, a, bq::BM, false) ||
         !map_of(&mk, a.k, a, bq::BN, false) || !map_of(&mkm, a.k, a, bq::BN, true) ||
-        !map_of(&mv, a.v, a, bq::BN, false) || !out_map(&mdq, a.out, a, bq::BM))
+        !map_of(&mv, a.v, a, bq::BN, false) || !out_map(&mdq, a.out, ld, a, bq::BM))
       return cudaErrorNotSupported;
     static cudaError_t attr = set_smem(attn_bwd_q, bq::SMEM);
     if (attr != cudaSuccess) return attr;
@@ -691,11 +695,10 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.kind != AttnKind::BwdKV || !a.dsum) return cudaErrorNotSupported;
   p.dsum = a.dsum; p.d_sb = a.d_sb; p.d_sh = a.d_sh; p.d_st = a.d_st;
   CUtensorMap mk, mv, mq, mdo, mqm, mdom, mdk, mdv;
-  const size_t n = (size_t)a.B * a.T * a.H * HD;
   if (!map_of(&mk, a.k, a, bkv::BN, false) || !map_of(&mv, a.v, a, bkv::BN, false) ||
       !map_of(&mq, a.q, a, bkv::BQ, false) || !map_of(&mdo, a.dy, a, bkv::BQ, false) ||
       !map_of(&mqm, a.q, a, bkv::BQ, true) || !map_of(&mdom, a.dy, a, bkv::BQ, true) ||
-      !out_map(&mdk, a.out, a, bkv::BN) || !out_map(&mdv, a.out + n, a, bkv::BN))
+      !out_map(&mdk, a.out, ld, a, bkv::BN) || !out_map(&mdv, out_v, ld, a, bkv::BN))
     return cudaErrorNotSupported;
   static cudaError_t attr = set_smem(attn_bwd_kv, bkv::SMEM);
   if (attr != cudaSuccess) return attr;

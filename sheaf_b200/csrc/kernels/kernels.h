@@ -79,10 +79,17 @@ struct AttnArgs {
   int64_t l_sb = 0, l_sh = 0, l_st = 0;
   const float* dsum = nullptr; // [B,H,T] rowsum(dY * Y) (BwdKV)
   int64_t d_sb = 0, d_sh = 0, d_st = 0;
+  // Default packing (out_ld, stats, out_v unset):
   // Fwd:   [Y (B,T,H,64) | L (B,H,T)]
   // BwdQ:  [dQ (B,T,H,64) | D (B,H,T)]
   // BwdKV: [dK (B,T,H,64) | dV (B,T,H,64)]
+  // out_ld (elements between consecutive tokens of the (B,T,H,64) outputs,
+  // a multiple of 4, at least H*64), stats (L / D) and out_v (dV) override
+  // it, e.g. to interleave dQ, dK, dV as one (B,T,3,H,64) buffer.
   float* out = nullptr;
+  int64_t out_ld = 0;
+  float* stats = nullptr;
+  float* out_v = nullptr;
 };
 cudaError_t attention(const AttnArgs& a, cudaStream_t stream);
 

@@ -40,7 +40,7 @@ const char* opkind_name(OpKind k) {
       "negate", "sine", "cosine", "not", "sign", "floor", "ceil", "logistic", "clamp",
       "convert", "select", "compare", "broadcast_in_dim", "reshape", "transpose", "iota",
       "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather",
-      "attention_fwd", "attention_bwd_q", "attention_bwd_kv", "bitcast_convert", "sort"};
+      "attention_fwd", "attention_bwd", "bitcast_convert", "sort", "strided_view"};
   return names[(int)k];
 }
 

@@ -33,29 +33,6 @@ std::vector<int64_t> row_major(const std::vector<int64_t>& shape) {
   return s;
 }
 
-namespace {
-
-constexpr int kDup = -2;   // duplicable (never materialized)
-constexpr int kConst = -3; // dense constant buffer
-constexpr int kParam = -4;
-constexpr int kAbsorbed = -5;  // batched dot_general folded into the GEMM of its batch reduction
-
-bool is_dup_kind(const Op& op) {
-  switch (op.kind) {
-    case OpKind::BroadcastInDim: case OpKind::Reshape: case OpKind::Transpose:
-    case OpKind::Slice: case OpKind::Reverse: case OpKind::Iota:
-      return true;
-    case OpKind::Constant:
-      return op.values.size() == 1;
-    default:
-      return false;
-  }
-}
-
-[[noreturn]] void fail(const Op& op, const std::string& msg) {
-  throw std::runtime_error("line " + std::to_string(op.line) + " (" + opkind_name(op.kind) + "): " + msg);
-}
-
 // numpy-style no-copy reshape of a strided view; returns false if impossible.
 bool reshape_view(const std::vector<int64_t>& oshape, const std::vector<int64_t>& ostr,
                   const std::vector<int64_t>& nshape, std::vector<int64_t>* nstr) {
@@ -91,6 +68,30 @@ bool reshape_view(const std::vector<int64_t>& oshape, const std::vector<int64_t>
   }
   return oi == (size_t)on;
 }
+
+namespace {
+
+constexpr int kDup = -2;   // duplicable (never materialized)
+constexpr int kConst = -3; // dense constant buffer
+constexpr int kParam = -4;
+constexpr int kAbsorbed = -5;  // batched dot_general folded into the GEMM of its batch reduction
+
+bool is_dup_kind(const Op& op) {
+  switch (op.kind) {
+    case OpKind::BroadcastInDim: case OpKind::Reshape: case OpKind::Transpose:
+    case OpKind::Slice: case OpKind::Reverse: case OpKind::Iota: case OpKind::StridedView:
+      return true;
+    case OpKind::Constant:
+      return op.values.size() == 1;
+    default:
+      return false;
+  }
+}
+
+[[noreturn]] void fail(const Op& op, const std::string& msg) {
+  throw std::runtime_error("line " + std::to_string(op.line) + " (" + opkind_name(op.kind) + "): " + msg);
+}
+
 
 struct Planner {
   const Function& f;
@@ -502,6 +503,18 @@ struct Planner {
         out->strides = ns;
         return true;
       }
+      case OpKind::StridedView: {
+        // offsets and strides address the operand's row-major layout
+        if (!view_of(op->operands[0], &in)) return false;
+        const auto rm = row_major(in.shape);
+        for (size_t i = 0; i < in.shape.size(); ++i)
+          if (in.shape[i] != 1 && in.strides[i] != rm[i]) return false;
+        out->value = in.value;
+        out->offset = in.offset + op->a0[0];
+        out->shape = op->type.shape;
+        out->strides = op->a2;
+        return true;
+      }
       default:
         return false;
     }
@@ -526,6 +539,13 @@ struct Planner {
   // view, so the maps above it (e.g. a transpose feeding a GEMM) stay views.
   void force_for_view(int v) {
     const Op* op = producer(v);
+    if (op && cluster[v] == kDup && op->kind == OpKind::StridedView) {
+      // a strided view needs a row-major operand: materialize the operand
+      if (!materialized(op->operands[0])) {
+        forced.insert(op->operands[0]);
+        return;
+      }
+    }
     if (op && cluster[v] == kDup && op->kind != OpKind::Iota && op->kind != OpKind::Constant) {
       View in;
       if (!view_of(op->operands[0], &in)) {
@@ -672,6 +692,20 @@ void verify(const Function& f) {
       case OpKind::Iota:
         need(op.axis >= 0 && op.axis < rr, "iota dim");
         break;
+      case OpKind::StridedView: {
+        need(op.operands.size() == 1 && op.a0.size() == 1 && (int)op.a2.size() == rr, "strided view arity");
+        if (op.operands.size() != 1 || op.a0.size() != 1 || (int)op.a2.size() != rr) break;
+        int64_t hi = op.a0[0];
+        bool empty = false;
+        for (int i = 0; i < rr; ++i) {
+          need(op.a2[i] >= 0, "strided view stride");
+          if (rs[i] == 0) empty = true;
+          else hi += (rs[i] - 1) * op.a2[i];
+        }
+        need(op.a0[0] >= 0 && (empty || hi < T(op.operands[0]).numel()), "strided view bounds");
+        need(T(op.operands[0]).dtype == op.type.dtype, "strided view element type");
+        break;
+      }
       case OpKind::Slice: {
         const auto& is = T(op.operands[0]).shape;
         need(op.a0.size() == is.size() && op.a1.size() == is.size() && op.a2.size() == is.size() &&
@@ -768,7 +802,7 @@ void verify(const Function& f) {
           if (op.offset_dims[k] >= 0 && op.offset_dims[k] < rr) need(rs[op.offset_dims[k]] == offs_sizes[k], "gather offset extent");
         break;
       }
-      case OpKind::AttnFwd: case OpKind::AttnBwdQ: case OpKind::AttnBwdKV: {
+      case OpKind::AttnFwd: case OpKind::AttnBwd: {
         const size_t arity = op.kind == OpKind::AttnFwd ? 3 : 6;
         need(op.operands.size() == arity, "attention arity");
         if (op.operands.size() != arity) break;
@@ -776,13 +810,13 @@ void verify(const Function& f) {
         need(q.size() == 4 && q[3] == 64, "attention operand shape");
         if (q.size() != 4) break;
         const std::vector<int64_t> rows{q[0], q[1], q[2]};
-        const int n4 = op.kind == OpKind::AttnFwd ? 3 : (op.kind == OpKind::AttnBwdQ ? 5 : 4);
+        const int n4 = op.kind == OpKind::AttnFwd ? 3 : 5;
         for (size_t s = 0; s < op.operands.size(); ++s) {
           need(T(op.operands[s]).dtype == DType::F32, "attention operands are f32");
           need(T(op.operands[s]).shape == ((int)s < n4 ? q : rows), "attention operand shape");
         }
         const int64_t N = q[0] * q[1] * q[2] * 64, R = q[0] * q[1] * q[2];
-        need(rs == std::vector<int64_t>{op.kind == OpKind::AttnBwdKV ? 2 * N : N + R}, "attention result size");
+        need(rs == std::vector<int64_t>{op.kind == OpKind::AttnBwd ? 3 * N + R : N + R}, "attention result size");
         break;
       }
       default:
@@ -925,12 +959,11 @@ Plan plan_function(const Function& f, Precision prec) {
       if (op.kind == OpKind::AttnFwd) {
         st.flops = 2 * prod;
         st.bytes_moved = 4 * (3 * N + N + R);
-      } else if (op.kind == OpKind::AttnBwdQ) {
-        st.flops = 3 * prod;
-        st.bytes_moved = 4 * (5 * N + R + N + R);
       } else {
-        st.flops = 4 * prod;
-        st.bytes_moved = 4 * (4 * N + 2 * R + 2 * N);
+        // dQ pass (3 products): q, k, v, dY, Y, L in, dQ, D out; dK/dV pass
+        // (4 products): q, k, v, dY, L, D in, dK, dV out
+        st.flops = 7 * prod;
+        st.bytes_moved = 4 * ((5 * N + R + N + R) + (4 * N + 2 * R + 2 * N));
       }
     } else if (op.kind == OpKind::SortPairs) {
       // operands are materialized dense buffers (a sort consumer blocks fusion)
@@ -1192,6 +1225,11 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
   if (prec == Precision::TF32 && fuse_attention) cur.reset(rewrite_attention(f, &log).release());
   if (auto m = merge_reduce_chains(cur ? *cur : f)) cur.reset(m.release());
   if (auto m = transpose_dot_outputs(cur ? *cur : f)) cur.reset(m.release());
+  std::string mlog;
+  if (auto m = merge_sibling_dots(cur ? *cur : f, &mlog)) {
+    cur.reset(m.release());
+    log += (log.empty() ? "" : "; ") + mlog;
+  }
   if (cur) {
     Plan p = plan_function(*cur, prec);
     p.rewritten = cur;

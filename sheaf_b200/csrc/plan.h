@@ -34,7 +34,7 @@ struct GatherDesc {
   int table = -1;
 };
 
-// Fused attention step (OpKind::AttnFwd / AttnBwdQ / AttnBwdKV).  Operand
+// Fused attention step (OpKind::AttnFwd / AttnBwd).  Operand
 // views in the op's operand order; dims B, H, T, head dim 64.
 struct AttnDesc {
   OpKind kind = OpKind::AttnFwd;
@@ -93,7 +93,19 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention = true);
 // attention ops.  Returns nullptr when nothing matched (attn_rewrite.cpp).
 std::unique_ptr<Function> rewrite_attention(const Function& f, std::string* log);
 
+// Merges sibling GEMMs: dot_generals (or batch-reduced dot_generals) that
+// share one operand while their other operands are adjacent blocks of one
+// buffer become one wider GEMM whose result the siblings slice; sums of
+// dot_generals over adjacent blocks of the contraction become one deeper
+// GEMM; and a sum of zero-pads that reassembles a sliced value becomes that
+// value.  Returns nullptr when nothing changed (merge_dots.cpp).
+std::unique_ptr<Function> merge_sibling_dots(const Function& f, std::string* log);
+
 // Row-major strides of a shape.
 std::vector<int64_t> row_major(const std::vector<int64_t>& shape);
+
+// numpy-style no-copy reshape of a strided view; false if impossible.
+bool reshape_view(const std::vector<int64_t>& oshape, const std::vector<int64_t>& ostr,
+                  const std::vector<int64_t>& nshape, std::vector<int64_t>* nstr);
 
 }  // namespace sb

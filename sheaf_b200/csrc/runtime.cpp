@@ -349,7 +349,7 @@ std::string step_name(const Step& st) {
   if (st.kind == StepKind::Gemm) return "gemm";
   if (st.kind == StepKind::Sort) return "sort";
   if (st.kind == StepKind::Attn)
-    return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : (st.attn.kind == OpKind::AttnBwdQ ? "attn_bwd_q" : "attn_bwd_kv");
+    return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : "attn_bwd";
   return st.kernel;
 }
 
@@ -466,7 +466,7 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     if (st.kind == StepKind::Attn) {
       const AttnDesc& d = st.attn;
       AttnArgs a;
-      a.kind = d.kind == OpKind::AttnFwd ? AttnKind::Fwd : (d.kind == OpKind::AttnBwdQ ? AttnKind::BwdQ : AttnKind::BwdKV);
+      a.kind = AttnKind::Fwd;
       a.B = d.B; a.H = d.H; a.T = d.T; a.hd = 64;
       a.scale = (float)d.scale;
       a.causal = d.causal;
@@ -479,21 +479,35 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
         r.sb = w.strides[0]; r.sh = w.strides[1]; r.st = w.strides[2];
         return r;
       };
-      auto rows = [&](size_t i, const float** p, int64_t* sb, int64_t* sh, int64_t* stt) {
-        const View& w = d.in[i];
-        *p = (const float*)ptr[w.value] + w.offset;
-        *sb = w.strides[0]; *sh = w.strides[1]; *stt = w.strides[2];
-      };
       a.q = view(0); a.k = view(1); a.v = view(2);
-      if (a.kind != AttnKind::Fwd) a.dy = view(3);
-      if (a.kind == AttnKind::BwdQ) {
+      cudaError_t e = cudaSuccess;
+      if (d.kind == OpKind::AttnFwd) {
+        e = attention(a, stream);
+      } else {
+        // [dQ, dK, dV as (B,T,3,H,64) | D (B,H,T)]: the dQ pass writes dQ
+        // and D, the dK/dV pass reads D
+        const int64_t hd = d.H * 64, n = d.B * d.T * hd;
+        float* base = (float*)ptr[st.root];
+        const View& l = d.in[5];
+        a.dy = view(3);
         a.y = view(4);
-        rows(5, &a.lse, &a.l_sb, &a.l_sh, &a.l_st);
-      } else if (a.kind == AttnKind::BwdKV) {
-        rows(4, &a.lse, &a.l_sb, &a.l_sh, &a.l_st);
-        rows(5, &a.dsum, &a.d_sb, &a.d_sh, &a.d_st);
+        a.lse = (const float*)ptr[l.value] + l.offset;
+        a.l_sb = l.strides[0]; a.l_sh = l.strides[1]; a.l_st = l.strides[2];
+        a.out_ld = 3 * hd;
+        a.stats = base + 3 * n;
+        a.kind = AttnKind::BwdQ;
+        a.out = base;
+        e = attention(a, stream);
+        if (e == cudaSuccess) {
+          a.kind = AttnKind::BwdKV;
+          a.dsum = base + 3 * n;
+          a.d_sb = d.H * d.T; a.d_sh = d.T; a.d_st = 1;
+          a.out = base + hd;
+          a.out_v = base + 2 * hd;
+          a.stats = nullptr;
+          e = attention(a, stream);
+        }
       }
-      cudaError_t e = attention(a, stream);
       s->used_tc = true;
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "attention"); }
       continue;

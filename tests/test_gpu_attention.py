@@ -75,7 +75,7 @@ def _check(outs, ref, scalar_first=True):
 @pytest.mark.parametrize("causal", [True, False])
 def test_attention_value_and_grad(tf32_session, T, causal):
     low = attention_vag(2, 3, T, causal)
-    assert _fused_steps(low) == 3
+    assert _fused_steps(low) == 2
     ins = _inputs(low, seed=T + causal)
     tf32_session.load_stablehlo(low.text)
     outs = tf32_session.call(low.qualified, ins)
@@ -104,7 +104,7 @@ def test_fused_attention_is_deterministic(tf32_session):
 def test_gpt_layer_with_fused_attention(tf32_session):
     c = M.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=128, vocab_size=65, batch=2)
     low = M.gpt_vag(c)
-    assert _fused_steps(low) == 3
+    assert _fused_steps(low) == 2
     inp = M.gpt_inputs(c, seed=4)
     ins = [inp[n] for n in low.arg_names]
     tf32_session.load_stablehlo(low.text)
