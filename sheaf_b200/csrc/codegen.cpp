@@ -804,27 +804,30 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
       }
       src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
       src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
-      // same block shape as the main kernel: 8 row lanes take every 8th split
-      src_ << "  __shared__ float4 part_[8][32];\n";
-      src_ << "  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;\n";
-      src_ << "  const " << c.idx << " o4 = (" << c.idx << ")blockIdx.x * 32 + cx;\n";
+      // 8 float4 columns x 32 split lanes per block (lane ry takes every 32nd
+      // split), then a fixed tree over the 32 lanes: deterministic
+      src_ << "  __shared__ float4 part_[32][8];\n";
+      src_ << "  const int cx = threadIdx.x & 7, ry = threadIdx.x >> 3;\n";
+      src_ << "  const " << c.idx << " o4 = (" << c.idx << ")blockIdx.x * 8 + cx;\n";
       src_ << "  float a0 = " << ident << ", a1 = " << ident << ", a2 = " << ident << ", a3 = " << ident << ";\n";
       src_ << "  if (o4 < " << O4 << ") {\n";
-      src_ << "#pragma unroll 4\n    for (" << c.idx << " s = ry; s < " << splits << "; s += 8) {\n";
+      src_ << "#pragma unroll 4\n    for (" << c.idx << " s = ry; s < " << splits << "; s += 32) {\n";
       src_ << "      const float4 q = *(const float4*)(S + s * " << O << " + o4 * 4);\n";
       src_ << "      a0 = " << combine("a0", "q.x") << "; a1 = " << combine("a1", "q.y") << "; a2 = "
            << combine("a2", "q.z") << "; a3 = " << combine("a3", "q.w") << ";\n    }\n  }\n";
       src_ << "  part_[ry][cx] = make_float4(a0, a1, a2, a3);\n  __syncthreads();\n";
+      src_ << "  for (int w = 16; w > 0; w >>= 1) {\n    if (ry < w) {\n";
+      src_ << "      const float4 p = part_[ry][cx], q = part_[ry + w][cx];\n";
+      src_ << "      part_[ry][cx] = make_float4(" << combine("p.x", "q.x") << ", " << combine("p.y", "q.y") << ", "
+           << combine("p.z", "q.z") << ", " << combine("p.w", "q.w") << ");\n    }\n    __syncthreads();\n  }\n";
       src_ << "  if (ry == 0 && o4 < " << O4 << ") {\n";
-      src_ << "    for (int j = 1; j < 8; ++j) {\n      const float4 q = part_[j][cx];\n";
-      src_ << "      a0 = " << combine("a0", "q.x") << "; a1 = " << combine("a1", "q.y") << "; a2 = "
-           << combine("a2", "q.z") << "; a3 = " << combine("a3", "q.w") << ";\n    }\n";
+      src_ << "    const float4 q = part_[0][cx];\n    a0 = q.x; a1 = q.y; a2 = q.z; a3 = q.w;\n";
       src_ << init_code << "    *(float4*)(O + o4 * 4) = make_float4(" << store(root, combine("a0", init.name)) << ", "
            << store(root, combine("a1", init.name)) << ", " << store(root, combine("a2", init.name)) << ", "
            << store(root, combine("a3", init.name)) << ");\n  }\n}\n\n";
       names_.push_back(fin);
       st->finish_kernel = fin;
-      st->finish_grid = (O4 + 31) / 32;
+      st->finish_grid = (O4 + 7) / 8;
       st->splits = splits;
       st->scratch_elems = splits * O;
     }

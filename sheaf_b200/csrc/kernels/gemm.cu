@@ -109,24 +109,31 @@ bool pad_plan(const GemmArgs& g, Padding* pd, GemmArgs* view) {
   return true;
 }
 
-__global__ void pad_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t batch, int64_t rows,
-                                int64_t inner, int64_t s_row, int64_t s_batch, int64_t ld) {
+// One thread per element of the padded copy's logical extent.  Index math in
+// the narrowest type that holds it (64-bit division is slow).
+template <typename I>
+__global__ void __launch_bounds__(256) pad_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, I batch,
+                                                       I rows, I inner, int64_t s_row, int64_t s_batch, I ld) {
   pdl_prologue();
-  const int64_t n = batch * rows * inner;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t c = i % inner;
-    const int64_t r = (i / inner) % rows;
-    const int64_t b = i / (inner * rows);
-    dst[(b * rows + r) * ld + c] = src[b * s_batch + r * s_row + c];
+  const I n = batch * rows * inner;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (I)gridDim.x * blockDim.x) {
+    const I rr = i / inner;
+    const I c = i - rr * inner;
+    const I b = rr / rows;
+    const I r = rr - b * rows;
+    dst[((int64_t)b * rows + r) * ld + c] = src[(int64_t)b * s_batch + (int64_t)r * s_row + c];
   }
 }
 
 cudaError_t pad_copy(const float* src, float* dst, int64_t batch, const PadOp& o, cudaStream_t stream) {
   const int64_t n = batch * o.rows * o.inner;
   if (n <= 0) return cudaSuccess;
-  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
-  return launch_pdl(pad_copy_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, batch, o.rows, o.inner,
-                    o.s_row, o.s_batch, o.ld);
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  if (n < (int64_t(1) << 31) - 148 * 16 * 256)
+    return launch_pdl(pad_copy_kernel<uint32_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst,
+                      (uint32_t)batch, (uint32_t)o.rows, (uint32_t)o.inner, o.s_row, o.s_batch, (uint32_t)o.ld);
+  return launch_pdl(pad_copy_kernel<int64_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, batch, o.rows,
+                    o.inner, o.s_row, o.s_batch, o.ld);
 }
 
 }  // namespace
