@@ -87,10 +87,34 @@ const char* const kPdlPrologue =
     "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
     "  asm volatile(\"griddepcontrol.launch_dependents;\");\n";
 
-int lane_of(const std::string& s) {
-  for (int j = 0; j < 4; ++j)
-    if (s == kLane[j]) return j;
+// Lane coordinates of 4-wide code: "<b>" or "(<b>+k)", k = 1..3, where the
+// base b is "cL" (one float4 group per thread) or "cL<j>" (chunk j of a row
+// held in registers by a row group).  Returns k and the base, or -1.
+int lane_of(const std::string& s, std::string* base = nullptr) {
+  auto is_base = [](const std::string& b) {
+    if (b.size() < 2 || b[0] != 'c' || b[1] != 'L') return false;
+    for (size_t i = 2; i < b.size(); ++i)
+      if (b[i] < '0' || b[i] > '9') return false;
+    return true;
+  };
+  if (is_base(s)) {
+    if (base) *base = s;
+    return 0;
+  }
+  if (s.size() > 5 && s.front() == '(' && s.back() == ')') {
+    const size_t plus = s.find('+');
+    if (plus == std::string::npos || plus + 3 != s.size()) return -1;
+    const std::string b = s.substr(1, plus - 1);
+    const char k = s[plus + 1];
+    if (!is_base(b) || k < '1' || k > '3') return -1;
+    if (base) *base = b;
+    return k - '0';
+  }
   return -1;
+}
+
+std::string lane_coord(const std::string& base, int k) {
+  return k == 0 ? base : "(" + base + "+" + std::to_string(k) + ")";
 }
 
 bool uses_lane(const std::string& s) { return s.find("cL") != std::string::npos; }
@@ -110,6 +134,20 @@ std::string CodeGen::index_type(const Op& root, int64_t extra) const {
 }
 
 CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& coords) {
+  auto rit = c.reg_kind.find(v);
+  if (rit != c.reg_kind.end()) {
+    // an earlier row-group member's output: its registers
+    std::string key = std::to_string(v) + "@row";
+    if (rit->second == 0) {
+      std::string base;
+      const int k = coords.empty() ? -1 : lane_of(coords.back(), &base);
+      if (k < 0) throw VecFail{};
+      key = std::to_string(v) + "@" + base + ":" + std::to_string(k);
+    }
+    auto it2 = c.regs.find(key);
+    if (it2 == c.regs.end()) throw VecFail{};
+    return it2->second;
+  }
   auto it = c.leaf_index.find(v);
   int li;
   if (it == c.leaf_index.end()) {
@@ -124,9 +162,10 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
   if (t.dtype == DType::BF16) throw std::runtime_error("bf16 buffers are not supported in fused kernels");
   if (c.vec) {
     int lane = -1;
+    std::string base = "cL";
     for (size_t i = 0; i < coords.size(); ++i) {
       if (!uses_lane(coords[i])) continue;
-      if (i + 1 != coords.size() || (lane = lane_of(coords[i])) < 0) throw VecFail{};
+      if (i + 1 != coords.size() || (lane = lane_of(coords[i], &base)) < 0) throw VecFail{};
     }
     if (lane >= 0) {
       // innermost index is the lane coordinate itself: lanes 0..3 read 4
@@ -135,7 +174,7 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
       if (t.dtype != DType::F32 || t.shape.back() % 4 || c.memo.size() > 1) throw VecFail{};
       std::string off0 = "0";
       for (size_t i = 0; i + 1 < coords.size(); ++i) off0 = c_add(off0, c_mul(coords[i], st[i]));
-      off0 = c_add(off0, "cL");
+      off0 = c_add(off0, base);
       const std::string key = std::to_string(li) + ":" + off0;
       auto vit = c.vloads.find(key);
       std::string var;
@@ -594,7 +633,7 @@ bool CodeGen::gen_loop_vec4(const Op& root, Step* st) {
 // order, so results are deterministic.  Returns false (nothing emitted) when an
 // access does not vectorize or the shape does not qualify.
 std::string CodeGen::epilogue_code(Ctx& c, const Op& red, const Op& epi, const std::vector<std::string>& oc,
-                                   int indent, std::string* val) {
+                                   int indent, std::string* val, const std::string& rv) {
   auto saved_memo = std::move(c.memo);
   const int saved_root = c.root, saved_indent = c.indent;
   const bool saved_vec = c.vec;
@@ -613,7 +652,7 @@ std::string CodeGen::epilogue_code(Ctx& c, const Op& red, const Op& epi, const s
   std::vector<std::string> rc;
   size_t k = 0;
   for (int64_t e : epi.type.shape) rc.push_back(e == 1 ? "0" : nu[k++]);
-  c.memo[0][std::to_string(red.result) + "@" + join(xc, ",")] = Val{"rv_", "float"};
+  c.memo[0][std::to_string(red.result) + "@" + join(xc, ",")] = Val{rv, "float"};
   c.root = epi.result;
   c.indent = indent;
   c.vec = false;
@@ -757,9 +796,20 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
          << "; o += (" << c.idx << ")gridDim.x * " << kThreads / 32 << ") {\n";
     src_ << pre.str();
     src_ << "    float acc = " << ident << ";\n";
-    src_ << "    for (" << c.idx << " k4 = lane; k4 < " << R / 4 << "; k4 += 32) {\n" << loop_code;
-    for (int j = 0; j < 4; ++j) src_ << "      acc = " << combine("acc", lanes[j]) << ";\n";
-    src_ << "    }\n";
+    const int64_t J = (R / 4 + 31) / 32;
+    if (J <= 16) {
+      // unrolled lane-strided passes: every load of the row in flight at once
+      src_ << "#pragma unroll\n    for (int j_ = 0; j_ < " << J << "; ++j_) {\n      const " << c.idx
+           << " k4 = lane + 32 * j_;\n";
+      src_ << ((R / 4) % 32 ? "      if (k4 < " + std::to_string(R / 4) + ") {\n" : std::string("      {\n"))
+           << loop_code;
+      for (int j = 0; j < 4; ++j) src_ << "      acc = " << combine("acc", lanes[j]) << ";\n";
+      src_ << "    }}\n";
+    } else {
+      src_ << "    for (" << c.idx << " k4 = lane; k4 < " << R / 4 << "; k4 += 32) {\n" << loop_code;
+      for (int j = 0; j < 4; ++j) src_ << "      acc = " << combine("acc", lanes[j]) << ";\n";
+      src_ << "    }\n";
+    }
     src_ << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
          << combine("acc", "y_") << "; }\n";
     src_ << "    if (lane == 0) {\n" << final_store("acc") << "    }\n  }\n}\n\n";
@@ -1076,6 +1126,177 @@ std::string CodeGen::prelude() {
          "  asm(\"cvt.rna.tf32.f32 %0, %1;\" : \"=r\"(u) : \"f\"(x));\n"
          "  return __uint_as_float(u);\n"
          "}\n";
+}
+
+bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t C, Step* st) {
+  // each lane owns J float4 groups of a row (chunk j: columns
+  // (lane + 32 j) * 4 .. +3); every member's row values stay in registers
+  if (ms.size() < 2 || R <= 0 || C % 128 || C / 128 > 8) return false;
+  const int J = (int)(C / 128);
+  Ctx c;
+  c.idx = index_type(*ms[0].root, R * C);
+  c.memo.assign(1, {});
+  c.vec = true;
+  c.indent = 2;
+  std::vector<int> outs;
+  std::ostringstream rows;
+  for (int j = 0; j < J; ++j)
+    rows << "    const " << c.idx << " cL" << j << " = (lane + " << 32 * j << ") * 4;\n";
+  // coordinates of a shape whose leading dims hold the row index `row`
+  // (innermost dim excluded when `full`); declared once per row shape, so
+  // members of the same shape share loads and subexpressions
+  std::map<std::vector<int64_t>, std::vector<std::string>> coord_of;
+  auto row_coords = [&](const std::vector<int64_t>& sh, bool full, const std::string&) {
+    std::vector<int64_t> key(sh.begin(), sh.end() - (full ? 1 : 0));
+    auto it = coord_of.find(key);
+    if (it != coord_of.end()) {
+      std::vector<std::string> co = it->second;
+      if (full) co.push_back("0");
+      return co;
+    }
+    const std::string tag = "r" + std::to_string(coord_of.size()) + "_";
+    const int n = (int)key.size();
+    std::vector<std::string> co(sh.size(), "0");
+    c.body << "    " << c.idx << " " << tag << "_ = row;\n";
+    for (int d = n - 1; d >= 0; --d) {
+      if (sh[d] == 1) continue;
+      co[d] = tag + std::to_string(d);
+      c.body << "    const " << c.idx << " " << co[d] << " = " << tag << "_ % " << sh[d] << "; " << tag << "_ /= "
+             << sh[d] << ";\n";
+    }
+    coord_of[key] = std::vector<std::string>(co.begin(), co.begin() + n);
+    return co;
+  };
+  auto reg = [&](const std::string& expr) {
+    const std::string n = fresh(c, "g");
+    c.body << "    const float " << n << " = " << expr << ";\n";
+    return Val{n, "float"};
+  };
+  try {
+    for (size_t mi = 0; mi < ms.size(); ++mi) {
+      const RowMember& m = ms[mi];
+      const Op& root = *m.root;
+      const Op& out_op = m.epi ? *m.epi : root;
+      const int out_v = out_op.result;
+      if (out_op.type.dtype != DType::F32) return false;
+      const std::string W = "O" + std::to_string(outs.size());
+      outs.push_back(out_v);
+      const std::string tag = "m" + std::to_string(mi) + "r";
+      c.indent = 2;
+      if (m.kind == 0) {
+        const auto& sh = root.type.shape;
+        if (sh.empty() || sh.back() != C) return false;
+        std::vector<std::string> co = row_coords(sh, true, tag);
+        c.root = root.result;
+        for (int j = 0; j < J; ++j) {
+          const std::string b = "cL" + std::to_string(j);
+          std::string g[4];
+          for (int k = 0; k < 4; ++k) {
+            co.back() = lane_coord(b, k);
+            const Val v = reg(store(root, eval(c, root.result, co).name));
+            // later members see the stored (possibly TF32-rounded) value
+            c.memo[0][std::to_string(root.result) + "@" + join(co, ",")] = v;
+            c.regs[std::to_string(out_v) + "@" + b + ":" + std::to_string(k)] = v;
+            g[k] = v.name;
+          }
+          c.body << "    *(float4*)(" << W << " + row * " << C << " + " << b << ") = make_float4(" << g[0] << ", "
+                 << g[1] << ", " << g[2] << ", " << g[3] << ");\n";
+        }
+        c.reg_kind[out_v] = 0;
+      } else if (m.kind == 1) {
+        if (root.type.numel() != R) return false;
+        std::vector<std::string> co = row_coords(root.type.shape, false, tag);
+        c.root = root.result;
+        const Val v = reg(store(root, eval(c, root.result, co).name));
+        c.memo[0][std::to_string(root.result) + "@" + join(co, ",")] = v;
+        c.body << "    if (lane == 0) " << W << "[row] = " << v.name << ";\n";
+        c.regs[std::to_string(out_v) + "@row"] = v;
+        c.reg_kind[out_v] = 1;
+      } else {
+        const Type& in = f_.value_types[root.operands[0]];
+        const auto& ish = in.shape;
+        const int r = (int)ish.size();
+        if (r == 0 || ish.back() != C || root.dims.size() != 1 || root.dims[0] != r - 1 ||
+            root.type.dtype != DType::F32 || in.dtype != DType::F32 || root.type.numel() != R)
+          return false;
+        const char* ident = root.body == ReduceBody::Add ? "0.f"
+                            : root.body == ReduceBody::Max ? "__int_as_float(0xff800000)"
+                            : root.body == ReduceBody::Min ? "__int_as_float(0x7f800000)" : "1.f";
+        auto combine = [&](const std::string& a, const std::string& b) {
+          switch (root.body) {
+            case ReduceBody::Add: return a + " + " + b;
+            case ReduceBody::Max: return "fmaxf(" + a + ", " + b + ")";
+            case ReduceBody::Min: return "fminf(" + a + ", " + b + ")";
+            case ReduceBody::Mul: return a + " * " + b;
+          }
+          return a;
+        };
+        std::vector<std::string> oc = row_coords(root.type.shape, false, tag);
+        std::vector<std::string> ic(r);
+        for (int d = 0; d + 1 < r; ++d) ic[d] = oc[d];
+        c.root = root.result;
+        // per lane in the order of the 4-wide row reduction kernel (chunk by
+        // chunk, x y z w), then the xor tree: every lane holds the total
+        const std::string acc = fresh(c, "acc");
+        c.body << "    float " << acc << " = " << ident << ";\n";
+        for (int j = 0; j < J; ++j) {
+          std::string lv[4];
+          for (int k = 0; k < 4; ++k) {
+            ic[r - 1] = lane_coord("cL" + std::to_string(j), k);
+            lv[k] = eval(c, root.operands[0], ic).name;
+          }
+          for (int k = 0; k < 4; ++k) c.body << "    " << acc << " = " << combine(acc, lv[k]) << ";\n";
+        }
+        c.body << "    for (int s = 16; s > 0; s >>= 1) { const float y_ = __shfl_xor_sync(0xffffffffu, " << acc
+               << ", s); " << acc << " = " << combine(acc, "y_") << "; }\n";
+        const bool saved_vec = c.vec;
+        c.vec = false;
+        const Val init = eval(c, root.operands[1], {});
+        const Val rv = reg(combine(acc, init.name));
+        Val out = rv;
+        if (m.epi) {
+          std::string ev;
+          const std::string code = epilogue_code(c, root, *m.epi, oc, 2, &ev, rv.name);
+          c.body << code;
+          out = reg(store(*m.epi, ev));
+        } else {
+          out = reg(store(root, rv.name));
+        }
+        c.vec = saved_vec;
+        c.body << "    if (lane == 0) " << W << "[row] = " << out.name << ";\n";
+        c.regs[std::to_string(out_v) + "@row"] = out;
+        c.reg_kind[out_v] = 1;
+      }
+    }
+  } catch (const VecFail&) {
+    return false;
+  }
+  const std::string start_text = src_.str();
+  struct Snip {
+    CodeGen* g; size_t start;
+    ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
+  } snip{this, start_text.size()};
+  std::string name = "k" + std::to_string(names_.size());
+  src_ << header(name, c, (int)outs.size() - 1);
+  for (size_t j = 0; j < outs.size(); ++j)
+    src_ << "  float* __restrict__ O" << j << " = (float*)a.p[" << c.leaves.size() + j << "];\n";
+  src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+  src_ << "  for (" << c.idx << " row = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; row < " << R
+       << "; row += (" << c.idx << ")gridDim.x * " << kThreads / 32 << ") {\n";
+  src_ << rows.str() << c.body.str() << "  }\n}\n\n";
+  names_.push_back(name);
+  st->kernel = name;
+  st->leaves = c.leaves;
+  st->root = outs[0];
+  st->extra_roots.assign(outs.begin() + 1, outs.end());
+  st->block = kThreads;
+  st->grid = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, kMaxGrid));
+  st->elements = R * C;
+  int64_t bytes = 0;
+  for (int o : outs) bytes += f_.value_types[o].numel() * 4;
+  for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
+  st->bytes_moved = bytes;
+  return true;
 }
 
 std::string CodeGen::store(const Op& root, const std::string& expr) const {

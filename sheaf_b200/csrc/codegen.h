@@ -25,6 +25,19 @@ class CodeGen {
   // root's shape, reading root at the output coordinates) is evaluated on each
   // reduced value and stored instead.
   void gen_reduce(const Op& root, Step* st, const Op* epi = nullptr);
+  // A row group: steps over the same R rows of C columns, run back to back
+  // for each row by one warp in a single kernel.  kind 0: loop over
+  // [rows..., C]; 1: loop over the rows (R elements); 2: reduction over the
+  // innermost C of a [rows..., C] operand (root = the reduce op, optional
+  // element-wise epilogue epi).  Later members read earlier members' outputs
+  // only at their own row (the caller checks), after a __syncwarp.  Returns
+  // false (nothing emitted) when a member does not fit the scheme.
+  struct RowMember {
+    int kind;
+    const Op* root;
+    const Op* epi;
+  };
+  bool gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t C, Step* st);
   std::string source() const;
   static std::string prelude();
   std::vector<std::string> kernel_names() const { return names_; }
@@ -48,6 +61,11 @@ class CodeGen {
     // or "(cL+j)"; contiguous f32 leaf reads become one float4 load per lane group
     bool vec = false;
     std::map<std::string, std::string> vloads;  // leaf:offset -> float4 variable
+    // row groups: outputs of earlier members held in registers (value ->
+    // 0: one register per row element of this lane, 1: one per row) and the
+    // registers, keyed "<value>@<lane base>:<k>" or "<value>@row"
+    std::map<int, int> reg_kind;
+    std::map<std::string, Val> regs;
     std::string pad() const { return std::string(indent * 2, ' '); }
   };
 
@@ -56,7 +74,7 @@ class CodeGen {
   // Code of the epilogue expression at output coordinates oc, with the
   // reduced value in the variable r_; *val receives its name.
   std::string epilogue_code(Ctx& c, const Op& red, const Op& epi, const std::vector<std::string>& oc, int indent,
-                            std::string* val);
+                            std::string* val, const std::string& rv = "rv_");
   Val eval(Ctx& c, int v, const std::vector<std::string>& coords);
   Val leaf_load(Ctx& c, int v, const std::vector<std::string>& coords);
   std::string fresh(Ctx& c, const char* p = "t") { return p + std::to_string(c.tmp++); }

@@ -65,7 +65,7 @@ struct Smem {
   // two 32 x 16 f32 staging buffers per epilogue warp
   static constexpr int EPI_BYTES = 4 * 2 * 32 * 16 * 4;
   // the dynamic shared memory window is 1024-byte aligned (checked at entry),
-  // so two CTAs of every configuration fit in an SM's 228 KB
+  // so PER_SM CTAs of every configuration fit in an SM's 228 KB
   static constexpr int BYTES = STAGES * STAGE + EPI_BYTES + 256;
 };
 
@@ -120,50 +120,77 @@ __device__ __forceinline__ void store_chunk(float* slot, const float* v, int lan
   __syncwarp();
 }
 
+// Orders uses of registers written by an asynchronous tcgen05.ld after the
+// tcgen05.wait::ld that completes it.
+__device__ __forceinline__ void reg_fence16(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// One 16-column chunk of this warp's 32 accumulator rows to C: through the
+// warp's double-buffered staging tile and a TMA store, or by plain stores.
+__device__ __forceinline__ void epilogue_chunk(const uint32_t* r, float* bufs, int lane, int* sb,
+                                               const CUtensorMap* tmC, bool c_tma, bool c3d, int z, float* cz,
+                                               int row0, int n, int M, int N, long long ldc, bool vec, bool zero,
+                                               int round_out) {
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    v[q] = zero ? 0.f : __uint_as_float(r[q]);
+    if (round_out) v[q] = rna_tf32(v[q]);
+  }
+  if (c_tma) {
+    float* buf = bufs + *sb * 512;
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      ((float4*)(buf + lane * 16))[u ^ ((lane >> 1) & 3)] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      if (c3d) tma_store_3d(tmC, buf, n, row0, z);
+      else tma_store_2d(tmC, buf, n, row0);
+      bulk_commit();
+    }
+    *sb ^= 1;
+  } else {
+    store_chunk(bufs, v, lane, cz, row0, n, M, N, ldc, vec);
+  }
+}
+
 // Epilogue of one warp's 32 accumulator rows (TMEM lane quadrant at `acc`) to
 // rows row0..row0+31, columns n0..n0+BN-1 of output slice z.  With a C tensor
 // map (c_tma) each 32 x 16 chunk is staged in one of the warp's two 2 KB
 // buffers (64-byte swizzle) and lane 0 issues a TMA store for it, so the
-// stores drain asynchronously while the next chunk is read from TMEM; a buffer
-// is rewritten only after the store issued from it two chunks earlier has read
-// it.  Without a map (row stride or base not 16-byte aligned) store_chunk
-// writes through the first buffer.
+// stores drain asynchronously; a buffer is rewritten only after the store
+// issued from it two chunks earlier has read it.  Without a map (row stride
+// or base not 16-byte aligned) store_chunk writes through the first buffer.
+// Software pipelined: the TMEM load of the next 16 columns is in flight while
+// the current ones are staged and stored.
 template <int BN>
 __device__ __forceinline__ void epilogue_warp(uint32_t acc, float* bufs, int lane, int* sb, const CUtensorMap* tmC,
                                               bool c_tma, bool c3d, int z, float* cz, int row0, int n0, int M, int N,
                                               long long ldc, bool vec, bool zero, int round_out) {
-  if (row0 >= M) return;
+  if (row0 >= M || n0 >= N) return;
+  uint32_t r0[16], r1[16];
+  tmem_ld16_async(acc, r0);
+  tmem_wait_ld();
+  reg_fence16(r0);
 #pragma unroll 1
-  for (int c = 0; c < BN && n0 + c < N; c += 16) {
-    float v[16];
-    tmem_ld16(acc + (uint32_t)c, v);
-    if (zero) {
-#pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] = 0.f;
-    }
-    if (round_out) {
-#pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] = rna_tf32(v[q]);
-    }
-    if (c_tma) {
-      float* buf = bufs + *sb * 512;
-      if (lane == 0) bulk_wait_read1();
-      __syncwarp();
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        ((float4*)(buf + lane * 16))[u ^ ((lane >> 1) & 3)] =
-            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        if (c3d) tma_store_3d(tmC, buf, n0 + c, row0, z);
-        else tma_store_2d(tmC, buf, n0 + c, row0);
-        bulk_commit();
-      }
-      *sb ^= 1;
-    } else {
-      store_chunk(bufs, v, lane, cz, row0, n0 + c, M, N, ldc, vec);
-    }
+  for (int c = 0; c < BN && n0 + c < N; c += 32) {
+    const bool has1 = c + 16 < BN && n0 + c + 16 < N;
+    const bool has2 = c + 32 < BN && n0 + c + 32 < N;
+    if (has1) tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
+    epilogue_chunk(r0, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c, M, N, ldc, vec, zero, round_out);
+    if (!has1) break;
+    tmem_wait_ld();
+    reg_fence16(r1);
+    if (has2) tmem_ld16_async(acc + (uint32_t)(c + 32), r0);
+    epilogue_chunk(r1, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c + 16, M, N, ldc, vec, zero, round_out);
+    if (!has2) break;
+    tmem_wait_ld();
+    reg_fence16(r0);
   }
 }
 
@@ -729,6 +756,7 @@ constexpr TcCfg kCfgs[] = {
     {true, 128, 2, 2, 4},   // 2
     {true, 192, 1, 2, 3},   // 3
     {true, 256, 1, 2, 3},   // 4
+    {true, 256, 2, 1, 6},   // 5
 };
 constexpr int kNumCfgs = (int)(sizeof(kCfgs) / sizeof(kCfgs[0]));
 
@@ -838,6 +866,7 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) {
     case 2: return launch_pair<128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
     case 3: return launch_pair<192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
     case 4: return launch_pair<256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+    case 5: return launch_pair<256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
   }
   return cudaErrorNotSupported;
 }

@@ -16,6 +16,7 @@
 #include "plan.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <functional>
 #include <map>
@@ -168,6 +169,76 @@ struct Planner {
     return d;
   }
   // True when every use of v (seen through index maps) is a GEMM operand.
+  // Row groups: does the cluster of step root `member` (evaluated from node n
+  // at coordinate class cls: 0 = [rows..., C] element, 1 = row, 2 = other)
+  // read each value of `inside` (an earlier member's output -> its class)
+  // only at its own row?  Index maps that keep the row: same-shape operands,
+  // reshapes that keep (rows, C) or the row count, broadcasts of a row vector
+  // along C, and the innermost-dim reduction of a [rows..., C] operand.
+  bool row_local(int n, int cls, int member, const std::map<int, int>& inside, int64_t R, int64_t C,
+                 std::set<std::pair<int, int>>& seen) const {
+    if (!seen.insert({n, cls}).second) return true;
+    const int cl = cluster[n];
+    if (cl == kParam || cl == kConst || (cl == n && n != member)) {
+      auto it = inside.find(n);
+      return it == inside.end() || (cls != 2 && it->second == cls);
+    }
+    const Op* op = producer(n);
+    if (!op) return true;
+    const auto& os = f.value_types[n].shape;
+    auto visit_all = [&](int c2) {
+      for (int o : op->operands)
+        if (!row_local(o, c2, member, inside, R, C, seen)) return false;
+      return true;
+    };
+    if (is_elementwise(op->kind)) {
+      for (int o : op->operands) {
+        const int oc = f.value_types[o].shape == os ? cls : 2;
+        if (!row_local(o, oc, member, inside, R, C, seen)) return false;
+      }
+      return true;
+    }
+    switch (op->kind) {
+      case OpKind::Constant: case OpKind::Iota:
+        return true;
+      case OpKind::Reduce: {
+        const auto& is = f.value_types[op->operands[0]].shape;
+        const bool rowred = cls == 1 && op->dims.size() == 1 && !is.empty() && op->dims[0] == (int64_t)is.size() - 1 &&
+                            is.back() == C && f.value_types[n].numel() == R;
+        if (!row_local(op->operands[0], rowred ? 0 : 2, member, inside, R, C, seen)) return false;
+        return row_local(op->operands[1], 2, member, inside, R, C, seen);
+      }
+      case OpKind::Reshape: {
+        const Type& it = f.value_types[op->operands[0]];
+        int oc = 2;
+        if (cls == 0 && !it.shape.empty() && !os.empty() && it.shape.back() == C && os.back() == C) oc = 0;
+        if (cls == 1 && it.numel() == R) oc = 1;
+        return row_local(op->operands[0], oc, member, inside, R, C, seen);
+      }
+      case OpKind::BroadcastInDim: {
+        const Type& it = f.value_types[op->operands[0]];
+        int oc = 2;
+        if (it.shape == os) {
+          oc = cls;
+        } else if ((cls == 0 || cls == 1) && it.numel() == R) {
+          // non-unit input dims map in order onto equal row dims of the output
+          bool ok = true;
+          int64_t last = -1;
+          for (size_t i = 0; i < it.shape.size(); ++i) {
+            if (it.shape[i] == 1) continue;
+            const int64_t d = op->dims[i];
+            ok = ok && d > last && os[d] == it.shape[i] && (cls == 1 || d + 1 < (int64_t)os.size());
+            last = d;
+          }
+          if (ok) oc = 1;
+        }
+        return row_local(op->operands[0], oc, member, inside, R, C, seen);
+      }
+      default:
+        return visit_all(2);
+    }
+  }
+
   bool only_gemm_consumers(int v) const {
     if (returned[v]) return false;
     for (auto [oi, slot] : consumers[v]) {
@@ -922,10 +993,131 @@ Plan plan_function(const Function& f, Precision prec) {
   CodeGen cg(f, pl.cluster);
   cg.set_round_roots(round_roots);
   std::map<int, int> step_of_value;
+  // Consecutive loop / row-reduction steps over the same rows run as one row
+  // group (CodeGen::gen_row_group): one launch, and each row's intermediates
+  // are re-read from L1/L2 by the warp that just wrote them.
+  struct Member {
+    CodeGen::RowMember m;
+    int op_index, value;
+  };
+  std::vector<Member> group;
+  std::map<int, int> inside;  // member output -> 0 ([rows..., C]) or 1 (row)
+  int64_t gR = 0, gC = 0;
+  // SHEAF_B200_ROW_GROUPS=0 plans every step as its own kernel (for comparison)
+  const char* rg_env = std::getenv("SHEAF_B200_ROW_GROUPS");
+  const bool row_groups = !(rg_env && std::string(rg_env) == "0");
+  auto emit_single = [&](size_t i) {
+    const Op& op = f.ops[i];
+    const int v = op.result;
+    Step st;
+    st.root = v;
+    st.elements = op.type.numel();
+    st.kind = StepKind::Reduce;
+    if (op.kind == OpKind::Reduce) {
+      cg.gen_reduce(op, &st);
+    } else if (pl.epilogue_of.count(v)) {
+      cg.gen_reduce(f.ops[f.producer[pl.epilogue_of[v]]], &st, &op);
+    } else {
+      st.kind = StepKind::Loop;
+      cg.gen_loop(op, &st);
+    }
+    step_of_value[v] = (int)plan.steps.size();
+    plan.materialized.push_back(v);
+    plan.steps.push_back(std::move(st));
+  };
+  // Emits the pending members: the longest run from the first one that the
+  // row-group generator accepts (a member it cannot express, e.g. a gather,
+  // is emitted as its own kernel), and so on.
+  auto flush = [&]() {
+    size_t b = 0;
+    while (b < group.size()) {
+      size_t done = 0;
+      for (size_t e = group.size(); e >= b + 2 && !done; --e) {
+        std::vector<CodeGen::RowMember> ms;
+        for (size_t k = b; k < e; ++k) ms.push_back(group[k].m);
+        Step st;
+        st.kind = StepKind::Loop;
+        if (!cg.gen_row_group(ms, gR, gC, &st)) continue;
+        for (size_t k = b; k < e; ++k) {
+          step_of_value[group[k].value] = (int)plan.steps.size();
+          plan.materialized.push_back(group[k].value);
+        }
+        plan.steps.push_back(std::move(st));
+        done = e - b;
+      }
+      if (done) {
+        b += done;
+      } else {
+        emit_single((size_t)group[b].op_index);
+        ++b;
+      }
+    }
+    group.clear();
+    inside.clear();
+  };
+  // row-group role of the loop / reduction step rooted at op i: kind (-1: none)
+  auto row_role = [&](size_t i, int64_t* R, int64_t* C, CodeGen::RowMember* m) {
+    const Op& op = f.ops[i];
+    const int v = op.result;
+    if (op.type.dtype != DType::F32) return -1;
+    const Op* red = nullptr;
+    if (op.kind == OpKind::Reduce) red = &op;
+    else if (pl.epilogue_of.count(v)) red = &f.ops[f.producer[pl.epilogue_of[v]]];
+    if (red) {
+      const auto& is = f.value_types[red->operands[0]].shape;
+      if (red->dims.size() != 1 || is.empty() || red->dims[0] != (int64_t)is.size() - 1 ||
+          f.value_types[red->operands[0]].dtype != DType::F32)
+        return -1;
+      *R = red->type.numel();
+      *C = is.back();
+      *m = {2, red, red == &op ? nullptr : &op};
+      return 2;
+    }
+    const auto& sh = op.type.shape;
+    if (sh.empty()) return -1;
+    *R = op.type.numel() / std::max<int64_t>(sh.back(), 1);
+    *C = sh.back();
+    *m = {0, &op, nullptr};
+    return 0;
+  };
   for (size_t i = 0; i < f.ops.size(); ++i) {
     const Op& op = f.ops[i];
     int v = op.result;
     if (!pl.live[v] || pl.cluster[v] != v) continue;
+    const bool generated = !(pl.is_gemm_root(op) || is_attention(op.kind) || op.kind == OpKind::SortPairs);
+    if (generated) {
+      int64_t R = 0, C = 0;
+      CodeGen::RowMember m{};
+      int kind = row_role(i, &R, &C, &m);
+      const int member_root = m.epi ? m.epi->result : (m.root ? m.root->result : -1);
+      if (!group.empty() && kind == 0 && op.type.numel() == gR && R * C == gR) {
+        kind = 1;  // a loop over the group's rows
+        m.kind = 1;
+        R = gR;
+        C = gC;
+      }
+      if (!row_groups) kind = -1;
+      const bool fits = kind >= 0 && R == gR && C == gC && !group.empty();
+      std::set<std::pair<int, int>> seen;
+      if (fits && pl.row_local(member_root, kind == 0 ? 0 : 1, member_root, inside, gR, gC, seen)) {
+        group.push_back({m, (int)i, v});
+        inside[v] = kind == 0 ? 0 : 1;
+        continue;
+      }
+      flush();
+      if (kind == 0 || kind == 2) {
+        if (R >= 1024 && C >= 32 && C <= 2048) {
+          gR = R;
+          gC = C;
+          group.push_back({m, (int)i, v});
+          inside[v] = kind == 0 ? 0 : 1;
+          continue;
+        }
+      }
+      emit_single(i);
+      continue;
+    }
+    flush();
     Step st;
     st.root = v;
     st.elements = op.type.numel();
@@ -976,20 +1168,12 @@ Plan plan_function(const Function& f, Precision prec) {
       st.gemm.N = n;
       st.gemm.K = op.axis;  // 1: descending
       st.bytes_moved = 16 * f.value_types[op.operands[0]].numel();
-    } else if (op.kind == OpKind::Reduce) {
-      st.kind = StepKind::Reduce;
-      cg.gen_reduce(op, &st);
-    } else if (pl.epilogue_of.count(v)) {
-      st.kind = StepKind::Reduce;
-      cg.gen_reduce(f.ops[f.producer[pl.epilogue_of[v]]], &st, &op);
-    } else {
-      st.kind = StepKind::Loop;
-      cg.gen_loop(op, &st);
     }
     step_of_value[v] = (int)plan.steps.size();
     plan.materialized.push_back(v);
     plan.steps.push_back(std::move(st));
   }
+  flush();
   plan.source = cg.source();
   plan.snippets = cg.snippets();
   plan.prelude = CodeGen::prelude();
@@ -1015,11 +1199,14 @@ Plan plan_function(const Function& f, Precision prec) {
   for (int s = 0; s < (int)plan.steps.size(); ++s)
     for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], s);
   for (int s = 0; s < (int)plan.steps.size(); ++s) {
-    int v = plan.steps[s].root;
-    if (pl.returned[v]) continue;
-    int64_t bytes = f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype);
-    iv.push_back({bytes, s, std::max(s, last_use[v]), v, -1});
-    if (plan.steps[s].scratch_elems)
+    std::vector<int> written{plan.steps[s].root};
+    written.insert(written.end(), plan.steps[s].extra_roots.begin(), plan.steps[s].extra_roots.end());
+    for (int v : written) {
+      if (pl.returned[v]) continue;
+      int64_t bytes = f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype);
+      iv.push_back({bytes, s, std::max(s, last_use[v]), v, -1});
+    }
+    if (plan.steps[s].scratch_elems && !pl.returned[plan.steps[s].root])
       iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
   }
   for (int s = 0; s < (int)plan.steps.size(); ++s)

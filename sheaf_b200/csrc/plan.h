@@ -51,6 +51,7 @@ enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort };
 struct Step {
   StepKind kind = StepKind::Loop;
   int root = -1;                // value written by this step
+  std::vector<int> extra_roots; // further values written (row groups), kernel arguments after root
   std::vector<int> leaves;      // materialized values read (kernel argument order)
   std::string kernel;           // generated kernel name (Loop / Reduce)
   int64_t grid = 1, block = 256, grid_y = 1;

@@ -515,6 +515,7 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     args.clear();
     for (int l : st.leaves) args.push_back(ptr[l]);
     args.push_back(ptr[st.root]);
+    for (int e : st.extra_roots) args.push_back(ptr[e]);
     void* scratch = nullptr;
     if (st.splits > 1) {
       scratch = (char*)lf->arena + plan.scratch_offset[si];

@@ -258,7 +258,7 @@ def test_large_gemm_shapes_match_oracle(tf32_session):
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 2e-3
 
 
-@pytest.mark.parametrize("config", [None, 0, 1, 2, 3, 4])
+@pytest.mark.parametrize("config", [None, 0, 1, 2, 3, 4, 5])
 @pytest.mark.parametrize("shape", [(1000, 1100, 520, 1), (300, 512, 200, 1), (260, 512, 96, 3), (700, 64, 300, 1),
                                    (1000, 300, 800, 1), (520, 272, 1000, 2), (384, 384, 4096, 1),
                                    # row strides that are not a multiple of 4 floats (padded operand copies)
@@ -325,7 +325,7 @@ def test_gemm_configs_bit_identical(tf32_session, monkeypatch, shape, layout):
     name, text = module([sa, sb], body, [("%0", ty(M_, N_))])
     ins = [rnd(K_, M_) if at else rnd(M_, K_), rnd(N_, K_) if bt else rnd(K_, N_)]
     outs = []
-    for cfg in range(5):
+    for cfg in range(6):
         monkeypatch.setenv("SHEAF_B200_GEMM_CONFIG", str(cfg))
         tf32_session.load_stablehlo(text)
         outs.append(tf32_session.call(name, ins)[0])
