@@ -262,7 +262,7 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     from sheaf_b200 import build
     from sheaf_b200.programs import models as M
-    from sheaf_b200.session import B200Session, nccl_unique_id
+    from sheaf_b200.session import B200Session, library, nccl_unique_id
     build.build()
     low, inp, data_names, units, unit, scaling, cfg, vag = program(args, world, rank)
     nid = None
@@ -307,6 +307,8 @@ def run_ours(args):
     barrier()
     stream = torch.cuda.ExternalStream(sess.cuda_stream, device=torch.device("cuda", local))
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lib = library()
+    n_launch0 = lib.sb_kernel_launch_count()
     with Clocks(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
@@ -314,6 +316,9 @@ def run_ours(args):
                 o.release()
         ev1.record(stream)
         ev1.synchronize()
+    # kernels this library launched in the timed region (counted by every
+    # launch path of the library)
+    timed_launches = int(lib.sb_kernel_launch_count() - n_launch0)
     ms = ev0.elapsed_time(ev1)
     barrier()
     if dist:
@@ -360,7 +365,7 @@ def run_ours(args):
             e2e["loss"] = float(np.asarray(first))
 
     # per-kernel device time (separate pass of the same steps, CUDA events per launch)
-    roof, launches, breakdown = None, None, None
+    roof, breakdown = None, None
     if not args.no_profile:
         sess.set_profiling(True)
         for _ in range(args.steps):
@@ -376,9 +381,6 @@ def run_ours(args):
                     fh.write(f"{r['step']},{r['kind']},{r['kernel']},{r['calls']},{r['total_ms']:.6f},"
                              f"{r['elements']},{r['bytes']},{r['flops']}\n")
         calls = max(1, rows[0]["calls"]) if rows else 1
-        launches = sum(r["launches_per_call"] for r in rows if r["function"] == q)
-        if train:
-            launches += 2  # optimizer: gradient norm pass + fused clip/AdamW pass
         kinds = ("gemm", "attention", "loop", "reduce")
         tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in kinds}
         allms = sum(tot.values())
@@ -401,7 +403,7 @@ def run_ours(args):
               "warmup": args.warmup, "ms_per_step": ms_step, "steps_per_s": 1e3 / ms_step,
               "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
               "contraction": args.precision, "data": data, "config": cfg,
-              "clocks": clk.summary(), "e2e": e2e, "gpu_launches": (launches or 0) * args.steps,
+              "clocks": clk.summary(), "e2e": e2e, "gpu_launches": timed_launches,
               "roofline": roof, "breakdown": breakdown, "module_load_s": load_s}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

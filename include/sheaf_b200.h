@@ -234,6 +234,13 @@ SB_API sb_status* sb_module_kernel_source(const char* text, size_t length, const
 /* Library version string. */
 SB_API const char* sb_version(void);
 
+/* Number of CUDA kernels this library has launched in this process (all
+ * sessions and devices): generated loop / reduction kernels, tensor-core
+ * GEMMs and their split-K reductions and operand copies, attention, sort and
+ * optimizer kernels.  Diagnostics: the difference across a call is the
+ * number of kernels that call launched. */
+SB_API uint64_t sb_kernel_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

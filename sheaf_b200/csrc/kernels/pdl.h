@@ -6,9 +6,18 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <utility>
 
 namespace sb {
+
+// Kernel launches issued by this library in this process (every launch path
+// counts itself here; read by sb_kernel_launch_count).
+inline std::atomic<uint64_t>& launch_counter() {
+  static std::atomic<uint64_t> n{0};
+  return n;
+}
 
 __device__ __forceinline__ void pdl_prologue() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -31,6 +40,7 @@ cudaError_t launch_pdl(void (*kern)(K...), dim3 grid, dim3 block, size_t smem, c
   pdl_attribute(&at[0]);
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
 }
 

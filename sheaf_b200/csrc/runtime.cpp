@@ -22,6 +22,7 @@
 #include "ir.h"
 #include "jit.h"
 #include "kernels/kernels.h"
+#include "kernels/pdl.h"
 #include "nccl_dl.h"
 #include "plan.h"
 
@@ -367,6 +368,7 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   SB_CUDA(cudaLaunchKernelExC(&cfg, (const void*)k, args));
   return nullptr;
 }
@@ -570,6 +572,8 @@ sb_status_code sb_status_code_of(const sb_status* s) { return s ? s->code : SB_S
 const char* sb_status_message(const sb_status* s) { return s ? s->message.c_str() : "OK"; }
 void sb_status_free(sb_status* s) { delete s; }
 const char* sb_version(void) { return "sheaf_b200 0.1 (sm_100a)"; }
+
+uint64_t sb_kernel_launch_count(void) { return sb::launch_counter().load(std::memory_order_relaxed); }
 
 void sb_session_options_initialize(sb_session_options* o) {
   std::memset(o, 0, sizeof *o);

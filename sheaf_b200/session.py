@@ -102,6 +102,7 @@ SIGNATURES = {
     "sb_module_plan_steps": (_P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_int32,
                                   ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     "sb_version": (ctypes.c_char_p, []),
+    "sb_kernel_launch_count": (ctypes.c_uint64, []),
 }
 
 _lib = None
