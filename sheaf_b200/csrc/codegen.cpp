@@ -5,6 +5,8 @@
 // (node, coordinates) so a node shared inside one cluster is computed once.
 #include "codegen.h"
 
+#include <functional>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -1139,9 +1141,34 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   c.vec = true;
   c.indent = 2;
   std::vector<int> outs;
-  std::ostringstream rows;
+  std::ostringstream rows;  // before the row loop: lane columns, column accumulators
   for (int j = 0; j < J; ++j)
-    rows << "    const " << c.idx << " cL" << j << " = (lane + " << 32 * j << ") * 4;\n";
+    rows << "  const " << c.idx << " cL" << j << " = (lane + " << 32 * j << ") * 4;\n";
+  // column reductions (kind 3): output index, reduce op, accumulator names
+  struct ColRed {
+    int out;
+    const Op* op;
+    std::vector<std::string> acc;  // J x 4, chunk-major
+    std::string init_code, init_val;
+  };
+  std::vector<ColRed> cols;
+  auto body_op = [](const Op& r) {
+    return std::function<std::string(const std::string&, const std::string&)>(
+        [&r](const std::string& a, const std::string& b) {
+          switch (r.body) {
+            case ReduceBody::Add: return a + " + " + b;
+            case ReduceBody::Max: return "fmaxf(" + a + ", " + b + ")";
+            case ReduceBody::Min: return "fminf(" + a + ", " + b + ")";
+            case ReduceBody::Mul: return a + " * " + b;
+          }
+          return a;
+        });
+  };
+  auto ident_of = [](const Op& r) {
+    return std::string(r.body == ReduceBody::Add ? "0.f"
+                       : r.body == ReduceBody::Max ? "__int_as_float(0xff800000)"
+                       : r.body == ReduceBody::Min ? "__int_as_float(0x7f800000)" : "1.f");
+  };
   // coordinates of a shape whose leading dims hold the row index `row`
   // (innermost dim excluded when `full`); declared once per row shape, so
   // members of the same shape share loads and subexpressions
@@ -1212,6 +1239,47 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
         c.body << "    if (lane == 0) " << W << "[row] = " << v.name << ";\n";
         c.regs[std::to_string(out_v) + "@row"] = v;
         c.reg_kind[out_v] = 1;
+      } else if (m.kind == 3) {
+        // reduction over all rows: each lane accumulates its columns over the
+        // rows its warp visits; the block and the finish kernel combine the
+        // lanes' partials in a fixed order after the row loop
+        const Type& in = f_.value_types[root.operands[0]];
+        const auto& ish = in.shape;
+        const int r = (int)ish.size();
+        if (r < 2 || ish.back() != C || in.numel() != R * C || root.type.numel() != C ||
+            root.type.dtype != DType::F32 || in.dtype != DType::F32 || (int)root.dims.size() != r - 1)
+          return false;
+        for (int d = 0; d + 1 < r; ++d)
+          if (root.dims[d] != d) return false;
+        auto combine = body_op(root);
+        std::vector<std::string> co = row_coords(ish, true, tag);
+        c.root = root.result;
+        ColRed cr;
+        cr.out = (int)outs.size() - 1;
+        cr.op = &root;
+        for (int j = 0; j < J; ++j)
+          for (int k = 0; k < 4; ++k) {
+            co.back() = lane_coord("cL" + std::to_string(j), k);
+            const std::string v = eval(c, root.operands[0], co).name;
+            const std::string a = "ca" + std::to_string(cols.size()) + "_" + std::to_string(4 * j + k);
+            c.body << "    " << a << " = " << combine(a, v) << ";\n";
+            cr.acc.push_back(a);
+            rows << "  float " << a << " = " << ident_of(root) << ";\n";
+          }
+        const bool saved_vec = c.vec;
+        c.vec = false;
+        const std::string saved_body = c.body.str();
+        c.body.str("");
+        c.body.clear();
+        auto saved_memo = std::move(c.memo);
+        c.memo.assign(1, {});
+        cr.init_val = eval(c, root.operands[1], {}).name;
+        cr.init_code = c.body.str();
+        c.memo = std::move(saved_memo);
+        c.body.str(saved_body);
+        c.body.seekp(0, std::ios_base::end);
+        c.vec = saved_vec;
+        cols.push_back(cr);
       } else {
         const Type& in = f_.value_types[root.operands[0]];
         const auto& ish = in.shape;
@@ -1277,20 +1345,77 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
     ~Snip() { g->snippets_.push_back(g->src_.str().substr(start)); }
   } snip{this, start_text.size()};
   std::string name = "k" + std::to_string(names_.size());
-  src_ << header(name, c, (int)outs.size() - 1);
+  // with column reductions the grid is one full wave (8 blocks per SM), so
+  // the per-block partials stay few while every warp slot is used
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, cols.empty() ? kMaxGrid : 148 * 8));
+  const size_t np = c.leaves.size() + outs.size();
+  src_ << header(name, c, (int)outs.size() - 1 + (cols.empty() ? 0 : 1));
   for (size_t j = 0; j < outs.size(); ++j)
     src_ << "  float* __restrict__ O" << j << " = (float*)a.p[" << c.leaves.size() + j << "];\n";
   src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+  src_ << rows.str();
   src_ << "  for (" << c.idx << " row = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; row < " << R
        << "; row += (" << c.idx << ")gridDim.x * " << kThreads / 32 << ") {\n";
-  src_ << rows.str() << c.body.str() << "  }\n}\n\n";
+  src_ << c.body.str() << "  }\n";
+  if (!cols.empty()) {
+    // per block: the 8 warps' lane partials, combined in warp order
+    src_ << "  float* __restrict__ S = (float*)a.p[" << np << "];\n";
+    src_ << "  __shared__ float cs_[" << kThreads / 32 << "][" << C << "];\n";
+    for (size_t q = 0; q < cols.size(); ++q) {
+      auto combine = body_op(*cols[q].op);
+      for (int j = 0; j < J; ++j)
+        for (int k = 0; k < 4; ++k)
+          src_ << "  cs_[warp][cL" << j << " + " << k << "] = " << cols[q].acc[4 * j + k] << ";\n";
+      src_ << "  __syncthreads();\n";
+      src_ << "  for (int c_ = threadIdx.x; c_ < " << C << "; c_ += " << kThreads << ") {\n";
+      src_ << "    float v_ = cs_[0][c_];\n";
+      src_ << "    for (int w_ = 1; w_ < " << kThreads / 32 << "; ++w_) v_ = " << combine("v_", "cs_[w_][c_]") << ";\n";
+      src_ << "    S[" << q * grid * C << " + (" << c.idx << ")blockIdx.x * " << C << " + c_] = v_;\n  }\n";
+      src_ << "  __syncthreads();\n";
+    }
+  }
+  src_ << "}\n\n";
   names_.push_back(name);
   st->kernel = name;
   st->leaves = c.leaves;
   st->root = outs[0];
   st->extra_roots.assign(outs.begin() + 1, outs.end());
   st->block = kThreads;
-  st->grid = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, kMaxGrid));
+  st->grid = grid;
+  if (!cols.empty()) {
+    // finish: 8 columns x 32 block lanes per block, a fixed tree over the lanes
+    const std::string fin = name + "f";
+    src_ << "struct __align__(8) A_" << fin << " { const void* p[" << np + 1 << "]; };\n";
+    src_ << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << fin << "(const A_" << fin
+         << " a) {\n" << kPdlPrologue;
+    for (size_t i = 0; i < c.leaves.size(); ++i) {
+      const Type& t = f_.value_types[c.leaves[i]];
+      src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+           << "*)a.p[" << i << "];\n";
+    }
+    src_ << "  const float* __restrict__ S = (const float*)a.p[" << np << "];\n";
+    src_ << "  __shared__ float part_[32][8];\n";
+    src_ << "  const int cx = threadIdx.x & 7, ry = threadIdx.x >> 3;\n";
+    src_ << "  const int col = blockIdx.x * 8 + cx;\n";
+    for (size_t q = 0; q < cols.size(); ++q) {
+      auto combine = body_op(*cols[q].op);
+      src_ << "  {\n    float v_ = " << ident_of(*cols[q].op) << ";\n";
+      src_ << "    if (col < " << C << ")\n#pragma unroll 4\n      for (int b_ = ry; b_ < " << grid << "; b_ += 32) v_ = "
+           << combine("v_", "S[" + std::to_string(q * grid * C) + " + b_ * " + std::to_string(C) + " + col]") << ";\n";
+      src_ << "    part_[ry][cx] = v_;\n    __syncthreads();\n";
+      src_ << "    for (int w_ = 16; w_ > 0; w_ >>= 1) {\n      if (ry < w_) part_[ry][cx] = "
+           << combine("part_[ry][cx]", "part_[ry + w_][cx]") << ";\n      __syncthreads();\n    }\n";
+      src_ << "    if (ry == 0 && col < " << C << ") {\n" << cols[q].init_code << "      ((float*)a.p["
+           << c.leaves.size() + cols[q].out << "])[col] = " << store(*cols[q].op, combine("part_[0][cx]", cols[q].init_val))
+           << ";\n    }\n    __syncthreads();\n  }\n";
+    }
+    src_ << "}\n\n";
+    names_.push_back(fin);
+    st->finish_kernel = fin;
+    st->finish_grid = (C + 7) / 8;
+    st->splits = grid;
+    st->scratch_elems = (int64_t)cols.size() * grid * C;
+  }
   st->elements = R * C;
   int64_t bytes = 0;
   for (int o : outs) bytes += f_.value_types[o].numel() * 4;

@@ -203,6 +203,13 @@ struct Planner {
         return true;
       case OpKind::Reduce: {
         const auto& is = f.value_types[op->operands[0]].shape;
+        bool colred = n == member && is.size() >= 2 && op->dims.size() == is.size() - 1 && is.back() == C &&
+                      f.value_types[op->operands[0]].numel() == R * C;
+        for (size_t d = 0; colred && d + 1 < is.size(); ++d) colred = op->dims[d] == (int64_t)d;
+        if (colred) {
+          if (!row_local(op->operands[0], 0, member, inside, R, C, seen)) return false;
+          return row_local(op->operands[1], 2, member, inside, R, C, seen);
+        }
         const bool rowred = cls == 1 && op->dims.size() == 1 && !is.empty() && op->dims[0] == (int64_t)is.size() - 1 &&
                             is.back() == C && f.value_types[n].numel() == R;
         if (!row_local(op->operands[0], rowred ? 0 : 2, member, inside, R, C, seen)) return false;
@@ -1065,6 +1072,16 @@ Plan plan_function(const Function& f, Precision prec) {
     else if (pl.epilogue_of.count(v)) red = &f.ops[f.producer[pl.epilogue_of[v]]];
     if (red) {
       const auto& is = f.value_types[red->operands[0]].shape;
+      // column reduction over every dim but the innermost
+      bool col = red == &op && is.size() >= 2 && red->dims.size() == is.size() - 1 &&
+                 f.value_types[red->operands[0]].dtype == DType::F32;
+      for (size_t d = 0; col && d + 1 < is.size(); ++d) col = red->dims[d] == (int64_t)d;
+      if (col) {
+        *C = is.back();
+        *R = f.value_types[red->operands[0]].numel() / std::max<int64_t>(*C, 1);
+        *m = {3, red, nullptr};
+        return 3;
+      }
       if (red->dims.size() != 1 || is.empty() || red->dims[0] != (int64_t)is.size() - 1 ||
           f.value_types[red->operands[0]].dtype != DType::F32)
         return -1;
@@ -1099,18 +1116,21 @@ Plan plan_function(const Function& f, Precision prec) {
       if (!row_groups) kind = -1;
       const bool fits = kind >= 0 && R == gR && C == gC && !group.empty();
       std::set<std::pair<int, int>> seen;
-      if (fits && pl.row_local(member_root, kind == 0 ? 0 : 1, member_root, inside, gR, gC, seen)) {
+      // class of the member's output inside the group: 0 per element, 1 per
+      // row, 2 not readable by later members (a column reduction)
+      const int cls = kind == 0 ? 0 : kind == 3 ? 2 : 1;
+      if (fits && pl.row_local(member_root, cls, member_root, inside, gR, gC, seen)) {
         group.push_back({m, (int)i, v});
-        inside[v] = kind == 0 ? 0 : 1;
+        inside[v] = cls;
         continue;
       }
       flush();
-      if (kind == 0 || kind == 2) {
+      if (kind == 0 || kind == 2 || kind == 3) {
         if (R >= 1024 && C >= 32 && C <= 2048) {
           gR = R;
           gC = C;
           group.push_back({m, (int)i, v});
-          inside[v] = kind == 0 ? 0 : 1;
+          inside[v] = cls;
           continue;
         }
       }
