@@ -339,17 +339,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     load_tile(sK, &mK, bar_kv, BN, 0, h, b);
     load_tile(sV, &mV, bar_kv, BN, 0, h, b);
   }
-  // D = rowsum(dY * Y), L: this thread's row
+  // D = rowsum(dY * Y) of this thread's row: computed in the first iteration,
+  // while the first S / dP MMAs run
   float D = 0.f;
-  {
-    const float* yr = p.y + b * p.y_sb + h * p.y_sh + row * p.y_st;
-    const float* dr = p.dy + b * p.dy_sb + h * p.dy_sh + row * p.dy_st;
-#pragma unroll 4
-    for (int c = 0; c < HD; c += 4) {
-      const float4 a = *(const float4*)(yr + c), g = *(const float4*)(dr + c);
-      D += a.x * g.x + a.y * g.y + a.z * g.z + a.w * g.w;
-    }
-  }
   const float L2 = p.lse[b * p.l_sb + h * p.l_sh + row * p.l_st];
   const float scale2 = p.scale * kLog2e;
   const uint32_t id_s = idesc_tf32(BM, BN, 0, 0), id_q = idesc_tf32(BM, HD, 0, 1);
@@ -363,6 +355,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         issue_mma_k64(tmem, smem_u32(sQ), BM, smem_u32(sK), BN, false, id_s, false);
         issue_mma_k64(tmem + 64, smem_u32(sDO), BM, smem_u32(sV), BN, false, id_s, false);
         mma_commit(bar_s);
+      }
+    }
+    if (j == 0) {
+      const float* yr = p.y + b * p.y_sb + h * p.y_sh + row * p.y_st;
+      const float* dr = p.dy + b * p.dy_sb + h * p.dy_sh + row * p.dy_st;
+#pragma unroll 4
+      for (int c = 0; c < HD; c += 4) {
+        const float4 a = *(const float4*)(yr + c), g = *(const float4*)(dr + c);
+        D += a.x * g.x + a.y * g.y + a.z * g.z + a.w * g.w;
       }
     }
     mbar_wait(bar_s, ph, abort_flag, err, 23);
