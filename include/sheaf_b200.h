@@ -195,8 +195,8 @@ SB_API sb_status* sb_optimizer_adamw_step(sb_session* session, size_t leaf_count
 
 /* --- allocation-free GEMM --------------------------------------------------- *
  * No counterpart in the reference.  For callers that must not allocate device
- * memory: work recorded in a CUDA stream capture, code running under another
- * framework's memory manager, or latency paths that may not touch the
+ * memory: code running under another framework's memory manager, which owns
+ * every device byte, or latency-critical paths that may not touch the CUDA
  * allocator.  Computes C = A @ B for row-major f32 device matrices A (m x k),
  * B (k x n), C (m x n) on the current device with the CUDA-core GEMM, enqueued
  * on `cuda_stream` (NULL = default stream); it allocates nothing.  When the

@@ -1,9 +1,8 @@
 // Split-K f32 GEMM for callers that cannot allocate device memory.
 //
 // Who needs it: code that runs where cudaMalloc is unavailable or forbidden --
-// work recorded inside a CUDA stream capture (allocation calls break the
-// capture), host code inside another framework's memory manager that owns every
-// device byte, or real-time paths that must not hit the allocator.  Such a
+// host code inside another framework's memory manager that owns every device
+// byte, or real-time paths that must not hit the allocator.  Such a
 // caller still owns A, B and C; the only extra memory the split-K GEMM needs,
 // the partial products of the K slices, lives in a fixed static device array of
 // this library instead of a workspace the caller would have to allocate.

@@ -354,3 +354,18 @@ def test_returned_parameter_and_duplicate_outputs(fp32_session):
         "%1 = stablehlo.exponential %arg0 : tensor<3xf32>"],
         [("%arg0", "tensor<3xf32>"), ("%1", "tensor<3xf32>"), ("%1", "tensor<3xf32>"), ("%0", "tensor<2x2xf32>")])
     check(fp32_session, name, text, [rnd(3)])
+
+
+def test_merged_sibling_projections(fp32_session):
+    """The q/k/v projections merged into one GEMM give the three products."""
+    from test_abi import QKV
+    check(fp32_session, "qkv.f", QKV, [rnd(8, 128, 64), rnd(192, 64)], rtol=1e-4, atol=1e-4)
+
+
+def test_row_group_with_column_reduction(fp32_session):
+    """Row group with a column-reduction member (per-block partials, finish
+    kernel) against the oracle, twice (the partials buffer is reused)."""
+    from test_abi import LN_BWD_COLS
+    for _ in range(2):
+        ins = [rnd(16, 128, 128), rnd(16, 128, 128)]
+        check(fp32_session, "lnc.f", LN_BWD_COLS, ins, rtol=1e-4, atol=1e-4)

@@ -1,7 +1,7 @@
 """The allocation-free split-K GEMM entry point against the session GEMM.
 
 `sb_gemm_f32_splitk_noalloc` serves callers that cannot allocate device memory
-(stream capture, memory owned by another framework): its split-K partial
+(memory owned by another framework, allocator-free paths): its split-K partial
 products live in a static device array instead of a workspace.  Here it is
 called through the C ABI on device buffers owned by a session, twice in a row
 with different shapes (both split K, so the second call reuses the array the
