@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-profile", action="store_true")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="data parallel: one all-reduce after the backward instead of buckets during it")
     return p.parse_args()
 
 
@@ -271,7 +273,7 @@ def run_ours(args):
         dist.broadcast_object_list(obj, src=0)
         nid = obj[0]
     sess = B200Session(device=local, precision=args.precision, rank=rank, world_size=world, nccl_id=nid,
-                       timeout_ms=300000)
+                       timeout_ms=300000, overlap_allreduce=not args.no_overlap)
     t0 = time.time()
     sess.load_stablehlo(low.text)
     load_s = time.time() - t0

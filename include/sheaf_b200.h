@@ -80,6 +80,11 @@ typedef struct sb_session_options {
 /* TF32: keep the attention region on the generic fused-loop + GEMM path instead
  * of the fused tcgen05 attention kernels (for A/B parity checks). */
 #define SB_SESSION_FLAG_NO_ATTENTION_FUSION 2u
+/* Data parallel (world_size > 1): all-reduce the reduced outputs (the
+ * gradients) in buckets on a second stream as soon as the backward has
+ * written them, overlapping the rest of the backward; without it one grouped
+ * all-reduce runs after the last step. */
+#define SB_SESSION_FLAG_OVERLAP_ALLREDUCE 4u
 
 typedef struct sb_allocator_stats {
   /* field meaning follows iree_hal_allocator_statistics_t as read by

@@ -71,6 +71,10 @@ uint32_t dtype_to_etype(DType t) {
 struct Device {
   int ordinal = 0;
   cudaStream_t stream = nullptr;
+  // data parallel with SB_SESSION_FLAG_OVERLAP_ALLREDUCE: gradient buckets are
+  // all-reduced on comm_stream while the backward continues on `stream`
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ready = nullptr, reduced = nullptr;
   std::atomic<uint64_t> allocated{0}, freed{0}, live{0}, peak{0};
   void note_alloc(size_t n) {
     allocated += n;
@@ -83,6 +87,13 @@ struct Device {
     live -= n;
   }
   ~Device() {
+    if (comm_stream) {
+      cudaSetDevice(ordinal);
+      cudaStreamSynchronize(comm_stream);
+      cudaStreamDestroy(comm_stream);
+      cudaEventDestroy(ready);
+      cudaEventDestroy(reduced);
+    }
     if (stream) {
       cudaSetDevice(ordinal);
       cudaStreamSynchronize(stream);
@@ -420,8 +431,71 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     if (e != cudaSuccess) { cleanup(); return cuda_status(e, "round_tf32_copy"); }
     rounded[v] = dst;
   }
+  // Data parallel, overlapped: each reduced output is all-reduced on the comm
+  // stream once the step that writes it and every step that reads it have
+  // been enqueued, in buckets of >= 8 MB (configurable), while later steps run
+  // on `stream`.
+  // Every rank has the same plan, so every rank issues the same buckets.
+  const bool overlap = s->opts.world_size > 1 && reduce && s->dev->comm_stream;
+  std::vector<std::vector<int>> ready_at(plan.steps.size());
+  std::vector<int> bucket;
+  size_t bucket_bytes = 0;
+  // SHEAF_B200_ALLREDUCE_BUCKET_BYTES overrides the bucket size (tests use
+  // small buckets to exercise many of them)
+  size_t bucket_limit = 8u << 20;
+  if (const char* bb = std::getenv("SHEAF_B200_ALLREDUCE_BUCKET_BYTES"))
+    if (std::atoll(bb) > 0) bucket_limit = (size_t)std::atoll(bb);
+  bool comm_used = false;
+  if (overlap) {
+    std::vector<int> last(f.num_values(), -1);
+    for (int si = 0; si < (int)plan.steps.size(); ++si)
+      for (int l : plan.steps[si].leaves) last[l] = si;
+    std::vector<int> times(f.num_values(), 0);
+    for (int v : f.returns) ++times[v];
+    for (size_t j = 0; j < f.returns.size(); ++j) {
+      if (reduce[j] == SB_REDUCE_NONE) continue;
+      if (outs[j]->type.dtype != DType::F32) { cleanup(); return make_status(SB_STATUS_UNIMPLEMENTED, "reduce of non-f32 output"); }
+      const int v = f.returns[j];
+      // outputs copied after the steps, and values returned more than once
+      // (their copies read the first buffer), go to the last bucket
+      if (plan.output_step[j] < 0 || times[v] > 1) continue;
+      ready_at[std::max(plan.output_step[j], last[v])].push_back((int)j);
+    }
+  }
+  auto flush_bucket = [&]() -> sb_status* {
+    if (bucket.empty()) return nullptr;
+    const NcclApi& api = nccl_api();
+    if (!s->nccl.comm) return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available");
+    SB_CUDA(cudaEventRecord(s->dev->ready, stream));
+    SB_CUDA(cudaStreamWaitEvent(s->dev->comm_stream, s->dev->ready, 0));
+    api.group_start();
+    for (int j : bucket) {
+      ncclRedOp_t op = reduce[j] == SB_REDUCE_MEAN ? ncclAvg : ncclSum;
+      ncclResult_t r = api.all_reduce(outs[j]->ptr, outs[j]->ptr, (size_t)outs[j]->type.numel(), ncclFloat32, op,
+                                      s->nccl.comm, s->dev->comm_stream);
+      if (r != ncclSuccess && r != ncclInProgress) {
+        api.group_end();
+        return make_status(SB_STATUS_INTERNAL, std::string("ncclAllReduce: ") + api.error_string(r));
+      }
+    }
+    ncclResult_t r = api.group_end();
+    if (r != ncclSuccess && r != ncclInProgress)
+      return make_status(SB_STATUS_INTERNAL, std::string("ncclGroupEnd: ") + api.error_string(r));
+    bucket.clear();
+    bucket_bytes = 0;
+    comm_used = true;
+    return nccl_settle(s);
+  };
   std::vector<const void*> args;
   for (size_t si = 0; si < plan.steps.size(); ++si) {
+    if (overlap && si > 0) {
+      for (int j : ready_at[si - 1]) {
+        bucket.push_back(j);
+        bucket_bytes += outs[j]->bytes;
+      }
+      if (bucket_bytes >= bucket_limit)
+        if (sb_status* e = flush_bucket()) { cleanup(); return e; }
+    }
     const Step& st = plan.steps[si];
     if (!ptr[st.root] && st.elements) { cleanup(); return make_status(SB_STATUS_INTERNAL, "unplaced value"); }
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
@@ -538,7 +612,22 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       SB_CUDA(cudaMemcpyAsync(outs[j]->ptr, ptr[v], outs[j]->bytes, cudaMemcpyDeviceToDevice, stream));
   }
   // data-parallel combine of outputs
-  if (s->opts.world_size > 1 && reduce) {
+  if (overlap) {
+    // the outputs of the last step and those copied above, then `stream`
+    // waits for every bucket
+    if (!plan.steps.empty())
+      for (int j : ready_at.back()) bucket.push_back(j);
+    std::vector<char> queued(f.returns.size(), 0);
+    for (auto& r : ready_at)
+      for (int j : r) queued[j] = 1;
+    for (size_t j = 0; j < f.returns.size(); ++j)
+      if (reduce[j] != SB_REDUCE_NONE && !queued[j]) bucket.push_back((int)j);
+    if (sb_status* e = flush_bucket()) { cleanup(); return e; }
+    if (comm_used) {
+      SB_CUDA(cudaEventRecord(s->dev->reduced, s->dev->comm_stream));
+      SB_CUDA(cudaStreamWaitEvent(stream, s->dev->reduced, 0));
+    }
+  } else if (s->opts.world_size > 1 && reduce) {
     if (!s->nccl.comm) { cleanup(); return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available"); }
     const NcclApi& api = nccl_api();
     api.group_start();
@@ -610,6 +699,11 @@ sb_status* sb_session_create(const sb_session_options* o, sb_session** out) {
   s->dev->ordinal = o->device_ordinal;
   SB_CUDA(cudaSetDevice(o->device_ordinal));
   SB_CUDA(cudaStreamCreateWithFlags(&s->dev->stream, cudaStreamNonBlocking));
+  if (o->world_size > 1 && (o->flags & SB_SESSION_FLAG_OVERLAP_ALLREDUCE)) {
+    SB_CUDA(cudaStreamCreateWithFlags(&s->dev->comm_stream, cudaStreamNonBlocking));
+    SB_CUDA(cudaEventCreateWithFlags(&s->dev->ready, cudaEventDisableTiming));
+    SB_CUDA(cudaEventCreateWithFlags(&s->dev->reduced, cudaEventDisableTiming));
+  }
   if (o->world_size > 1) {
     const NcclApi& api = nccl_api();
     if (!api.ok) return make_status(SB_STATUS_UNAVAILABLE, api.error);

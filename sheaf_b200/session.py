@@ -233,6 +233,7 @@ class DeviceBuffer:
 
 
 FLAG_NO_ATTENTION_FUSION = 2  # SB_SESSION_FLAG_NO_ATTENTION_FUSION
+FLAG_OVERLAP_ALLREDUCE = 4  # SB_SESSION_FLAG_OVERLAP_ALLREDUCE
 
 
 class B200Session:
@@ -241,12 +242,14 @@ class B200Session:
 
     def __init__(self, device: int = 0, precision: str = "tf32", rank: int = 0, world_size: int = 1,
                  nccl_id: Optional[bytes] = None, timeout_ms: int = 600000, cache_dir: Optional[str] = None,
-                 fuse_attention: bool = True):
+                 fuse_attention: bool = True, overlap_allreduce: bool = False):
         lib = library()
         o = _Options()
         lib.sb_session_options_initialize(ctypes.byref(o))
         if not fuse_attention:
             o.flags |= FLAG_NO_ATTENTION_FUSION
+        if overlap_allreduce:
+            o.flags |= FLAG_OVERLAP_ALLREDUCE
         o.device_ordinal = device
         o.precision = PRECISIONS[precision]
         o.rank = rank

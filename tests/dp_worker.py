@@ -4,6 +4,8 @@ Each rank runs the GPT value-and-grad on its half of the batch through a
 world-size-2 session; the session all-reduces (mean) the loss and every
 gradient with NCCL.  Rank 0 compares the result with a single-GPU session on the
 full batch and writes the max relative error to the file given as argv[1].
+With argv[2] == "overlap" the gradients are all-reduced in buckets on a second
+stream while the backward runs (SB_SESSION_FLAG_OVERLAP_ALLREDUCE).
 """
 import datetime
 import json
@@ -30,8 +32,9 @@ def main():
     inp = M.gpt_inputs(c, seed=3)
     obj = [nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
+    overlap = len(sys.argv) > 2 and sys.argv[2] == "overlap"
     sess = B200Session(device=local, precision="fp32", rank=rank, world_size=world, nccl_id=obj[0],
-                       timeout_ms=60000)
+                       timeout_ms=60000, overlap_allreduce=overlap)
     low = M.gpt_vag(c, batch=b)
     sess.load_stablehlo(low.text)
     ins = [inp[n][rank * b:(rank + 1) * b] if n in ("x", "y") else inp[n] for n in low.arg_names]
