@@ -141,6 +141,7 @@ struct LoadedFunction {
   Plan plan;
   std::vector<double> prof_ms;
   std::vector<uint64_t> prof_n;
+  std::vector<uint64_t> prof_launches;  // kernels launched by the step (last profiled call)
   std::vector<cudaKernel_t> kern, fin;
   std::map<int, void*> const_ptr;
   void* arena = nullptr;
@@ -179,6 +180,7 @@ struct sb_session {
     sb::LoadedFunction* fn;
     int step;
     cudaEvent_t a, b;
+    uint64_t launches;  // the launch counter at the step's start, then the step's launches
   };
   std::vector<Pending> pending;
   std::vector<cudaEvent_t> free_events;
@@ -503,13 +505,19 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       ev_a = s->event();
       ev_b = s->event();
       cudaEventRecord(ev_a, stream);
-      s->pending.push_back({lf, (int)si, ev_a, ev_b});
+      s->pending.push_back({lf, (int)si, ev_a, ev_b, launch_counter().load()});
     }
     struct EndEvent {
       cudaEvent_t e;
       cudaStream_t s;
-      ~EndEvent() { if (e) cudaEventRecord(e, s); }
-    } end_event{ev_b, stream};
+      sb_session* ss;
+      ~EndEvent() {
+        if (!e) return;
+        cudaEventRecord(e, s);
+        auto& p = ss->pending.back();
+        p.launches = launch_counter().load() - p.launches;
+      }
+    } end_event{ev_b, stream, s};
     if (st.kind == StepKind::Gemm) {
       const GemmDesc& g = st.gemm;
       GemmArgs a;
@@ -788,9 +796,11 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
     if (lf->prof_ms.size() != lf->plan.steps.size()) {
       lf->prof_ms.assign(lf->plan.steps.size(), 0.0);
       lf->prof_n.assign(lf->plan.steps.size(), 0);
+      lf->prof_launches.assign(lf->plan.steps.size(), 0);
     }
     lf->prof_ms[p.step] += ms;
     lf->prof_n[p.step] += 1;
+    lf->prof_launches[p.step] = p.launches;
     s->free_events.push_back(p.a);
     s->free_events.push_back(p.b);
   }
@@ -807,7 +817,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
         if (!lf->prof_n[i]) continue;
         os << lf->qname << "," << i << "," << kinds[(int)st.kind] << ","
            << step_name(st) << "," << lf->prof_n[i] << "," << lf->prof_ms[i]
-           << "," << st.elements << "," << st.bytes_moved << "," << st.flops << "," << (st.splits > 1 ? 2 : 1)
+           << "," << st.elements << "," << st.bytes_moved << "," << st.flops << "," << lf->prof_launches[i]
            << "\n";
       }
       if (reset) {

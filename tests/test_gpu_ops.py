@@ -369,3 +369,27 @@ def test_row_group_with_column_reduction(fp32_session):
     for _ in range(2):
         ins = [rnd(16, 128, 128), rnd(16, 128, 128)]
         check(fp32_session, "lnc.f", LN_BWD_COLS, ins, rtol=1e-4, atol=1e-4)
+
+
+def test_profile_report_counts_every_launch(fp32_session):
+    """The per-step launch counts of the profile report add up to the kernels
+    the library's launch counter sees for the same call (fp32: no rounded
+    parameter copies outside the steps)."""
+    from sheaf_b200.programs import models as M
+    from sheaf_b200.session import library
+    c = M.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=128, vocab_size=65, batch=2)
+    low = M.gpt_vag(c)
+    inp = M.gpt_inputs(c, seed=1)
+    ins = [inp[n] for n in low.arg_names]
+    fp32_session.load_stablehlo(low.text)
+    fp32_session.call(low.qualified, ins)
+    lib = library()
+    n0 = lib.sb_kernel_launch_count()
+    fp32_session.call(low.qualified, ins)
+    per_call = lib.sb_kernel_launch_count() - n0
+    fp32_session.profile_report(reset=True)
+    fp32_session.set_profiling(True)
+    fp32_session.call(low.qualified, ins)
+    fp32_session.set_profiling(False)
+    rows = [r for r in fp32_session.profile_report() if r["function"] == low.qualified]
+    assert rows and sum(r["launches_per_call"] for r in rows) == per_call
