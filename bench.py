@@ -313,9 +313,13 @@ def run_ours(args):
     n_launch0 = lib.sb_kernel_launch_count()
     with Clocks(local) as clk:
         ev0.record(stream)
+        h0 = time.perf_counter()
         for _ in range(args.steps):
             for o in step(bufs):
                 o.release()
+        # host time to enqueue the steps: when it approaches the device time
+        # per step, the step is launch-bound on the host
+        host_ms = (time.perf_counter() - h0) * 1e3
         ev1.record(stream)
         ev1.synchronize()
     # kernels this library launched in the timed region (counted by every
@@ -406,7 +410,8 @@ def run_ours(args):
               "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
               "contraction": args.precision, "data": data, "config": cfg,
               "clocks": clk.summary(), "e2e": e2e, "gpu_launches": timed_launches,
-              "roofline": roof, "breakdown": breakdown, "module_load_s": load_s}
+              "roofline": roof, "breakdown": breakdown, "module_load_s": load_s,
+              "host_enqueue_ms_per_step": host_ms / args.steps}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             result["cpu_baseline"] = cpu_baseline(args)

@@ -211,7 +211,11 @@ SB_API sb_status* sb_optimizer_adamw_step(sb_session* session, size_t leaf_count
  * process exits).  Calls whose partials would exceed it return
  * SB_STATUS_RESOURCE_EXHAUSTED and launch nothing.  The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture.  All calls on a device share the array:
+ * call before any stream capture.  The address is kept for the life of the
+ * device's primary context: after a device reset in the same process this
+ * entry point must not be called again.  m is at most 65535 * 128 (one
+ * CUDA-core launch); larger m returns SB_STATUS_INVALID_ARGUMENT.  All calls
+ * on a device share the array:
  * calls that overlap on the GPU race on it, so serialize them.  Returns
  * SB_STATUS_OK, SB_STATUS_INVALID_ARGUMENT, SB_STATUS_RESOURCE_EXHAUSTED,
  * SB_STATUS_UNAVAILABLE (no device / array not reachable) or

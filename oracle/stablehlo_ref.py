@@ -241,6 +241,11 @@ def _parse_op(st: str) -> Op:
     raise NotImplementedError(f"oracle: unsupported op {kind}")
 
 
+# Optional operand transform of dot_general (tests use it to model reduced-
+# precision tensor-core operands); None in normal use.
+_DOT_HOOK = None
+
+
 def _wrap32(x):
     """Two's-complement wraparound of integers to 32 bits (StableHLO i32)."""
     x = np.asarray(x, dtype=np.int64)
@@ -264,8 +269,18 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
         if tuple(a.shape) != tuple(shape):
             raise ValueError(f"input {i}: shape {a.shape} != {shape}")
         env[f"%arg{i}"] = _as(a, dt, dtype)
-    for op in f.ops:
+    # last use of every value, so that dead intermediates are dropped (the VAG
+    # graphs hold thousands of values; keeping them all exhausts host memory)
+    last: Dict[str, int] = {}
+    for i, op in enumerate(f.ops):
+        for o in op.operands:
+            last[o] = i
+    keep = set(f.ret)
+    for oi, op in enumerate(f.ops):
         v = [env[o] for o in op.operands]
+        for o in set(op.operands):
+            if last.get(o) == oi and o not in keep:
+                del env[o]
         (oshape, odt), = op.out_types[:1]
         k = op.kind
         if k == "sort":
@@ -384,7 +399,10 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
             M = int(np.prod([a.shape[d] for d in lf]))
             N = int(np.prod([b.shape[d] for d in rf]))
             K = int(np.prod([a.shape[d] for d in lc]))
-            r = np.matmul(at.reshape(bshape + (M, K)), bt.reshape(bshape + (K, N)))
+            am, bm = at.reshape(bshape + (M, K)), bt.reshape(bshape + (K, N))
+            if _DOT_HOOK is not None:
+                am, bm = _DOT_HOOK(op, am, bm)
+            r = np.matmul(am, bm)
             r = r.reshape(oshape)
         elif k == "compare":
             a, b = v
@@ -417,7 +435,8 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
             raise NotImplementedError(k)
         r = np.asarray(r)
         if odt in ("f32", "bf16", "f64"):
-            r = r.astype(dtype)
+            # no copy when the type already matches (broadcast views stay views)
+            r = r.astype(dtype, copy=False)
         elif odt == "i32":
             r = _wrap32(r)
         if tuple(r.shape) != tuple(oshape):

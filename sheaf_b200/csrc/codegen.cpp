@@ -521,7 +521,9 @@ void CodeGen::gen_loop(const Op& root, Step* st) {
   } snip{this, start_text.size()};
   if (root.type.numel() == 0) {
     std::string name = "k" + std::to_string(names_.size());
-    src_ << "extern \"C\" __global__ void " << name << "(const void* p) {}\n\n";
+    // launched with programmatic dependent launch like every other kernel, so
+    // it waits for its predecessor too: a later kernel's wait then covers it
+    src_ << "extern \"C\" __global__ void " << name << "(const void* p) {\n" << kPdlPrologue << "}\n\n";
     names_.push_back(name);
     st->kernel = name;
     st->grid = 1;

@@ -11,14 +11,12 @@
 #include "pdl.h"
 
 namespace sb {
-namespace {
 
-struct Split {
-  int64_t splits = 1, k_chunk = 0;
-};
-
-Split choose_split(const GemmArgs& g, int64_t tile_m, int64_t tile_n, int64_t granule) {
-  Split s;
+// The CUDA-core GEMM's split-K rule: when the 128 x 128 output tiles of a
+// single GEMM cannot fill the GPU and K is long, K is cut into ranges of at
+// least 512 (multiples of `granule`) for about two waves of CTAs.
+static SimtSplit choose_split(const GemmArgs& g, int64_t tile_m, int64_t tile_n, int64_t granule) {
+  SimtSplit s;
   if (g.batch != 1 || g.K < 2048) return s;
   int64_t tiles = ((g.M + tile_m - 1) / tile_m) * ((g.N + tile_n - 1) / tile_n);
   if (tiles >= 120) return s;
@@ -32,6 +30,17 @@ Split choose_split(const GemmArgs& g, int64_t tile_m, int64_t tile_n, int64_t gr
   s.splits = (g.K + chunk - 1) / chunk;
   return s;
 }
+
+SimtSplit simt_split(int64_t M, int64_t N, int64_t K, int64_t batch) {
+  GemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.batch = batch;
+  return choose_split(g, 128, 128, 8);
+}
+
+namespace {
 
 // An operand whose unit-stride (inner) dimension is fine but whose row stride
 // or base address is not 16-byte aligned (e.g. a vocabulary of 65 as the
@@ -146,7 +155,7 @@ size_t gemm_workspace(const GemmArgs& g, int precision) {
     GemmArgs v;
     if (pad_plan(g, &pd, &v)) return pd.total;
   }
-  Split s = choose_split(g, 128, 128, 8);
+  SimtSplit s = choose_split(g, 128, 128, 8);
   return s.splits > 1 ? (size_t)(s.splits * g.M * g.N) * sizeof(float) : 0;
 }
 
@@ -253,7 +262,7 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
       }
     }
   }
-  Split s = choose_split(g, 128, 128, 8);
+  SimtSplit s = choose_split(g, 128, 128, 8);
   const bool split = s.splits > 1 && ws && ws_bytes >= (size_t)(s.splits * g.M * g.N) * sizeof(float);
   cudaError_t e = gemm_simt(split ? split_args(g, s.splits, s.k_chunk, ws) : g, stream);
   if (e != cudaSuccess || !split) return e;

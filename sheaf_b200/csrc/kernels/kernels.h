@@ -27,6 +27,15 @@ struct GemmArgs {
 cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64_t M, int64_t N, int64_t ldc,
                           int round_tf32, cudaStream_t stream);
 
+// Split-K rule of the CUDA-core GEMM (shared by the session path and the
+// allocation-free entry point, so both compute identical partial sums).
+struct SimtSplit {
+  int64_t splits = 1, k_chunk = 0;
+};
+SimtSplit simt_split(int64_t M, int64_t N, int64_t K, int64_t batch);
+// Largest M the CUDA-core GEMM launches in one grid (65535 row tiles of 128).
+constexpr int64_t kSimtMaxM = 65535ll * 128;
+
 // Dispatch: precision 1 (TF32) tries the tcgen05 kernel, anything else or an
 // unsupported layout runs on CUDA cores; split-K through `ws` when the output
 // has few tiles.  *used_tc reports whether the tensor-core kernel ran.

@@ -31,7 +31,9 @@ std::mutex g_setup_mu;
 
 // Device address of the static array on `dev` (current device).  In host code
 // the symbol name is only a handle; the address comes from the runtime, once
-// per device.
+// per device, and stays valid while the device's primary context lives (a
+// host framework that resets the device must not call this entry point
+// afterwards in the same process).
 sb_status_code partials_on(int dev, float** out) {
   std::lock_guard<std::mutex> g(g_setup_mu);
   if (!g_partials_ptr[dev]) {
@@ -56,7 +58,8 @@ extern "C" SB_API sb_status_code sb_gemm_f32_splitk_noalloc(const float* a, cons
   if (m < 0 || n < 0 || k < 0) return SB_STATUS_INVALID_ARGUMENT;
   if (m == 0 || n == 0) return SB_STATUS_OK;
   if (!c || (k > 0 && (!a || !b))) return SB_STATUS_INVALID_ARGUMENT;
-  if (m > (1ll << 31) || n > (1ll << 31) || k > (1ll << 40)) return SB_STATUS_INVALID_ARGUMENT;
+  // one CUDA-core launch covers at most kSimtMaxM rows (65535 row tiles)
+  if (m > kSimtMaxM || n > (1ll << 31) || k > (1ll << 40)) return SB_STATUS_INVALID_ARGUMENT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
@@ -77,19 +80,9 @@ extern "C" SB_API sb_status_code sb_gemm_f32_splitk_noalloc(const float* a, cons
   g.sbb = 0; g.sbk = n; g.sbn = 1;   // B row-major k x n
   g.scb = m * n; g.scm = n; g.scn = 1;
 
-  // Split-K policy of the session's CUDA-core path: when the 128 x 128 output
-  // tiles cannot fill the GPU, slice K (multiples of 8, at least 512 each).
-  int64_t tiles = ((m + 127) / 128) * ((n + 127) / 128);
-  int64_t splits = 1, chunk = 0;
-  if (k >= 2048 && tiles < 120) {
-    int64_t want = (2 * 148 + tiles - 1) / tiles;
-    int64_t cap = k / 512;
-    int64_t s = want < cap ? want : cap;
-    if (s >= 2) {
-      chunk = ((k + s - 1) / s + 7) / 8 * 8;
-      splits = (k + chunk - 1) / chunk;
-    }
-  }
+  // the session's CUDA-core split-K rule, so both paths sum in the same order
+  const SimtSplit sp = simt_split(m, n, k, 1);
+  const int64_t splits = sp.splits, chunk = sp.k_chunk;
   cudaError_t e;
   if (splits > 1) {
     if (splits * m * n > (int64_t)SB_GEMM_SPLITK_NOALLOC_MAX_FLOATS) return SB_STATUS_RESOURCE_EXHAUSTED;
@@ -106,9 +99,7 @@ extern "C" SB_API sb_status_code sb_gemm_f32_splitk_noalloc(const float* a, cons
   } else {
     e = gemm_simt(g, stream);
   }
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return SB_STATUS_INTERNAL;
-  }
-  return SB_STATUS_OK;
+  // shapes are validated above, so a launch error here is the device's (it
+  // stays visible to the caller's own error checks)
+  return e == cudaSuccess ? SB_STATUS_OK : SB_STATUS_INTERNAL;
 }

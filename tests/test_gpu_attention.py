@@ -120,11 +120,9 @@ def _errs(outs, ref):
 
 
 def test_nanogpt_full_batch_fused_matches_fp32(tf32_session, fp32_session):
-    """Full nanoGPT batch (64 x 256), the oracle being too slow at this size:
-    the fused TF32 step and the unfused TF32 step of the same graph, both
-    against the exact-f32 step.  TF32 operand rounding alone puts the deepest
-    (layer 0) gradients near 2e-3 here, so the fused path is held to the 2e-3
-    bound or, if the unfused TF32 graph is already there, to within 10% of it:
+    """Full nanoGPT batch (64 x 256): the fused TF32 step and the unfused TF32
+    step of the same graph, both against the exact-f32 step, each within the
+    2e-3 tensor-core bound (loss relative, every gradient norm-relative):
     fusing attention must not cost accuracy."""
     from sheaf_b200.session import B200Session
     low = M.gpt_vag(M.NANOGPT)
@@ -141,4 +139,5 @@ def test_nanogpt_full_batch_fused_matches_fp32(tf32_session, fp32_session):
     finally:
         unfused_sess.close()
     ef, eu = _errs(fused, exact), _errs(unfused, exact)
-    assert max(ef) <= max(2e-3, 1.1 * max(eu)), (max(ef), max(eu))
+    assert max(ef) <= 2e-3, max(ef)
+    assert max(eu) <= 2e-3, max(eu)

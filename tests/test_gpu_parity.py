@@ -2,9 +2,9 @@
 value-and-grad graphs, checked against the CPU oracle.
 
 Tolerances: fp32 mode 1e-5 relative on the loss and 1e-4 max-relative on
-gradients (f32 re-association through deep graphs); tf32/bf16 tensor-core
-modes 2e-3 relative on the loss and 2e-3 norm-relative on gradients (the
-north-star bound for tensor-core contractions).
+gradients (f32 re-association through deep graphs); tf32 tensor-core
+mode 2e-3 relative on the loss and 2e-3 norm-relative on gradients (the
+stated bound for tensor-core contractions).
 """
 import json
 import os
@@ -82,7 +82,7 @@ def test_small_gpt_forward_fp32(fp32_session):
     np.testing.assert_allclose(outs[0], ref[0], rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("prec", ["tf32", "bf16"])
+@pytest.mark.parametrize("prec", ["tf32"])
 def test_nanogpt_dims_value_and_grad_tensor_cores(request, prec):
     """nanoGPT model dimensions (6 layers, D384, H6, T256, V65) at batch 4."""
     sess = request.getfixturevalue(f"{prec}_session")

@@ -30,9 +30,19 @@ def _noalloc(lib, sess, a, b, c, m, n, k):
                                           ctypes.c_void_p(sess.cuda_stream))
 
 
+def _device_free_bytes():
+    import torch
+    torch.cuda.synchronize(0)
+    return torch.cuda.mem_get_info(0)[0]
+
+
 @pytest.mark.parametrize("shapes", [[(256, 256, 16384), (200, 136, 4096)]])
 def test_noalloc_gemm_matches_session_gemm_on_two_calls(lib, fp32_session, shapes):
     rng = np.random.default_rng(7)
+    # everything the session allocates (reference results, operand buffers) is
+    # set up first, so that only the two allocation-free calls run between the
+    # two readings of the device's free memory
+    cases = []
     for call, (m, n, k) in enumerate(shapes):
         a_h = rng.standard_normal((m, k), dtype=np.float32)
         b_h = rng.standard_normal((k, n), dtype=np.float32)
@@ -41,7 +51,15 @@ def test_noalloc_gemm_matches_session_gemm_on_two_calls(lib, fp32_session, shape
         ref = fp32_session.call(f"{name}.f", [a_h, b_h])[0]
         a, b = fp32_session.buffer(a_h), fp32_session.buffer(b_h)
         c = fp32_session.buffer(np.full((m, n), np.nan, np.float32))
+        cases.append((m, n, k, a, b, c, ref))
+    fp32_session.synchronize()
+    free_before = _device_free_bytes()
+    for m, n, k, a, b, c, _ in cases:
         assert _noalloc(lib, fp32_session, a, b, c, m, n, k) == 0
+    fp32_session.synchronize()
+    # the calls took no device memory (the static array was there already)
+    assert _device_free_bytes() == free_before
+    for m, n, k, a, b, c, ref in cases:
         out = c.to_host()
         np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-5 * np.sqrt(k))
         # both entry points run the same CUDA-core split-K schedule
@@ -54,3 +72,5 @@ def test_noalloc_gemm_rejects_partials_beyond_the_static_array(lib, fp32_session
     a = fp32_session.buffer(np.zeros((m, 1), np.float32))  # never read: the call is rejected first
     assert _noalloc(lib, fp32_session, a, a, a, m, n, k) == 8  # SB_STATUS_RESOURCE_EXHAUSTED
     assert _noalloc(lib, fp32_session, a, a, a, -1, n, k) == 3  # SB_STATUS_INVALID_ARGUMENT
+    # more rows than one CUDA-core launch covers (65535 tiles of 128)
+    assert _noalloc(lib, fp32_session, a, a, a, 65535 * 128 + 1, 1, 1) == 3
