@@ -968,6 +968,7 @@ Plan plan_function(const Function& f, Precision prec) {
   // (GEMM and attention steps in their epilogues, loops as they store).
   std::set<int> round_gemm_outputs;
   std::vector<int> round_roots;
+  std::map<int, int> shadow_of;  // value -> index into plan.shadows
   if (prec == Precision::TF32) {
     std::set<int> bases, attn_bases;
     for (const Op& op : f.ops) {
@@ -986,6 +987,7 @@ Plan plan_function(const Function& f, Precision prec) {
         bases.insert(g.b.value);
       }
     }
+    const std::set<int> gemm_bases = bases;
     bases.insert(attn_bases.begin(), attn_bases.end());
     for (int v : bases) {
       if (pl.cluster[v] == kParam && f.value_types[v].dtype == DType::F32) {
@@ -994,6 +996,16 @@ Plan plan_function(const Function& f, Precision prec) {
         const Op* p = pl.producer(v);
         if (p && (pl.is_gemm_root(*p) || is_attention(p->kind))) round_gemm_outputs.insert(v);
         else round_roots.push_back(v);
+      } else if (pl.cluster[v] == v && gemm_bases.count(v) && f.value_types[v].dtype == DType::F32) {
+        // read by GEMMs and by other steps (e.g. the residual-stream gradient,
+        // which feeds a projection's backward GEMMs and the next residual
+        // add): the GEMMs read a rounded shadow copy.  Unrounded, the tensor
+        // cores would truncate it -- a one-sided error that does not average
+        // out over the contraction.
+        Shadow sh;
+        sh.value = v;
+        shadow_of[v] = (int)plan.shadows.size();
+        plan.shadows.push_back(sh);
       }
     }
   }
@@ -1149,6 +1161,8 @@ Plan plan_function(const Function& f, Precision prec) {
         if (st.gemm.a.value == rp) st.gemm.a_rounded = true;
         if (st.gemm.b.value == rp) st.gemm.b_rounded = true;
       }
+      if (shadow_of.count(st.gemm.a.value)) st.gemm.a_shadow = shadow_of[st.gemm.a.value];
+      if (shadow_of.count(st.gemm.b.value)) st.gemm.b_shadow = shadow_of[st.gemm.b.value];
       check_view_bounds(f, st.gemm.a, "GEMM lhs");
       check_view_bounds(f, st.gemm.b, "GEMM rhs");
       st.leaves = {st.gemm.a.value, st.gemm.b.value};
@@ -1194,6 +1208,43 @@ Plan plan_function(const Function& f, Precision prec) {
     plan.steps.push_back(std::move(st));
   }
   flush();
+  // conversion steps of the operand shadows, each right after the step that
+  // writes its value
+  if (!plan.shadows.empty()) {
+    std::vector<Step> steps;
+    std::vector<int> new_index(plan.steps.size(), -1);
+    for (size_t si = 0; si < plan.steps.size(); ++si) {
+      Step& st0 = plan.steps[si];
+      std::vector<int> written{st0.root};
+      written.insert(written.end(), st0.extra_roots.begin(), st0.extra_roots.end());
+      new_index[si] = (int)steps.size();
+      steps.push_back(std::move(st0));
+      for (int w : written) {
+        auto it = shadow_of.find(w);
+        if (it == shadow_of.end()) continue;
+        Shadow& sh = plan.shadows[it->second];
+        Step cs;
+        cs.kind = StepKind::Convert;
+        cs.root = w;
+        cs.leaves = {w};
+        cs.shadow = it->second;
+        cs.elements = f.value_types[w].numel();
+        cs.bytes_moved = cs.elements * (4 + dtype_bytes(sh.dtype));
+        sh.step = (int)steps.size();
+        steps.push_back(std::move(cs));
+      }
+    }
+    plan.steps = std::move(steps);
+    for (auto& [v, si] : step_of_value) si = new_index[si];
+    for (int si = 0; si < (int)plan.steps.size(); ++si) {
+      const Step& st0 = plan.steps[si];
+      if (st0.kind != StepKind::Gemm) continue;
+      for (int k : {st0.gemm.a_shadow, st0.gemm.b_shadow})
+        if (k >= 0) plan.shadows[k].last_use = std::max(plan.shadows[k].last_use, si);
+    }
+    for (const Shadow& sh : plan.shadows)
+      if (sh.step < 0) throw std::runtime_error("internal: operand shadow without a producing step");
+  }
   plan.source = cg.source();
   plan.snippets = cg.snippets();
   plan.prelude = CodeGen::prelude();
@@ -1237,6 +1288,12 @@ Plan plan_function(const Function& f, Precision prec) {
     if (plan.steps[s2].kind == StepKind::Gemm || plan.steps[s2].kind == StepKind::Attn) last_gemm = s2;
   for (int rp : plan.rounded_params)
     iv.push_back({f.value_types[rp].numel() * 4, 0, std::max(last_gemm, 0), -1, -2 - rp});
+  // operand shadows: step_scratch encodes -(2 + NV + shadow index)
+  for (size_t k = 0; k < plan.shadows.size(); ++k) {
+    const Shadow& sh = plan.shadows[k];
+    iv.push_back({f.value_types[sh.value].numel() * dtype_bytes(sh.dtype), sh.step, std::max(sh.step, sh.last_use), -1,
+                  -2 - NV - (int)k});
+  }
   std::vector<int> order(iv.size());
   for (size_t i = 0; i < iv.size(); ++i) order[i] = (int)i;
   std::sort(order.begin(), order.end(), [&](int x, int y) { return iv[x].bytes > iv[y].bytes; });
@@ -1263,7 +1320,9 @@ Plan plan_function(const Function& f, Precision prec) {
   for (size_t k = 0; k < iv.size(); ++k) {
     if (iv[k].value >= 0) plan.value_offset[iv[k].value] = off[k];
     else if (iv[k].step_scratch >= 0) plan.scratch_offset[iv[k].step_scratch] = off[k];
-    else {
+    else if (-2 - iv[k].step_scratch >= NV) {
+      plan.shadows[-2 - NV - iv[k].step_scratch].offset = off[k];
+    } else {
       int rp = -2 - iv[k].step_scratch;
       for (size_t j = 0; j < plan.rounded_params.size(); ++j)
         if (plan.rounded_params[j] == rp) plan.rounded_offset[j] = off[k];
@@ -1450,18 +1509,20 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
 std::string Plan::summary() const {
   std::ostringstream os;
   os.precision(17);
-  int loops = 0, reds = 0, gemms = 0, attn = 0, sorts = 0;
+  int loops = 0, reds = 0, gemms = 0, attn = 0, sorts = 0, converts = 0;
   double flops = 0, aflops = 0;
   for (auto& s : steps) {
     if (s.kind == StepKind::Loop) ++loops;
     else if (s.kind == StepKind::Reduce) ++reds;
     else if (s.kind == StepKind::Attn) { ++attn; aflops += s.flops; continue; }
     else if (s.kind == StepKind::Sort) { ++sorts; continue; }
+    else if (s.kind == StepKind::Convert) { ++converts; continue; }
     else ++gemms;
     flops += s.flops;
   }
   os << "steps=" << steps.size() << " loop=" << loops << " reduce=" << reds << " gemm=" << gemms
-     << " attention=" << attn << (sorts ? " sort=" + std::to_string(sorts) : std::string()) << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
+     << " attention=" << attn << (sorts ? " sort=" + std::to_string(sorts) : std::string())
+     << (converts ? " convert=" + std::to_string(converts) : std::string()) << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
      << " gemm_flops=" << flops << " attention_flops=" << aflops;
   return os.str();
 }

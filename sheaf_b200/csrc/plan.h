@@ -28,6 +28,19 @@ struct GemmDesc {
   int64_t sbb = 0, sbk = 0, sbn = 0;
   bool a_rounded = false, b_rounded = false;  // read the TF32-rounded copy of a parameter
   bool round_out = false;                     // store the result rounded to TF32
+  int a_shadow = -1, b_shadow = -1;           // read operand shadow Plan::shadows[i] instead
+};
+
+// Copy of a GEMM operand in the form the tensor cores read: f32 rounded to
+// nearest TF32, written by a conversion step right after the step that
+// produces the value.  Used for operands that other (non-GEMM) steps also
+// read, so their producer cannot store them rounded.
+struct Shadow {
+  int value = -1;       // the materialized value copied
+  int step = -1;        // the conversion step
+  int last_use = -1;    // last step that reads the shadow
+  int64_t offset = -1;  // arena byte offset
+  DType dtype = DType::F32;
 };
 
 struct GatherDesc {
@@ -46,7 +59,7 @@ struct AttnDesc {
   bool round_out = false;  // Y / dQ / dK / dV stored rounded to TF32
 };
 
-enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort };
+enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort, Convert };
 
 struct Step {
   StepKind kind = StepKind::Loop;
@@ -63,6 +76,7 @@ struct Step {
   int64_t elements = 0;         // output elements
   int64_t bytes_moved = 0;      // algorithmic bytes (inputs read once + output)
   double flops = 0;
+  int shadow = -1;              // Convert: index into Plan::shadows
 };
 
 struct Plan {
@@ -77,6 +91,7 @@ struct Plan {
   std::vector<int> output_step;       // per return slot: step that writes it (-1: copy)
   std::vector<int> rounded_params;    // parameters read by tf32 GEMMs through a rounded copy
   std::vector<int64_t> rounded_offset;  // arena offset of each rounded copy
+  std::vector<Shadow> shadows;        // GEMM operand copies (see Shadow)
   int64_t arena_bytes = 0;
   std::string source;                 // CUDA C++ of all generated kernels
   std::vector<std::string> snippets;  // the same, one independent piece per step

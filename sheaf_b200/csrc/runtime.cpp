@@ -362,6 +362,7 @@ sb_status* load_module(sb_session* s, const std::string& text, const Prebuilt* p
 std::string step_name(const Step& st) {
   if (st.kind == StepKind::Gemm) return "gemm";
   if (st.kind == StepKind::Sort) return "sort";
+  if (st.kind == StepKind::Convert) return "operand_shadow";
   if (st.kind == StepKind::Attn)
     return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : "attn_bwd";
   return st.kernel;
@@ -518,11 +519,22 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
         p.launches = launch_counter().load() - p.launches;
       }
     } end_event{ev_b, stream, s};
+    if (st.kind == StepKind::Convert) {
+      const Shadow& sh = plan.shadows[st.shadow];
+      float* dst = (float*)((char*)lf->arena + sh.offset);
+      cudaError_t e = round_tf32_copy((const float*)ptr[sh.value], dst, st.elements, stream);
+      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "operand shadow"); }
+      continue;
+    }
     if (st.kind == StepKind::Gemm) {
       const GemmDesc& g = st.gemm;
       GemmArgs a;
-      a.a = (g.a_rounded ? rounded[g.a.value] : (const float*)ptr[g.a.value]) + g.a.offset;
-      a.b = (g.b_rounded ? rounded[g.b.value] : (const float*)ptr[g.b.value]) + g.b.offset;
+      auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
+        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset) + w.offset;
+        return (rnd ? rounded[w.value] : (const float*)ptr[w.value]) + w.offset;
+      };
+      a.a = operand(g.a, g.a_rounded, g.a_shadow);
+      a.b = operand(g.b, g.b_rounded, g.b_shadow);
       a.c = (float*)ptr[st.root];
       a.round_out = g.round_out ? 1 : 0;
       a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
@@ -808,7 +820,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
   std::ostringstream os;
   os.precision(9);
   os << "function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert"};
   for (auto& m : s->modules)
     for (auto& lf : m->fns) {
       if (lf->prof_ms.empty()) continue;
@@ -1182,7 +1194,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   std::ostringstream os;
   os.precision(17);
   os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
     const GemmDesc& g = st.gemm;
