@@ -252,8 +252,22 @@ def _wrap32(x):
     return ((x + (1 << 31)) & 0xFFFFFFFF) - (1 << 31)
 
 
+def _bf16_rne(x):
+    """Values rounded to bf16, round to nearest even (of the f32 value), as an
+    op on bf16 tensors produces; NaN and infinities pass through."""
+    f = np.asarray(x, np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+    return np.where(np.isfinite(f), r, f)
+
+
 def _as(x, dt, dtype):
-    if dt in ("f32", "bf16", "f64"):
+    if dt == "bf16":
+        # a bf16 argument holds the upper 16 bits of the host f32 value (the
+        # runtime truncates on upload, sheaf/src/runtime/buffer_convert.rs:28-40)
+        f = np.ascontiguousarray(x, np.float32)
+        return (f.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32).astype(dtype)
+    if dt in ("f32", "f64"):
         return np.asarray(x, dtype=dtype)
     if dt == "i1":
         return np.asarray(x, dtype=np.bool_)
@@ -437,6 +451,8 @@ def evaluate(f: Func, inputs: Sequence[np.ndarray], dtype=np.float64) -> List[np
         if odt in ("f32", "bf16", "f64"):
             # no copy when the type already matches (broadcast views stay views)
             r = r.astype(dtype, copy=False)
+            if odt == "bf16":
+                r = _bf16_rne(r).astype(dtype)
         elif odt == "i32":
             r = _wrap32(r)
         if tuple(r.shape) != tuple(oshape):

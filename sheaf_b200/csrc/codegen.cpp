@@ -26,6 +26,22 @@ const char* ctype_of(DType t) {
   return "float";
 }
 
+// Element type in memory: bf16 values are stored as their 16 bits and
+// computed on as f32.
+const char* mtype_of(DType t) { return t == DType::BF16 ? "unsigned short" : ctype_of(t); }
+
+// x rounded to bf16 (round to nearest even on the f32 value; NaN and
+// infinities pass through).
+double bf16_round(double x) {
+  float f = (float)x;
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
 namespace {
 
 constexpr int kDup = -2, kConst = -3, kParam = -4;
@@ -161,7 +177,6 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
   }
   const Type& t = f_.value_types[v];
   auto st = row_major(t.shape);
-  if (t.dtype == DType::BF16) throw std::runtime_error("bf16 buffers are not supported in fused kernels");
   if (c.vec) {
     int lane = -1;
     std::string base = "cL";
@@ -193,7 +208,10 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
   std::string off = "0";
   for (size_t i = 0; i < coords.size(); ++i) off = c_add(off, c_mul(coords[i], st[i]));
   Val r{fresh(c), ctype_of(t.dtype)};
-  c.body << c.pad() << "const " << r.ctype << " " << r.name << " = L" << li << "[" << off << "];\n";
+  if (t.dtype == DType::BF16)
+    c.body << c.pad() << "const float " << r.name << " = sb_bf16_ld(L" << li << "[" << off << "]);\n";
+  else
+    c.body << c.pad() << "const " << r.ctype << " " << r.name << " = L" << li << "[" << off << "];\n";
   return r;
 }
 
@@ -215,9 +233,13 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
   if (!(cluster_[v] == c.root || cluster_[v] == kDup))
     throw std::runtime_error(std::string("codegen: node outside cluster (") + opkind_name(op.kind) + ")");
   std::string ct = ctype_of(op.type.dtype);
+  // bf16 arithmetic: each op's f32 result is rounded to bf16 (round to
+  // nearest even), as an op on bf16 tensors produces bf16 values
+  const bool bf = op.type.dtype == DType::BF16;
   auto emit = [&](const std::string& expr) {
     Val r{fresh(c), ct};
-    c.body << c.pad() << "const " << ct << " " << r.name << " = " << expr << ";\n";
+    c.body << c.pad() << "const " << ct << " " << r.name << " = " << (bf ? "sb_bf16_rn(" + expr + ")" : expr)
+           << ";\n";
     return r;
   };
   // integer a OP b modulo 2^width, computed unsigned (no signed overflow)
@@ -230,7 +252,7 @@ CodeGen::Val CodeGen::eval(Ctx& c, int v, const std::vector<std::string>& coords
   const auto& osh = op.type.shape;
   switch (op.kind) {
     case OpKind::Constant:
-      out = Val{literal(op.values[0], ct), ct};
+      out = Val{literal(bf ? bf16_round(op.values[0]) : op.values[0], ct), ct};
       break;
     case OpKind::Iota:
       out = emit("(" + ct + ")(" + coords[op.axis] + ")");
@@ -501,7 +523,7 @@ std::string CodeGen::header(const std::string& name, const Ctx& c, int extra_ptr
     << " a) {\n" << kPdlPrologue;
   for (size_t i = 0; i < c.leaves.size(); ++i) {
     const Type& t = f_.value_types[c.leaves[i]];
-    h << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+    h << "  const " << mtype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << mtype_of(t.dtype)
       << "*)a.p[" << i << "];\n";
   }
   return h.str();
@@ -550,7 +572,7 @@ void CodeGen::gen_loop(const Op& root, Step* st) {
   // The root itself is evaluated as a cluster node: force non-materialized view.
   Val v = eval(c, root.result, coords);
   std::string name = "k" + std::to_string(names_.size());
-  const char* ot = ctype_of(root.type.dtype);
+  const char* ot = mtype_of(root.type.dtype);
   int64_t n = root.type.numel();
   src_ << header(name, c, 0);
   src_ << "  " << ot << "* __restrict__ O = (" << ot << "*)a.p[" << c.leaves.size() << "];\n";
@@ -853,7 +875,7 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
            << " a) {\n" << kPdlPrologue;
       for (size_t i = 0; i < c.leaves.size(); ++i) {
         const Type& t = f_.value_types[c.leaves[i]];
-        src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+        src_ << "  const " << mtype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << mtype_of(t.dtype)
              << "*)a.p[" << i << "];\n";
       }
       src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
@@ -927,8 +949,10 @@ void CodeGen::gen_reduce(const Op& root, Step* st, const Op* epi) {
     }
     return a;
   };
-  if (root.type.dtype != DType::F32 || in.dtype != DType::F32)
-    throw std::runtime_error("reduce: only f32 reductions are supported");
+  // bf16 reductions accumulate in f32 and round the result once
+  auto fp = [](DType t) { return t == DType::F32 || t == DType::BF16; };
+  if (!fp(root.type.dtype) || !fp(in.dtype) || (epi && !fp(epi->type.dtype)))
+    throw std::runtime_error("reduce: only f32 and bf16 reductions are supported");
 
   Ctx c;
   c.root = root.result;
@@ -1012,7 +1036,10 @@ void CodeGen::gen_reduce(const Op& root, Step* st, const Op* epi) {
   };
 
   src_ << header(name, c, splits > 1 ? 1 : 0);
-  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  {
+    const char* ot = mtype_of((epi ? *epi : root).type.dtype);
+    src_ << "  " << ot << "* __restrict__ O = (" << ot << "*)a.p[" << c.leaves.size() << "];\n";
+  }
   if (mode == 0) {
     src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
     src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; o < " << O
@@ -1075,10 +1102,13 @@ void CodeGen::gen_reduce(const Op& root, Step* st, const Op* epi) {
            << " a) {\n" << kPdlPrologue;
       for (size_t i = 0; i < c.leaves.size(); ++i) {
         const Type& t = f_.value_types[c.leaves[i]];
-        src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+        src_ << "  const " << mtype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << mtype_of(t.dtype)
              << "*)a.p[" << i << "];\n";
       }
-      src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+      {
+        const char* ot = mtype_of((epi ? *epi : root).type.dtype);
+        src_ << "  " << ot << "* __restrict__ O = (" << ot << "*)a.p[" << c.leaves.size() << "];\n";
+      }
       src_ << "  const float* __restrict__ S = (const float*)a.p[" << c.leaves.size() + 1 << "];\n";
       const bool block_per_output = O <= 2 * 148;
       if (block_per_output) {
@@ -1129,7 +1159,16 @@ std::string CodeGen::prelude() {
          "  unsigned u;\n"
          "  asm(\"cvt.rna.tf32.f32 %0, %1;\" : \"=r\"(u) : \"f\"(x));\n"
          "  return __uint_as_float(u);\n"
-         "}\n";
+         "}\n"
+         "// bf16 <-> f32: bf16 is the upper half of an f32; f32 -> bf16 rounds to\n"
+         "// nearest even (cvt.rn.bf16.f32)\n"
+         "__device__ __forceinline__ float sb_bf16_ld(unsigned short h) { return __uint_as_float((unsigned)h << 16); }\n"
+         "__device__ __forceinline__ unsigned short sb_bf16_bits(float x) {\n"
+         "  unsigned short h;\n"
+         "  asm(\"cvt.rn.bf16.f32 %0, %1;\" : \"=h\"(h) : \"f\"(x));\n"
+         "  return h;\n"
+         "}\n"
+         "__device__ __forceinline__ float sb_bf16_rn(float x) { return sb_bf16_ld(sb_bf16_bits(x)); }\n";
 }
 
 bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t C, Step* st) {
@@ -1392,7 +1431,7 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
          << " a) {\n" << kPdlPrologue;
     for (size_t i = 0; i < c.leaves.size(); ++i) {
       const Type& t = f_.value_types[c.leaves[i]];
-      src_ << "  const " << ctype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << ctype_of(t.dtype)
+      src_ << "  const " << mtype_of(t.dtype) << "* __restrict__ L" << i << " = (const " << mtype_of(t.dtype)
            << "*)a.p[" << i << "];\n";
     }
     src_ << "  const float* __restrict__ S = (const float*)a.p[" << np << "];\n";
@@ -1427,6 +1466,7 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
 }
 
 std::string CodeGen::store(const Op& root, const std::string& expr) const {
+  if (root.type.dtype == DType::BF16) return "sb_bf16_bits(" + expr + ")";
   if (root.type.dtype == DType::F32 &&
       std::find(round_roots_.begin(), round_roots_.end(), root.result) != round_roots_.end())
     return "sb_rna_tf32(" + expr + ")";

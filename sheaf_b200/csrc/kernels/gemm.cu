@@ -64,14 +64,14 @@ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Describes operand (rows x inner per batch) with strides (s_row, 1) and
 // batch stride s_batch as a padded dense copy; the padded view has row stride
 // ld and batch stride rows * ld.
-PadOp pad_op(int64_t batch, int64_t rows, int64_t inner, int64_t s_row, int64_t s_batch) {
+PadOp pad_op(int64_t batch, int64_t rows, int64_t inner, int64_t s_row, int64_t s_batch, int64_t q) {
   PadOp o;
   o.on = true;
   o.rows = rows;
   o.inner = inner;
   o.s_row = s_row;
   o.s_batch = s_batch;
-  o.ld = (inner + 3) / 4 * 4;
+  o.ld = (inner + q - 1) / q * q;
   o.elems = (size_t)(batch * rows * o.ld);
   return o;
 }
@@ -82,24 +82,26 @@ PadOp pad_op(int64_t batch, int64_t rows, int64_t inner, int64_t s_row, int64_t 
 bool pad_plan(const GemmArgs& g, Padding* pd, GemmArgs* view) {
   if (g.batch > 1 && (g.sab < 0 || g.sbb < 0)) return false;
   GemmArgs v = g;
+  const int64_t q = g.bf16 ? 8 : 4;  // elements per 16 bytes
+  const size_t es = g.bf16 ? 2 : 4;
   // A: K-major (sak == 1, rows M) or M-major (sam == 1, rows K)
   const bool a_ok = ((uintptr_t)g.a & 15) == 0 &&
-                    ((g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) || (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M)) &&
-                    (g.batch == 1 || g.sab % 4 == 0);
+                    ((g.sak == 1 && g.sam % q == 0 && g.sam >= g.K) || (g.sam == 1 && g.sak % q == 0 && g.sak >= g.M)) &&
+                    (g.batch == 1 || g.sab % q == 0);
   if (!a_ok) {
-    if (g.sak == 1 && g.sam >= g.K) pd->a = pad_op(g.batch, g.M, g.K, g.sam, g.sab);
-    else if (g.sam == 1 && g.sak >= g.M) pd->a = pad_op(g.batch, g.K, g.M, g.sak, g.sab);
+    if (g.sak == 1 && g.sam >= g.K) pd->a = pad_op(g.batch, g.M, g.K, g.sam, g.sab, q);
+    else if (g.sam == 1 && g.sak >= g.M) pd->a = pad_op(g.batch, g.K, g.M, g.sak, g.sab, q);
     else return false;
     if (g.sak == 1) { v.sam = pd->a.ld; v.sak = 1; }
     else { v.sak = pd->a.ld; v.sam = 1; }
     v.sab = pd->a.rows * pd->a.ld;
   }
   const bool b_ok = ((uintptr_t)g.b & 15) == 0 &&
-                    ((g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) || (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N)) &&
-                    (g.batch == 1 || g.sbb % 4 == 0);
+                    ((g.sbk == 1 && g.sbn % q == 0 && g.sbn >= g.K) || (g.sbn == 1 && g.sbk % q == 0 && g.sbk >= g.N)) &&
+                    (g.batch == 1 || g.sbb % q == 0);
   if (!b_ok) {
-    if (g.sbk == 1 && g.sbn >= g.K) pd->b = pad_op(g.batch, g.N, g.K, g.sbn, g.sbb);
-    else if (g.sbn == 1 && g.sbk >= g.N) pd->b = pad_op(g.batch, g.K, g.N, g.sbk, g.sbb);
+    if (g.sbk == 1 && g.sbn >= g.K) pd->b = pad_op(g.batch, g.N, g.K, g.sbn, g.sbb, q);
+    else if (g.sbn == 1 && g.sbk >= g.N) pd->b = pad_op(g.batch, g.K, g.N, g.sbk, g.sbb, q);
     else return false;
     if (g.sbk == 1) { v.sbn = pd->b.ld; v.sbk = 1; }
     else { v.sbk = pd->b.ld; v.sbn = 1; }
@@ -112,16 +114,16 @@ bool pad_plan(const GemmArgs& g, Padding* pd, GemmArgs* view) {
   if (!tc_plan(v, &pd->plan)) return false;
   pd->split_bytes = pd->plan.splits > 1 ? align256((size_t)(pd->plan.splits * g.M * g.N) * sizeof(float)) : 0;
   pd->a_off = pd->split_bytes;
-  pd->b_off = pd->a_off + (pd->a.on ? align256(pd->a.elems * sizeof(float)) : 0);
-  pd->total = pd->b_off + (pd->b.on ? align256(pd->b.elems * sizeof(float)) : 0);
+  pd->b_off = pd->a_off + (pd->a.on ? align256(pd->a.elems * es) : 0);
+  pd->total = pd->b_off + (pd->b.on ? align256(pd->b.elems * es) : 0);
   *view = v;
   return true;
 }
 
 // One thread per element of the padded copy's logical extent.  Index math in
 // the narrowest type that holds it (64-bit division is slow).
-template <typename I>
-__global__ void __launch_bounds__(256) pad_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, I batch,
+template <typename T, typename I>
+__global__ void __launch_bounds__(256) pad_copy_kernel(const T* __restrict__ src, T* __restrict__ dst, I batch,
                                                        I rows, I inner, int64_t s_row, int64_t s_batch, I ld) {
   pdl_prologue();
   const I n = batch * rows * inner;
@@ -134,21 +136,28 @@ __global__ void __launch_bounds__(256) pad_copy_kernel(const float* __restrict__
   }
 }
 
-cudaError_t pad_copy(const float* src, float* dst, int64_t batch, const PadOp& o, cudaStream_t stream) {
+template <typename T>
+cudaError_t pad_copy_t(const T* src, T* dst, int64_t batch, const PadOp& o, cudaStream_t stream) {
   const int64_t n = batch * o.rows * o.inner;
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
   if (n < (int64_t(1) << 31) - 148 * 16 * 256)
-    return launch_pdl(pad_copy_kernel<uint32_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst,
+    return launch_pdl(pad_copy_kernel<T, uint32_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst,
                       (uint32_t)batch, (uint32_t)o.rows, (uint32_t)o.inner, o.s_row, o.s_batch, (uint32_t)o.ld);
-  return launch_pdl(pad_copy_kernel<int64_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, batch, o.rows,
-                    o.inner, o.s_row, o.s_batch, o.ld);
+  return launch_pdl(pad_copy_kernel<T, int64_t>, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, batch,
+                    o.rows, o.inner, o.s_row, o.s_batch, o.ld);
+}
+
+// Padded copy of an operand of f32 or (bf16) 16-bit elements.
+cudaError_t pad_copy(const float* src, float* dst, int64_t batch, const PadOp& o, bool bf16, cudaStream_t stream) {
+  if (bf16) return pad_copy_t((const uint16_t*)src, (uint16_t*)dst, batch, o, stream);
+  return pad_copy_t(src, dst, batch, o, stream);
 }
 
 }  // namespace
 
 size_t gemm_workspace(const GemmArgs& g, int precision) {
-  if (precision == 1) {
+  if (precision == 1 || g.bf16) {
     TcPlan p;
     if (tc_plan(g, &p)) return p.splits > 1 ? (size_t)(p.splits * g.M * g.N) * sizeof(float) : 0;
     Padding pd;
@@ -189,7 +198,7 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
   if (tc_forced_config() >= 0) return proposed;
   const TuneKey key = {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
                        run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
-                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), 0};
+                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16};
   std::lock_guard<std::mutex> lock(tune_mu);
   auto it = tune_cache.find(key);
   if (it != tune_cache.end()) return it->second;
@@ -225,7 +234,9 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
 cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
   *used_tc = false;
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
-  if (precision == 1) {
+  // bf16 operands run on the tensor cores in every precision mode (their
+  // products are exact in f32, so kind::f16 is the graph's arithmetic)
+  if (precision == 1 || g.bf16) {
     TcPlan p;
     if (tc_plan(g, &p)) {
       const bool split = p.splits > 1 && ws && ws_bytes >= (size_t)(p.splits * g.M * g.N) * sizeof(float);
@@ -244,12 +255,12 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
         char* base = (char*)ws;
         if (pd.a.on) {
           v.a = (const float*)(base + pd.a_off);
-          cudaError_t e = pad_copy(g.a, (float*)v.a, g.batch, pd.a, stream);
+          cudaError_t e = pad_copy(g.a, (float*)v.a, g.batch, pd.a, g.bf16 != 0, stream);
           if (e != cudaSuccess) return e;
         }
         if (pd.b.on) {
           v.b = (const float*)(base + pd.b_off);
-          cudaError_t e = pad_copy(g.b, (float*)v.b, g.batch, pd.b, stream);
+          cudaError_t e = pad_copy(g.b, (float*)v.b, g.batch, pd.b, g.bf16 != 0, stream);
           if (e != cudaSuccess) return e;
         }
         const bool split = pd.plan.splits > 1;

@@ -10,6 +10,12 @@ namespace {
 
 constexpr int BM = 128, BN = 128, BK = 8;
 
+// operand element as f32: f32 as is, bf16 widened (bf16 is the top half of
+// an f32)
+__device__ __forceinline__ float ld_elem(const float* p) { return *p; }
+__device__ __forceinline__ float ld_elem(const uint16_t* p) { return __uint_as_float((uint32_t)*p << 16); }
+
+template <typename T>
 __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
   pdl_prologue();
   __shared__ float As[2][BK][BM + 4];
@@ -21,12 +27,12 @@ __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
   const bool b_kc = p.sbk == 1 && p.sbn != 1;
 
   for (int64_t bz = blockIdx.z; bz < p.batch; bz += gridDim.z) {
-    const float* A = p.a + bz * p.sab;
-    const float* B = p.b + bz * p.sbb;
+    const T* A = (const T*)p.a + bz * p.sab;
+    const T* B = (const T*)p.b + bz * p.sbb;
     int64_t kbeg = 0, kend = p.K;
     if (p.k_chunk > 0) {  // split-K: z indexes the K range, operands are shared
-      A = p.a;
-      B = p.b;
+      A = (const T*)p.a;
+      B = (const T*)p.b;
       kbeg = bz * p.k_chunk;
       kend = kbeg + p.k_chunk < p.K ? kbeg + p.k_chunk : p.K;
     }
@@ -50,9 +56,9 @@ __global__ void __launch_bounds__(256) sgemm_strided(GemmArgs p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int64_t m = m0 + am[e], k = k0 + ak[e];
-        ra[e] = (m < p.M && k < kend) ? A[m * p.sam + k * p.sak] : 0.f;
+        ra[e] = (m < p.M && k < kend) ? ld_elem(A + m * p.sam + k * p.sak) : 0.f;
         int64_t kb = k0 + bk[e], n = n0 + bn[e];
-        rb[e] = (kb < kend && n < p.N) ? B[kb * p.sbk + n * p.sbn] : 0.f;
+        rb[e] = (kb < kend && n < p.N) ? ld_elem(B + kb * p.sbk + n * p.sbn) : 0.f;
       }
     };
     auto store = [&](int buf) {
@@ -111,7 +117,8 @@ cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream) {
   dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM),
             (unsigned)(g.batch < 65535 ? g.batch : 65535));
   if (grid.y > 65535) return cudaErrorInvalidConfiguration;
-  return launch_pdl(sgemm_strided, grid, dim3(256), 0, stream, g);
+  if (g.bf16) return launch_pdl(sgemm_strided<uint16_t>, grid, dim3(256), 0, stream, g);
+  return launch_pdl(sgemm_strided<float>, grid, dim3(256), 0, stream, g);
 }
 
 }  // namespace sb

@@ -1,6 +1,9 @@
 // tcgen05 tensor-core GEMM for sm_100a: C[z] = A[z] @ B[z] with f32 operands in
-// global memory read by the tensor cores as TF32 (kind::tf32), f32 accumulation
-// in TMEM.  z is a batch index or, for split-K, a K range.
+// global memory read by the tensor cores as TF32 (kind::tf32), or bf16 operands
+// (kind::f16 with bf16 A and B), f32 accumulation in TMEM and f32 C.  z is a
+// batch index or, for split-K, a K range.  A pipeline stage holds 128 bytes of
+// K per operand row either way (32 tf32 or 64 bf16 values), so the shared-
+// memory layout, the ring and the epilogue are the same for both.
 //
 // Persistent: PER_SM CTAs per SM walk the 128 x BN output tiles t = blockIdx.x,
 // blockIdx.x + gridDim.x, ... (grouped order, see Tiles, so CTAs that run
@@ -194,12 +197,26 @@ __device__ __forceinline__ void epilogue_warp(uint32_t acc, float* bufs, int lan
   }
 }
 
+// Descriptor of an MN-major operand tile at `addr`: chunks of 128-byte rows
+// (one row per K value), 32 f32 or 64 bf16 M/N values wide, BK rows deep per
+// chunk (4096 / 8192 bytes apart: the leading byte offset).  tf32: the 128-byte
+// swizzle with 32-byte atoms, 4-row groups 512 B apart; bf16: the plain
+// 128-byte swizzle, 8-row groups 1024 B apart (stride byte offset).
+template <bool BF>
+__device__ __forceinline__ uint64_t mn_desc(uint32_t addr) {
+  return BF ? smem_desc(addr, 64 * 128, 1024, 2) : smem_desc(addr, BK * 128, 512, 1);
+}
+// start-address step (16-byte units) between the 4 MMAs of a stage on an
+// MN-major tile: 8 rows (tf32, K = 8) or 16 rows (bf16, K = 16) of 128 B
+template <bool BF>
+constexpr uint64_t kMnStep = BF ? (2048 >> 4) : (1024 >> 4);
+
 // TMEM allocations are powers of two of at least 32 columns.
 __host__ __device__ constexpr uint32_t tmem_cols(int n) { return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u; }
 
-template <int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                       long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
                       int c3d, int round_out, int kchunk, Tiles tl, int* err) {
@@ -222,7 +239,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ktiles_all = (K + BK - 1) / BK;
+  // K values per 128-byte stage row (also M/N values per 128-byte row of an
+  // MN-major tile): 32 f32 or 64 bf16
+  constexpr int BKE = BF ? 64 : 32;
+  const int ktiles_all = (K + BKE - 1) / BKE;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
 
   if (threadIdx.x == 0) {
@@ -272,20 +292,22 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
           if (!a_mn) {
-            tma_ld(a, &tmA, &full[s], kt * BK, m0, zab, a3d);
+            tma_ld(a, &tmA, &full[s], kt * BKE, m0, zab, a3d);
           } else if (a_chunks) {
-            tma_ld_chunks(a, &tmA, &full[s], kt * BK, m0 / 32, zab, a3d);
+            tma_ld_chunks(a, &tmA, &full[s], kt * BKE, m0 / BKE, zab, a3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j) tma_ld(a + j * BK * 128, &tmA, &full[s], m0 + 32 * j, kt * BK, zab, a3d);
+            for (int j = 0; j < BM / BKE; ++j)
+              tma_ld(a + j * BKE * 128, &tmA, &full[s], m0 + BKE * j, kt * BKE, zab, a3d);
           }
           if (!b_mn) {
-            tma_ld(b, &tmB, &full[s], kt * BK, n0, zab, b3d);
+            tma_ld(b, &tmB, &full[s], kt * BKE, n0, zab, b3d);
           } else if (b_chunks) {
-            tma_ld_chunks(b, &tmB, &full[s], kt * BK, n0 / 32, zab, b3d);
+            tma_ld_chunks(b, &tmB, &full[s], kt * BKE, n0 / BKE, zab, b3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j) tma_ld(b + j * BK * 128, &tmB, &full[s], n0 + 32 * j, kt * BK, zab, b3d);
+            for (int j = 0; j < BN / BKE; ++j)
+              tma_ld(b + j * BKE * 128, &tmB, &full[s], n0 + BKE * j, kt * BKE, zab, b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -293,11 +315,11 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(BM, BN, a_mn, b_mn);
+      const uint32_t idesc = BF ? idesc_bf16(BM, BN, a_mn, b_mn) : idesc_tf32(BM, BN, a_mn, b_mn);
       // descriptors of slot 0, K slice 0 (see the CTA-pair kernel)
-      const uint64_t a_d0 = a_mn ? smem_desc(smem_u32(sA), BK * 128, 512, 1) : smem_desc(smem_u32(sA), 16, 1024, 2);
-      const uint64_t b_d0 = b_mn ? smem_desc(smem_u32(sB), BK * 128, 512, 1) : smem_desc(smem_u32(sB), 16, 1024, 2);
-      const uint64_t a_kk = a_mn ? 1024 >> 4 : 32 >> 4, b_kk = b_mn ? 1024 >> 4 : 32 >> 4;
+      const uint64_t a_d0 = a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
+      const uint64_t b_d0 = b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
+      const uint64_t a_kk = a_mn ? kMnStep<BF> : 32 >> 4, b_kk = b_mn ? kMnStep<BF> : 32 >> 4;
       int it = 0, j = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -319,8 +341,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           const uint64_t ad = a_d0 + (uint64_t)((s * S::A_BYTES) >> 4);
           const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk)
-            mma_tf32(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            if (BF) mma_bf16(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else mma_tf32(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -367,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 // (BN = 256) fewer operand bytes per FLOP than the 128 x 128 single-CTA tile.
 // Completion is signalled to both CTAs with one non-multicast commit each; the
 // peer's epilogue releases an accumulator with a remote mbarrier arrive.
-template <int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tf32_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                    long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
                    int c3d, int round_out, int kchunk, Tiles tl, int* err) {
@@ -397,7 +421,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
-  const int ktiles_all = (K + BK - 1) / BK;
+  // K values per 128-byte stage row (also M/N values per 128-byte row of an
+  // MN-major tile): 32 f32 or 64 bf16
+  constexpr int BKE = BF ? 64 : 32;
+  const int ktiles_all = (K + BKE - 1) / BKE;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
 
   if (threadIdx.x == 0) {
@@ -458,20 +485,20 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
           if (!a_mn) {
-            ld(a, &tmA, bar, kt * BK, ma, zab, a3d);
+            ld(a, &tmA, bar, kt * BKE, ma, zab, a3d);
           } else if (a_chunks) {
-            ld_chunks(a, &tmA, bar, kt * BK, ma / 32, zab, a3d);
+            ld_chunks(a, &tmA, bar, kt * BKE, ma / BKE, zab, a3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j) ld(a + j * BK * 128, &tmA, bar, ma + 32 * j, kt * BK, zab, a3d);
+            for (int j = 0; j < BM / BKE; ++j) ld(a + j * BKE * 128, &tmA, bar, ma + BKE * j, kt * BKE, zab, a3d);
           }
           if (!b_mn) {
-            ld(b, &tmB, bar, kt * BK, nb, zab, b3d);
+            ld(b, &tmB, bar, kt * BKE, nb, zab, b3d);
           } else if (b_chunks) {
-            ld_chunks(b, &tmB, bar, kt * BK, nb / 32, zab, b3d);
+            ld_chunks(b, &tmB, bar, kt * BKE, nb / BKE, zab, b3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BNH / 32; ++j) ld(b + j * BK * 128, &tmB, bar, nb + 32 * j, kt * BK, zab, b3d);
+            for (int j = 0; j < BNH / BKE; ++j) ld(b + j * BKE * 128, &tmB, bar, nb + BKE * j, kt * BKE, zab, b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -479,13 +506,14 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      const uint32_t idesc = idesc_tf32(2 * BM, BN, a_mn, b_mn);
+      const uint32_t idesc = BF ? idesc_bf16(2 * BM, BN, a_mn, b_mn) : idesc_tf32(2 * BM, BN, a_mn, b_mn);
       // descriptors of slot 0, K slice 0; a slot adds its byte offset and a
-      // K slice 32 B (K-major) or 1024 B (MN-major), in 16-byte units, to the
-      // start-address field (shared addresses stay below 2^18, no carry)
-      const uint64_t a_d0 = a_mn ? smem_desc(smem_u32(sA), BK * 128, 512, 1) : smem_desc(smem_u32(sA), 16, 1024, 2);
-      const uint64_t b_d0 = b_mn ? smem_desc(smem_u32(sB), BK * 128, 512, 1) : smem_desc(smem_u32(sB), 16, 1024, 2);
-      const uint64_t a_kk = a_mn ? 1024 >> 4 : 32 >> 4, b_kk = b_mn ? 1024 >> 4 : 32 >> 4;
+      // K slice 32 B (K-major) or 1024 / 2048 B (MN-major tf32 / bf16), in
+      // 16-byte units, to the start-address field (shared addresses stay below
+      // 2^18, no carry)
+      const uint64_t a_d0 = a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
+      const uint64_t b_d0 = b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
+      const uint64_t a_kk = a_mn ? kMnStep<BF> : 32 >> 4, b_kk = b_mn ? kMnStep<BF> : 32 >> 4;
       const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
       int it = 0, j = 0, s = 0;
       uint32_t ph = 0;
@@ -504,8 +532,10 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           const uint64_t ad = a_d0 + (uint64_t)((s * S::A_BYTES) >> 4);
           const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk)
-            mma_tf32_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            if (BF) mma_bf16_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else mma_tf32_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit_pair(empty0 + (uint32_t)(s * 8));
           mma_commit_pair(empty1 + (uint32_t)(s * 8));
           if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -545,30 +575,34 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   }
 }
 
-// 2-D or 3-D f32 map: inner (contiguous) extent d0, outer d1, batch d2.
-bool make_map(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
-              uint64_t s2_bytes, uint32_t box0, uint32_t box1, bool is3d, bool mn_major) {
-  (void)box0;
+// 2-D or 3-D operand map: inner (contiguous) extent d0, outer d1, batch d2;
+// the box is one 128-byte swizzle row wide and box1 rows tall.
+bool make_map(CUtensorMap* m, bool bf, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+              uint64_t s2_bytes, uint32_t box1, bool is3d, bool mn_major) {
   const uint64_t dims[3] = {d0, d1, d2};
   const uint64_t strides[2] = {s1_bytes, s2_bytes};
+  if (bf) return tc_make_map_bf16(m, base, is3d ? 3 : 2, dims, strides, box1);
   return tc_make_map(m, base, is3d ? 3 : 2, dims, strides, box1, mn_major);
 }
 
 // Chunked map of an MN-major operand (MN values contiguous, rows of K):
-// dims {32, K, MN / 32[, batch]} with the 32-value chunks 128 B apart, box
-// {32, BK, chunks}, so one load fills a stage's chunks BK * 128 B apart.
-// Only when MN is a multiple of 32 (the last chunk ends inside the row).
-bool make_chunk_map(CUtensorMap* m, const float* base, uint64_t mn, uint64_t k, uint64_t batch, uint64_t ld_bytes,
-                    uint64_t batch_bytes, uint32_t chunks, bool batched) {
-  if (mn % 32) return false;
+// dims {W, K, MN / W[, batch]} with the W-value chunks 128 B apart (W = 32 f32
+// or 64 bf16), box {W, BKE, chunks}, so one load fills a stage's chunks
+// BKE * 128 B apart.  Only when MN is a multiple of W (the last chunk ends
+// inside the row).
+bool make_chunk_map(CUtensorMap* m, bool bf, const float* base, uint64_t mn, uint64_t k, uint64_t batch,
+                    uint64_t ld_bytes, uint64_t batch_bytes, uint32_t chunks, bool batched) {
+  const uint64_t w = bf ? 64 : 32;
+  if (mn % w) return false;
   auto enc = encode_fn();
   if (!enc) return false;
-  cuuint64_t d[4] = {32, (cuuint64_t)k, (cuuint64_t)(mn / 32), (cuuint64_t)batch};
+  cuuint64_t d[4] = {w, (cuuint64_t)k, (cuuint64_t)(mn / w), (cuuint64_t)batch};
   cuuint64_t st[3] = {(cuuint64_t)ld_bytes, 128, (cuuint64_t)batch_bytes};
-  cuuint32_t box[4] = {32, (cuuint32_t)BK, chunks, 1}, es[4] = {1, 1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, batched ? 4u : 3u, (void*)base, d, st, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  cuuint32_t box[4] = {(cuuint32_t)w, (cuuint32_t)w, chunks, 1}, es[4] = {1, 1, 1, 1};
+  return enc(m, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, batched ? 4u : 3u,
+             (void*)base, d, st, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             bf ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Store map of C (f32, inner extent N, rows M, slices `batch`): 32-row x
@@ -598,27 +632,47 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int STAGES, int PER_SM, int ACC>
-cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
-  CUtensorMap ta, tb;
+// Operand maps of g for a tile of BM_CTA rows of A and BN_CTA columns of B
+// per CTA.  false when a map cannot be encoded (the caller reports
+// cudaErrorNotSupported).
+template <bool BF>
+bool operand_maps(const GemmArgs& g, bool a_mn, bool b_mn, int bn_cta, CUtensorMap* ta, CUtensorMap* tb,
+                  int* a_chunks, int* b_chunks, bool* a3d, bool* b3d) {
+  constexpr int BKE = BF ? 64 : 32;
+  constexpr int64_t es = BF ? 2 : 4;
   const int64_t lda = a_mn ? g.sak : g.sam;
   const int64_t ldb = b_mn ? g.sbk : g.sbn;
   const bool split = g.k_chunk > 0;
-  const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
-  const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
-  // A: K-major dims {K, M}, box {32, 128}; M-major dims {M, K}, box {32, 32}
-  const int a_chunks = a_mn && make_chunk_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, BM / 32, a3d);
-  const int b_chunks = b_mn && make_chunk_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, BN / 32, b3d);
-  bool ok = a_chunks || (a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
-                              : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false));
-  ok = ok && (b_chunks || (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
-                                : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BN, b3d, false)));
-  if (!ok) return cudaErrorNotSupported;
+  *a3d = !split && g.batch > 1 && g.sab != 0;
+  *b3d = !split && g.batch > 1 && g.sbb != 0;
+  // A: K-major dims {K, M}, box {row, 128}; M-major dims {M, K}, box {row, BKE}
+  *a_chunks = a_mn && make_chunk_map(ta, BF, g.a, g.M, g.K, g.batch, lda * es, g.sab * es, BM / BKE, *a3d);
+  *b_chunks = b_mn && (bn_cta % BKE == 0) &&
+              make_chunk_map(tb, BF, g.b, g.N, g.K, g.batch, ldb * es, g.sbb * es, bn_cta / BKE, *b3d);
+  bool ok = *a_chunks || (a_mn ? make_map(ta, BF, g.a, g.M, g.K, g.batch, lda * es, g.sab * es, BKE, *a3d, true)
+                                : make_map(ta, BF, g.a, g.K, g.M, g.batch, lda * es, g.sab * es, BM, *a3d, false));
+  ok = ok && (*b_chunks || (b_mn ? make_map(tb, BF, g.b, g.N, g.K, g.batch, ldb * es, g.sbb * es, BKE, *b3d, true)
+                                  : make_map(tb, BF, g.b, g.K, g.N, g.batch, ldb * es, g.sbb * es, bn_cta, *b3d,
+                                             false)));
+  return ok;
+}
+
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
+  constexpr int BKE = BF ? 64 : 32;
+  // an MN-major tile is loaded in whole 128-byte-wide chunks
+  if (BF && b_mn && BN % BKE) return cudaErrorNotSupported;
+  CUtensorMap ta, tb;
+  int a_chunks = 0, b_chunks = 0;
+  bool a3d = false, b3d = false;
+  if (!operand_maps<BF>(g, a_mn, b_mn, BN, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
+    return cudaErrorNotSupported;
+  const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
   const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tf32_tcgen05<BN, STAGES, PER_SM, ACC>;
+  auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -639,27 +693,23 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
                     a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, err);
 }
 
-template <int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
   constexpr int BNH = BN / 2;
+  constexpr int BKE = BF ? 64 : 32;
+  // each CTA loads BN / 2 columns of B: whole 128-byte chunks when MN-major
+  if (b_mn && BNH % BKE) return cudaErrorNotSupported;
   CUtensorMap ta, tb;
-  const int64_t lda = a_mn ? g.sak : g.sam;
-  const int64_t ldb = b_mn ? g.sbk : g.sbn;
-  const bool split = g.k_chunk > 0;
-  const int kchunk = split ? (int)(g.k_chunk / BK) : 0;
-  const bool a3d = !split && g.batch > 1 && g.sab != 0, b3d = !split && g.batch > 1 && g.sbb != 0;
-  const int a_chunks = a_mn && make_chunk_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, BM / 32, a3d);
-  const int b_chunks = b_mn && make_chunk_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, BNH / 32, b3d);
-  bool ok = a_chunks || (a_mn ? make_map(&ta, g.a, g.M, g.K, g.batch, lda * 4, g.sab * 4, 32, BK, a3d, true)
-                              : make_map(&ta, g.a, g.K, g.M, g.batch, lda * 4, g.sab * 4, 32, BM, a3d, false));
-  ok = ok && (b_chunks || (b_mn ? make_map(&tb, g.b, g.N, g.K, g.batch, ldb * 4, g.sbb * 4, 32, BK, b3d, true)
-                                : make_map(&tb, g.b, g.K, g.N, g.batch, ldb * 4, g.sbb * 4, 32, BNH, b3d, false)));
-  if (!ok) return cudaErrorNotSupported;
+  int a_chunks = 0, b_chunks = 0;
+  bool a3d = false, b3d = false;
+  if (!operand_maps<BF>(g, a_mn, b_mn, BNH, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
+    return cudaErrorNotSupported;
+  const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
   const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BNH, STAGES>;
-  auto kern = gemm_tf32_pair<BN, STAGES, PER_SM, ACC>;
+  auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -691,8 +741,7 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
                             (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
-                            g.round_out,
-                            kchunk, tl, err);
+                            g.round_out, kchunk, tl, err);
 }
 
 int* error_word() { return tc_error_word(); }
@@ -728,6 +777,24 @@ bool tc_make_map(CUtensorMap* m, const float* base, int rank, const uint64_t* di
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
                    mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool tc_make_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes, uint32_t box_rows) {
+  auto enc = encode_fn();
+  if (!enc || rank < 2 || rank > 5) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t box[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    box[i] = i == 0 ? 64u : (i == 1 ? box_rows : 1u);
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, (void*)base, d, st, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -769,12 +836,14 @@ constexpr int kNumCfgs = (int)(sizeof(kCfgs) / sizeof(kCfgs[0]));
 // the nanoGPT and GPT-2 shapes).
 constexpr double kSmBytesPerUs = 110e3, kSmFlopsPerUs = 5.5e6, kFillUs = 2.0, kEpiBytesPerUs = 50e3;
 
-double est_us(const TcCfg& c, int64_t M, int64_t N, int64_t K, int64_t units_z, int sms) {
+double est_us(const TcCfg& c, int64_t M, int64_t N, int64_t K, int64_t units_z, int sms, bool bf) {
   const int tm = c.pair ? 256 : 128;
   const double tiles = (double)((M + tm - 1) / tm) * (double)((N + c.bn - 1) / c.bn) * (double)units_z;
   const double slots = c.pair ? c.per_sm * sms / 2.0 : (double)c.per_sm * sms;
   const double waves = std::ceil(tiles / slots);
-  const double ksteps = std::ceil((double)K / BK);
+  // a stage is 128 bytes of K per row either way: 32 tf32 or 64 bf16 values,
+  // and the bf16 rate is twice the tf32 rate, so a stage costs the same
+  const double ksteps = std::ceil((double)K / (bf ? 2 * BK : BK));
   const int bcols = c.pair ? c.bn / 2 : c.bn;
   const double t_mem = (128.0 + bcols) * 128.0 / (kSmBytesPerUs / c.per_sm);
   const double t_mma = 2.0 * 128 * c.bn * BK / (kSmFlopsPerUs / c.per_sm);
@@ -783,18 +852,21 @@ double est_us(const TcCfg& c, int64_t M, int64_t N, int64_t K, int64_t units_z, 
   return waves * unit + (c.acc == 2 ? t_epi : 0.0);
 }
 
+// Operand strides must be multiples of 16 bytes (tensor maps): 4 f32 or 8
+// bf16 elements.
 bool tc_layout(const GemmArgs& g, bool* a_mn, bool* b_mn) {
   if (g.M < 64 || g.N < 32 || g.K < 32 || g.batch < 1 || g.batch > 65535) return false;
   if (g.M > (1ll << 30) || g.N > (1ll << 30) || g.K > (1ll << 30)) return false;
   if (g.scn != 1 || g.scm < g.N) return false;
-  if (g.sak == 1 && g.sam % 4 == 0 && g.sam >= g.K) *a_mn = false;
-  else if (g.sam == 1 && g.sak % 4 == 0 && g.sak >= g.M) *a_mn = true;
+  const int64_t q = g.bf16 ? 8 : 4;
+  if (g.sak == 1 && g.sam % q == 0 && g.sam >= g.K) *a_mn = false;
+  else if (g.sam == 1 && g.sak % q == 0 && g.sak >= g.M) *a_mn = true;
   else return false;
-  if (g.sbk == 1 && g.sbn % 4 == 0 && g.sbn >= g.K) *b_mn = false;
-  else if (g.sbn == 1 && g.sbk % 4 == 0 && g.sbk >= g.N) *b_mn = true;
+  if (g.sbk == 1 && g.sbn % q == 0 && g.sbn >= g.K) *b_mn = false;
+  else if (g.sbn == 1 && g.sbk % q == 0 && g.sbk >= g.N) *b_mn = true;
   else return false;
   if ((((uintptr_t)g.a) & 15) || (((uintptr_t)g.b) & 15)) return false;
-  if (g.batch > 1 && ((g.sab % 4) || (g.sbb % 4) || g.sab < 0 || g.sbb < 0)) return false;
+  if (g.batch > 1 && ((g.sab % q) || (g.sbb % q) || g.sab < 0 || g.sbb < 0)) return false;
   return true;
 }
 
@@ -828,8 +900,10 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
   if (g.batch == 1 && tiles < sms) {
     const int64_t s = std::min<int64_t>(2 * sms / tiles, g.K / 512);
     if (s >= 2) {
+      // K ranges in whole stages (32 tf32 or 64 bf16 values)
+      const int64_t gran = g.bf16 ? 2 * BK : BK;
       int64_t chunk = (g.K + s - 1) / s;
-      chunk = (chunk + BK - 1) / BK * BK;
+      chunk = (chunk + gran - 1) / gran * gran;
       p->splits = (g.K + chunk - 1) / chunk;
       p->k_chunk = p->splits > 1 ? chunk : 0;
     }
@@ -847,7 +921,9 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
     const TcCfg& c = kCfgs[ci];
     if (c.pair && g.M <= 128) continue;
     if (c.bn > 64 && g.N <= 32) continue;
-    const double t = est_us(c, g.M, g.N, kc, p->splits * g.batch, sms);
+    // bf16 MN-major B is loaded in 64-wide chunks: a CTA-pair half of 96 does not fit
+    if (g.bf16 && b_mn && c.pair && (c.bn / 2) % 64) continue;
+    const double t = est_us(c, g.M, g.N, kc, p->splits * g.batch, sms, g.bf16 != 0);
     if (t < best) {
       best = t;
       p->cfg = ci;
@@ -861,13 +937,24 @@ cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) {
   if (!tc_layout(g, &a_mn, &b_mn)) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
+  if (g.bf16) {
+    switch (cfg) {
+      case 0: return launch<true, 64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+      case 1: return launch<true, 128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
+      case 2: return launch_pair<true, 128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+      case 3: return launch_pair<true, 192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+      case 4: return launch_pair<true, 256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+      case 5: return launch_pair<true, 256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
+    }
+    return cudaErrorNotSupported;
+  }
   switch (cfg) {
-    case 0: return launch<64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 1: return launch<128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 2: return launch_pair<128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 3: return launch_pair<192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-    case 4: return launch_pair<256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-    case 5: return launch_pair<256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
+    case 0: return launch<false, 64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 1: return launch<false, 128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 2: return launch_pair<false, 128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
+    case 3: return launch_pair<false, 192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+    case 4: return launch_pair<false, 256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
+    case 5: return launch_pair<false, 256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
   }
   return cudaErrorNotSupported;
 }

@@ -17,6 +17,9 @@ struct GemmArgs {
   int64_t sbb, sbk, sbn;
   int64_t scb, scm, scn;
   int round_out = 0;  // tcgen05 path: store C rounded to nearest TF32
+  // A and B hold bf16 elements (a, b address bf16 data; strides in elements):
+  // tcgen05 kind::f16, or the CUDA-core kernel widening each element to f32
+  int bf16 = 0;
   // split-K (batch == 1 only): when > 0, "batch" index s computes the K range
   // [s*k_chunk, min(K, (s+1)*k_chunk)) into c + s*scb
   int64_t k_chunk = 0;
@@ -41,6 +44,9 @@ constexpr int64_t kSimtMaxM = 65535ll * 128;
 // has few tiles.  *used_tc reports whether the tensor-core kernel ran.
 size_t gemm_workspace(const GemmArgs& g, int precision);
 cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc);
+
+// dst[i] = bf16(src[i]), round to nearest even, n elements.
+cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t stream);
 
 // dst[i] = src[i] rounded to nearest TF32 (cvt.rna), n elements.
 cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream);

@@ -16,6 +16,11 @@ namespace sb {
 // needs for MN-major operands, else the plain 128-byte swizzle.
 bool tc_make_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                  uint32_t box_rows, bool mn_major);
+// The same for a bf16 tensor: the box is 64 bf16 (128 bytes) wide; MN-major
+// tiles use the plain 128-byte swizzle (16-bit MMA operands need no 32-byte
+// atoms).
+bool tc_make_map_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes, uint32_t box_rows);
 
 // Device word that every tcgen05 kernel sets when a bounded wait expires.
 int* tc_error_word();
@@ -153,6 +158,24 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t ad, uint64_t 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// kind::f16 instruction descriptor with bf16 A and B: D f32 (bits 4-5 = 1),
+// A and B format bf16 (1), transpose bits, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (TMEM) (+)= A * B with bf16 operands (K = 16 per instruction, 32 bytes of
+// each operand row, like one kind::tf32 instruction's K = 8).
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
       : "memory");
 }
@@ -295,6 +318,16 @@ __device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t ad, uint
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
       : "memory");
 }

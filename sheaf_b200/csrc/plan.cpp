@@ -855,8 +855,10 @@ void verify(const Function& f) {
         for (size_t i = 0; i < a.size(); ++i) if (!ua[i]) res.push_back(a[i]);
         for (size_t i = 0; i < b.size(); ++i) if (!ub[i]) res.push_back(b[i]);
         need(res == rs, "dot_general result shape");
-        need(T(op.operands[0]).dtype == DType::F32 && T(op.operands[1]).dtype == DType::F32 &&
-                 op.type.dtype == DType::F32, "dot_general supports f32 operands");
+        need(T(op.operands[0]).dtype == T(op.operands[1]).dtype &&
+                 (T(op.operands[0]).dtype == DType::F32 || T(op.operands[0]).dtype == DType::BF16) &&
+                 op.type.dtype == DType::F32,
+             "dot_general supports f32 x f32 or bf16 x bf16 operands with an f32 result");
         break;
       }
       case OpKind::Gather: {
@@ -969,7 +971,7 @@ Plan plan_function(const Function& f, Precision prec) {
   std::set<int> round_gemm_outputs;
   std::vector<int> round_roots;
   std::map<int, int> shadow_of;  // value -> index into plan.shadows
-  if (prec == Precision::TF32) {
+  if (prec == Precision::TF32 || prec == Precision::BF16) {
     std::set<int> bases, attn_bases;
     for (const Op& op : f.ops) {
       if (!pl.live[op.result]) continue;
@@ -988,6 +990,20 @@ Plan plan_function(const Function& f, Precision prec) {
       }
     }
     const std::set<int> gemm_bases = bases;
+    if (prec == Precision::BF16) {
+      // bf16 contractions: every f32 GEMM operand (parameter or step result)
+      // is read through a bf16 shadow; attention keeps TF32 operands
+      bases.clear();
+      for (int v : gemm_bases) {
+        if (f.value_types[v].dtype != DType::F32) continue;
+        if (pl.cluster[v] != kParam && pl.cluster[v] != v) continue;
+        Shadow sh;
+        sh.value = v;
+        sh.dtype = DType::BF16;
+        shadow_of[v] = (int)plan.shadows.size();
+        plan.shadows.push_back(sh);
+      }
+    }
     bases.insert(attn_bases.begin(), attn_bases.end());
     for (int v : bases) {
       if (pl.cluster[v] == kParam && f.value_types[v].dtype == DType::F32) {
@@ -996,7 +1012,8 @@ Plan plan_function(const Function& f, Precision prec) {
         const Op* p = pl.producer(v);
         if (p && (pl.is_gemm_root(*p) || is_attention(p->kind))) round_gemm_outputs.insert(v);
         else round_roots.push_back(v);
-      } else if (pl.cluster[v] == v && gemm_bases.count(v) && f.value_types[v].dtype == DType::F32) {
+      } else if (prec == Precision::TF32 && pl.cluster[v] == v && gemm_bases.count(v) &&
+                 f.value_types[v].dtype == DType::F32) {
         // read by GEMMs and by other steps (e.g. the residual-stream gradient,
         // which feeds a projection's backward GEMMs and the next residual
         // add): the GEMMs read a rounded shadow copy.  Unrounded, the tensor
@@ -1161,13 +1178,28 @@ Plan plan_function(const Function& f, Precision prec) {
         if (st.gemm.a.value == rp) st.gemm.a_rounded = true;
         if (st.gemm.b.value == rp) st.gemm.b_rounded = true;
       }
-      if (shadow_of.count(st.gemm.a.value)) st.gemm.a_shadow = shadow_of[st.gemm.a.value];
-      if (shadow_of.count(st.gemm.b.value)) st.gemm.b_shadow = shadow_of[st.gemm.b.value];
+      {
+        const int sa = shadow_of.count(st.gemm.a.value) ? shadow_of[st.gemm.a.value] : -1;
+        const int sb = shadow_of.count(st.gemm.b.value) ? shadow_of[st.gemm.b.value] : -1;
+        const bool bf_a = sa >= 0 && plan.shadows[sa].dtype == DType::BF16;
+        const bool bf_b = sb >= 0 && plan.shadows[sb].dtype == DType::BF16;
+        if (bf_a == bf_b) {  // bf16 shadows only in pairs: both operands or neither
+          st.gemm.a_shadow = sa;
+          st.gemm.b_shadow = sb;
+        } else {
+          st.gemm.a_shadow = bf_a ? -1 : sa;
+          st.gemm.b_shadow = bf_b ? -1 : sb;
+        }
+        st.gemm.bf16 = (bf_a && bf_b) || f.value_types[st.gemm.a.value].dtype == DType::BF16;
+      }
       check_view_bounds(f, st.gemm.a, "GEMM lhs");
       check_view_bounds(f, st.gemm.b, "GEMM rhs");
       st.leaves = {st.gemm.a.value, st.gemm.b.value};
       st.flops = 2.0 * st.gemm.batch * st.gemm.M * st.gemm.N * st.gemm.K;
-      st.bytes_moved = 4 * (st.gemm.batch * (st.gemm.M * st.gemm.K + st.gemm.K * st.gemm.N + st.gemm.M * st.gemm.N));
+      {
+        const int64_t es = st.gemm.bf16 ? 2 : 4;  // operand bytes; C is f32
+        st.bytes_moved = st.gemm.batch * (es * (st.gemm.M * st.gemm.K + st.gemm.K * st.gemm.N) + 4 * st.gemm.M * st.gemm.N);
+      }
     } else if (is_attention(op.kind)) {
       st.kind = StepKind::Attn;
       if (!pl.attn_of(op, &st.attn)) fail(op, "internal: attention operand views changed after planning");
@@ -1211,8 +1243,45 @@ Plan plan_function(const Function& f, Precision prec) {
   // conversion steps of the operand shadows, each right after the step that
   // writes its value
   if (!plan.shadows.empty()) {
+    // drop shadows no GEMM reads (a bf16 shadow whose partner operand has none)
+    {
+      std::vector<char> used(plan.shadows.size(), 0);
+      for (const Step& st0 : plan.steps)
+        if (st0.kind == StepKind::Gemm)
+          for (int k : {st0.gemm.a_shadow, st0.gemm.b_shadow})
+            if (k >= 0) used[k] = 1;
+      std::vector<int> remap(plan.shadows.size(), -1);
+      std::vector<Shadow> kept;
+      shadow_of.clear();
+      for (size_t k = 0; k < plan.shadows.size(); ++k)
+        if (used[k]) {
+          remap[k] = (int)kept.size();
+          shadow_of[plan.shadows[k].value] = (int)kept.size();
+          kept.push_back(plan.shadows[k]);
+        }
+      plan.shadows = std::move(kept);
+      for (Step& st0 : plan.steps)
+        if (st0.kind == StepKind::Gemm) {
+          if (st0.gemm.a_shadow >= 0) st0.gemm.a_shadow = remap[st0.gemm.a_shadow];
+          if (st0.gemm.b_shadow >= 0) st0.gemm.b_shadow = remap[st0.gemm.b_shadow];
+        }
+    }
     std::vector<Step> steps;
     std::vector<int> new_index(plan.steps.size(), -1);
+    // shadows of parameters: converted first, once per call
+    for (size_t k = 0; k < plan.shadows.size(); ++k) {
+      Shadow& sh = plan.shadows[k];
+      if (pl.cluster[sh.value] != kParam) continue;
+      Step cs;
+      cs.kind = StepKind::Convert;
+      cs.root = sh.value;
+      cs.leaves = {sh.value};
+      cs.shadow = (int)k;
+      cs.elements = f.value_types[sh.value].numel();
+      cs.bytes_moved = cs.elements * (4 + dtype_bytes(sh.dtype));
+      sh.step = (int)steps.size();
+      steps.push_back(std::move(cs));
+    }
     for (size_t si = 0; si < plan.steps.size(); ++si) {
       Step& st0 = plan.steps[si];
       std::vector<int> written{st0.root};
@@ -1488,7 +1557,8 @@ std::unique_ptr<Function> transpose_dot_outputs(const Function& f) {
 Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
   std::shared_ptr<Function> cur;
   std::string log;
-  if (prec == Precision::TF32 && fuse_attention) cur.reset(rewrite_attention(f, &log).release());
+  if ((prec == Precision::TF32 || prec == Precision::BF16) && fuse_attention)
+    cur.reset(rewrite_attention(f, &log).release());
   if (auto m = merge_reduce_chains(cur ? *cur : f)) cur.reset(m.release());
   if (auto m = transpose_dot_outputs(cur ? *cur : f)) cur.reset(m.release());
   std::string mlog;

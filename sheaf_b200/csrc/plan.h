@@ -29,12 +29,14 @@ struct GemmDesc {
   bool a_rounded = false, b_rounded = false;  // read the TF32-rounded copy of a parameter
   bool round_out = false;                     // store the result rounded to TF32
   int a_shadow = -1, b_shadow = -1;           // read operand shadow Plan::shadows[i] instead
+  bool bf16 = false;                          // both operands are read as bf16
 };
 
-// Copy of a GEMM operand in the form the tensor cores read: f32 rounded to
-// nearest TF32, written by a conversion step right after the step that
-// produces the value.  Used for operands that other (non-GEMM) steps also
-// read, so their producer cannot store them rounded.
+// Copy of a GEMM operand in the form the tensor cores read, written by a
+// conversion step right after the step that produces the value (parameters:
+// first in the call): f32 rounded to nearest TF32 (TF32 mode, for operands
+// that other steps also read, so that their producer cannot store them
+// rounded), or bf16 (bf16 mode, every f32 GEMM operand).
 struct Shadow {
   int value = -1;       // the materialized value copied
   int step = -1;        // the conversion step

@@ -521,20 +521,27 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     } end_event{ev_b, stream, s};
     if (st.kind == StepKind::Convert) {
       const Shadow& sh = plan.shadows[st.shadow];
-      float* dst = (float*)((char*)lf->arena + sh.offset);
-      cudaError_t e = round_tf32_copy((const float*)ptr[sh.value], dst, st.elements, stream);
+      char* dst = (char*)lf->arena + sh.offset;
+      const float* src = (const float*)ptr[sh.value];
+      cudaError_t e = sh.dtype == DType::BF16 ? bf16_copy(src, (uint16_t*)dst, st.elements, stream)
+                                              : round_tf32_copy(src, (float*)dst, st.elements, stream);
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "operand shadow"); }
       continue;
     }
     if (st.kind == StepKind::Gemm) {
       const GemmDesc& g = st.gemm;
       GemmArgs a;
+      // operand address: view offsets count elements of the buffer read (f32,
+      // or bf16 for bf16 operands and bf16 shadows)
       auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
-        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset) + w.offset;
-        return (rnd ? rounded[w.value] : (const float*)ptr[w.value]) + w.offset;
+        const int64_t es = g.bf16 ? 2 : 4;
+        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset + w.offset * es);
+        const char* base = rnd ? (const char*)rounded[w.value] : (const char*)ptr[w.value];
+        return (const float*)(base + w.offset * es);
       };
       a.a = operand(g.a, g.a_rounded, g.a_shadow);
       a.b = operand(g.b, g.b_rounded, g.b_shadow);
+      a.bf16 = g.bf16 ? 1 : 0;
       a.c = (float*)ptr[st.root];
       a.round_out = g.round_out ? 1 : 0;
       a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;

@@ -214,6 +214,12 @@ class DeviceBuffer:
         return int(library().sb_buffer_device_pointer(self._h) or 0)
 
     def to_host(self, timeout_ms: int = 0) -> np.ndarray:
+        if self.element_type == ELEMENT_TYPE_BFLOAT_16:
+            # bf16 -> f32 by widening the 16 bits (device_buffer.rs:53-75)
+            raw = np.empty(self.shape, dtype=np.uint16)
+            _check(library().sb_buffer_d2h(self._s._h, self._h, raw.ctypes.data_as(ctypes.c_void_p), raw.nbytes,
+                                           timeout_ms))
+            return (raw.astype(np.uint32) << 16).view(np.float32)
         dt = _NP_OF_ETYPE.get(self.element_type, np.float32)
         out = np.empty(self.shape, dtype=dt)
         _check(library().sb_buffer_d2h(self._s._h, self._h, out.ctypes.data_as(ctypes.c_void_p), out.nbytes,
@@ -324,7 +330,19 @@ class B200Session:
         return {n: getattr(st, n) for n, _ in _Stats._fields_}
 
     # buffers -----------------------------------------------------------------
-    def buffer(self, array) -> DeviceBuffer:
+    def buffer(self, array, bf16: bool = False) -> DeviceBuffer:
+        """Device copy of a host tensor.  With bf16=True the f32 values are
+        stored as bf16 by keeping their upper 16 bits, as Sheaf uploads a
+        bf16 tensor (buffer_convert.rs:28-40)."""
+        if bf16:
+            a = np.ascontiguousarray(array, dtype=np.float32)
+            bits = (a.view(np.uint32) >> 16).astype(np.uint16)
+            shape = (ctypes.c_uint64 * max(a.ndim, 1))(*a.shape)
+            h = ctypes.c_void_p()
+            _check(library().sb_buffer_allocate_copy(self._h, a.ndim, shape, ELEMENT_TYPE_BFLOAT_16,
+                                                     bits.ctypes.data_as(ctypes.c_void_p), bits.nbytes,
+                                                     ctypes.byref(h)))
+            return DeviceBuffer(self, h)
         a = np.ascontiguousarray(array)
         if a.dtype == np.float64 or a.dtype.kind in "iub" and a.dtype != np.int32:
             a = a.astype(np.float32)

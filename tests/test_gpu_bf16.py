@@ -1,0 +1,152 @@
+"""bf16 on the GPU through the C ABI.
+
+* Graphs with bf16 tensors (Sheaf's `(cast x :bf16)`, uploaded by truncating
+  f32 to its upper 16 bits): dot_general of bf16 operands with an f32 result
+  runs on tcgen05 kind::f16 (bf16 A and B, f32 accumulation) in every
+  operand layout, tile configuration, batched and split-K, checked against an
+  f64 product of the same bf16 values: 1e-5 norm-relative (the products are
+  exact in f32; only the f32 accumulation order differs).
+* Element-wise and reduction ops on bf16 tensors against the oracle's bf16
+  semantics (each op's result rounded to bf16, reductions accumulated wider
+  and rounded once): within one bf16 unit (2^-8 relative) where transcendental
+  functions of two math libraries round differently.
+* SB_PRECISION_BF16 on an f32 graph (GEMM operands converted to bf16, f32
+  accumulation and f32 everything else, attention in TF32): the nanoGPT
+  dimensions' value-and-grad against the f64 oracle.  bf16 operands carry
+  2^-9 relative rounding error, about 4x TF32's; the stated bound for this
+  mode is 5e-3 relative on the loss and 2e-2 norm-relative on gradients.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle.stablehlo_ref import run
+from sheaf_b200.programs import models as M
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_trunc(x):
+    x = np.ascontiguousarray(x, np.float32)
+    return (x.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def _matmul_module(name, m, n, k, layout, batch=0):
+    """(@ a b) on bf16 tensors, a stored transposed for layout[0] == "t", b
+    for layout[1] == "t", as x @ W^T and X^T @ G appear in Sheaf graphs."""
+    pre = [batch] if batch else []
+    ty = lambda *d: "tensor<" + "x".join(str(x) for x in pre + list(d)) + "x{}>"
+    at, bt = layout[0] == "t", layout[1] == "t"
+    sa = (ty(k, m) if at else ty(m, k)).format("bf16")
+    sb = (ty(n, k) if bt else ty(k, n)).format("bf16")
+    perm = "[0, 2, 1]" if batch else "[1, 0]"
+    body, lhs, rhs = [], "%arg0", "%arg1"
+    if at:
+        body.append(f"    %ta = stablehlo.transpose %arg0, dims = {perm} : ({sa}) -> {ty(m, k).format('bf16')}")
+        lhs = "%ta"
+    if bt:
+        body.append(f"    %tb = stablehlo.transpose %arg1, dims = {perm} : ({sb}) -> {ty(k, n).format('bf16')}")
+        rhs = "%tb"
+    dims = "batching_dims = [0] x [0], contracting_dims = [2] x [1]" if batch else "contracting_dims = [1] x [0]"
+    out = ty(m, n).format("f32")
+    body.append(f"    %0 = stablehlo.dot_general {lhs}, {rhs}, {dims} : "
+                f"({ty(m, k).format('bf16')}, {ty(k, n).format('bf16')}) -> {out}")
+    return (f"module @{name} {{\n func.func @f(%arg0: {sa}, %arg1: {sb}) -> {out} {{\n" + "\n".join(body) +
+            f"\n    return %0 : {out}\n }}\n}}\n")
+
+
+def _run_matmul(sess, m, n, k, layout, batch=0, seed=0):
+    rng = np.random.default_rng(seed)
+    pre = (batch,) if batch else ()
+    a = rng.standard_normal(pre + ((k, m) if layout[0] == "t" else (m, k)), dtype=np.float32)
+    b = rng.standard_normal(pre + ((n, k) if layout[1] == "t" else (k, n)), dtype=np.float32)
+    name = f"bf16mm_{m}_{n}_{k}_{layout}_{batch}_{seed}"
+    text = _matmul_module(name, m, n, k, layout, batch)
+    if not sess.has_function(f"{name}.f"):
+        sess.load_stablehlo(text)
+    outs = sess.call_device(f"{name}.f", [sess.buffer(a, bf16=True), sess.buffer(b, bf16=True)])
+    got = outs[0].to_host()
+    for o in outs:
+        o.release()
+    at, bt = _bf16_trunc(a).astype(np.float64), _bf16_trunc(b).astype(np.float64)
+    if layout[0] == "t":
+        at = np.swapaxes(at, -1, -2)
+    if layout[1] == "t":
+        bt = np.swapaxes(bt, -1, -2)
+    return got, at @ bt
+
+
+def _rel(o, r):
+    return float(np.linalg.norm(np.asarray(o, np.float64) - r) / max(np.linalg.norm(r), 1e-30))
+
+
+@pytest.mark.parametrize("layout", ["nn", "nt", "tn", "tt"])
+@pytest.mark.parametrize("shape", [(200, 136, 100), (384, 256, 320), (1024, 512, 256)])
+def test_bf16_matmul_layouts(fp32_session, layout, shape):
+    got, ref = _run_matmul(fp32_session, *shape, layout)
+    assert _rel(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("cfg", range(6))
+@pytest.mark.parametrize("layout", ["nn", "tn", "nt"])
+def test_bf16_matmul_every_tile_configuration(fp32_session, cfg, layout):
+    os.environ["SHEAF_B200_GEMM_CONFIG"] = str(cfg)
+    try:
+        got, ref = _run_matmul(fp32_session, 520, 384, 448, layout, seed=cfg)
+    finally:
+        del os.environ["SHEAF_B200_GEMM_CONFIG"]
+    assert _rel(got, ref) <= 1e-5
+
+
+def test_bf16_matmul_batched_and_split_k(fp32_session):
+    got, ref = _run_matmul(fp32_session, 256, 192, 128, "nt", batch=3)
+    assert _rel(got, ref) <= 1e-5
+    got, ref = _run_matmul(fp32_session, 128, 128, 8192, "nn")  # one tile: K is split
+    assert _rel(got, ref) <= 1e-5
+
+
+def test_bf16_elementwise_and_reductions(fp32_session):
+    t = "tensor<512x384x{}>"
+    text = f"""module @bf16ops {{
+ func.func @f(%arg0: {t.format('f32')}, %arg1: {t.format('bf16')}) -> ({t.format('bf16')}, tensor<512xbf16>, tensor<384xf32>) {{
+    %0 = stablehlo.convert %arg0 : ({t.format('f32')}) -> {t.format('bf16')}
+    %1 = stablehlo.multiply %0, %arg1 : {t.format('bf16')}
+    %2 = stablehlo.exponential %1 : {t.format('bf16')}
+    %3 = stablehlo.add %2, %0 : {t.format('bf16')}
+    %c = stablehlo.constant dense<0.000000e+00> : tensor<bf16>
+    %4 = stablehlo.reduce(%3 init: %c) applies stablehlo.add across dimensions = [1] : ({t.format('bf16')}, tensor<bf16>) -> tensor<512xbf16>
+    %5 = stablehlo.convert %3 : ({t.format('bf16')}) -> {t.format('f32')}
+    %cf = stablehlo.constant dense<0.000000e+00> : tensor<f32>
+    %6 = stablehlo.reduce(%5 init: %cf) applies stablehlo.add across dimensions = [0] : ({t.format('f32')}, tensor<f32>) -> tensor<384xf32>
+    return %3, %4, %6 : {t.format('bf16')}, tensor<512xbf16>, tensor<384xf32>
+ }}
+}}
+"""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((512, 384), dtype=np.float32)
+    y = rng.standard_normal((512, 384), dtype=np.float32) * 0.5
+    fp32_session.load_stablehlo(text)
+    outs = fp32_session.call_device("bf16ops.f", [fp32_session.buffer(x), fp32_session.buffer(y, bf16=True)])
+    got = [o.to_host() for o in outs]
+    ref = run(text, "bf16ops.f", [x, y], dtype=np.float32)
+    # element-wise: equal up to one bf16 unit (exp of two math libraries)
+    np.testing.assert_allclose(got[0], ref[0], rtol=2 ** -7, atol=1e-6)
+    assert np.mean(got[0] == ref[0]) > 0.9
+    np.testing.assert_allclose(got[1], ref[1], rtol=2 ** -7, atol=1e-3)
+    np.testing.assert_allclose(got[2], ref[2], rtol=1e-4, atol=1e-3)
+
+
+def test_bf16_precision_nanogpt_dims_value_and_grad(bf16_session):
+    """nanoGPT model dimensions (6 layers, D384, H6, T256, V65) at batch 4,
+    bf16 contractions, against the f64 oracle."""
+    low = M.gpt_vag(M.NANOGPT, batch=4)
+    inp = M.gpt_inputs(M.NANOGPT, batch=4, seed=0)
+    ins = [inp[n] for n in low.arg_names]
+    if not bf16_session.has_function(low.qualified):
+        bf16_session.load_stablehlo(low.text)
+    outs = bf16_session.call(low.qualified, ins)
+    ref = run(low.text, low.qualified, ins)
+    assert abs(float(outs[0]) - float(ref[0])) <= 5e-3 * abs(float(ref[0]))
+    errs = [_rel(o, r) for o, r in zip(outs[1:], ref[1:])]
+    assert max(errs) <= 2e-2, max(errs)
