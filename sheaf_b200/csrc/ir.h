@@ -61,6 +61,11 @@ enum class OpKind : uint8_t {
   // the planner's sibling-GEMM merge, never parsed: element i of the result
   // is operand_flat[a0[0] + sum_d i_d * a2[d]].  A pure index map.
   StridedView,
+  // Row scatter-add, created by the planner's embedding-gradient rewrite,
+  // never parsed.  Operands: idx (n index values, f32 or i32), adj (n rows of
+  // d, row-major).  Result [V, d]: row k = sum of the adj rows whose index is
+  // k, in row order (indices that are not integers in [0, V) hit no row).
+  ScatterAddRows,
 };
 const char* opkind_name(OpKind k);
 

@@ -1,0 +1,185 @@
+// Row scatter-add: out[v, :] = sum of adj[r, :] over the rows r whose index
+// key(r) equals v, r in increasing order; rows of out that no key hits are 0.
+//
+// This is the gradient of an embedding lookup (table[idx]).  Sheaf's reverse-
+// mode rule writes it as transpose(one_hot(idx, V)) @ adj
+// (sheaf/src/autodiff/reverse.rs:1015-1041); the planner replaces that product
+// by this op (csrc/embed_grad.cpp).  Keys are the index values: f32 (Sheaf
+// passes token ids as f32) or i32; a key that is not an integer in [0, V) hits
+// no row, as its one-hot row is all zeros.
+//
+// Deterministic, no floating-point atomics: the rows are put in (key, row)
+// order by a stable counting sort, and each output row is summed by one warp
+// in that order.
+//   1. per chunk of kChunk rows, a key histogram (integer atomics: the counts
+//      do not depend on the order of the increments);
+//   2. per key, the exclusive prefix of the chunk counts (where the chunk's
+//      rows of that key start among all rows of that key) and the total;
+//   3. the exclusive prefix of the totals over the keys (segment starts);
+//   4. per row, its position in the sorted order: segment start + chunk
+//      prefix + the number of earlier rows of the same key inside the chunk;
+//   5. per key, one warp sums its segment's adj rows (float4 columns).
+#include <algorithm>
+
+#include "kernels.h"
+#include "pdl.h"
+
+namespace sb {
+namespace {
+
+constexpr int kChunk = 1024;
+constexpr int kThreads = 256;
+
+// Index of row r, or v when it hits no row.
+__device__ __forceinline__ int key_of(const void* idx, int idx_f32, int64_t r, int v) {
+  if (idx_f32) {
+    const float x = ((const float*)idx)[r];
+    // integers in [0, v) only (NaN fails both comparisons)
+    if (!(x >= 0.f && x < (float)v) || x != floorf(x)) return v;
+    return (int)x;
+  }
+  const int k = ((const int*)idx)[r];
+  return (k >= 0 && k < v) ? k : v;
+}
+
+__global__ void __launch_bounds__(kThreads) hist_kernel(const void* idx, int idx_f32, int64_t n, int v,
+                                                        int* __restrict__ hist) {
+  pdl_prologue();
+  const int64_t c = blockIdx.x;
+  const int64_t r0 = c * kChunk, r1 = min(n, r0 + kChunk);
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += kThreads) {
+    const int k = key_of(idx, idx_f32, r, v);
+    if (k < v) atomicAdd(&hist[c * v + k], 1);
+  }
+}
+
+// hist[c][k] := rows of key k in chunks before c; total[k] := all rows of key k
+__global__ void __launch_bounds__(kThreads) colscan_kernel(int* __restrict__ hist, int* __restrict__ total,
+                                                           int chunks, int v) {
+  pdl_prologue();
+  for (int k = blockIdx.x * kThreads + threadIdx.x; k < v; k += gridDim.x * kThreads) {
+    int run = 0;
+    for (int c = 0; c < chunks; ++c) {
+      const int t = hist[(int64_t)c * v + k];
+      hist[(int64_t)c * v + k] = run;
+      run += t;
+    }
+    total[k] = run;
+  }
+}
+
+// offs[k] := exclusive prefix of total over keys, offs[v] = rows with a key
+__global__ void __launch_bounds__(1024) offsets_kernel(const int* __restrict__ total, int* __restrict__ offs, int v) {
+  pdl_prologue();
+  __shared__ int part[1024];
+  const int per = (v + 1023) / 1024;
+  const int k0 = threadIdx.x * per, k1 = min(v, k0 + per);
+  int s = 0;
+  for (int k = k0; k < k1; ++k) s += total[k];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  // inclusive scan of the 1024 partial sums (Hillis-Steele)
+  for (int d = 1; d < 1024; d <<= 1) {
+    const int x = threadIdx.x >= d ? part[threadIdx.x - d] : 0;
+    __syncthreads();
+    part[threadIdx.x] += x;
+    __syncthreads();
+  }
+  int run = threadIdx.x ? part[threadIdx.x - 1] : 0;
+  for (int k = k0; k < k1; ++k) {
+    offs[k] = run;
+    run += total[k];
+  }
+  if (threadIdx.x == 1023) offs[v] = part[1023];
+}
+
+__global__ void __launch_bounds__(kThreads) place_kernel(const void* idx, int idx_f32, int64_t n, int v,
+                                                         const int* __restrict__ hist, const int* __restrict__ offs,
+                                                         int* __restrict__ perm) {
+  pdl_prologue();
+  __shared__ int keys[kChunk];
+  const int64_t c = blockIdx.x;
+  const int64_t r0 = c * kChunk;
+  const int m = (int)(n - r0 < kChunk ? n - r0 : kChunk);
+  for (int i = threadIdx.x; i < m; i += kThreads) keys[i] = key_of(idx, idx_f32, r0 + i, v);
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += kThreads) {
+    const int k = keys[i];
+    if (k >= v) continue;
+    int lr = 0;
+    for (int j = 0; j < i; ++j) lr += keys[j] == k;
+    perm[offs[k] + hist[c * v + k] + lr] = (int)(r0 + i);
+  }
+}
+
+// one warp per output row k: out[k, :] = sum over its segment, in order
+__global__ void __launch_bounds__(kThreads) segsum_kernel(const float* __restrict__ adj, const int* __restrict__ offs,
+                                                          const int* __restrict__ perm, float* __restrict__ out,
+                                                          int v, int64_t d, int vec) {
+  pdl_prologue();
+  const int lane = threadIdx.x & 31;
+  const int warps = kThreads / 32;
+  for (int64_t k = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); k < v; k += (int64_t)gridDim.x * warps) {
+    const int s0 = offs[k], s1 = offs[k + 1];
+    float* o = out + k * d;
+    if (vec) {
+      for (int64_t col = lane * 4; col < d; col += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = s0; s < s1; ++s) {
+          const float4 x = *(const float4*)(adj + (int64_t)perm[s] * d + col);
+          acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+        }
+        *(float4*)(o + col) = acc;
+      }
+    } else {
+      for (int64_t col = lane; col < d; col += 32) {
+        float acc = 0.f;
+        for (int s = s0; s < s1; ++s) acc += adj[(int64_t)perm[s] * d + col];
+        o[col] = acc;
+      }
+    }
+  }
+}
+
+int64_t chunks_of(int64_t n) { return (n + kChunk - 1) / kChunk; }
+
+}  // namespace
+
+size_t scatter_add_rows_workspace(int64_t n, int64_t v) {
+  // hist [chunks][v], total [v], offs [v + 1], perm [n] (ints)
+  return (size_t)(chunks_of(n) * v + v + (v + 1) + n) * sizeof(int);
+}
+
+cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, float* out, int64_t n, int64_t d,
+                             int64_t v, void* ws, cudaStream_t stream) {
+  if (v <= 0 || d <= 0) return cudaSuccess;
+  if (n < 0 || v >= (1ll << 31) - 1 || n >= (1ll << 31)) return cudaErrorInvalidValue;
+  const int64_t chunks = chunks_of(n);
+  int* hist = (int*)ws;
+  int* total = hist + chunks * v;
+  int* offs = total + v;
+  int* perm = offs + v + 1;
+  cudaError_t e;
+  if (n > 0) {
+    e = cudaMemsetAsync(hist, 0, (size_t)(chunks * v) * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(hist_kernel, dim3((unsigned)chunks), dim3(kThreads), 0, stream, idx, (int)idx_f32, n, (int)v, hist);
+    if (e != cudaSuccess) return e;
+  }
+  const unsigned vb = (unsigned)std::min<int64_t>((v + kThreads - 1) / kThreads, 148 * 8);
+  e = launch_pdl(colscan_kernel, dim3(vb), dim3(kThreads), 0, stream, hist, total, (int)chunks, (int)v);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(offsets_kernel, dim3(1), dim3(1024), 0, stream, (const int*)total, offs, (int)v);
+  if (e != cudaSuccess) return e;
+  if (n > 0) {
+    e = launch_pdl(place_kernel, dim3((unsigned)chunks), dim3(kThreads), 0, stream, idx, (int)idx_f32, n, (int)v,
+                   (const int*)hist, (const int*)offs, perm);
+    if (e != cudaSuccess) return e;
+  }
+  const int vec = (d % 4 == 0) && ((((uintptr_t)adj) | ((uintptr_t)out)) & 15) == 0;
+  const unsigned sb = (unsigned)std::min<int64_t>((v + kThreads / 32 - 1) / (kThreads / 32), 148 * 16);
+  return launch_pdl(segsum_kernel, dim3(sb), dim3(kThreads), 0, stream, adj, (const int*)offs, (const int*)perm, out,
+                    (int)v, d, vec);
+}
+
+}  // namespace sb

@@ -40,7 +40,7 @@ const char* opkind_name(OpKind k) {
       "negate", "sine", "cosine", "not", "sign", "floor", "ceil", "logistic", "clamp",
       "convert", "select", "compare", "broadcast_in_dim", "reshape", "transpose", "iota",
       "slice", "pad", "concatenate", "reverse", "reduce", "dot_general", "gather",
-      "attention_fwd", "attention_bwd", "bitcast_convert", "sort", "strided_view"};
+      "attention_fwd", "attention_bwd", "bitcast_convert", "sort", "strided_view", "scatter_add_rows"};
   return names[(int)k];
 }
 

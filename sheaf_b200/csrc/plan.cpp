@@ -25,6 +25,7 @@
 #include <stdexcept>
 
 #include "codegen.h"
+#include "kernels/kernels.h"
 
 namespace sb {
 
@@ -126,7 +127,7 @@ struct Planner {
       if (!live[op.result]) continue;
       for (int s = 0; s < (int)op.operands.size(); ++s) consumers[op.operands[s]].push_back({i, s});
       // the sort kernel reads dense buffers: its operands are materialized
-      if (op.kind == OpKind::SortPairs)
+      if (op.kind == OpKind::SortPairs || op.kind == OpKind::ScatterAddRows)
         for (int o : op.operands) forced.insert(o);
     }
     find_batch_reduced_dots();
@@ -267,7 +268,8 @@ struct Planner {
   void collect(int v, std::set<int>& cs, bool& blocked, std::set<int>& seen) {
     for (auto [oi, slot] : consumers[v]) {
       const Op& c = f.ops[oi];
-      if (c.kind == OpKind::DotGeneral || is_attention(c.kind) || c.kind == OpKind::SortPairs) {
+      if (c.kind == OpKind::DotGeneral || is_attention(c.kind) || c.kind == OpKind::SortPairs ||
+          c.kind == OpKind::ScatterAddRows) {
         blocked = true;
         continue;
       }
@@ -378,7 +380,7 @@ struct Planner {
       for (auto& [rv, di] : fused_dot) if (di == i) absorbed = true;
       if (absorbed) { cluster[v] = kAbsorbed; continue; }
       if (returned[v] || forced.count(v) || op.kind == OpKind::Reduce || op.kind == OpKind::DotGeneral ||
-          is_attention(op.kind) || op.kind == OpKind::SortPairs) {
+          is_attention(op.kind) || op.kind == OpKind::SortPairs || op.kind == OpKind::ScatterAddRows) {
         cluster[v] = v;
         continue;
       }
@@ -726,6 +728,15 @@ void verify(const Function& f) {
       case OpKind::Constant:
         need(op.values.size() == 1 || (int64_t)op.values.size() == op.type.numel(), "constant payload size");
         break;
+      case OpKind::ScatterAddRows: {
+        const Type& ix = T(op.operands[0]);
+        const Type& ad = T(op.operands[1]);
+        need(op.operands.size() == 2 && rs.size() == 2 && !ad.shape.empty() && ad.shape.back() == rs[1] &&
+                 ix.numel() * rs[1] == ad.numel() && (ix.dtype == DType::F32 || ix.dtype == DType::I32) &&
+                 ad.dtype == DType::F32 && op.type.dtype == DType::F32,
+             "scatter_add_rows operand shapes");
+        break;
+      }
       case OpKind::SortPairs:
         need(op.operands.size() == 2 && T(op.operands[0]).shape == T(op.operands[1]).shape && !rs.empty() &&
                  rs.back() == 2 * T(op.operands[0]).shape.back(),
@@ -1130,7 +1141,8 @@ Plan plan_function(const Function& f, Precision prec) {
     const Op& op = f.ops[i];
     int v = op.result;
     if (!pl.live[v] || pl.cluster[v] != v) continue;
-    const bool generated = !(pl.is_gemm_root(op) || is_attention(op.kind) || op.kind == OpKind::SortPairs);
+    const bool generated = !(pl.is_gemm_root(op) || is_attention(op.kind) || op.kind == OpKind::SortPairs ||
+                             op.kind == OpKind::ScatterAddRows);
     if (generated) {
       int64_t R = 0, C = 0;
       CodeGen::RowMember m{};
@@ -1223,6 +1235,19 @@ Plan plan_function(const Function& f, Precision prec) {
         st.flops = 7 * prod;
         st.bytes_moved = 4 * ((5 * N + R + N + R) + (4 * N + 2 * R + 2 * N));
       }
+    } else if (op.kind == OpKind::ScatterAddRows) {
+      st.kind = StepKind::Scatter;
+      for (int o : op.operands)
+        if (!pl.materialized(o)) fail(op, "internal: scatter operand is not materialized");
+      st.leaves = {op.operands[0], op.operands[1]};
+      const int64_t n = f.value_types[op.operands[0]].numel(), V = op.type.shape[0], D = op.type.shape[1];
+      st.gemm.M = V;
+      st.gemm.N = D;
+      st.gemm.K = n;
+      // workspace (ints) for the counting sort, in the step's scratch
+      st.scratch_elems = ((int64_t)scatter_add_rows_workspace(n, V) + 3) / 4;
+      st.splits = 1;
+      st.bytes_moved = 4 * (n + n * D + V * D);
     } else if (op.kind == OpKind::SortPairs) {
       // operands are materialized dense buffers (a sort consumer blocks fusion)
       st.kind = StepKind::Sort;
@@ -1339,6 +1364,8 @@ Plan plan_function(const Function& f, Precision prec) {
   for (int s = 0; s < (int)plan.steps.size(); ++s)
     for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], s);
   for (int s = 0; s < (int)plan.steps.size(); ++s) {
+    // a conversion step writes a shadow (placed below), not its root value
+    if (plan.steps[s].kind == StepKind::Convert) continue;
     std::vector<int> written{plan.steps[s].root};
     written.insert(written.end(), plan.steps[s].extra_roots.begin(), plan.steps[s].extra_roots.end());
     for (int v : written) {
@@ -1559,6 +1586,13 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
   std::string log;
   if ((prec == Precision::TF32 || prec == Precision::BF16) && fuse_attention)
     cur.reset(rewrite_attention(f, &log).release());
+  {
+    std::string elog;
+    if (auto m = rewrite_embedding_grad(cur ? *cur : f, &elog)) {
+      cur.reset(m.release());
+      log += (log.empty() ? "" : "; ") + elog;
+    }
+  }
   if (auto m = merge_reduce_chains(cur ? *cur : f)) cur.reset(m.release());
   if (auto m = transpose_dot_outputs(cur ? *cur : f)) cur.reset(m.release());
   std::string mlog;
@@ -1579,7 +1613,7 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention) {
 std::string Plan::summary() const {
   std::ostringstream os;
   os.precision(17);
-  int loops = 0, reds = 0, gemms = 0, attn = 0, sorts = 0, converts = 0;
+  int loops = 0, reds = 0, gemms = 0, attn = 0, sorts = 0, converts = 0, scatters = 0;
   double flops = 0, aflops = 0;
   for (auto& s : steps) {
     if (s.kind == StepKind::Loop) ++loops;
@@ -1587,12 +1621,14 @@ std::string Plan::summary() const {
     else if (s.kind == StepKind::Attn) { ++attn; aflops += s.flops; continue; }
     else if (s.kind == StepKind::Sort) { ++sorts; continue; }
     else if (s.kind == StepKind::Convert) { ++converts; continue; }
+    else if (s.kind == StepKind::Scatter) { ++scatters; continue; }
     else ++gemms;
     flops += s.flops;
   }
   os << "steps=" << steps.size() << " loop=" << loops << " reduce=" << reds << " gemm=" << gemms
      << " attention=" << attn << (sorts ? " sort=" + std::to_string(sorts) : std::string())
-     << (converts ? " convert=" + std::to_string(converts) : std::string()) << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
+     << (converts ? " convert=" + std::to_string(converts) : std::string())
+     << (scatters ? " scatter=" + std::to_string(scatters) : std::string()) << " constants=" << constants.size() << " arena_bytes=" << arena_bytes
      << " gemm_flops=" << flops << " attention_flops=" << aflops;
   return os.str();
 }

@@ -61,7 +61,7 @@ struct AttnDesc {
   bool round_out = false;  // Y / dQ / dK / dV stored rounded to TF32
 };
 
-enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort, Convert };
+enum class StepKind : uint8_t { Loop, Reduce, Gemm, Attn, Sort, Convert, Scatter };
 
 struct Step {
   StepKind kind = StepKind::Loop;
@@ -110,6 +110,11 @@ Plan build_plan(const Function& f, Precision prec, bool fuse_attention = true);
 // Replaces attention regions (and their reverse-mode gradients) by fused
 // attention ops.  Returns nullptr when nothing matched (attn_rewrite.cpp).
 std::unique_ptr<Function> rewrite_attention(const Function& f, std::string* log);
+
+// Replaces transpose(one_hot(idx, V)) @ adj (+ its batch reduce), Sheaf's
+// embedding gradient, by OpKind::ScatterAddRows (embed_grad.cpp).  Returns
+// nullptr when nothing matched.
+std::unique_ptr<Function> rewrite_embedding_grad(const Function& f, std::string* log);
 
 // Merges sibling GEMMs: dot_generals (or batch-reduced dot_generals) that
 // share one operand while their other operands are adjacent blocks of one

@@ -363,6 +363,7 @@ std::string step_name(const Step& st) {
   if (st.kind == StepKind::Gemm) return "gemm";
   if (st.kind == StepKind::Sort) return "sort";
   if (st.kind == StepKind::Convert) return "operand_shadow";
+  if (st.kind == StepKind::Scatter) return "scatter_add_rows";
   if (st.kind == StepKind::Attn)
     return st.attn.kind == OpKind::AttnFwd ? "attn_fwd" : "attn_bwd";
   return st.kernel;
@@ -558,6 +559,14 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
       if (tc) s->used_tc = true;
       if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
+      continue;
+    }
+    if (st.kind == StepKind::Scatter) {
+      const bool f32 = f.value_types[st.leaves[0]].dtype == DType::F32;
+      cudaError_t e = scatter_add_rows(ptr[st.leaves[0]], f32, (const float*)ptr[st.leaves[1]], (float*)ptr[st.root],
+                                       st.gemm.K, st.gemm.N, st.gemm.M, (char*)lf->arena + plan.scratch_offset[si],
+                                       stream);
+      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "scatter_add_rows"); }
       continue;
     }
     if (st.kind == StepKind::Sort) {
@@ -827,7 +836,7 @@ sb_status* sb_session_profile_report(sb_session* s, int reset, char* out, size_t
   std::ostringstream os;
   os.precision(9);
   os << "function,step,kind,kernel,calls,total_ms,elements,bytes,flops,launches_per_call\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert", "scatter"};
   for (auto& m : s->modules)
     for (auto& lf : m->fns) {
       if (lf->prof_ms.empty()) continue;
@@ -1201,7 +1210,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   std::ostringstream os;
   os.precision(17);
   os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
-  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert"};
+  static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert", "scatter"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
     const GemmDesc& g = st.gemm;

@@ -52,6 +52,12 @@ def test_noalloc_gemm_matches_session_gemm_on_two_calls(lib, fp32_session, shape
         a, b = fp32_session.buffer(a_h), fp32_session.buffer(b_h)
         c = fp32_session.buffer(np.full((m, n), np.nan, np.float32))
         cases.append((m, n, k, a, b, c, ref))
+    # the first call on the device looks up the static array's address, which
+    # makes CUDA load the module holding it (lazy loading): the array's 16 MiB
+    # appear then, once per process, like any module's code and data
+    w = fp32_session.buffer(np.zeros((128, 2048), np.float32))
+    assert _noalloc(lib, fp32_session, w, fp32_session.buffer(np.zeros((2048, 128), np.float32)),
+                    fp32_session.buffer(np.zeros((128, 128), np.float32)), 128, 128, 2048) == 0
     fp32_session.synchronize()
     free_before = _device_free_bytes()
     for m, n, k, a, b, c, _ in cases:
