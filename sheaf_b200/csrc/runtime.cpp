@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <functional>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -105,6 +106,12 @@ struct Device {
 }  // namespace
 }  // namespace sb
 
+namespace sb {
+namespace {
+struct OutSlot;
+}
+}  // namespace sb
+
 struct sb_buffer {
   std::atomic<int> refs{1};
   std::shared_ptr<sb::Device> dev;
@@ -112,6 +119,7 @@ struct sb_buffer {
   size_t bytes = 0;
   bool owned = false;
   sb::Type type;
+  std::shared_ptr<sb::OutSlot> slot;  // output of a graph replay: memory owned by the slot
 };
 
 namespace sb {
@@ -135,6 +143,26 @@ sb_buffer* new_device_buffer(const std::shared_ptr<Device>& dev, const Type& t, 
   return b;
 }
 
+// Output memory of one replayable CUDA graph of a function: every output of a
+// call lives in one allocation; the sb_buffers returned by the call share it
+// and hand it back (held drops to 0) once they are all released, after which
+// the next call can replay the graph into the same memory.
+struct OutSlot {
+  std::shared_ptr<Device> dev;
+  void* base = nullptr;
+  std::vector<size_t> off;          // byte offset of each output
+  std::atomic<int> held{0};         // outputs of the last replay still referenced
+  cudaGraphExec_t exec = nullptr;   // the function's steps, captured with these outputs
+  std::vector<void*> direct_in;     // input addresses baked into exec (staged inputs: nullptr)
+  uint64_t kernels = 0;             // kernels in exec
+  ~OutSlot() {
+    if (!dev) return;
+    cudaSetDevice(dev->ordinal);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (base) cudaFree(base);
+  }
+};
+
 struct LoadedFunction {
   std::string qname;
   const Function* fn = nullptr;
@@ -149,6 +177,12 @@ struct LoadedFunction {
   void* ws = nullptr;
   size_t ws_cap = 0;
   uint64_t calls = 0;
+  // CUDA-graph replay (see run_graph)
+  std::vector<std::shared_ptr<OutSlot>> slots;
+  std::vector<void*> last_in;      // input addresses of the previous call
+  std::vector<char> staged;        // per input: the graph reads a staging copy
+  std::vector<void*> stage_buf;    // the staging copies (library-owned)
+  bool graphs_off = false;         // capture failed: eager from now on
 };
 
 struct LoadedModule {
@@ -388,6 +422,322 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
   return nullptr;
 }
 
+// Enqueues a call's work on `stream`: TF32 copies of parameters, every plan
+// step, and the copies of outputs that no step writes (to outp[j]).  ptr holds
+// the device address of every materialized value.  before(si), if set, runs
+// before step si is enqueued (the data-parallel bucket flushes).  capturing:
+// the stream is being captured into a graph, so nothing may allocate.
+sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& ptr, const std::vector<void*>& outp,
+                         const std::function<sb_status*(size_t)>& before, bool capturing) {
+  const Function& f = *lf->plan.fn;
+  const Plan& plan = lf->plan;
+  cudaStream_t stream = s->dev->stream;
+  // TF32-rounded copies of parameters read by tensor-core GEMMs
+  std::map<int, const float*> rounded;
+  for (size_t j = 0; j < plan.rounded_params.size(); ++j) {
+    int v = plan.rounded_params[j];
+    float* dst = (float*)((char*)lf->arena + plan.rounded_offset[j]);
+    cudaError_t e = round_tf32_copy((const float*)ptr[v], dst, f.value_types[v].numel(), stream);
+    if (e != cudaSuccess) { return cuda_status(e, "round_tf32_copy"); }
+    rounded[v] = dst;
+  }
+  std::vector<const void*> args;
+  for (size_t si = 0; si < plan.steps.size(); ++si) {
+    if (before)
+      if (sb_status* e = before(si)) return e;
+    const Step& st = plan.steps[si];
+    if (!ptr[st.root] && st.elements) { return make_status(SB_STATUS_INTERNAL, "unplaced value"); }
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    if (s->profiling) {
+      ev_a = s->event();
+      ev_b = s->event();
+      cudaEventRecord(ev_a, stream);
+      s->pending.push_back({lf, (int)si, ev_a, ev_b, launch_counter().load()});
+    }
+    struct EndEvent {
+      cudaEvent_t e;
+      cudaStream_t s;
+      sb_session* ss;
+      ~EndEvent() {
+        if (!e) return;
+        cudaEventRecord(e, s);
+        auto& p = ss->pending.back();
+        p.launches = launch_counter().load() - p.launches;
+      }
+    } end_event{ev_b, stream, s};
+    if (st.kind == StepKind::Convert) {
+      const Shadow& sh = plan.shadows[st.shadow];
+      char* dst = (char*)lf->arena + sh.offset;
+      const float* src = (const float*)ptr[sh.value];
+      cudaError_t e = sh.dtype == DType::BF16 ? bf16_copy(src, (uint16_t*)dst, st.elements, stream)
+                                              : round_tf32_copy(src, (float*)dst, st.elements, stream);
+      if (e != cudaSuccess) { return cuda_status(e, "operand shadow"); }
+      continue;
+    }
+    if (st.kind == StepKind::Gemm) {
+      const GemmDesc& g = st.gemm;
+      GemmArgs a;
+      // operand address: view offsets count elements of the buffer read (f32,
+      // or bf16 for bf16 operands and bf16 shadows)
+      auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
+        const int64_t es = g.bf16 ? 2 : 4;
+        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset + w.offset * es);
+        const char* base = rnd ? (const char*)rounded[w.value] : (const char*)ptr[w.value];
+        return (const float*)(base + w.offset * es);
+      };
+      a.a = operand(g.a, g.a_rounded, g.a_shadow);
+      a.b = operand(g.b, g.b_rounded, g.b_shadow);
+      a.bf16 = g.bf16 ? 1 : 0;
+      a.c = (float*)ptr[st.root];
+      a.round_out = g.round_out ? 1 : 0;
+      a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
+      a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
+      a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
+      a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
+      size_t need = gemm_workspace(a, s->opts.precision);
+      // a stream being captured into a graph must not allocate: the eager
+      // call that precedes every capture sized the workspace
+      if (need > lf->ws_cap && capturing) return make_status(SB_STATUS_UNAVAILABLE, "workspace grows during capture");
+      if (need > lf->ws_cap) {
+        if (lf->ws) cudaFreeAsync(lf->ws, stream);
+        if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+        else lf->ws_cap = need;
+      }
+      bool tc = false;
+      cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
+      if (tc) s->used_tc = true;
+      if (e != cudaSuccess) { return cuda_status(e, "gemm"); }
+      continue;
+    }
+    if (st.kind == StepKind::Scatter) {
+      const bool f32 = f.value_types[st.leaves[0]].dtype == DType::F32;
+      cudaError_t e = scatter_add_rows(ptr[st.leaves[0]], f32, (const float*)ptr[st.leaves[1]], (float*)ptr[st.root],
+                                       st.gemm.K, st.gemm.N, st.gemm.M, (char*)lf->arena + plan.scratch_offset[si],
+                                       stream);
+      if (e != cudaSuccess) { return cuda_status(e, "scatter_add_rows"); }
+      continue;
+    }
+    if (st.kind == StepKind::Sort) {
+      cudaError_t e = sort_pairs((const float*)ptr[st.leaves[0]], (const int*)ptr[st.leaves[1]], (float*)ptr[st.root],
+                                 st.gemm.M, st.gemm.N, st.gemm.K != 0, stream);
+      if (e != cudaSuccess) { return cuda_status(e, "sort"); }
+      continue;
+    }
+    if (st.kind == StepKind::Attn) {
+      const AttnDesc& d = st.attn;
+      AttnArgs a;
+      a.kind = AttnKind::Fwd;
+      a.B = d.B; a.H = d.H; a.T = d.T; a.hd = 64;
+      a.scale = (float)d.scale;
+      a.causal = d.causal;
+      a.round_out = d.round_out;
+      a.out = (float*)ptr[st.root];
+      auto view = [&](size_t i) {
+        const View& w = d.in[i];
+        AttnView r;
+        r.p = (d.rounded[i] ? rounded[w.value] : (const float*)ptr[w.value]) + w.offset;
+        r.sb = w.strides[0]; r.sh = w.strides[1]; r.st = w.strides[2];
+        return r;
+      };
+      a.q = view(0); a.k = view(1); a.v = view(2);
+      cudaError_t e = cudaSuccess;
+      if (d.kind == OpKind::AttnFwd) {
+        e = attention(a, stream);
+      } else {
+        // [dQ, dK, dV as (B,T,3,H,64) | D (B,H,T)]: the dQ pass writes dQ
+        // and D, the dK/dV pass reads D
+        const int64_t hd = d.H * 64, n = d.B * d.T * hd;
+        float* base = (float*)ptr[st.root];
+        const View& l = d.in[5];
+        a.dy = view(3);
+        a.y = view(4);
+        a.lse = (const float*)ptr[l.value] + l.offset;
+        a.l_sb = l.strides[0]; a.l_sh = l.strides[1]; a.l_st = l.strides[2];
+        a.out_ld = 3 * hd;
+        a.stats = base + 3 * n;
+        a.kind = AttnKind::BwdQ;
+        a.out = base;
+        e = attention(a, stream);
+        if (e == cudaSuccess) {
+          a.kind = AttnKind::BwdKV;
+          a.dsum = base + 3 * n;
+          a.d_sb = d.H * d.T; a.d_sh = d.T; a.d_st = 1;
+          a.out = base + hd;
+          a.out_v = base + 2 * hd;
+          a.stats = nullptr;
+          e = attention(a, stream);
+        }
+      }
+      s->used_tc = true;
+      if (e != cudaSuccess) { return cuda_status(e, "attention"); }
+      continue;
+    }
+    args.clear();
+    for (int l : st.leaves) args.push_back(ptr[l]);
+    args.push_back(ptr[st.root]);
+    for (int e : st.extra_roots) args.push_back(ptr[e]);
+    void* scratch = nullptr;
+    if (st.splits > 1) {
+      scratch = (char*)lf->arena + plan.scratch_offset[si];
+      args.push_back(scratch);
+    }
+    sb_status* e = launch_generated(lf->kern[si], args, st.grid, st.grid_y, st.block, stream);
+    if (e) { return e; }
+    if (st.splits > 1) {
+      e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
+      if (e) { return e; }
+    }
+  }
+  // outputs not written by a step: copies
+  for (size_t j = 0; j < f.returns.size(); ++j) {
+    if (plan.output_step[j] >= 0) continue;
+    int v = f.returns[j];
+    const size_t bytes = (size_t)f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype);
+    if (bytes && ptr[v]) SB_CUDA(cudaMemcpyAsync(outp[j], ptr[v], bytes, cudaMemcpyDeviceToDevice, stream));
+  }
+  return nullptr;
+}
+
+// CUDA-graph replay of a function.  Launching ~150-300 kernels per call costs
+// the host milliseconds (tensor-map encoding, launch calls), as much as the
+// GPU needs for the step itself at small batch.  From the second call on, the
+// function's steps are captured once into a graph and replayed: one launch per
+// call.  A graph bakes in addresses, so
+//  * outputs go to library-owned slots (OutSlot): a replay needs a slot whose
+//    outputs the caller has released; up to kMaxSlots slots are kept;
+//  * inputs whose address changed since the previous call (a new token batch
+//    each step) are "staged": the graph reads a library-owned copy, refreshed
+//    by one device-to-device copy per call; inputs at a stable address (the
+//    resident parameters) are read in place, and a change of one of them
+//    recaptures the slot's graph.
+// The first call runs eagerly (it also picks the GEMM tile configurations and
+// sizes the workspace), so capture never allocates.  Data-parallel calls with
+// a reduction and profiled calls always run eagerly.  *used = false: the
+// caller runs the call eagerly.
+constexpr int kMaxSlots = 4;
+constexpr size_t kMaxStagedBytes = 64u << 20;
+
+bool graphs_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SHEAF_B200_GRAPHS");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
+sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin, sb_buffer** out,
+                     size_t* nout, bool* used) {
+  *used = false;
+  const Function& f = *lf->plan.fn;
+  const Plan& plan = lf->plan;
+  cudaStream_t stream = s->dev->stream;
+  const bool first = lf->calls == 0;
+  if (lf->last_in.size() != nin) {
+    lf->last_in.assign(nin, nullptr);
+    lf->staged.assign(nin, 0);
+    lf->stage_buf.assign(nin, nullptr);
+  }
+  // inputs that moved since the previous call are staged from now on
+  bool restage = false;
+  for (size_t i = 0; i < nin; ++i) {
+    if (!first && !lf->staged[i] && in[i]->ptr != lf->last_in[i] && in[i]->bytes <= kMaxStagedBytes) {
+      lf->staged[i] = 1;
+      restage = true;
+    }
+    lf->last_in[i] = in[i]->ptr;
+  }
+  if (first) return nullptr;  // eager: tunes the GEMMs, sizes the workspace
+  if (restage)                // graphs captured before read those inputs in place
+    for (auto& sl : lf->slots)
+      if (sl->exec) {
+        cudaGraphExecDestroy(sl->exec);
+        sl->exec = nullptr;
+      }
+  for (size_t i = 0; i < nin; ++i)
+    if (lf->staged[i] && !lf->stage_buf[i] && in[i]->bytes)
+      SB_CUDA(cudaMalloc(&lf->stage_buf[i], in[i]->bytes));
+  // a slot whose outputs are free, preferring one whose graph reads these inputs
+  std::vector<void*> direct(nin, nullptr);
+  for (size_t i = 0; i < nin; ++i)
+    if (!lf->staged[i]) direct[i] = in[i]->ptr;
+  std::shared_ptr<OutSlot> slot;
+  for (auto& sl : lf->slots)
+    if (sl->held.load() == 0 && sl->exec && sl->direct_in == direct) { slot = sl; break; }
+  if (!slot)
+    for (auto& sl : lf->slots)
+      if (sl->held.load() == 0) { slot = sl; break; }
+  if (!slot) {
+    if ((int)lf->slots.size() >= kMaxSlots) return nullptr;  // all outputs held: eager
+    auto sl = std::make_shared<OutSlot>();
+    sl->dev = s->dev;
+    size_t total = 0;
+    for (int v : f.returns) {
+      sl->off.push_back(total);
+      total += ((size_t)f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype) + 255) & ~size_t(255);
+    }
+    if (total) SB_CUDA(cudaMalloc(&sl->base, total));
+    lf->slots.push_back(sl);
+    slot = sl;
+  }
+  std::vector<void*> outp(f.returns.size());
+  for (size_t j = 0; j < outp.size(); ++j) outp[j] = (char*)slot->base + slot->off[j];
+  if (!slot->exec || slot->direct_in != direct) {
+    if (slot->exec) {
+      cudaGraphExecDestroy(slot->exec);
+      slot->exec = nullptr;
+    }
+    std::vector<void*> ptr(f.num_values(), nullptr);
+    for (size_t i = 0; i < nin; ++i) ptr[i] = lf->staged[i] ? lf->stage_buf[i] : in[i]->ptr;
+    for (auto& [v, p] : lf->const_ptr) ptr[v] = p;
+    for (size_t j = 0; j < f.returns.size(); ++j)
+      if (plan.output_step[j] >= 0) ptr[f.returns[j]] = outp[j];
+    for (int v : plan.materialized)
+      if (!ptr[v] && plan.value_offset[v] >= 0) ptr[v] = (char*)lf->arena + plan.value_offset[v];
+    SB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    const uint64_t k0 = launch_counter().load();
+    sb_status* st = enqueue_steps(s, lf, ptr, outp, nullptr, true);
+    // kernels recorded into the graph (counted by the launch paths; taken
+    // back off the counter, which counts kernels that run)
+    slot->kernels = launch_counter().load() - k0;
+    launch_counter().fetch_sub(slot->kernels, std::memory_order_relaxed);
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(stream, &graph);
+    if (!st && e == cudaSuccess) e = cudaGraphInstantiate(&slot->exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (st || e != cudaSuccess) {
+      // not capturable (e.g. the workspace would have to grow): eager from now on
+      if (st) sb_status_free(st);
+      cudaGetLastError();
+      slot->exec = nullptr;
+      lf->graphs_off = true;
+      return nullptr;
+    }
+    slot->direct_in = direct;
+  }
+  // refresh the staged inputs, then replay
+  for (size_t i = 0; i < nin; ++i)
+    if (lf->staged[i] && in[i]->bytes)
+      SB_CUDA(cudaMemcpyAsync(lf->stage_buf[i], in[i]->ptr, in[i]->bytes, cudaMemcpyDeviceToDevice, stream));
+  SB_CUDA(cudaGraphLaunch(slot->exec, stream));
+  // the replay launches the captured kernels
+  launch_counter().fetch_add(slot->kernels, std::memory_order_relaxed);
+  for (size_t j = 0; j < f.returns.size(); ++j) {
+    auto* b = new sb_buffer();
+    b->dev = s->dev;
+    b->type = f.value_types[f.returns[j]];
+    b->bytes = (size_t)b->type.numel() * dtype_bytes(b->type.dtype);
+    b->ptr = outp[j];
+    b->owned = false;
+    b->slot = slot;
+    out[j] = b;
+  }
+  slot->held.store((int)f.returns.size());
+  *nout = f.returns.size();
+  lf->calls++;
+  *used = true;
+  return nullptr;
+}
+
 sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin,
                         const int32_t* reduce, sb_buffer** out, size_t cap, size_t* nout) {
   const Function& f = *lf->plan.fn;
@@ -408,6 +758,18 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   cudaStream_t stream = s->dev->stream;
   SB_CUDA(cudaSetDevice(s->dev->ordinal));
   const Plan& plan = lf->plan;
+  // calls without a data-parallel reduction replay a CUDA graph
+  bool no_reduce = true;
+  if (reduce && s->opts.world_size > 1) {
+    no_reduce = true;
+    for (size_t j = 0; j < f.returns.size(); ++j)
+      if (reduce[j] != SB_REDUCE_NONE) no_reduce = false;
+  }
+  if (graphs_enabled() && !s->profiling && no_reduce && !lf->graphs_off) {
+    bool used = false;
+    sb_status* st = run_graph(s, lf, in, nin, out, nout, &used);
+    if (st || used) return st;
+  }
   // outputs
   std::vector<sb_buffer*> outs(f.returns.size(), nullptr);
   auto cleanup = [&]() {
@@ -426,15 +788,6 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   for (int v : plan.materialized)
     if (!ptr[v] && plan.value_offset[v] >= 0) ptr[v] = (char*)lf->arena + plan.value_offset[v];
 
-  // TF32-rounded copies of parameters read by tensor-core GEMMs
-  std::map<int, const float*> rounded;
-  for (size_t j = 0; j < plan.rounded_params.size(); ++j) {
-    int v = plan.rounded_params[j];
-    float* dst = (float*)((char*)lf->arena + plan.rounded_offset[j]);
-    cudaError_t e = round_tf32_copy((const float*)ptr[v], dst, f.value_types[v].numel(), stream);
-    if (e != cudaSuccess) { cleanup(); return cuda_status(e, "round_tf32_copy"); }
-    rounded[v] = dst;
-  }
   // Data parallel, overlapped: each reduced output is all-reduced on the comm
   // stream once the step that writes it and every step that reads it have
   // been enqueued, in buckets of >= 8 MB (configurable), while later steps run
@@ -490,162 +843,19 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     comm_used = true;
     return nccl_settle(s);
   };
-  std::vector<const void*> args;
-  for (size_t si = 0; si < plan.steps.size(); ++si) {
-    if (overlap && si > 0) {
-      for (int j : ready_at[si - 1]) {
-        bucket.push_back(j);
-        bucket_bytes += outs[j]->bytes;
-      }
-      if (bucket_bytes >= bucket_limit)
-        if (sb_status* e = flush_bucket()) { cleanup(); return e; }
+  const std::function<sb_status*(size_t)> before = [&](size_t si) -> sb_status* {
+    if (!overlap || si == 0) return nullptr;
+    for (int j : ready_at[si - 1]) {
+      bucket.push_back(j);
+      bucket_bytes += outs[j]->bytes;
     }
-    const Step& st = plan.steps[si];
-    if (!ptr[st.root] && st.elements) { cleanup(); return make_status(SB_STATUS_INTERNAL, "unplaced value"); }
-    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
-    if (s->profiling) {
-      ev_a = s->event();
-      ev_b = s->event();
-      cudaEventRecord(ev_a, stream);
-      s->pending.push_back({lf, (int)si, ev_a, ev_b, launch_counter().load()});
-    }
-    struct EndEvent {
-      cudaEvent_t e;
-      cudaStream_t s;
-      sb_session* ss;
-      ~EndEvent() {
-        if (!e) return;
-        cudaEventRecord(e, s);
-        auto& p = ss->pending.back();
-        p.launches = launch_counter().load() - p.launches;
-      }
-    } end_event{ev_b, stream, s};
-    if (st.kind == StepKind::Convert) {
-      const Shadow& sh = plan.shadows[st.shadow];
-      char* dst = (char*)lf->arena + sh.offset;
-      const float* src = (const float*)ptr[sh.value];
-      cudaError_t e = sh.dtype == DType::BF16 ? bf16_copy(src, (uint16_t*)dst, st.elements, stream)
-                                              : round_tf32_copy(src, (float*)dst, st.elements, stream);
-      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "operand shadow"); }
-      continue;
-    }
-    if (st.kind == StepKind::Gemm) {
-      const GemmDesc& g = st.gemm;
-      GemmArgs a;
-      // operand address: view offsets count elements of the buffer read (f32,
-      // or bf16 for bf16 operands and bf16 shadows)
-      auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
-        const int64_t es = g.bf16 ? 2 : 4;
-        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset + w.offset * es);
-        const char* base = rnd ? (const char*)rounded[w.value] : (const char*)ptr[w.value];
-        return (const float*)(base + w.offset * es);
-      };
-      a.a = operand(g.a, g.a_rounded, g.a_shadow);
-      a.b = operand(g.b, g.b_rounded, g.b_shadow);
-      a.bf16 = g.bf16 ? 1 : 0;
-      a.c = (float*)ptr[st.root];
-      a.round_out = g.round_out ? 1 : 0;
-      a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
-      a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
-      a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
-      a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
-      size_t need = gemm_workspace(a, s->opts.precision);
-      if (need > lf->ws_cap) {
-        if (lf->ws) cudaFreeAsync(lf->ws, stream);
-        if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
-        else lf->ws_cap = need;
-      }
-      bool tc = false;
-      cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
-      if (tc) s->used_tc = true;
-      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "gemm"); }
-      continue;
-    }
-    if (st.kind == StepKind::Scatter) {
-      const bool f32 = f.value_types[st.leaves[0]].dtype == DType::F32;
-      cudaError_t e = scatter_add_rows(ptr[st.leaves[0]], f32, (const float*)ptr[st.leaves[1]], (float*)ptr[st.root],
-                                       st.gemm.K, st.gemm.N, st.gemm.M, (char*)lf->arena + plan.scratch_offset[si],
-                                       stream);
-      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "scatter_add_rows"); }
-      continue;
-    }
-    if (st.kind == StepKind::Sort) {
-      cudaError_t e = sort_pairs((const float*)ptr[st.leaves[0]], (const int*)ptr[st.leaves[1]], (float*)ptr[st.root],
-                                 st.gemm.M, st.gemm.N, st.gemm.K != 0, stream);
-      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "sort"); }
-      continue;
-    }
-    if (st.kind == StepKind::Attn) {
-      const AttnDesc& d = st.attn;
-      AttnArgs a;
-      a.kind = AttnKind::Fwd;
-      a.B = d.B; a.H = d.H; a.T = d.T; a.hd = 64;
-      a.scale = (float)d.scale;
-      a.causal = d.causal;
-      a.round_out = d.round_out;
-      a.out = (float*)ptr[st.root];
-      auto view = [&](size_t i) {
-        const View& w = d.in[i];
-        AttnView r;
-        r.p = (d.rounded[i] ? rounded[w.value] : (const float*)ptr[w.value]) + w.offset;
-        r.sb = w.strides[0]; r.sh = w.strides[1]; r.st = w.strides[2];
-        return r;
-      };
-      a.q = view(0); a.k = view(1); a.v = view(2);
-      cudaError_t e = cudaSuccess;
-      if (d.kind == OpKind::AttnFwd) {
-        e = attention(a, stream);
-      } else {
-        // [dQ, dK, dV as (B,T,3,H,64) | D (B,H,T)]: the dQ pass writes dQ
-        // and D, the dK/dV pass reads D
-        const int64_t hd = d.H * 64, n = d.B * d.T * hd;
-        float* base = (float*)ptr[st.root];
-        const View& l = d.in[5];
-        a.dy = view(3);
-        a.y = view(4);
-        a.lse = (const float*)ptr[l.value] + l.offset;
-        a.l_sb = l.strides[0]; a.l_sh = l.strides[1]; a.l_st = l.strides[2];
-        a.out_ld = 3 * hd;
-        a.stats = base + 3 * n;
-        a.kind = AttnKind::BwdQ;
-        a.out = base;
-        e = attention(a, stream);
-        if (e == cudaSuccess) {
-          a.kind = AttnKind::BwdKV;
-          a.dsum = base + 3 * n;
-          a.d_sb = d.H * d.T; a.d_sh = d.T; a.d_st = 1;
-          a.out = base + hd;
-          a.out_v = base + 2 * hd;
-          a.stats = nullptr;
-          e = attention(a, stream);
-        }
-      }
-      s->used_tc = true;
-      if (e != cudaSuccess) { cleanup(); return cuda_status(e, "attention"); }
-      continue;
-    }
-    args.clear();
-    for (int l : st.leaves) args.push_back(ptr[l]);
-    args.push_back(ptr[st.root]);
-    for (int e : st.extra_roots) args.push_back(ptr[e]);
-    void* scratch = nullptr;
-    if (st.splits > 1) {
-      scratch = (char*)lf->arena + plan.scratch_offset[si];
-      args.push_back(scratch);
-    }
-    sb_status* e = launch_generated(lf->kern[si], args, st.grid, st.grid_y, st.block, stream);
-    if (e) { cleanup(); return e; }
-    if (st.splits > 1) {
-      e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
-      if (e) { cleanup(); return e; }
-    }
-  }
-  // outputs not written by a step: copies
-  for (size_t j = 0; j < f.returns.size(); ++j) {
-    if (plan.output_step[j] >= 0) continue;
-    int v = f.returns[j];
-    if (outs[j]->bytes && ptr[v])
-      SB_CUDA(cudaMemcpyAsync(outs[j]->ptr, ptr[v], outs[j]->bytes, cudaMemcpyDeviceToDevice, stream));
+    if (bucket_bytes >= bucket_limit) return flush_bucket();
+    return nullptr;
+  };
+  {
+    std::vector<void*> outp(outs.size());
+    for (size_t j = 0; j < outs.size(); ++j) outp[j] = outs[j]->ptr;
+    if (sb_status* e = enqueue_steps(s, lf, ptr, outp, before, false)) { cleanup(); return e; }
   }
   // data-parallel combine of outputs
   if (overlap) {
@@ -782,6 +992,8 @@ void sb_session_release(sb_session* s) {
       for (auto& [v, p] : lf->const_ptr) cudaFree(p);
       if (lf->arena) cudaFree(lf->arena);
       if (lf->ws) cudaFree(lf->ws);
+      for (void* p : lf->stage_buf)
+        if (p) cudaFree(p);
     }
     for (auto lib : m->libs) cudaLibraryUnload(lib);
   }
@@ -1134,6 +1346,11 @@ void sb_buffer_retain(sb_buffer* b) {
 void sb_buffer_release(sb_buffer* b) {
   if (!b) return;
   if (b->refs.fetch_sub(1) != 1) return;
+  if (b->slot) {
+    b->slot->held.fetch_sub(1);
+    delete b;
+    return;
+  }
   if (b->owned && b->ptr && b->dev) {
     cudaSetDevice(b->dev->ordinal);
     cudaFreeAsync(b->ptr, b->dev->stream);

@@ -197,9 +197,23 @@ class DeviceBuffer:
         self._s = session
         self._h = handle
         self._keep = keepalive
-        lib = library()
-        self.shape = tuple(int(lib.sb_buffer_dim(handle, i)) for i in range(lib.sb_buffer_rank(handle)))
-        self.element_type = int(lib.sb_buffer_element_type(handle))
+        self._shape = None
+        self._et = None
+
+    # shape and element type are read from the library on first use (a call
+    # returns one buffer per gradient leaf; most are only passed on)
+    @property
+    def shape(self):
+        if self._shape is None:
+            lib = library()
+            self._shape = tuple(int(lib.sb_buffer_dim(self._h, i)) for i in range(lib.sb_buffer_rank(self._h)))
+        return self._shape
+
+    @property
+    def element_type(self):
+        if self._et is None:
+            self._et = int(library().sb_buffer_element_type(self._h))
+        return self._et
 
     @property
     def handle(self):
