@@ -390,7 +390,7 @@ def run_ours(args):
                     fh.write(f"{r['step']},{r['kind']},{r['kernel']},{r['calls']},{r['total_ms']:.6f},"
                              f"{r['elements']},{r['bytes']},{r['flops']}\n")
         calls = max(1, rows[0]["calls"]) if rows else 1
-        kinds = ("gemm", "attention", "loop", "reduce")
+        kinds = ("gemm", "attention", "loop", "reduce", "convert", "scatter", "sort")
         tot = {k: sum(r["total_ms"] for r in rows if r["kind"] == k) / calls for k in kinds}
         allms = sum(tot.values())
         breakdown = {k: {"ms_per_step": v, "share": v / allms if allms else 0} for k, v in tot.items()}

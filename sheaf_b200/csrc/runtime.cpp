@@ -6,6 +6,7 @@
 // call without a host synchronization.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <functional>
@@ -17,6 +18,7 @@
 #include <sstream>
 #include <string>
 #include <thread>
+#include <tuple>
 #include <vector>
 
 #include "../../include/sheaf_b200.h"
@@ -143,6 +145,12 @@ sb_buffer* new_device_buffer(const std::shared_ptr<Device>& dev, const Type& t, 
   return b;
 }
 
+// One all-reduce of a replayed data-parallel call: a byte range of the slot.
+struct Bucket {
+  size_t begin = 0, end = 0;
+  int32_t op = SB_REDUCE_MEAN;
+};
+
 // Output memory of one replayable CUDA graph of a function: every output of a
 // call lives in one allocation; the sb_buffers returned by the call share it
 // and hand it back (held drops to 0) once they are all released, after which
@@ -155,6 +163,7 @@ struct OutSlot {
   cudaGraphExec_t exec = nullptr;   // the function's steps, captured with these outputs
   std::vector<void*> direct_in;     // input addresses baked into exec (staged inputs: nullptr)
   uint64_t kernels = 0;             // kernels in exec
+  std::vector<Bucket> buckets;      // captured all-reduces (data parallel)
   ~OutSlot() {
     if (!dev) return;
     cudaSetDevice(dev->ordinal);
@@ -625,13 +634,137 @@ bool graphs_enabled() {
   return on;
 }
 
-sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin, sb_buffer** out,
-                     size_t* nout, bool* used) {
+// Data-parallel calls: the gradient all-reduce is captured into the graph too.
+// The outputs are laid out in the order in which the backward completes them,
+// so that a bucket of outputs is one contiguous byte range of the slot and
+// takes a single ncclAllReduce (on the comm stream, overlapped with the rest
+// of the backward when the session overlaps); the replay issues no NCCL call
+// from the host.
+
+sb_status* capture_reductions(sb_session* s, LoadedFunction* lf, const int32_t* reduce, OutSlot* slot,
+                              std::vector<void*>& ptr, const std::vector<void*>& outp);
+
+// Step after which output j is complete and read by no later step (outputs
+// copied after the steps, and values returned more than once: past the end).
+std::vector<int> ready_steps(const LoadedFunction* lf) {
+  const Function& f = *lf->plan.fn;
+  const Plan& plan = lf->plan;
+  std::vector<int> last(f.num_values(), -1);
+  for (int si = 0; si < (int)plan.steps.size(); ++si)
+    for (int l : plan.steps[si].leaves) last[l] = si;
+  std::vector<int> times(f.num_values(), 0);
+  for (int v : f.returns) ++times[v];
+  std::vector<int> r(f.returns.size());
+  for (size_t j = 0; j < f.returns.size(); ++j) {
+    const int v = f.returns[j];
+    r[j] = (plan.output_step[j] < 0 || times[v] > 1) ? (int)plan.steps.size()
+                                                     : std::max(plan.output_step[j], last[v]);
+  }
+  return r;
+}
+
+// Byte layout order of a slot's outputs: with reductions, the reduced outputs
+// by the step that completes them (then by reduction), the others after.
+std::vector<int> output_order(const LoadedFunction* lf, const int32_t* reduce) {
+  const size_t n = lf->plan.fn->returns.size();
+  std::vector<int> order(n);
+  for (size_t j = 0; j < n; ++j) order[j] = (int)j;
+  if (!reduce) return order;
+  const std::vector<int> ready = ready_steps(lf);
+  auto key = [&](int j) {
+    const bool red = reduce[j] != SB_REDUCE_NONE;
+    return std::make_tuple(red ? 0 : 1, red ? ready[j] : 0, red ? reduce[j] : 0, j);
+  };
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return key(a) < key(b); });
+  return order;
+}
+
+sb_status* capture_reductions(sb_session* s, LoadedFunction* lf, const int32_t* reduce, OutSlot* slot,
+                              std::vector<void*>& ptr, const std::vector<void*>& outp) {
+  const Function& f = *lf->plan.fn;
+  const Plan& plan = lf->plan;
+  cudaStream_t stream = s->dev->stream;
+  const bool overlap = s->dev->comm_stream != nullptr;
+  cudaStream_t cs = overlap ? s->dev->comm_stream : stream;
+  for (size_t j = 0; j < f.returns.size(); ++j)
+    if (reduce[j] != SB_REDUCE_NONE && f.value_types[f.returns[j]].dtype != DType::F32)
+      return make_status(SB_STATUS_UNIMPLEMENTED, "reduce of non-f32 output");
+  if (!s->nccl.comm) return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available");
+  size_t bucket_limit = 8u << 20;
+  if (const char* bb = std::getenv("SHEAF_B200_ALLREDUCE_BUCKET_BYTES"))
+    if (std::atoll(bb) > 0) bucket_limit = (size_t)std::atoll(bb);
+  const std::vector<int> ready = ready_steps(lf);
+  const std::vector<int> order = output_order(lf, reduce);
+  // outputs of one bucket are adjacent in `order`, hence in the slot
+  size_t next = 0;  // position in `order` of the first output not yet queued
+  Bucket cur;
+  bool open = false, forked = false;
+  auto bytes_of = [&](int j) {
+    const int v = f.returns[j];
+    return ((size_t)f.value_types[v].numel() * 4 + 255) & ~size_t(255);
+  };
+  auto flush = [&]() -> sb_status* {
+    if (!open) return nullptr;
+    open = false;
+    if (overlap) {
+      SB_CUDA(cudaEventRecord(s->dev->ready, stream));
+      SB_CUDA(cudaStreamWaitEvent(cs, s->dev->ready, 0));
+      forked = true;
+    }
+    const NcclApi& api = nccl_api();
+    char* base = (char*)slot->base;
+    ncclResult_t r = api.all_reduce(base + cur.begin, base + cur.begin, (cur.end - cur.begin) / 4, ncclFloat32,
+                                    cur.op == SB_REDUCE_MEAN ? ncclAvg : ncclSum, s->nccl.comm, cs);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return make_status(SB_STATUS_INTERNAL, std::string("ncclAllReduce: ") + api.error_string(r));
+    slot->buckets.push_back(cur);
+    return nccl_settle(s);
+  };
+  // queue the reduced outputs completed by step `upto` (inclusive)
+  auto queue = [&](int upto) -> sb_status* {
+    while (next < order.size()) {
+      const int j = order[next];
+      if (reduce[j] == SB_REDUCE_NONE || ready[j] > upto) break;
+      const size_t b = slot->off[j], e = b + bytes_of(j);
+      if (open && (reduce[j] != cur.op || b != cur.end))
+        if (sb_status* st = flush()) return st;
+      if (!open) {
+        cur.begin = b;
+        cur.end = b;
+        cur.op = reduce[j];
+        open = true;
+      }
+      cur.end = e;
+      ++next;
+      if (overlap && cur.end - cur.begin >= bucket_limit)
+        if (sb_status* st = flush()) return st;
+    }
+    return nullptr;
+  };
+  slot->buckets.clear();
+  const std::function<sb_status*(size_t)> before = [&](size_t si) -> sb_status* {
+    return (overlap && si > 0) ? queue((int)si - 1) : nullptr;
+  };
+  if (sb_status* st = enqueue_steps(s, lf, ptr, outp, before, true)) return st;
+  if (sb_status* st = queue((int)plan.steps.size())) return st;
+  if (sb_status* st = flush()) return st;
+  if (overlap && forked) {
+    SB_CUDA(cudaEventRecord(s->dev->reduced, cs));
+    SB_CUDA(cudaStreamWaitEvent(stream, s->dev->reduced, 0));
+  }
+  return nullptr;
+}
+
+sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, size_t nin, const int32_t* reduce,
+                     sb_buffer** out, size_t* nout, bool* used) {
   *used = false;
   const Function& f = *lf->plan.fn;
   const Plan& plan = lf->plan;
   cudaStream_t stream = s->dev->stream;
   const bool first = lf->calls == 0;
+  bool dp = false;
+  if (reduce && s->opts.world_size > 1)
+    for (size_t j = 0; j < f.returns.size(); ++j) dp = dp || reduce[j] != SB_REDUCE_NONE;
   if (lf->last_in.size() != nin) {
     lf->last_in.assign(nin, nullptr);
     lf->staged.assign(nin, 0);
@@ -671,8 +804,10 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
     auto sl = std::make_shared<OutSlot>();
     sl->dev = s->dev;
     size_t total = 0;
-    for (int v : f.returns) {
-      sl->off.push_back(total);
+    sl->off.assign(f.returns.size(), 0);
+    for (int j : output_order(lf, dp ? reduce : nullptr)) {
+      const int v = f.returns[j];
+      sl->off[j] = total;
       total += ((size_t)f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype) + 255) & ~size_t(255);
     }
     if (total) SB_CUDA(cudaMalloc(&sl->base, total));
@@ -695,7 +830,8 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
       if (!ptr[v] && plan.value_offset[v] >= 0) ptr[v] = (char*)lf->arena + plan.value_offset[v];
     SB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
     const uint64_t k0 = launch_counter().load();
-    sb_status* st = enqueue_steps(s, lf, ptr, outp, nullptr, true);
+    sb_status* st = dp ? capture_reductions(s, lf, reduce, slot.get(), ptr, outp)
+                       : enqueue_steps(s, lf, ptr, outp, nullptr, true);
     // kernels recorded into the graph (counted by the launch paths; taken
     // back off the counter, which counts kernels that run)
     slot->kernels = launch_counter().load() - k0;
@@ -758,16 +894,10 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   cudaStream_t stream = s->dev->stream;
   SB_CUDA(cudaSetDevice(s->dev->ordinal));
   const Plan& plan = lf->plan;
-  // calls without a data-parallel reduction replay a CUDA graph
-  bool no_reduce = true;
-  if (reduce && s->opts.world_size > 1) {
-    no_reduce = true;
-    for (size_t j = 0; j < f.returns.size(); ++j)
-      if (reduce[j] != SB_REDUCE_NONE) no_reduce = false;
-  }
-  if (graphs_enabled() && !s->profiling && no_reduce && !lf->graphs_off) {
+  // calls replay a CUDA graph from the second call on (run_graph)
+  if (graphs_enabled() && !s->profiling && !lf->graphs_off) {
     bool used = false;
-    sb_status* st = run_graph(s, lf, in, nin, out, nout, &used);
+    sb_status* st = run_graph(s, lf, in, nin, reduce, out, nout, &used);
     if (st || used) return st;
   }
   // outputs
@@ -986,6 +1116,15 @@ void sb_session_release(sb_session* s) {
   if (!s) return;
   cudaSetDevice(s->dev->ordinal);
   cudaStreamSynchronize(s->dev->stream);
+  // graphs that hold NCCL operations go before the communicator (the slots
+  // themselves may outlive the session while the caller holds outputs)
+  for (auto& m : s->modules)
+    for (auto& lf : m->fns)
+      for (auto& sl : lf->slots)
+        if (sl->exec) {
+          cudaGraphExecDestroy(sl->exec);
+          sl->exec = nullptr;
+        }
   if (s->nccl.comm) nccl_api().comm_destroy(s->nccl.comm);
   for (auto& m : s->modules) {
     for (auto& lf : m->fns) {
