@@ -68,7 +68,7 @@ def env_rank():
 
 def workload(name, world, batch=0):
     """(config, global batch, per-rank batch, scaling) of a GPT workload."""
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     if name in ("nanogpt", "nanogpt-fwd", "nanogpt-train"):
         c = M.NANOGPT
         gb = batch or c.batch
@@ -84,7 +84,7 @@ def program(args, world, rank):
     """The timed program: lowered module, host inputs of this rank, the names of
     the per-step data inputs, work units per step (all ranks), unit, scaling,
     config, and whether the outputs are data-parallel means (value-and-grad)."""
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     if args.workload == "mlp":
         gb = args.batch or 256
         if gb % world:
@@ -99,8 +99,8 @@ def program(args, world, rank):
                "l2": "operands fit in L2 (3.4 MB), no flush: launch-latency bound by design"}
         return low, inp, ["x", "y"], gb, "samples/s", "strong", cfg, True
     if args.workload == "nanogpt-generate":
-        from sheaf_b200.programs import generate as G
-        from sheaf_b200.programs import random as RG
+        from sheaf_lowering import generate as G
+        from sheaf_lowering import random as RG
         c = M.NANOGPT
         low = G.gpt_generate_program(c, 200, 0.8)
         inp = M.gpt_inputs(c, batch=1, seed=0)
@@ -194,7 +194,7 @@ def cpu_baseline(args, steps=2):
     the full MLP batch, or 2 sequences of the GPT model (GPT-2: 1 sequence of
     256 tokens), same graph (value-and-grad or forward) as the device run."""
     from oracle.stablehlo_ref import evaluate, parse_module
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     if args.workload == "mlp":
         low, inp, units, unit = M.mlp_vag(batch=256), M.mlp_inputs(batch=256), 256, "samples/s"
         sample = "the full 256-sample batch"
@@ -266,7 +266,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     from sheaf_b200 import build
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     from sheaf_b200.session import B200Session, library, nccl_unique_id
     build.build()
     low, inp, data_names, units, unit, scaling, cfg, vag = program(args, world, rank)
@@ -336,6 +336,29 @@ def run_ours(args):
         ms = float(t.item())
     ms_step = ms / args.steps
     value = units / (ms_step / 1e3)
+
+    # exposed communication: the same steps without the all-reduce (every
+    # rank skips it, so no rank waits on a collective); the difference in
+    # device time per step is what the all-reduce adds to the step
+    comm_exposed = None
+    if world > 1 and vag and not args.no_profile:
+        def plain_step(buffers):
+            return sess.call_device(q, buffers, None)
+        for _ in range(2):
+            for o in plain_step(bufs):
+                o.release()
+        barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        for _ in range(args.steps):
+            for o in plain_step(bufs):
+                o.release()
+        p1.record(stream)
+        p1.synchronize()
+        t = torch.tensor([p0.elapsed_time(p1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        comm_exposed = {"ms_per_step": ms_step - float(t.item()) / args.steps,
+                        "compute_only_ms_per_step": float(t.item()) / args.steps}
 
     # end to end: per step, H2D of the step's data inputs from pinned host
     # memory, the call, and the first output (the loss; the logits of a
@@ -414,7 +437,7 @@ def run_ours(args):
               "contraction": args.precision, "data": data, "config": cfg,
               "clocks": clk.summary(), "e2e": e2e, "gpu_launches": timed_launches,
               "roofline": roof, "breakdown": breakdown, "module_load_s": load_s,
-              "host_enqueue_ms_per_step": host_ms / args.steps}
+              "host_enqueue_ms_per_step": host_ms / args.steps, "allreduce_exposed": comm_exposed}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             result["cpu_baseline"] = cpu_baseline(args)

@@ -20,7 +20,7 @@ def main():
     import numpy as np
     import torch
     import torch.distributed as dist
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     from sheaf_b200.session import B200Session, nccl_unique_id
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])

@@ -8,14 +8,17 @@ reference code is executed):
   README.md:33-43                          mse-loss value-and-grad example
   sheaf/tests/interpreter_tests.yaml:623-628  adamw-step with and without decay
 
-Run from the repo root:  python tests/golden/make_goldens.py [reference_root]
+Run from the repo root:  python tests/golden/make_goldens.py <reference_root>
+(the directory holding the reference's sheaf/ and README.md).
 """
 import json
 import os
 import re
 import sys
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    raise SystemExit("usage: python tests/golden/make_goldens.py <reference_root>")
+REF = sys.argv[1]
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "vag_goldens.json")
 OUT_OPTIM = os.path.join(os.path.dirname(os.path.abspath(__file__)), "optim_goldens.json")
 

@@ -8,7 +8,7 @@ import numpy as np
 
 
 def inputs(cfg_name, batch, seed):
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     cfg = getattr(M, cfg_name)
     return M.gpt_inputs(cfg, batch=batch, seed=seed)
 

@@ -7,8 +7,8 @@ with stdlib functions inlined the way Sheaf's JIT inlines sheaf/lib/nn.shf.
 """
 import numpy as np
 
-from sheaf_b200.programs import models as M
-from sheaf_b200.programs.lower import Kw, Vec, lower_value_and_grad
+from sheaf_lowering import models as M
+from sheaf_lowering.lower import Kw, Vec, lower_value_and_grad
 
 AX, KEEP = Kw("axis"), Kw("keepdims")
 

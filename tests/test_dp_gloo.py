@@ -23,7 +23,7 @@ def _worker(rank, world, port, q):
     import torch
     import torch.distributed as dist
     from oracle.stablehlo_ref import run
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -46,7 +46,7 @@ def _worker(rank, world, port, q):
 
 def test_two_rank_mean_equals_full_batch():
     from oracle.stablehlo_ref import run
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

@@ -4,9 +4,9 @@ import numpy as np
 import pytest
 
 from oracle.stablehlo_ref import run
-from sheaf_b200.programs import generate as G
-from sheaf_b200.programs import models as M
-from sheaf_b200.programs import random as RG
+from sheaf_lowering import generate as G
+from sheaf_lowering import models as M
+from sheaf_lowering import random as RG
 
 
 def sort_module(rows, n, k, direction="GT"):

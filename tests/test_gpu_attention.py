@@ -14,8 +14,8 @@ import pytest
 
 from oracle.stablehlo_ref import run
 from sheaf_b200 import session as S
-from sheaf_b200.programs import models as M
-from sheaf_b200.programs.lower import Vec, lower_forward, lower_value_and_grad
+from sheaf_lowering import models as M
+from sheaf_lowering.lower import Vec, lower_forward, lower_value_and_grad
 
 pytestmark = pytest.mark.gpu
 HD = 64

@@ -22,7 +22,7 @@ import numpy as np
 import pytest
 
 from oracle.stablehlo_ref import run
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 
 pytestmark = pytest.mark.gpu
 

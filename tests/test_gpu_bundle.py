@@ -6,7 +6,7 @@ import os
 import numpy as np
 import pytest
 
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 from sheaf_b200.session import B200Error, B200Session, build_bundle
 
 pytestmark = pytest.mark.gpu

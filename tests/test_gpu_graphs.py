@@ -9,7 +9,7 @@ changing any result; the launch counter counts the replayed kernels.
 import numpy as np
 import pytest
 
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 
 pytestmark = pytest.mark.gpu
 

@@ -375,7 +375,7 @@ def test_profile_report_counts_every_launch(fp32_session):
     """The per-step launch counts of the profile report add up to the kernels
     the library's launch counter sees for the same call (fp32: no rounded
     parameter copies outside the steps)."""
-    from sheaf_b200.programs import models as M
+    from sheaf_lowering import models as M
     from sheaf_b200.session import library
     c = M.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=128, vocab_size=65, batch=2)
     low = M.gpt_vag(c)

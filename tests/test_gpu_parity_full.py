@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 
 import oracle_jobs
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 
 pytestmark = pytest.mark.gpu
 

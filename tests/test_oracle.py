@@ -8,7 +8,7 @@ import pytest
 from oracle.rng import random_normal
 from oracle.stablehlo_ref import run
 from sheaf_cases import CASES
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 
 GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "vag_goldens.json")))["cases"]
 

@@ -1,7 +1,7 @@
 """Execution plans built on the host (no GPU): what the planner's rewrites do
 to the benchmark graphs."""
 from sheaf_b200 import session as S
-from sheaf_b200.programs import models as M
+from sheaf_lowering import models as M
 
 
 def _summary(text, prec="tf32"):

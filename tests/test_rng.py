@@ -1,5 +1,5 @@
 """Sheaf's JIT random ops (random-key/split/uniform/normal/randint) as device
-kernels: the emitted StableHLO (sheaf_b200/programs/random.py) checked against
+kernels: the emitted StableHLO (sheaf_lowering/random.py) checked against
 an independent restatement of the i32 hash on the host, and the device
 results against the oracle: the integer hash, uniforms, randints and keys bit
 for bit, normals (log/cos/sqrt on two math libraries) to a few ulps."""
@@ -7,8 +7,8 @@ import numpy as np
 import pytest
 
 from oracle.stablehlo_ref import run
-from sheaf_b200.programs import models as M
-from sheaf_b200.programs import random as RG
+from sheaf_lowering import models as M
+from sheaf_lowering import random as RG
 
 
 def _w(x):
