@@ -111,8 +111,8 @@ cudaError_t attention(const AttnArgs& a, cudaStream_t stream);
 // Row scatter-add (kernels/scatter.cu): out[k, :] = sum over rows r of adj
 // (n x d, row-major) with key(r) == k, in row order; out is v x d.  Keys from
 // idx (n values, f32 holding integers, or i32); keys outside [0, v) or not
-// integral hit nothing.  ws holds scatter_add_rows_workspace(n, v) bytes.
-size_t scatter_add_rows_workspace(int64_t n, int64_t v);
+// integral hit nothing.  ws holds scatter_add_rows_workspace(n, v, d) bytes.
+size_t scatter_add_rows_workspace(int64_t n, int64_t v, int64_t d);
 cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, float* out, int64_t n, int64_t d,
                              int64_t v, void* ws, cudaStream_t stream);
 

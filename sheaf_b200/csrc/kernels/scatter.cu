@@ -68,14 +68,18 @@ __global__ void __launch_bounds__(kThreads) colscan_kernel(int* __restrict__ his
   }
 }
 
-// offs[k] := exclusive prefix of total over keys, offs[v] = rows with a key
-__global__ void __launch_bounds__(1024) offsets_kernel(const int* __restrict__ total, int* __restrict__ offs, int v) {
+// offs[k] := exclusive prefix over keys of total (rounded up to a multiple of
+// `round`: segments padded to whole chunks), offs[v] = the sum
+__device__ __forceinline__ int rounded(int x, int round) { return (x + round - 1) / round * round; }
+
+__global__ void __launch_bounds__(1024) offsets_kernel(const int* __restrict__ total, int* __restrict__ offs, int v,
+                                                       int round) {
   pdl_prologue();
   __shared__ int part[1024];
   const int per = (v + 1023) / 1024;
   const int k0 = threadIdx.x * per, k1 = min(v, k0 + per);
   int s = 0;
-  for (int k = k0; k < k1; ++k) s += total[k];
+  for (int k = k0; k < k1; ++k) s += rounded(total[k], round);
   part[threadIdx.x] = s;
   __syncthreads();
   // inclusive scan of the 1024 partial sums (Hillis-Steele)
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(1024) offsets_kernel(const int* __restrict__ t
   int run = threadIdx.x ? part[threadIdx.x - 1] : 0;
   for (int k = k0; k < k1; ++k) {
     offs[k] = run;
-    run += total[k];
+    run += rounded(total[k], round);
   }
   if (threadIdx.x == 1023) offs[v] = part[1023];
 }
@@ -141,13 +145,71 @@ __global__ void __launch_bounds__(kThreads) segsum_kernel(const float* __restric
   }
 }
 
+// Few keys, many rows each (a small vocabulary): one warp per key would sum
+// hundreds of rows in sequence.  Instead every key's segment is padded to
+// whole chunks of kRun positions (padding rows are -1), pass 1 sums each chunk
+// (one warp per 128 columns of a chunk), pass 2 sums each key's chunk
+// partials in chunk order.
+constexpr int kRun = 32;
+
+__global__ void __launch_bounds__(kThreads) chunk_sum_kernel(const float* __restrict__ adj, const int* __restrict__ offs,
+                                                             const int* __restrict__ perm, float* __restrict__ part,
+                                                             int v, int64_t d, int64_t max_chunks) {
+  pdl_prologue();
+  const int lane = threadIdx.x & 31;
+  const int64_t chunks = offs[v] / kRun;
+  const int64_t cols = (d + 127) / 128;
+  for (int64_t w = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); w < chunks * cols;
+       w += (int64_t)gridDim.x * (kThreads / 32)) {
+    const int64_t c = w / cols, col = (w % cols) * 128 + lane * 4;
+    if (col >= d) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int i = 0; i < kRun; ++i) {
+      const int r = perm[c * kRun + i];
+      if (r < 0) continue;
+      const float4 x = *(const float4*)(adj + (int64_t)r * d + col);
+      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    *(float4*)(part + c * d + col) = acc;
+  }
+  (void)max_chunks;
+}
+
+__global__ void __launch_bounds__(kThreads) key_sum_kernel(const float* __restrict__ part, const int* __restrict__ offs,
+                                                           float* __restrict__ out, int v, int64_t d) {
+  pdl_prologue();
+  const int lane = threadIdx.x & 31;
+  const int64_t cols = (d + 127) / 128;
+  for (int64_t w = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); w < (int64_t)v * cols;
+       w += (int64_t)gridDim.x * (kThreads / 32)) {
+    const int64_t k = w / cols, col = (w % cols) * 128 + lane * 4;
+    if (col >= d) continue;
+    const int c0 = offs[k] / kRun, c1 = offs[k + 1] / kRun;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = c0; c < c1; ++c) {
+      const float4 x = *(const float4*)(part + (int64_t)c * d + col);
+      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    *(float4*)(out + k * d + col) = acc;
+  }
+}
+
 int64_t chunks_of(int64_t n) { return (n + kChunk - 1) / kChunk; }
+
+// the chunked two-pass sum: few keys for the rows, float4 columns
+bool chunked(int64_t n, int64_t v, int64_t d) { return v * 8 <= n && d % 4 == 0; }
 
 }  // namespace
 
-size_t scatter_add_rows_workspace(int64_t n, int64_t v) {
-  // hist [chunks][v], total [v], offs [v + 1], perm [n] (ints)
-  return (size_t)(chunks_of(n) * v + v + (v + 1) + n) * sizeof(int);
+size_t scatter_add_rows_workspace(int64_t n, int64_t v, int64_t d) {
+  // hist [chunks][v], total [v], offs [v + 1], perm [n] (ints); chunked:
+  // perm padded to n + v * kRun, then the chunk partials (floats, 16-byte
+  // aligned)
+  if (!chunked(n, v, d)) return (size_t)(chunks_of(n) * v + v + (v + 1) + n) * sizeof(int);
+  const int64_t ints = chunks_of(n) * v + v + (v + 1) + n + v * kRun;
+  const int64_t max_chunks = n / kRun + v;
+  return (size_t)((ints + 3) / 4 * 4) * sizeof(int) + (size_t)(max_chunks * d) * sizeof(float);
 }
 
 cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, float* out, int64_t n, int64_t d,
@@ -155,10 +217,14 @@ cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, fl
   if (v <= 0 || d <= 0) return cudaSuccess;
   if (n < 0 || v >= (1ll << 31) - 1 || n >= (1ll << 31)) return cudaErrorInvalidValue;
   const int64_t chunks = chunks_of(n);
+  const bool two_pass = chunked(n, v, d) && (((uintptr_t)adj | (uintptr_t)out) & 15) == 0;
   int* hist = (int*)ws;
   int* total = hist + chunks * v;
   int* offs = total + v;
   int* perm = offs + v + 1;
+  const int64_t perm_len = two_pass ? n + v * kRun : n;
+  const int64_t ints = chunks * v + v + (v + 1) + perm_len;
+  float* part = (float*)((int*)ws + (ints + 3) / 4 * 4);
   cudaError_t e;
   if (n > 0) {
     e = cudaMemsetAsync(hist, 0, (size_t)(chunks * v) * sizeof(int), stream);
@@ -169,12 +235,27 @@ cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, fl
   const unsigned vb = (unsigned)std::min<int64_t>((v + kThreads - 1) / kThreads, 148 * 8);
   e = launch_pdl(colscan_kernel, dim3(vb), dim3(kThreads), 0, stream, hist, total, (int)chunks, (int)v);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(offsets_kernel, dim3(1), dim3(1024), 0, stream, (const int*)total, offs, (int)v);
+  e = launch_pdl(offsets_kernel, dim3(1), dim3(1024), 0, stream, (const int*)total, offs, (int)v,
+                 two_pass ? kRun : 1);
   if (e != cudaSuccess) return e;
+  if (two_pass) {  // padding positions of the segments hold -1
+    e = cudaMemsetAsync(perm, 0xff, (size_t)perm_len * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
   if (n > 0) {
     e = launch_pdl(place_kernel, dim3((unsigned)chunks), dim3(kThreads), 0, stream, idx, (int)idx_f32, n, (int)v,
                    (const int*)hist, (const int*)offs, perm);
     if (e != cudaSuccess) return e;
+  }
+  if (two_pass) {
+    const int64_t max_chunks = n / kRun + v, cols = (d + 127) / 128;
+    const unsigned b1 = (unsigned)std::min<int64_t>((max_chunks * cols + 7) / 8, 148 * 16);
+    e = launch_pdl(chunk_sum_kernel, dim3(b1), dim3(kThreads), 0, stream, adj, (const int*)offs, (const int*)perm,
+                   part, (int)v, d, max_chunks);
+    if (e != cudaSuccess) return e;
+    const unsigned b2 = (unsigned)std::min<int64_t>((v * cols + 7) / 8, 148 * 16);
+    return launch_pdl(key_sum_kernel, dim3(b2), dim3(kThreads), 0, stream, (const float*)part, (const int*)offs, out,
+                      (int)v, d);
   }
   const int vec = (d % 4 == 0) && ((((uintptr_t)adj) | ((uintptr_t)out)) & 15) == 0;
   const unsigned sb = (unsigned)std::min<int64_t>((v + kThreads / 32 - 1) / (kThreads / 32), 148 * 16);
