@@ -285,11 +285,51 @@ class B200Session:
         self.precision = precision
         self.world_size = world_size
         self.rank = rank
+        # uploaded host tensors, per function and argument position
+        # (IreeSession's buffer cache, iree_session.rs:612-660)
+        self._uploads: dict = {}
+        self.upload_hits = 0
+        self.upload_misses = 0
 
     def close(self):
         if getattr(self, "_h", None):
+            for per_fn in self._uploads.values():
+                for entries in per_fn:
+                    for _, b in entries:
+                        b.release()
+            self._uploads = {}
             library().sb_session_release(self._h)
             self._h = None
+
+    # at most this many uploads are kept per argument position
+    UPLOAD_CACHE_ENTRIES = 8
+
+    def _upload(self, name: str, i: int, nargs: int, a) -> "DeviceBuffer":
+        """Device buffer for host argument i of function `name`.  As Sheaf's
+        session skips re-uploading a tensor it has seen (buffer_cache.rs:9-40:
+        identity of an immutable Arc'd tensor), an ndarray that cannot be
+        written (`a.flags.writeable` False) is uploaded once and found again by
+        identity (the cache holds a reference, so the identity stays unique);
+        the 8 most recent uploads per argument position are kept.  Writeable
+        arrays may change in place between calls and are uploaded every time."""
+        if not isinstance(a, np.ndarray) or a.flags.writeable:
+            return None
+        per_fn = self._uploads.setdefault(name, [])
+        while len(per_fn) < nargs:
+            per_fn.append([])
+        entries = per_fn[i]
+        for k, (arr, buf) in enumerate(entries):
+            if arr is a:
+                self.upload_hits += 1
+                if k:
+                    entries.insert(0, entries.pop(k))
+                return buf
+        self.upload_misses += 1
+        buf = self.buffer(a)
+        entries.insert(0, (a, buf))
+        if len(entries) > self.UPLOAD_CACHE_ENTRIES:
+            entries.pop()[1].release()
+        return buf
 
     def __del__(self):
         try:
@@ -383,7 +423,13 @@ class B200Session:
 
     # calls -------------------------------------------------------------------
     def call_device(self, name: str, args: Sequence, reduce: Optional[Sequence] = None) -> List[DeviceBuffer]:
-        bufs = [a if isinstance(a, DeviceBuffer) else self.buffer(a) for a in args]
+        bufs = []
+        for i, a in enumerate(args):
+            if isinstance(a, DeviceBuffer):
+                bufs.append(a)
+                continue
+            b = self._upload(name, i, len(args), a)
+            bufs.append(b if b is not None else self.buffer(a))
         arr = (ctypes.c_void_p * max(len(bufs), 1))(*[b.handle for b in bufs])
         cap = 4096
         outs = (ctypes.c_void_p * cap)()

@@ -89,3 +89,26 @@ def test_held_outputs_are_never_overwritten(gpt):
             assert np.array_equal(o.to_host(), h)
         for o in outs:
             o.release()
+
+
+def test_read_only_host_tensors_are_uploaded_once(gpt):
+    """IreeSession's buffer cache (iree_session.rs:612-660): an immutable host
+    tensor passed again is not uploaded again; a writeable one is."""
+    sess, low = gpt
+    inp = _inputs(5)
+    frozen = {}
+    for n in low.arg_names:
+        a = np.array(inp[n])
+        a.setflags(write=False)
+        frozen[n] = a
+    h0, m0 = sess.upload_hits, sess.upload_misses
+    first = sess.call(low.qualified, [frozen[n] for n in low.arg_names])
+    assert sess.upload_misses - m0 == len(low.arg_names)
+    second = sess.call(low.qualified, [frozen[n] for n in low.arg_names])
+    assert sess.upload_hits - h0 == len(low.arg_names)
+    for a, b in zip(first, second):
+        assert np.array_equal(a, b)
+    # a writeable array is uploaded on every call (it may have changed)
+    m1 = sess.upload_misses
+    sess.call(low.qualified, [inp[n] for n in low.arg_names])
+    assert sess.upload_misses == m1
