@@ -46,7 +46,8 @@ def parse():
     p.add_argument("--precision", default=os.environ.get("SHEAF_B200_PRECISION", "tf32"),
                    choices=["fp32", "tf32", "bf16"])
     p.add_argument("--workload", default="nanogpt",
-                   choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "nanogpt-generate", "gpt2", "mlp", "matmul"])
+                   choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "nanogpt-generate", "gpt2", "mlp", "matmul",
+                            "ref-vag", "ref-forward"])
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
     p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
@@ -98,6 +99,18 @@ def program(args, world, rank):
                "global_batch": gb, "parallelism": f"dp{world}",
                "l2": "operands fit in L2 (3.4 MB), no flush: launch-latency bound by design"}
         return low, inp, ["x", "y"], gb, "samples/s", "strong", cfg, True
+    if args.workload in ("ref-vag", "ref-forward"):
+        # the reference's own benchmark programs, one 64-token sequence per rank
+        c = M.GPT2_BENCH
+        vag = args.workload == "ref-vag"
+        low = M.bench_vag_program(c) if vag else M.bench_forward_program(c)
+        inp = M.bench_inputs(c, seed=42 + rank)
+        src = "benchmarks/bench_vag_sheaf.shf (loss = mean of the logits)" if vag else "benchmarks/bench_forward.shf"
+        cfg = {"workload": f"GPT-2 124M {'value-and-grad' if vag else 'forward'} {c.batch}x{c.T} ({src})",
+               "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}", "global_batch": world,
+               "seq_len": c.T, "parallelism": f"dp{world}",
+               "l2": "weights (0.5 GB) exceed L2; no flush"}
+        return low, inp, ["idx"], world * c.T, "tokens/s", "weak", cfg, vag
     if args.workload == "nanogpt-generate":
         from sheaf_lowering import generate as G
         from sheaf_lowering import random as RG
@@ -212,6 +225,9 @@ def cpu_baseline(args, steps=2):
     elif args.workload == "nanogpt-generate":
         low, inp, _, units, unit, _, _, _ = program(args, 1, 0)
         sample = "one generate-token step (1 token on the 256-token window)"
+    elif args.workload in ("ref-vag", "ref-forward"):
+        low, inp, _, units, unit, _, _, _ = program(args, 1, 0)
+        sample = "the full program (1 x 64 tokens)"
     else:
         c = workload(args.workload, 1)[0]
         b, T = (16, c.T) if c.T <= 256 else (1, c.T)

@@ -208,6 +208,57 @@ def gpt_inputs(c: GPTConfig, batch: int = None, seed: int = 0) -> Dict[str, np.n
 
 
 # ---------------------------------------------------------------------------
+# The reference's own benchmark programs (benchmarks/bench_vag_sheaf.shf,
+# benchmarks/bench_forward.shf): GPT-2 124M (12 layers, d768, 12 heads,
+# vocabulary 50257, block 1024) on one sequence of 64 tokens; the value-and-
+# grad program's loss is the mean of the logits.  The model code is the same
+# as examples/nanoGPT's (`(transpose W)` of a matrix is `(tr W)`).
+# ---------------------------------------------------------------------------
+
+GPT2_BENCH = GPTConfig(n_layer=12, n_head=12, n_embd=768, block_size=1024, vocab_size=50257, batch=1, seq=64)
+
+
+def bench_vag_program(c: GPTConfig = GPT2_BENCH) -> Lowered:
+    """`(value-and-grad (fn [p] (mean (forward idx p config))))`
+    (benchmarks/bench_vag_sheaf.shf:86-101)."""
+    leaves = gpt_param_leaves(c)
+
+    def build(t, s):
+        return t("mean", gpt_forward(t, s["idx"], s, c))
+    return lower_value_and_grad(build, leaves, [("idx", (c.batch, c.T))], key=f"bench-vag-{c}")
+
+
+def bench_forward_program(c: GPTConfig = GPT2_BENCH) -> Lowered:
+    """`(forward idx params config)` (benchmarks/bench_forward.shf:75-87)."""
+    args = gpt_param_leaves(c) + [("idx", (c.batch, c.T))]
+
+    def build(t, s):
+        return gpt_forward(t, s["idx"], s, c)
+    return lower_forward(build, args, "forward", key=f"bench-fwd-{c}")
+
+
+def bench_inputs(c: GPTConfig = GPT2_BENCH, seed: int = 42) -> Dict[str, np.ndarray]:
+    """Seeded stand-ins for init-params (bench_vag_sheaf.shf:57-76): matrices
+    N(0, 1) / sqrt(fan-in) (sqrt(D), or sqrt(4 D) for mlp.c_proj), LN gammas 1,
+    lm_head equal to wte (both drawn from key k1 there); idx U[0, V) of
+    [1, 64]."""
+    rng = np.random.default_rng(seed)
+    D = c.n_embd
+    out = {}
+    for n, shp in gpt_param_leaves(c):
+        if n.endswith(("ln_1.weight", "ln_2.weight", "ln_f.weight")):
+            out[n] = np.ones(shp, np.float32)
+        elif n == "lm_head.weight":
+            continue
+        else:
+            scale = np.sqrt(4 * D) if n.endswith("mlp.c_proj.weight") else np.sqrt(D)
+            out[n] = (rng.standard_normal(shp, dtype=np.float32) / np.float32(scale)).astype(np.float32)
+    out["lm_head.weight"] = out["transformer.wte.weight"].copy()
+    out["idx"] = rng.integers(0, c.vocab_size, size=(c.batch, c.T)).astype(np.float32)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # MLP value-and-grad: linear -> gelu -> linear, mse-loss
 # ---------------------------------------------------------------------------
 
