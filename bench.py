@@ -47,7 +47,12 @@ def parse():
                    choices=["fp32", "tf32", "bf16"])
     p.add_argument("--workload", default="nanogpt",
                    choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "nanogpt-generate", "gpt2", "mlp", "matmul",
-                            "ref-vag", "ref-forward"])
+                            "ref-vag", "ref-forward", "sweep"])
+    p.add_argument("--op", default="softmax", choices=["softmax", "layer-norm", "gelu"],
+                   help="sweep workload: the op (on [65536, --dim], gelu on 2^28 elements)")
+    p.add_argument("--dim", type=int, default=768, help="sweep workload: D of [65536, D]")
+    p.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="sweep workload: tensor type")
+    p.add_argument("--vjp", action="store_true", help="sweep workload: the VJP (value-and-grad) instead of the op")
     p.add_argument("--size", type=int, default=4096, help="matmul workload: M = N = K")
     p.add_argument("--shape", default="", help="matmul workload: M,N,K (overrides --size)")
     p.add_argument("--layout", default="nn", choices=["nn", "nt", "tn", "tt"],
@@ -541,12 +546,72 @@ def run_matmul(args):
     sess.close()
 
 
+def run_sweep(args):
+    """Op sweep: softmax / layer-norm on [65536, D] or gelu on 2^28 elements,
+    forward or VJP, f32 or bf16 tensors, as Sheaf lowers them.  Algorithmic
+    bytes: forward reads x and writes y (2 x elements x s), VJP reads x and the
+    cotangent and writes dx (3 x elements x s), s = 4 (f32) / 2 (bf16).  L2 is
+    flushed (a 256 MB write) before every timed call; only the call is inside
+    the CUDA events."""
+    import torch
+    from sheaf_b200 import build
+    from sheaf_b200.session import B200Session, library
+    from sheaf_lowering import models as M
+    build.build()
+    shape = (1 << 28,) if args.op == "gelu" else (65536, args.dim)
+    low = M.sweep_program(args.op, shape, args.vjp, args.dtype)
+    inp = M.sweep_inputs(args.op, shape, args.vjp)
+    sess = B200Session(precision="fp32")
+    sess.load_stablehlo(low.text)
+    bf = args.dtype == "bf16"
+    bufs = [sess.buffer(inp[n], bf16=bf) for n in low.arg_names]
+    q = low.qualified
+    stream = torch.cuda.ExternalStream(sess.cuda_stream)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        for o in sess.call_device(q, bufs):
+            o.release()
+    sess.synchronize()
+    lib = library()
+    n0 = lib.sb_kernel_launch_count()
+    total = 0.0
+    with Clocks(0) as clk:
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            outs = sess.call_device(q, bufs)
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+            for o in outs:
+                o.release()
+    launches = int(lib.sb_kernel_launch_count() - n0)
+    ms = total / args.steps
+    elems = int(np.prod(shape))
+    nbytes = (3 if args.vjp else 2) * elems * (2 if bf else 4)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    hbm, _, src = peaks()
+    what = f"{args.op} {'VJP' if args.vjp else 'forward'} {'x'.join(map(str, shape))} {args.dtype}"
+    print(json.dumps({"metric": "op sweep HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "scaling": "none", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic N(0,1)",
+                      "config": {"workload": f"op sweep: {what}", "l2": "flushed (256 MB write) before each call"},
+                      "clocks": clk.summary(), "gpu_launches": launches,
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                   "traffic": None, "peak_source": src, "algorithmic_bytes": nbytes}}), flush=True)
+    sess.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "matmul":
         run_matmul(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 

@@ -14,7 +14,7 @@ from typing import Dict, List, Tuple
 
 import numpy as np
 
-from .lower import Kw, Lowered, Sym, Vec, lower_forward, lower_value_and_grad
+from .lower import Kw, Lowered, Sym, Ty, Vec, lower_forward, lower_value_and_grad
 
 KEEP = Kw("keepdims")
 AXIS = Kw("axis")
@@ -290,3 +290,62 @@ def mlp_inputs(batch: int = 256, seed: int = 0) -> Dict[str, np.ndarray]:
         "b1": np.zeros(512, np.float32),
         "b2": np.zeros(10, np.float32),
     }
+
+
+# ---------------------------------------------------------------------------
+# Op-level sweep: softmax and layer-norm on [R, D], gelu on [N], each forward
+# and VJP.  The VJP is Sheaf's value-and-grad of sum(op(x) * g) with respect
+# to x, for a captured cotangent g: its gradient output is VJP_op(x, g).
+# ---------------------------------------------------------------------------
+
+SWEEP_OPS = ("softmax", "layer-norm", "gelu")
+
+
+def _sweep_body(op, t, s):
+    if op == "softmax":
+        return softmax(t, s["x"])
+    if op == "layer-norm":
+        return layer_norm(t, s["x"], s["gamma"], s["beta"])
+    if op == "gelu":
+        return gelu(t, s["x"])
+    raise ValueError(op)
+
+
+def sweep_program(op: str, shape: Tuple[int, ...], vjp: bool, dtype: str = "f32") -> Lowered:
+    """`(op x)` as a JIT forward function, or `((value-and-grad (fn [x] (sum
+    (* (op x) g)))) x)`.  dtype "bf16": the same program on bf16 tensors (every
+    tensor type of the f32 text, constants included, as bf16: each op then
+    rounds its result to bf16, as Sheaf's bf16 tensors compute)."""
+    D = shape[-1]
+    extra = [("gamma", (D,)), ("beta", (D,))] if op == "layer-norm" else []
+    key = f"sweep-{op}-{'x'.join(map(str, shape))}-{'vjp' if vjp else 'fwd'}"
+    if vjp:
+        def build(t, s):
+            return t("sum", t("*", _sweep_body(op, t, s), s["g"]))
+        low = lower_value_and_grad(build, [("x", shape)], [("g", shape)] + extra, key=key)
+    else:
+        def build(t, s):
+            return _sweep_body(op, t, s)
+        low = lower_forward(build, [("x", shape)] + extra, op.replace("-", "_"), key=key)
+    if dtype == "f32":
+        return low
+    if dtype != "bf16":
+        raise ValueError(dtype)
+    import re
+    text = re.sub(r"(tensor<(?:[0-9]+x)*)f32>", r"\1bf16>", low.text)
+    text = text.replace(low.module, low.module + "_bf16")
+    bf = [Ty(t.shape, "bf16") for t in low.arg_types]
+    rf = [Ty(t.shape, "bf16") for t in low.result_types]
+    return Lowered(text, low.module + "_bf16", low.function, low.arg_names, bf, rf)
+
+
+def sweep_inputs(op: str, shape: Tuple[int, ...], vjp: bool, seed: int = 0) -> Dict[str, np.ndarray]:
+    """Seeded N(0, 1) inputs (and cotangent); layer-norm gamma 1, beta 0."""
+    rng = np.random.default_rng(seed)
+    out = {"x": rng.standard_normal(shape, dtype=np.float32)}
+    if vjp:
+        out["g"] = rng.standard_normal(shape, dtype=np.float32)
+    if op == "layer-norm":
+        out["gamma"] = np.ones(shape[-1], np.float32)
+        out["beta"] = np.zeros(shape[-1], np.float32)
+    return out

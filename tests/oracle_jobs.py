@@ -20,6 +20,16 @@ def evaluate(text, qualified, arg_names, cfg_name, batch, seed):
     return run(text, qualified, [inp[n] for n in arg_names], dtype=np.float32)
 
 
+def sweep_last_output(op, shape, vjp, seed):
+    """Last output (the op's result, or the VJP's dx) of an op-sweep program on
+    its seeded inputs, f32."""
+    from oracle.stablehlo_ref import run
+    from sheaf_lowering import models as M
+    low = M.sweep_program(op, shape, vjp)
+    inp = M.sweep_inputs(op, shape, vjp, seed=seed)
+    return run(low.text, low.qualified, [inp[n] for n in low.arg_names], dtype=np.float32)[-1]
+
+
 _POOL = None
 
 
