@@ -73,7 +73,8 @@ int tc_forced_config();
 cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream);
 // Non-zero when a tcgen05 kernel gave up on a bounded wait (GEMM 1: ring slot,
 // 2: operand tiles, 3: accumulator; attention 11..35) or found its shared
-// memory window misaligned (9).  Reads a device word (synchronizing).
+// memory window misaligned (9), or the row scatter-add found inconsistent
+// segment offsets (41..43).  Reads a device word (synchronizing).
 int gemm_tcgen05_error();
 
 // Fused attention, head dim 64 (kernels/attention.cu).  Views are [B,H,T,64]

@@ -23,6 +23,7 @@
 
 #include "kernels.h"
 #include "pdl.h"
+#include "tc_common.h"
 
 namespace sb {
 namespace {
@@ -119,12 +120,16 @@ __global__ void __launch_bounds__(kThreads) place_kernel(const void* idx, int id
 // one warp per output row k: out[k, :] = sum over its segment, in order
 __global__ void __launch_bounds__(kThreads) segsum_kernel(const float* __restrict__ adj, const int* __restrict__ offs,
                                                           const int* __restrict__ perm, float* __restrict__ out,
-                                                          int v, int64_t d, int vec) {
+                                                          int v, int64_t d, int vec, int64_t n, int* err) {
   pdl_prologue();
   const int lane = threadIdx.x & 31;
   const int warps = kThreads / 32;
   for (int64_t k = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); k < v; k += (int64_t)gridDim.x * warps) {
-    const int s0 = offs[k], s1 = offs[k + 1];
+    int s0 = offs[k], s1 = offs[k + 1];
+    if (s0 < 0 || s1 < s0 || s1 > n) {  // inconsistent segment: recorded, and skipped
+      if (lane == 0) atomicExch(err, 41);
+      s0 = s1 = 0;
+    }
     float* o = out + k * d;
     if (vec) {
       for (int64_t col = lane * 4; col < d; col += 128) {
@@ -154,10 +159,14 @@ constexpr int kRun = 32;
 
 __global__ void __launch_bounds__(kThreads) chunk_sum_kernel(const float* __restrict__ adj, const int* __restrict__ offs,
                                                              const int* __restrict__ perm, float* __restrict__ part,
-                                                             int v, int64_t d, int64_t max_chunks) {
+                                                             int v, int64_t d, int64_t max_chunks, int64_t n, int* err) {
   pdl_prologue();
   const int lane = threadIdx.x & 31;
-  const int64_t chunks = offs[v] / kRun;
+  int64_t chunks = offs[v] / kRun;
+  if (chunks < 0 || chunks > max_chunks) {  // inconsistent offsets: recorded, nothing summed
+    if (threadIdx.x == 0) atomicExch(err, 42);
+    chunks = 0;
+  }
   const int64_t cols = (d + 127) / 128;
   for (int64_t w = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); w < chunks * cols;
        w += (int64_t)gridDim.x * (kThreads / 32)) {
@@ -167,17 +176,17 @@ __global__ void __launch_bounds__(kThreads) chunk_sum_kernel(const float* __rest
 #pragma unroll 8
     for (int i = 0; i < kRun; ++i) {
       const int r = perm[c * kRun + i];
-      if (r < 0) continue;
+      if (r < 0 || r >= n) continue;
       const float4 x = *(const float4*)(adj + (int64_t)r * d + col);
       acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
     }
     *(float4*)(part + c * d + col) = acc;
   }
-  (void)max_chunks;
 }
 
 __global__ void __launch_bounds__(kThreads) key_sum_kernel(const float* __restrict__ part, const int* __restrict__ offs,
-                                                           float* __restrict__ out, int v, int64_t d) {
+                                                           float* __restrict__ out, int v, int64_t d, int64_t max_chunks,
+                                                           int* err) {
   pdl_prologue();
   const int lane = threadIdx.x & 31;
   const int64_t cols = (d + 127) / 128;
@@ -185,7 +194,11 @@ __global__ void __launch_bounds__(kThreads) key_sum_kernel(const float* __restri
        w += (int64_t)gridDim.x * (kThreads / 32)) {
     const int64_t k = w / cols, col = (w % cols) * 128 + lane * 4;
     if (col >= d) continue;
-    const int c0 = offs[k] / kRun, c1 = offs[k + 1] / kRun;
+    int c0 = offs[k] / kRun, c1 = offs[k + 1] / kRun;
+    if (c0 < 0 || c1 < c0 || c1 > max_chunks) {
+      if (lane == 0) atomicExch(err, 43);
+      c0 = c1 = 0;
+    }
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int c = c0; c < c1; ++c) {
       const float4 x = *(const float4*)(part + (int64_t)c * d + col);
@@ -216,6 +229,8 @@ cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, fl
                              int64_t v, void* ws, cudaStream_t stream) {
   if (v <= 0 || d <= 0) return cudaSuccess;
   if (n < 0 || v >= (1ll << 31) - 1 || n >= (1ll << 31)) return cudaErrorInvalidValue;
+  int* err = tc_error_word();  // the device error word of the tensor-core kernels
+  if (!err) return cudaErrorNotSupported;
   const int64_t chunks = chunks_of(n);
   const bool two_pass = chunked(n, v, d) && (((uintptr_t)adj | (uintptr_t)out) & 15) == 0;
   int* hist = (int*)ws;
@@ -251,16 +266,16 @@ cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, fl
     const int64_t max_chunks = n / kRun + v, cols = (d + 127) / 128;
     const unsigned b1 = (unsigned)std::min<int64_t>((max_chunks * cols + 7) / 8, 148 * 16);
     e = launch_pdl(chunk_sum_kernel, dim3(b1), dim3(kThreads), 0, stream, adj, (const int*)offs, (const int*)perm,
-                   part, (int)v, d, max_chunks);
+                   part, (int)v, d, max_chunks, n, err);
     if (e != cudaSuccess) return e;
     const unsigned b2 = (unsigned)std::min<int64_t>((v * cols + 7) / 8, 148 * 16);
     return launch_pdl(key_sum_kernel, dim3(b2), dim3(kThreads), 0, stream, (const float*)part, (const int*)offs, out,
-                      (int)v, d);
+                      (int)v, d, max_chunks, err);
   }
   const int vec = (d % 4 == 0) && ((((uintptr_t)adj) | ((uintptr_t)out)) & 15) == 0;
   const unsigned sb = (unsigned)std::min<int64_t>((v + kThreads / 32 - 1) / (kThreads / 32), 148 * 16);
   return launch_pdl(segsum_kernel, dim3(sb), dim3(kThreads), 0, stream, adj, (const int*)offs, (const int*)perm, out,
-                    (int)v, d, vec);
+                    (int)v, d, vec, n, err);
 }
 
 }  // namespace sb

@@ -1357,34 +1357,12 @@ Plan plan_function(const Function& f, Precision prec) {
     }
   }
 
-  // Side-stream GEMMs (Step::side).  SHEAF_B200_SIDE_STREAM=0 keeps every
-  // step on the call's stream.
-  bool any_side = false;
-  {
-    const char* e = std::getenv("SHEAF_B200_SIDE_STREAM");
-    if (!(e && std::string(e) == "0")) {
-      std::vector<int> readers(NV, 0);
-      for (const Step& st : plan.steps)
-        for (int l : st.leaves) readers[l]++;
-      for (Step& st : plan.steps)
-        if (st.kind == StepKind::Gemm && pl.returned[st.root] && readers[st.root] == 0) {
-          st.side = true;
-          any_side = true;
-        }
-    }
-  }
-  const int end_step = (int)plan.steps.size();
-  for (const Step& st : plan.steps)
-    if (st.side)
-      for (int k : {st.gemm.a_shadow, st.gemm.b_shadow})
-        if (k >= 0) plan.shadows[k].last_use = end_step;
-
   // Arena: intermediates that are not outputs, plus split-reduction scratch.
   struct Interval { int64_t bytes; int start, end; int value; int step_scratch; };
   std::vector<Interval> iv;
   std::vector<int> last_use(NV, -1);
   for (int s = 0; s < (int)plan.steps.size(); ++s)
-    for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], plan.steps[s].side ? end_step : s);
+    for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], s);
   for (int s = 0; s < (int)plan.steps.size(); ++s) {
     // a conversion step writes a shadow (placed below), not its root value
     if (plan.steps[s].kind == StepKind::Convert) continue;
@@ -1404,7 +1382,6 @@ Plan plan_function(const Function& f, Precision prec) {
   int last_gemm = -1;
   for (int s2 = 0; s2 < (int)plan.steps.size(); ++s2)
     if (plan.steps[s2].kind == StepKind::Gemm || plan.steps[s2].kind == StepKind::Attn) last_gemm = s2;
-  if (any_side) last_gemm = end_step;
   for (int rp : plan.rounded_params)
     iv.push_back({f.value_types[rp].numel() * 4, 0, std::max(last_gemm, 0), -1, -2 - rp});
   // operand shadows: step_scratch encodes -(2 + NV + shadow index)

@@ -79,10 +79,6 @@ struct Step {
   int64_t bytes_moved = 0;      // algorithmic bytes (inputs read once + output)
   double flops = 0;
   int shadow = -1;              // Convert: index into Plan::shadows
-  // may run on the side stream: a GEMM whose result is an output that no
-  // later step reads (a weight gradient); its operands stay allocated until
-  // the end of the call, where the call joins the side stream
-  bool side = false;
 };
 
 struct Plan {

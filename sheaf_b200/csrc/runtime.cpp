@@ -78,10 +78,6 @@ struct Device {
   // all-reduced on comm_stream while the backward continues on `stream`
   cudaStream_t comm_stream = nullptr;
   cudaEvent_t ready = nullptr, reduced = nullptr;
-  // side stream: weight-gradient GEMMs run on it concurrently with the rest
-  // of the backward (Step::side); fork / join order it against `stream`
-  cudaStream_t side_stream = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
   std::atomic<uint64_t> allocated{0}, freed{0}, live{0}, peak{0};
   void note_alloc(size_t n) {
     allocated += n;
@@ -94,13 +90,6 @@ struct Device {
     live -= n;
   }
   ~Device() {
-    if (side_stream) {
-      cudaSetDevice(ordinal);
-      cudaStreamSynchronize(side_stream);
-      cudaStreamDestroy(side_stream);
-      cudaEventDestroy(fork);
-      cudaEventDestroy(join);
-    }
     if (comm_stream) {
       cudaSetDevice(ordinal);
       cudaStreamSynchronize(comm_stream);
@@ -195,7 +184,6 @@ struct LoadedFunction {
   void* arena = nullptr;
   size_t arena_cap = 0;
   void* ws = nullptr;
-  void* ws_side = nullptr;  // the side stream's GEMM workspace (same size)
   size_t ws_cap = 0;
   uint64_t calls = 0;
   // CUDA-graph replay (see run_graph)
@@ -229,8 +217,6 @@ struct sb_session {
   std::string cache_dir;
   sb::Nccl nccl;
   bool used_tc = false;  // a tcgen05 GEMM ran on this session
-  // the call being enqueued has work on the side stream not yet joined
-  bool side_active = false;
   // per-step CUDA-event timing (sb_session_set_profiling)
   bool profiling = false;
   struct Pending {
@@ -455,7 +441,6 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
   const Function& f = *lf->plan.fn;
   const Plan& plan = lf->plan;
   cudaStream_t stream = s->dev->stream;
-  s->side_active = false;
   // TF32-rounded copies of parameters read by tensor-core GEMMs
   std::map<int, const float*> rounded;
   for (size_t j = 0; j < plan.rounded_params.size(); ++j) {
@@ -524,25 +509,11 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       if (need > lf->ws_cap && capturing) return make_status(SB_STATUS_UNAVAILABLE, "workspace grows during capture");
       if (need > lf->ws_cap) {
         if (lf->ws) cudaFreeAsync(lf->ws, stream);
-        if (lf->ws_side) cudaFreeAsync(lf->ws_side, s->dev->side_stream);
-        lf->ws = lf->ws_side = nullptr;
-        lf->ws_cap = 0;
-        if (cudaMallocAsync(&lf->ws, need, stream) == cudaSuccess &&
-            cudaMallocAsync(&lf->ws_side, need, stream) == cudaSuccess)
-          lf->ws_cap = need;
-      }
-      // weight gradients run on the side stream (not while profiling: the
-      // per-step events are on the call's stream)
-      const bool on_side = st.side && !s->profiling;
-      cudaStream_t gs = stream;
-      if (on_side) {
-        SB_CUDA(cudaEventRecord(s->dev->fork, stream));
-        SB_CUDA(cudaStreamWaitEvent(s->dev->side_stream, s->dev->fork, 0));
-        gs = s->dev->side_stream;
-        s->side_active = true;
+        if (cudaMallocAsync(&lf->ws, need, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+        else lf->ws_cap = need;
       }
       bool tc = false;
-      cudaError_t e = gemm(a, s->opts.precision, on_side ? lf->ws_side : lf->ws, lf->ws_cap, gs, &tc);
+      cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
       if (tc) s->used_tc = true;
       if (e != cudaSuccess) { return cuda_status(e, "gemm"); }
       continue;
@@ -552,6 +523,7 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       cudaError_t e = scatter_add_rows(ptr[st.leaves[0]], f32, (const float*)ptr[st.leaves[1]], (float*)ptr[st.root],
                                        st.gemm.K, st.gemm.N, st.gemm.M, (char*)lf->arena + plan.scratch_offset[si],
                                        stream);
+      s->used_tc = true;  // its bounds checks report through the same error word
       if (e != cudaSuccess) { return cuda_status(e, "scatter_add_rows"); }
       continue;
     }
@@ -625,13 +597,6 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
       if (e) { return e; }
     }
-  }
-  // the side stream's GEMMs are done before the output copies (and before
-  // the call returns)
-  if (s->side_active) {
-    SB_CUDA(cudaEventRecord(s->dev->join, s->dev->side_stream));
-    SB_CUDA(cudaStreamWaitEvent(stream, s->dev->join, 0));
-    s->side_active = false;
   }
   // outputs not written by a step: copies
   for (size_t j = 0; j < f.returns.size(); ++j) {
@@ -745,10 +710,6 @@ sb_status* capture_reductions(sb_session* s, LoadedFunction* lf, const int32_t* 
     if (overlap) {
       SB_CUDA(cudaEventRecord(s->dev->ready, stream));
       SB_CUDA(cudaStreamWaitEvent(cs, s->dev->ready, 0));
-      if (s->side_active) {  // gradients written by side-stream GEMMs
-        SB_CUDA(cudaEventRecord(s->dev->join, s->dev->side_stream));
-        SB_CUDA(cudaStreamWaitEvent(cs, s->dev->join, 0));
-      }
       forked = true;
     }
     const NcclApi& api = nccl_api();
@@ -995,10 +956,6 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     if (!s->nccl.comm) return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available");
     SB_CUDA(cudaEventRecord(s->dev->ready, stream));
     SB_CUDA(cudaStreamWaitEvent(s->dev->comm_stream, s->dev->ready, 0));
-    if (s->side_active) {  // gradients written by side-stream GEMMs
-      SB_CUDA(cudaEventRecord(s->dev->join, s->dev->side_stream));
-      SB_CUDA(cudaStreamWaitEvent(s->dev->comm_stream, s->dev->join, 0));
-    }
     api.group_start();
     for (int j : bucket) {
       ncclRedOp_t op = reduce[j] == SB_REDUCE_MEAN ? ncclAvg : ncclSum;
@@ -1119,9 +1076,6 @@ sb_status* sb_session_create(const sb_session_options* o, sb_session** out) {
   s->dev->ordinal = o->device_ordinal;
   SB_CUDA(cudaSetDevice(o->device_ordinal));
   SB_CUDA(cudaStreamCreateWithFlags(&s->dev->stream, cudaStreamNonBlocking));
-  SB_CUDA(cudaStreamCreateWithFlags(&s->dev->side_stream, cudaStreamNonBlocking));
-  SB_CUDA(cudaEventCreateWithFlags(&s->dev->fork, cudaEventDisableTiming));
-  SB_CUDA(cudaEventCreateWithFlags(&s->dev->join, cudaEventDisableTiming));
   if (o->world_size > 1 && (o->flags & SB_SESSION_FLAG_OVERLAP_ALLREDUCE)) {
     SB_CUDA(cudaStreamCreateWithFlags(&s->dev->comm_stream, cudaStreamNonBlocking));
     SB_CUDA(cudaEventCreateWithFlags(&s->dev->ready, cudaEventDisableTiming));
@@ -1178,7 +1132,6 @@ void sb_session_release(sb_session* s) {
       for (auto& [v, p] : lf->const_ptr) cudaFree(p);
       if (lf->arena) cudaFree(lf->arena);
       if (lf->ws) cudaFree(lf->ws);
-      if (lf->ws_side) cudaFree(lf->ws_side);
       for (void* p : lf->stage_buf)
         if (p) cudaFree(p);
     }

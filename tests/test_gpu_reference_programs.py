@@ -5,7 +5,9 @@ logits).  The vocabulary of 50257 puts every lm_head operand off 16-byte rows
 (the padded-operand path of the tensor-core GEMMs).
 
 Tolerances: TF32 mode 2e-3 norm-relative on the logits and on every gradient
-leaf, 2e-3 relative on the loss; fp32 mode 1e-5 norm-relative on the logits.
+leaf; fp32 mode 1e-5 norm-relative on the logits.  The loss is the mean of
+3.2 M logits of magnitude ~1 that cancel to ~3e-4, so its error is bounded
+relative to the mean absolute logit: 2e-3 of it.
 """
 import numpy as np
 import pytest
@@ -45,6 +47,9 @@ def test_bench_value_and_grad(tf32_session, inputs):
     if not tf32_session.has_function(low.qualified):
         tf32_session.load_stablehlo(low.text)
     outs = tf32_session.call(low.qualified, ins)
-    assert abs(float(outs[0]) - float(ref[0])) <= 2e-3 * abs(float(ref[0])), (float(outs[0]), float(ref[0]))
+    fwd = M.bench_forward_program()
+    scale = float(np.mean(np.abs(run(fwd.text, fwd.qualified, [inputs[n] for n in fwd.arg_names],
+                                     dtype=np.float32)[0])))
+    assert abs(float(outs[0]) - float(ref[0])) <= 2e-3 * scale, (float(outs[0]), float(ref[0]), scale)
     errs = [_rel(o, r) for o, r in zip(outs[1:], ref[1:])]
     assert max(errs) <= 2e-3, max(errs)
