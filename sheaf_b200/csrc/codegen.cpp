@@ -188,7 +188,8 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
       // innermost index is the lane coordinate itself: lanes 0..3 read 4
       // consecutive floats starting at a multiple of 4 (row-major leaf whose
       // innermost extent is a multiple of 4, lane 0 coordinate cL % 4 == 0)
-      if (t.dtype != DType::F32 || t.shape.back() % 4 || c.memo.size() > 1) throw VecFail{};
+      if ((t.dtype != DType::F32 && t.dtype != DType::BF16) || t.shape.back() % 4 || c.memo.size() > 1)
+        throw VecFail{};
       std::string off0 = "0";
       for (size_t i = 0; i + 1 < coords.size(); ++i) off0 = c_add(off0, c_mul(coords[i], st[i]));
       off0 = c_add(off0, base);
@@ -197,7 +198,11 @@ CodeGen::Val CodeGen::leaf_load(Ctx& c, int v, const std::vector<std::string>& c
       std::string var;
       if (vit == c.vloads.end()) {
         var = fresh(c, "v");
-        c.body << c.pad() << "const float4 " << var << " = *(const float4*)(L" << li << " + " << off0 << ");\n";
+        if (t.dtype == DType::BF16)  // 4 bf16 in 8 bytes, widened
+          c.body << c.pad() << "const float4 " << var << " = sb_bf16x4(*(const uint2*)(L" << li << " + " << off0
+                 << "));\n";
+        else
+          c.body << c.pad() << "const float4 " << var << " = *(const float4*)(L" << li << " + " << off0 << ");\n";
         c.vloads[key] = var;
       } else {
         var = vit->second;
@@ -532,8 +537,8 @@ std::string CodeGen::header(const std::string& name, const Ctx& c, int extra_ptr
 void CodeGen::gen_loop(const Op& root, Step* st) {
   {
     const auto& sh = root.type.shape;
-    if (!sh.empty() && sh.back() % 4 == 0 && root.type.numel() > 0 && root.type.dtype == DType::F32 &&
-        gen_loop_vec4(root, st))
+    if (!sh.empty() && sh.back() % 4 == 0 && root.type.numel() > 0 &&
+        (root.type.dtype == DType::F32 || root.type.dtype == DType::BF16) && gen_loop_vec4(root, st))
       return;
   }
   const std::string start_text = src_.str();
@@ -632,20 +637,26 @@ bool CodeGen::gen_loop_vec4(const Op& root, Step* st) {
   } snip{this, start_text.size()};
   std::string name = "k" + std::to_string(names_.size());
   const int64_t nv = n / 4;
+  const bool obf = root.type.dtype == DType::BF16;
   src_ << header(name, c, 0);
-  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  src_ << "  " << mtype_of(root.type.dtype) << "* __restrict__ O = (" << mtype_of(root.type.dtype) << "*)a.p["
+       << c.leaves.size() << "];\n";
   src_ << "  for (" << c.idx << " i = (" << c.idx << ")blockIdx.x * " << kThreads << " + threadIdx.x; i < ("
        << c.idx << ")" << nv << "; i += (" << c.idx << ")gridDim.x * " << kThreads << ") {\n";
   src_ << pre.str();
   src_ << c.body.str();
-  src_ << "    *(float4*)(O + i * 4) = make_float4(" << lanes[0] << ", " << lanes[1] << ", " << lanes[2] << ", "
-       << lanes[3] << ");\n  }\n}\n\n";
+  if (obf)  // 4 bf16 in one 8-byte store
+    src_ << "    *(uint2*)(O + i * 4) = make_uint2(sb_pack2(" << lanes[0] << ", " << lanes[1] << "), sb_pack2("
+         << lanes[2] << ", " << lanes[3] << "));\n  }\n}\n\n";
+  else
+    src_ << "    *(float4*)(O + i * 4) = make_float4(" << lanes[0] << ", " << lanes[1] << ", " << lanes[2] << ", "
+         << lanes[3] << ");\n  }\n}\n\n";
   names_.push_back(name);
   st->kernel = name;
   st->leaves = c.leaves;
   st->block = kThreads;
   st->grid = std::max<int64_t>(1, std::min<int64_t>((nv + kThreads - 1) / kThreads, kMaxGrid));
-  int64_t bytes = n * 4;
+  int64_t bytes = n * dtype_bytes(root.type.dtype);
   for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
   st->bytes_moved = bytes;
   return true;
@@ -698,7 +709,12 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
   const Type& in = f_.value_types[root.operands[0]];
   const auto& ish = in.shape;
   const int r = (int)ish.size();
-  if (r == 0 || ish[r - 1] % 4 || root.type.dtype != DType::F32 || in.dtype != DType::F32) return false;
+  auto fp = [](DType t) { return t == DType::F32 || t == DType::BF16; };
+  if (r == 0 || ish[r - 1] % 4 || !fp(root.type.dtype) || !fp(in.dtype) || (epi && !fp(epi->type.dtype)))
+    return false;
+  // bf16 (input or stored output): row mode only (its stores are scalar)
+  const bool any_bf = root.type.dtype == DType::BF16 || in.dtype == DType::BF16 ||
+                      (epi && epi->type.dtype == DType::BF16);
   std::vector<int64_t> rd(root.dims.begin(), root.dims.end());
   std::sort(rd.begin(), rd.end());
   std::vector<int64_t> kd;
@@ -711,7 +727,7 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
   const bool inner_reduced = !rd.empty() && rd.back() == r - 1;
   int mode;
   if (trailing && R <= 4096 && inner_reduced) mode = 0;
-  else if (!epi && !trailing && !inner_reduced && !kd.empty() && kd.back() == r - 1) mode = 2;
+  else if (!any_bf && !epi && !trailing && !inner_reduced && !kd.empty() && kd.back() == r - 1) mode = 2;
   else return false;
   if (R == 0 || O == 0) return false;
   const char* ident = root.body == ReduceBody::Add ? "0.f"
@@ -815,7 +831,10 @@ bool CodeGen::gen_reduce_vec4(const Op& root, Step* st, const Op* epi) {
   } snip{this, start_text.size()};
   std::string name = "k" + std::to_string(names_.size());
   src_ << header(name, c, mode == 2 && splits > 1 ? 1 : 0);
-  src_ << "  float* __restrict__ O = (float*)a.p[" << c.leaves.size() << "];\n";
+  {
+    const char* ot = mtype_of((epi ? *epi : root).type.dtype);
+    src_ << "  " << ot << "* __restrict__ O = (" << ot << "*)a.p[" << c.leaves.size() << "];\n";
+  }
   if (mode == 0) {
     src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
     src_ << "  for (" << c.idx << " o = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; o < " << O
@@ -1168,7 +1187,14 @@ std::string CodeGen::prelude() {
          "  asm(\"cvt.rn.bf16.f32 %0, %1;\" : \"=h\"(h) : \"f\"(x));\n"
          "  return h;\n"
          "}\n"
-         "__device__ __forceinline__ float sb_bf16_rn(float x) { return sb_bf16_ld(sb_bf16_bits(x)); }\n";
+         "__device__ __forceinline__ float sb_bf16_rn(float x) { return sb_bf16_ld(sb_bf16_bits(x)); }\n"
+         "__device__ __forceinline__ float4 sb_bf16x4(uint2 u) {\n"
+         "  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),\n"
+         "                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));\n"
+         "}\n"
+         "__device__ __forceinline__ unsigned sb_pack2(unsigned short lo, unsigned short hi) {\n"
+         "  return (unsigned)lo | ((unsigned)hi << 16);\n"
+         "}\n";
 }
 
 bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t C, Step* st) {
