@@ -164,6 +164,7 @@ struct OutSlot {
   std::vector<void*> direct_in;     // input addresses baked into exec (staged inputs: nullptr)
   uint64_t kernels = 0;             // kernels in exec
   std::vector<Bucket> buckets;      // captured all-reduces (data parallel)
+  std::vector<int32_t> reduce_sig;  // per output reduction the graph applies (empty: none)
   ~OutSlot() {
     if (!dev) return;
     cudaSetDevice(dev->ordinal);
@@ -794,21 +795,25 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
   std::vector<void*> direct(nin, nullptr);
   for (size_t i = 0; i < nin; ++i)
     if (!lf->staged[i]) direct[i] = in[i]->ptr;
+  // slots are laid out and captured for one reduction signature
+  std::vector<int32_t> sig;
+  if (dp) sig.assign(reduce, reduce + f.returns.size());
   std::shared_ptr<OutSlot> slot;
   for (auto& sl : lf->slots)
-    if (sl->held.load() == 0 && sl->exec && sl->direct_in == direct) { slot = sl; break; }
+    if (sl->held.load() == 0 && sl->reduce_sig == sig && sl->exec && sl->direct_in == direct) { slot = sl; break; }
   if (!slot)
     for (auto& sl : lf->slots)
-      if (sl->held.load() == 0) { slot = sl; break; }
+      if (sl->held.load() == 0 && sl->reduce_sig == sig) { slot = sl; break; }
   if (!slot) {
     if ((int)lf->slots.size() >= kMaxSlots) return nullptr;  // all outputs held: eager
     auto sl = std::make_shared<OutSlot>();
     sl->dev = s->dev;
+    sl->reduce_sig = sig;
     size_t total = 0;
     sl->off.assign(f.returns.size(), 0);
-    for (int j : output_order(lf, dp ? reduce : nullptr)) {
-      const int v = f.returns[j];
-      sl->off[j] = total;
+    for (int jj : output_order(lf, dp ? reduce : nullptr)) {
+      const int v = f.returns[jj];
+      sl->off[jj] = total;
       total += ((size_t)f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype) + 255) & ~size_t(255);
     }
     if (total) SB_CUDA(cudaMalloc(&sl->base, total));
@@ -842,10 +847,16 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
     if (!st && e == cudaSuccess) e = cudaGraphInstantiate(&slot->exec, graph, 0);
     if (graph) cudaGraphDestroy(graph);
     if (st || e != cudaSuccess) {
+      slot->exec = nullptr;
+      if (dp) {
+        // every rank must issue the same collectives: no silent fallback to
+        // the eager path's per-leaf all-reduces
+        if (st) return st;
+        return cuda_status(e, "capturing a data-parallel call");
+      }
       // not capturable (e.g. the workspace would have to grow): eager from now on
       if (st) sb_status_free(st);
       cudaGetLastError();
-      slot->exec = nullptr;
       lf->graphs_off = true;
       return nullptr;
     }
