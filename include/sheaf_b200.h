@@ -50,12 +50,14 @@ typedef enum sb_status_code {
 #define SB_ELEMENT_TYPE_BFLOAT_16 ((0x31u << 24) | 16u)
 #define SB_ELEMENT_TYPE_INT_32 ((0x11u << 24) | 32u)
 
-/* Arithmetic used for dot_general contractions.  Non-contraction ops are
- * always computed in f32. */
+/* Arithmetic used for dot_general contractions of f32 tensors.  Other ops
+ * compute in the graph's types (f32; bf16 tensors as bf16, rounding every op's
+ * result).  A dot_general of bf16 tensors always runs on tcgen05 kind::f16. */
 typedef enum sb_precision {
   SB_PRECISION_FP32 = 0, /* f32 FMA on CUDA cores */
-  SB_PRECISION_TF32 = 1, /* tcgen05 kind::tf32, f32 accumulate */
-  SB_PRECISION_BF16 = 2, /* tcgen05 kind::f16 on bf16 operands, f32 accumulate */
+  SB_PRECISION_TF32 = 1, /* tcgen05 kind::tf32 on operands rounded to nearest TF32, f32 accumulate */
+  SB_PRECISION_BF16 = 2, /* GEMM operands converted to bf16 (round to nearest even), tcgen05 kind::f16,
+                            f32 accumulate; fused attention in TF32 */
 } sb_precision;
 
 /* How an output of a data-parallel call is combined across ranks. */
@@ -76,7 +78,9 @@ typedef struct sb_session_options {
   uint32_t flags;               /* SB_SESSION_FLAG_* */
 } sb_session_options;
 
-#define SB_SESSION_FLAG_NO_CUDA_GRAPH 1u /* launch kernels one by one instead of replaying a graph */
+/* Launch every call's kernels one by one.  By default a function's calls from
+ * the second on replay a CUDA graph of its steps (one launch per call). */
+#define SB_SESSION_FLAG_NO_CUDA_GRAPH 1u
 /* TF32: keep the attention region on the generic fused-loop + GEMM path instead
  * of the fused tcgen05 attention kernels (for A/B parity checks). */
 #define SB_SESSION_FLAG_NO_ATTENTION_FUSION 2u
@@ -128,7 +132,13 @@ SB_API int sb_session_has_function(sb_session* session, const char* qualified_na
  *     IreeSession::call_device, iree_session.rs:574) ---------------------- *
  * inputs are borrowed; each returned output carries one reference owned by the
  * caller.  `output_reduce` (may be NULL) gives an sb_reduce_op per output for
- * data-parallel sessions; NULL means SB_REDUCE_NONE for every output. */
+ * data-parallel sessions; NULL means SB_REDUCE_NONE for every output.
+ * From the second call of a function on, the call replays a CUDA graph of its
+ * steps (and, data parallel, of its all-reduce): the outputs then live in one
+ * of up to 4 output sets of the function, reused by a later call once every
+ * output of the set has been released; a call finding all sets held runs
+ * eagerly into fresh buffers.  Inputs whose address changes between calls are
+ * copied into library-owned staging buffers by the replay. */
 SB_API sb_status* sb_session_call(sb_session* session, const char* qualified_name,
                                   sb_buffer* const* inputs, size_t input_count,
                                   const int32_t* output_reduce,

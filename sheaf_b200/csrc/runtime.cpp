@@ -907,7 +907,7 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   SB_CUDA(cudaSetDevice(s->dev->ordinal));
   const Plan& plan = lf->plan;
   // calls replay a CUDA graph from the second call on (run_graph)
-  if (graphs_enabled() && !s->profiling && !lf->graphs_off) {
+  if (graphs_enabled() && !(s->opts.flags & SB_SESSION_FLAG_NO_CUDA_GRAPH) && !s->profiling && !lf->graphs_off) {
     bool used = false;
     sb_status* st = run_graph(s, lf, in, nin, reduce, out, nout, &used);
     if (st || used) return st;
