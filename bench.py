@@ -47,7 +47,7 @@ def parse():
                    choices=["fp32", "tf32", "bf16"])
     p.add_argument("--workload", default="nanogpt",
                    choices=["nanogpt", "nanogpt-fwd", "nanogpt-train", "nanogpt-generate", "gpt2", "mlp", "matmul",
-                            "ref-vag", "ref-forward", "sweep"])
+                            "ref-vag", "ref-forward", "sweep", "nanogpt-decode"])
     p.add_argument("--op", default="softmax", choices=["softmax", "layer-norm", "gelu"],
                    help="sweep workload: the op (on [65536, --dim], gelu on 2^28 elements)")
     p.add_argument("--dim", type=int, default=768, help="sweep workload: D of [65536, D]")
@@ -604,6 +604,87 @@ def run_sweep(args):
     sess.close()
 
 
+def run_decode(args):
+    """Decoding with the key/value cache: nanoGPT (6 layers, d384, T 256), one
+    new token per step (forward of one position against the cached keys and
+    values, top-k 200 sampling at temperature 0.8); the sampled id and the
+    updated caches feed the next step on the device.  W warm-up steps feed the
+    start of a random prompt; the K timed steps continue the sequence.  e2e
+    adds the read-back of each step's token id to the host."""
+    import torch
+    from sheaf_b200 import build
+    from sheaf_b200.session import B200Session, library
+    from sheaf_lowering import generate as G
+    from sheaf_lowering import models as M
+    from sheaf_lowering import random as RG
+    build.build()
+    c = M.NANOGPT
+    if args.warmup + args.steps > c.T:
+        raise SystemExit(f"--warmup + --steps must be <= {c.T} positions")
+    low = G.gpt_decode_program(c, 200, 0.8)
+    inp = M.gpt_inputs(c, batch=1, seed=0)
+    sess = B200Session(precision=args.precision)
+    t0 = time.time()
+    sess.load_stablehlo(low.text)
+    load_s = time.time() - t0
+    params = [sess.buffer(inp[n]) for n, _ in M.gpt_param_leaves(c)]
+    caches = [sess.buffer(np.zeros(sh, np.float32)) for _, sh in G.cache_leaves(c)]
+    key = sess.buffer(RG.key_of_seed(1337))
+    q = low.qualified
+    pos_bufs = [sess.buffer(np.float32([p])) for p in range(args.warmup + args.steps)]
+    tok = sess.buffer(np.float32([[inp["idx"][0, 0]]]))
+    # a [] -> [1, 1] reshape of the sampled id, as the sampling loop does
+    rs = ("module @tok_reshape {\n func.func @f(%arg0: tensor<f32>) -> tensor<1x1xf32> {\n"
+          "    %0 = stablehlo.reshape %arg0 : (tensor<f32>) -> tensor<1x1xf32>\n"
+          "    return %0 : tensor<1x1xf32>\n }\n}\n")
+    sess.load_stablehlo(rs)
+
+    def advance(p, tok, caches, key, read_back=False):
+        """One step; releases the step's inputs that earlier steps produced."""
+        outs = sess.call_device(q, params + caches + [tok, pos_bufs[p], key])
+        nt = sess.call_device("tok_reshape.f", [outs[0]])[0]
+        if read_back:
+            float(outs[0].to_host())
+        outs[0].release()
+        for b in [tok, key] + caches:
+            b.release()
+        return nt, outs[2:], outs[1]
+
+    for p in range(args.warmup):
+        tok, caches, key = advance(p, tok, caches, key)
+    sess.synchronize()
+    stream = torch.cuda.ExternalStream(sess.cuda_stream)
+    lib = library()
+    n0 = lib.sb_kernel_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        e0.record(stream)
+        for p in range(args.warmup, args.warmup + args.steps):
+            tok, caches, key = advance(p, tok, caches, key)
+        e1.record(stream)
+        e1.synchronize()
+    launches = int(lib.sb_kernel_launch_count() - n0)
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: the same positions again, each sampled id read back to the host
+    h0 = time.perf_counter()
+    for p in range(args.warmup, args.warmup + args.steps):
+        tok, caches, key = advance(p, tok, caches, key, read_back=True)
+    ems = (time.perf_counter() - h0) * 1e3 / args.steps
+    print(json.dumps({"metric": "KV-cache decode tokens/s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "scaling": "none", "vs_baseline": None, "dtype": "f32", "contraction": args.precision,
+                      "data": "synthetic: seeded N(0,0.02) weights, random prompt",
+                      "config": {"workload": f"nanogpt decode with key/value cache (top-k 200, temperature 0.8), "
+                                             f"positions {args.warmup}..{args.warmup + args.steps - 1} of {c.T}",
+                                 "model": f"L{c.n_layer} D{c.n_embd} H{c.n_head} T{c.T} V{c.vocab_size}",
+                                 "l2": "weights and caches (48 MB) fit in L2: latency-bound by design"},
+                      "clocks": clk.summary(), "gpu_launches": launches,
+                      "e2e": {"value": 1e3 / ems, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 4, "note": "host wall clock per step incl. the id read-back"},
+                      "module_load_s": load_s}), flush=True)
+    sess.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -612,6 +693,8 @@ def main():
         run_matmul(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "nanogpt-decode":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -94,3 +94,94 @@ def gpt_generate_program(c, top_k: int = 200, temp: float = 0.8) -> Lowered:
     out += body + rng.lines + e.body
     out += [f"    return {nid}, {new_key} : tensor<f32>, tensor<2xf32>", " }", "}"]
     return Lowered("\n".join(out) + "\n", fwd.module + "_gen", "generate_token", fwd.arg_names + ["key"], [], [])
+
+
+# ---------------------------------------------------------------------------
+# Decoding with a key/value cache (the roadmap's KV-cache item,
+# docs/roadmap.md:40-41; the reference's sample.shf reruns the whole window):
+# one new token at position `pos` per call.  Each layer's cache holds the keys
+# and values of positions 0..T-1 ([H, T, 64]); the call writes this
+# position's key and value into it (a 0/1 blend with one_hot(pos), exact in
+# float) and attends over positions <= pos (one_hot(pos) @ tril(ones) marks
+# them).  Fed a prompt one token at a time, the logits at position p equal the
+# full forward's logits at p on the prefix 0..p.
+# ---------------------------------------------------------------------------
+
+def cache_leaves(c):
+    Hd = c.n_embd // c.n_head
+    out = []
+    for i in range(c.n_layer):
+        out += [(f"cache.{i}.k", (c.n_head, c.T, Hd)), (f"cache.{i}.v", (c.n_head, c.T, Hd))]
+    return out
+
+
+def _decode_forward(t, s, c):
+    from .lower import Vec
+    D, H, T = c.n_embd, c.n_head, c.T
+    Hd = D // H
+    tok, pos = s["token"], s["pos"]
+    x = t("+", t("get", s["transformer.wte.weight"], tok),
+          t("reshape", t("get", s["transformer.wpe.weight"], pos), Vec([1, 1, D])))
+    oh = t("one-hot", pos, T)                                   # [1, T]
+    valid = t("@", oh, t("tril", t("ones", Vec([T, T]))))       # positions <= pos
+    m3 = t("reshape", oh, Vec([1, T, 1]))
+    keep = t("-", 1.0, m3)
+    caches = []
+    for i in range(c.n_layer):
+        p = f"transformer.h.{i}."
+        h = M.layer_norm_nb(t, x, s[p + "ln_1.weight"])
+        W = s[p + "attn.c_attn.weight"]
+
+        def heads(w):
+            return t("swapaxes", t("reshape", t("@", h, t("tr", w)), Vec([1, H, Hd])), 0, 1)  # [H, 1, Hd]
+        q = heads(t("slice", W, 0, D))
+        k = heads(t("slice", W, D, 2 * D))
+        v = heads(t("slice", W, 2 * D, 3 * D))
+        K = t("+", t("*", s[f"cache.{i}.k"], keep), t("*", k, m3))
+        Vc = t("+", t("*", s[f"cache.{i}.v"], keep), t("*", v, m3))
+        att = t("/", t("@", q, t("swapaxes", K, -1, -2)), t("sqrt", float(Hd)))    # [H, 1, T]
+        att = M.softmax(t, t("where", t("==", valid, 1.0), att, -1e10))
+        y = t("reshape", t("swapaxes", t("@", att, Vc), 0, 1), Vec([1, 1, D]))
+        x = t("+", x, t("@", y, t("tr", s[p + "attn.c_proj.weight"])))
+        x = t("+", x, M.mlp_block(t, M.layer_norm_nb(t, x, s[p + "ln_2.weight"]), s, p))
+        caches += [K, Vc]
+    x = M.layer_norm_nb(t, x, s["transformer.ln_f.weight"])
+    return [t("@", x, t("tr", s["lm_head.weight"]))] + caches   # logits [1, 1, V]
+
+
+def gpt_decode_forward_program(c) -> Lowered:
+    """The decoding step's forward: (params..., caches..., token [1, 1], pos [1])
+    -> (logits [1, 1, V], caches...)."""
+    from .lower import lower_forward
+    args = M.gpt_param_leaves(c) + cache_leaves(c) + [("token", (1, 1)), ("pos", (1,))]
+    return lower_forward(lambda t, s: _decode_forward(t, s, c), args, "decode_fwd", key=f"gpt-decode-{c}")
+
+
+def gpt_decode_program(c, top_k: int = 200, temp: float = 0.8) -> Lowered:
+    """One decoding step: (params..., caches..., token [1, 1], pos [1], key) ->
+    (next_id, new_key, caches...), sampling as generate-token does."""
+    fwd = gpt_decode_forward_program(c)
+    lines = fwd.text.splitlines()
+    fi = next(i for i, l in enumerate(lines) if "func.func" in l)
+    ri = next(i for i in range(len(lines) - 1, -1, -1) if lines[i].strip().startswith("return"))
+    ret = lines[ri].strip()[len("return"):].split(":")[0]
+    vals = [x.strip() for x in ret.split(",")]
+    logits, cache_vals = vals[0], vals[1:]
+    body = lines[fi + 1:ri]
+    top = max(int(n) for n in re.findall(r"%(\d+)\b", "\n".join(body)))
+    e = Emitter()
+    e.counter = top + 1
+    rng = RandomEmitter()
+    key = f"%arg{len(fwd.arg_names)}"
+    nid, new_key = _tail(e, rng, logits, 1, c.vocab_size, top_k, temp, key)
+    sig = lines[fi]
+    m = re.match(r"(\s*func\.func @)\w+\((.*)\)\s*->\s*.*\{\s*$", sig)
+    params = m.group(2) + f", {key}: tensor<2xf32>"
+    Hd = c.n_embd // c.n_head
+    ct = f"tensor<{c.n_head}x{c.T}x{Hd}xf32>"
+    head = [l.replace(f"module @{fwd.module} ", f"module @{fwd.module}_dec ") for l in lines[:fi]]
+    res_types = ", ".join(["tensor<f32>", "tensor<2xf32>"] + [ct] * len(cache_vals))
+    out = head + [f"{m.group(1)}decode_token({params}) -> ({res_types}) {{"]
+    out += body + rng.lines + e.body
+    out += [f"    return {', '.join([nid, new_key] + cache_vals)} : {res_types}", " }", "}"]
+    return Lowered("\n".join(out) + "\n", fwd.module + "_dec", "decode_token", fwd.arg_names + ["key"], [], [])

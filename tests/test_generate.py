@@ -73,3 +73,58 @@ def test_device_generate_tokens(fp32_session):
         # slide-window (sample.shf: append-and-roll)
         ids = np.concatenate([ids[:, 1:], np.float32([[nid]])], axis=1)
         key = nkey
+
+
+def test_decode_program_plans(lib):
+    from sheaf_b200.session import inspect_module
+    c = M.GPTConfig(2, 2, 64, 64, 65, 1, 64)
+    assert "sort=1" in inspect_module(G.gpt_decode_program(c).text, "fp32")
+
+
+@pytest.mark.gpu
+def test_kv_cache_logits_equal_full_forward(fp32_session):
+    """Decoding with the key/value cache: the logits at position p (prompt fed
+    one token per call) equal the full forward's last-position logits on the
+    prefix 0..p (the oracle), within the fp32 tolerance."""
+    c = M.GPTConfig(2, 2, 64, 64, 65, 1, 64)
+    dec = G.gpt_decode_forward_program(c)
+    inp = M.gpt_inputs(c, batch=1, seed=5)
+    params = [inp[n] for n, _ in M.gpt_param_leaves(c)]
+    caches = [np.zeros(s, np.float32) for _, s in G.cache_leaves(c)]
+    toks = inp["idx"][0, :5]
+    fp32_session.load_stablehlo(dec.text)
+    for p, tk in enumerate(toks):
+        outs = fp32_session.call(dec.qualified, params + caches + [np.float32([[tk]]), np.float32([p])])
+        logits, caches = outs[0], outs[1:]
+        f = M.gpt_fwd(M.GPTConfig(2, 2, 64, 64, 65, 1, p + 1), batch=1)
+        fi = {**inp, "idx": toks[None, :p + 1].astype(np.float32)}
+        ref = run(f.text, f.qualified, [fi[n] for n in f.arg_names])[0][0, -1]
+        assert np.max(np.abs(logits[0, 0] - ref)) <= 1e-5 * np.max(np.abs(ref))
+
+
+@pytest.mark.gpu
+def test_device_decode_tokens(fp32_session):
+    """A 4-token prompt fed through the cache, then 4 sampled tokens: every
+    call's next id, key and caches are those of the oracle run of the same
+    program."""
+    c = M.GPTConfig(2, 2, 64, 64, 65, 1, 64)
+    low = G.gpt_decode_program(c, 200, 0.8)
+    inp = M.gpt_inputs(c, batch=1, seed=6)
+    params = [inp[n] for n, _ in M.gpt_param_leaves(c)]
+    caches = [np.zeros(s, np.float32) for _, s in G.cache_leaves(c)]
+    rcaches = list(caches)
+    key = RG.key_of_seed(99)
+    fp32_session.load_stablehlo(low.text)
+    tok = float(inp["idx"][0, 0])
+    for p in range(8):
+        if p < 4:
+            tok = float(inp["idx"][0, p])
+        args = [np.float32([[tok]]), np.float32([p]), key]
+        outs = fp32_session.call(low.qualified, params + caches + args)
+        ref = run(low.text, low.qualified, params + rcaches + args, dtype=np.float32)
+        assert float(outs[0]) == float(ref[0])
+        assert np.array_equal(outs[1].view(np.int32), ref[1].view(np.int32))
+        for a, b in zip(outs[2:], ref[2:]):
+            np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-6)
+        caches, rcaches, key = outs[2:], ref[2:], outs[1]
+        tok = float(outs[0])
