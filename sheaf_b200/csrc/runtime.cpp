@@ -11,6 +11,7 @@
 #include <chrono>
 #include <functional>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -628,6 +629,20 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
 constexpr int kMaxSlots = 4;
 constexpr size_t kMaxStagedBytes = 64u << 20;
 
+// SHEAF_B200_GRAPH_LOG=1: one stderr line per call saying how it ran
+// (captured, replayed, or eager and why).
+bool graph_log_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("SHEAF_B200_GRAPH_LOG");
+    return e && std::string(e) == "1";
+  }();
+  return on;
+}
+
+void graph_log(const LoadedFunction* lf, const std::string& what) {
+  if (graph_log_on()) std::fprintf(stderr, "sheaf_b200: @%s: %s\n", lf->qname.c_str(), what.c_str());
+}
+
 bool graphs_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("SHEAF_B200_GRAPHS");
@@ -781,7 +796,10 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
     }
     lf->last_in[i] = in[i]->ptr;
   }
-  if (first) return nullptr;  // eager: tunes the GEMMs, sizes the workspace
+  if (first) {  // eager: tunes the GEMMs, sizes the workspace
+    graph_log(lf, "eager (first call)");
+    return nullptr;
+  }
   if (restage)                // graphs captured before read those inputs in place
     for (auto& sl : lf->slots)
       if (sl->exec) {
@@ -805,7 +823,10 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
     for (auto& sl : lf->slots)
       if (sl->held.load() == 0 && sl->reduce_sig == sig) { slot = sl; break; }
   if (!slot) {
-    if ((int)lf->slots.size() >= kMaxSlots) return nullptr;  // all outputs held: eager
+    if ((int)lf->slots.size() >= kMaxSlots) {
+      graph_log(lf, "eager (every output set is held)");
+      return nullptr;
+    }
     auto sl = std::make_shared<OutSlot>();
     sl->dev = s->dev;
     sl->reduce_sig = sig;
@@ -855,18 +876,22 @@ sb_status* run_graph(sb_session* s, LoadedFunction* lf, sb_buffer* const* in, si
         return cuda_status(e, "capturing a data-parallel call");
       }
       // not capturable (e.g. the workspace would have to grow): eager from now on
+      std::fprintf(stderr, "sheaf_b200: @%s is not captured into a CUDA graph (%s); its calls run eagerly\n",
+                   lf->qname.c_str(), st ? sb_status_message(st) : cudaGetErrorString(e));
       if (st) sb_status_free(st);
       cudaGetLastError();
       lf->graphs_off = true;
       return nullptr;
     }
     slot->direct_in = direct;
+    graph_log(lf, "captured (" + std::to_string(slot->kernels) + " kernels)");
   }
   // refresh the staged inputs, then replay
   for (size_t i = 0; i < nin; ++i)
     if (lf->staged[i] && in[i]->bytes)
       SB_CUDA(cudaMemcpyAsync(lf->stage_buf[i], in[i]->ptr, in[i]->bytes, cudaMemcpyDeviceToDevice, stream));
   SB_CUDA(cudaGraphLaunch(slot->exec, stream));
+  graph_log(lf, "replayed");
   // the replay launches the captured kernels
   launch_counter().fetch_add(slot->kernels, std::memory_order_relaxed);
   for (size_t j = 0; j < f.returns.size(); ++j) {
