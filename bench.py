@@ -36,6 +36,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "value-and-grad steps/s & tokens/s at 1/2/4/8 B200; % of TC/HBM roofline"
 
+# DRAM bytes (read + write) per GEMM launch, averaged over one step's GEMM
+# launches, from an ncu capture of the same workload on one GPU (the bench
+# itself runs no profiler): (workload, batch per rank, precision) -> (bytes,
+# capture summary)
+GEMM_TRAFFIC = {
+    ("nanogpt", 64, "tf32"): (76.85e6, "profiles/gemm_dram_traffic_nanogpt_vag.md"),
+}
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -464,6 +472,9 @@ def run_ours(args):
             roof = {"bound": "tensor", "kernel": "gemm (all dot_general launches)", "achieved": ach, "peak": tc,
                     "unit": "TFLOP/s", "frac": ach / tc, "traffic": None, "peak_source": src,
                     "flops_per_step": gflops, "launches_per_step": len(gem), "share_of_step": gms / allms}
+            key = (args.workload, (cfg.get("global_batch") or 0) // world, args.precision)
+            if key in GEMM_TRAFFIC:
+                roof["traffic"], roof["traffic_source"] = GEMM_TRAFFIC[key]
     data = ("synthetic: seeded N(0,1) inputs, Xavier-uniform weights, one-hot labels" if args.workload == "mlp"
             else "synthetic: seeded N(0,0.02) weights, uniform tokens")
     result = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
@@ -670,6 +681,20 @@ def run_decode(args):
     for p in range(args.warmup, args.warmup + args.steps):
         tok, caches, key = advance(p, tok, caches, key, read_back=True)
     ems = (time.perf_counter() - h0) * 1e3 / args.steps
+    dump = os.environ.get("SHEAF_B200_PROFILE_CSV")
+    if dump:
+        # per-kernel device time of the decode step (the last position again,
+        # CUDA events around each launch), for the profile summary
+        sess.set_profiling(True)
+        for _ in range(4):
+            tok, caches, key = advance(args.warmup + args.steps - 1, tok, caches, key)
+        rows = sess.profile_report()
+        sess.set_profiling(False)
+        with open(dump, "w") as fh:
+            fh.write("function,step,kind,kernel,calls,total_ms,elements,bytes,flops\n")
+            for r in rows:
+                fh.write(f"{r['function']},{r['step']},{r['kind']},{r['kernel']},{r['calls']},{r['total_ms']:.6f},"
+                         f"{r['elements']},{r['bytes']},{r['flops']}\n")
     print(json.dumps({"metric": "KV-cache decode tokens/s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                       "scaling": "none", "vs_baseline": None, "dtype": "f32", "contraction": args.precision,

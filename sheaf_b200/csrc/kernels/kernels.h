@@ -23,7 +23,18 @@ struct GemmArgs {
   // split-K (batch == 1 only): when > 0, "batch" index s computes the K range
   // [s*k_chunk, min(K, (s+1)*k_chunk)) into c + s*scb
   int64_t k_chunk = 0;
+  // split-K completed by the tensor-core kernel itself (the last K slice of
+  // each output tile adds the partials into fix_c, row stride fix_ldc, rounded
+  // to TF32 when fix_round): set with k_chunk by the dispatcher
+  float* fix_c = nullptr;
+  int64_t fix_ldc = 0;
+  int fix_round = 0;
+  // kFixupCounters ints, zero between launches, owned by the caller's stream
+  // (nullptr: split-K partials are added by a separate reduction kernel)
+  int* tile_counters = nullptr;
 };
+
+constexpr int64_t kFixupCounters = 8192;
 
 // C[i] = sum_s P[s*M*N + i] over `splits` partial products (row-major M x N
 // partials, C with leading dimension ldc), optionally rounded to TF32.
@@ -53,6 +64,12 @@ cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_
 
 // f32 FMA on CUDA cores; any strides.
 cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream);
+
+// GEMMs with at most kSkinnyMax rows (or, transposed, columns) run on the
+// CUDA cores, B streamed once: no workspace, f32 FMA in every precision mode.
+constexpr int64_t kSkinnyMax = 8;
+bool gemm_is_skinny(const GemmArgs& g);
+cudaError_t gemm_skinny(const GemmArgs& g, cudaStream_t stream);
 
 // tcgen05 tensor-core GEMM (kind::tf32 on f32 operands).  tc_plan fixes the
 // split-K factor of a problem by a rule on its shape and proposes a kernel

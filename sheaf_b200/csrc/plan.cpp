@@ -995,7 +995,9 @@ Plan plan_function(const Function& f, Precision prec) {
       }
       if (!pl.is_gemm_root(op)) continue;
       GemmDesc g;
-      if (pl.gemm_of(op, &g)) {
+      // skinny GEMMs (at most kSkinnyMax rows or columns) run in f32 on the
+      // CUDA cores: their operands need no TF32 rounding or bf16 copy
+      if (pl.gemm_of(op, &g) && g.M > kSkinnyMax && g.N > kSkinnyMax) {
         bases.insert(g.a.value);
         bases.insert(g.b.value);
       }
