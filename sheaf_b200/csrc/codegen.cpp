@@ -1467,8 +1467,12 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
     for (size_t q = 0; q < cols.size(); ++q) {
       auto combine = body_op(*cols[q].op);
       src_ << "  {\n    float v_ = " << ident_of(*cols[q].op) << ";\n";
-      src_ << "    if (col < " << C << ")\n#pragma unroll 4\n      for (int b_ = ry; b_ < " << grid << "; b_ += 32) v_ = "
-           << combine("v_", "S[" + std::to_string(q * grid * C) + " + b_ * " + std::to_string(C) + " + col]") << ";\n";
+      // a trip count known at compile time (ceil(grid / 32)): the loop is
+      // unrolled and all of a thread's partial loads are in flight together
+      src_ << "    if (col < " << C << ") {\n#pragma unroll\n      for (int i_ = 0; i_ < " << (grid + 31) / 32
+           << "; ++i_) {\n        const int b_ = ry + 32 * i_;\n        if (b_ < " << grid << ") v_ = "
+           << combine("v_", "S[" + std::to_string(q * grid * C) + " + b_ * " + std::to_string(C) + " + col]")
+           << ";\n      }\n    }\n";
       src_ << "    part_[ry][cx] = v_;\n    __syncthreads();\n";
       src_ << "    for (int w_ = 16; w_ > 0; w_ >>= 1) {\n      if (ry < w_) part_[ry][cx] = "
            << combine("part_[ry][cx]", "part_[ry + w_][cx]") << ";\n      __syncthreads();\n    }\n";

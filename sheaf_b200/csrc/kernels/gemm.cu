@@ -181,18 +181,7 @@ GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws
   run.scm = g.N;
   run.scn = 1;
   run.round_out = 0;
-  run.fix_c = nullptr;
   return run;
-}
-
-// The split launch `run` completing its own sum into g's output.
-GemmArgs with_fixup(const GemmArgs& run, const GemmArgs& g) {
-  GemmArgs f = run;
-  f.fix_c = g.c;
-  f.fix_ldc = g.scm;
-  f.fix_round = g.round_out;
-  f.tile_counters = g.tile_counters;
-  return f;
 }
 
 // Measured choice of the tensor-core configuration, once per problem
@@ -202,7 +191,7 @@ GemmArgs with_fixup(const GemmArgs& run, const GemmArgs& g) {
 // configurations differ only in tiling, not in summation order), and the
 // fastest is kept.  The cost model's proposal stands while the stream is being
 // captured into a graph, or when the environment forces a configuration.
-using TuneKey = std::array<int64_t, 20>;
+using TuneKey = std::array<int64_t, 19>;
 std::mutex tune_mu;
 std::map<TuneKey, int> tune_cache;
 
@@ -210,8 +199,7 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
   if (tc_forced_config() >= 0) return proposed;
   const TuneKey key = {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
                        run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
-                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16,
-                       (int64_t)(run.fix_c != nullptr)};
+                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16};
   std::lock_guard<std::mutex> lock(tune_mu);
   auto it = tune_cache.find(key);
   if (it != tune_cache.end()) return it->second;
@@ -255,17 +243,6 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
     if (tc_plan(g, &p)) {
       const bool split = p.splits > 1 && ws && ws_bytes >= (size_t)(p.splits * g.M * g.N) * sizeof(float);
       const GemmArgs run = split ? split_args(g, p.splits, p.k_chunk, ws) : g;
-      if (split && g.tile_counters) {
-        // the kernel adds the partials itself; without room for its
-        // counters it declines and the separate reduction runs
-        const GemmArgs fixed = with_fixup(run, g);
-        cudaError_t e = gemm_tcgen05(fixed, tuned_config(fixed, p.cfg, stream), stream);
-        if (e == cudaSuccess) {
-          *used_tc = true;
-          return cudaSuccess;
-        }
-        if (e != cudaErrorNotSupported) return e;
-      }
       cudaError_t e = gemm_tcgen05(run, tuned_config(run, p.cfg, stream), stream);
       if (e == cudaSuccess) {
         *used_tc = true;
@@ -290,15 +267,6 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
         }
         const bool split = pd.plan.splits > 1;
         const GemmArgs run = split ? split_args(v, pd.plan.splits, pd.plan.k_chunk, ws) : v;
-        if (split && g.tile_counters) {
-          const GemmArgs fixed = with_fixup(run, g);
-          cudaError_t e = gemm_tcgen05(fixed, tuned_config(fixed, pd.plan.cfg, stream), stream);
-          if (e == cudaSuccess) {
-            *used_tc = true;
-            return cudaSuccess;
-          }
-          if (e != cudaErrorNotSupported) return e;
-        }
         cudaError_t e = gemm_tcgen05(run, tuned_config(run, pd.plan.cfg, stream), stream);
         if (e != cudaSuccess) return e;
         *used_tc = true;

@@ -123,63 +123,6 @@ __device__ __forceinline__ void store_chunk(float* slot, const float* v, int lan
   __syncwarp();
 }
 
-// Split-K completed inside the GEMM.  The K slices of an output tile write
-// their partial sums to the workspace (slice z at ws + z * slice); each
-// epilogue warp then counts its 32-row quadrant's arrival on a per-quadrant
-// counter, and the warp that arrives last adds the slices' partials in slice
-// order 0, 1, ... and writes the result (optionally rounded to TF32).  The sum
-// is the same whichever slice finishes last, no warp waits for another, and no
-// separate reduction kernel runs.  Counters are zero between launches: the
-// last arrival resets its counter.
-struct Fixup {
-  float* c = nullptr;       // final output; nullptr: no split-K completion
-  long long ldc = 0;        // its row stride
-  int* counters = nullptr;  // per (tile, CTA of a pair, quadrant)
-  int splits = 0;
-  int round_out = 0;
-};
-
-template <int BN>
-__device__ __forceinline__ void fixup_quadrant(const Fixup& fx, const float* ws, long long slice, int row0, int n0,
-                                               int M, int N, int lane, int idx) {
-  if (row0 >= M || n0 >= N) return;
-  __threadfence();  // this lane's partial stores before the arrival
-  __syncwarp();
-  int old = 0;
-  if (lane == 0) old = atomicAdd(&fx.counters[idx], 1);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != fx.splits - 1) return;
-  if (lane == 0) fx.counters[idx] = 0;
-  __threadfence();  // the other slices' partials, published before their arrivals
-  const bool vec = (N & 3) == 0 && (fx.ldc & 3) == 0 && (((uintptr_t)fx.c) & 15) == 0 && (((uintptr_t)ws) & 15) == 0;
-  constexpr int Q = BN / 4;  // 4-column groups per row
-#pragma unroll 2
-  for (int i = lane; i < 32 * Q; i += 32) {
-    const int r = i / Q, row = row0 + r, col = n0 + 4 * (i - r * Q);
-    if (row >= M || col >= N) continue;
-    const float* p = ws + (long long)row * N + col;
-    float* dst = fx.c + (long long)row * fx.ldc + col;
-    if (vec) {
-      float4 a = __ldcg((const float4*)p);
-      for (int z = 1; z < fx.splits; ++z) {
-        const float4 v = __ldcg((const float4*)(p + z * slice));
-        a.x += v.x;
-        a.y += v.y;
-        a.z += v.z;
-        a.w += v.w;
-      }
-      if (fx.round_out) a = make_float4(rna_tf32(a.x), rna_tf32(a.y), rna_tf32(a.z), rna_tf32(a.w));
-      *(float4*)dst = a;
-    } else {
-      for (int e = 0; e < 4 && col + e < N; ++e) {
-        float a = __ldcg(p + e);
-        for (int z = 1; z < fx.splits; ++z) a += __ldcg(p + z * slice + e);
-        dst[e] = fx.round_out ? rna_tf32(a) : a;
-      }
-    }
-  }
-}
-
 // Orders uses of registers written by an asynchronous tcgen05.ld after the
 // tcgen05.wait::ld that completes it.
 __device__ __forceinline__ void reg_fence16(uint32_t* r) {
@@ -276,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                       long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                      int c3d, int round_out, int kchunk, Tiles tl, Fixup fx, int* err) {
+                      int c3d, int round_out, int kchunk, Tiles tl, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   pdl_prologue();
@@ -428,7 +371,6 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
                         kt1 <= kt0, round_out);
       fence_before();
       mbar_arrive(&acc_empty[b]);
-      if (fx.c) fixup_quadrant<BN>(fx, C, scb, row0, n0, M, N, lane, (t - z * tl.per_z) * 4 + quad);
     }
     if (c_tma && lane == 0) bulk_wait_all();
   }
@@ -454,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                    long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                   int c3d, int round_out, int kchunk, Tiles tl, Fixup fx, int* err) {
+                   int c3d, int round_out, int kchunk, Tiles tl, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -621,8 +563,6 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
                         kt1 <= kt0, round_out);
       fence_before();
       mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
-      if (fx.c)
-        fixup_quadrant<BN>(fx, C, scb, row0, n0, M, N, lane, ((t - z * tl.per_z) * 2 + (int)rank) * 4 + quad);
     }
     if (c_tma && lane == 0) bulk_wait_all();
   }
@@ -717,20 +657,6 @@ bool operand_maps(const GemmArgs& g, bool a_mn, bool b_mn, int bn_cta, CUtensorM
   return ok;
 }
 
-// Split-K completion of a split launch: set when the caller passes the final
-// output and a counter buffer (GemmArgs::fix_c, tile_counters).
-Fixup fixup_of(const GemmArgs& g) {
-  Fixup fx;
-  if (g.k_chunk > 0 && g.fix_c && g.tile_counters) {
-    fx.c = g.fix_c;
-    fx.ldc = (long long)g.fix_ldc;
-    fx.counters = g.tile_counters;
-    fx.splits = (int)g.batch;
-    fx.round_out = g.fix_round;
-  }
-  return fx;
-}
-
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
   constexpr int BKE = BF ? 64 : 32;
@@ -742,11 +668,8 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   if (!operand_maps<BF>(g, a_mn, b_mn, BN, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
     return cudaErrorNotSupported;
   const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  const Fixup fx = fixup_of(g);
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
-  // split-K partials are stored by plain stores, ordered before the counter
-  // arrival by the memory fence (no asynchronous-proxy writes to publish)
-  const int c_tma = !fx.c && make_store_map(&tc_map, g) ? 1 : 0;
+  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC>;
@@ -764,11 +687,10 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   const int64_t total = (int64_t)tl.per_z * g.batch;
   if (total > (1ll << 30)) return cudaErrorNotSupported;
   tl.total = (int)total;
-  if (fx.c && (int64_t)tl.per_z * 4 > kFixupCounters) return cudaErrorNotSupported;
   const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
   return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, ta, tb, tc_map, g.c, (int)g.M,
                     (int)g.N, (int)g.K, (long long)g.scb, (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d,
-                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, fx, err);
+                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, err);
 }
 
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
@@ -783,9 +705,8 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   if (!operand_maps<BF>(g, a_mn, b_mn, BNH, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
     return cudaErrorNotSupported;
   const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  const Fixup fx = fixup_of(g);
   CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
-  const int c_tma = !fx.c && make_store_map(&tc_map, g) ? 1 : 0;
+  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BNH, STAGES>;
   auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC>;
@@ -803,7 +724,6 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   const int64_t total = (int64_t)tl.per_z * g.batch;
   if (total > (1ll << 30)) return cudaErrorNotSupported;
   tl.total = (int)total;
-  if (fx.c && (int64_t)tl.per_z * 8 > kFixupCounters) return cudaErrorNotSupported;
   const int pairs = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
@@ -821,7 +741,7 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
                             (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
-                            g.round_out, kchunk, tl, fx, err);
+                            g.round_out, kchunk, tl, err);
 }
 
 int* error_word() { return tc_error_word(); }
@@ -973,7 +893,8 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
   // the result that depends on the plan) does not depend on the kernel
   // configuration: a single GEMM whose 128 x 128 tiles do not cover the SMs
   // is split into as many K ranges as fit one wave of 2 CTAs per SM (a partial
-  // second wave costs more than it saves), at least 512 of K each.
+  // second wave costs more than it saves), at least 512 of K each (measured on the nanoGPT step: 1024 or no split
+  // at all is slower at batch 8 and 64).
   p->splits = 1;
   p->k_chunk = 0;
   const int64_t tiles = ((g.M + 127) / 128) * ((g.N + 127) / 128);

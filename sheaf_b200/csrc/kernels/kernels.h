@@ -23,18 +23,7 @@ struct GemmArgs {
   // split-K (batch == 1 only): when > 0, "batch" index s computes the K range
   // [s*k_chunk, min(K, (s+1)*k_chunk)) into c + s*scb
   int64_t k_chunk = 0;
-  // split-K completed by the tensor-core kernel itself (the last K slice of
-  // each output tile adds the partials into fix_c, row stride fix_ldc, rounded
-  // to TF32 when fix_round): set with k_chunk by the dispatcher
-  float* fix_c = nullptr;
-  int64_t fix_ldc = 0;
-  int fix_round = 0;
-  // kFixupCounters ints, zero between launches, owned by the caller's stream
-  // (nullptr: split-K partials are added by a separate reduction kernel)
-  int* tile_counters = nullptr;
 };
-
-constexpr int64_t kFixupCounters = 8192;
 
 // C[i] = sum_s P[s*M*N + i] over `splits` partial products (row-major M x N
 // partials, C with leading dimension ldc), optionally rounded to TF32.

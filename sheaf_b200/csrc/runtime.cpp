@@ -79,9 +79,6 @@ struct Device {
   // all-reduced on comm_stream while the backward continues on `stream`
   cudaStream_t comm_stream = nullptr;
   cudaEvent_t ready = nullptr, reduced = nullptr;
-  // arrival counters of the GEMMs that complete their split-K sums in-kernel
-  // (kFixupCounters ints, zero between launches; used only on `stream`)
-  int* tile_counters = nullptr;
   std::atomic<uint64_t> allocated{0}, freed{0}, live{0}, peak{0};
   void note_alloc(size_t n) {
     allocated += n;
@@ -105,10 +102,6 @@ struct Device {
       cudaSetDevice(ordinal);
       cudaStreamSynchronize(stream);
       cudaStreamDestroy(stream);
-    }
-    if (tile_counters) {
-      cudaSetDevice(ordinal);
-      cudaFree(tile_counters);
     }
   }
 };
@@ -265,12 +258,9 @@ sb_status* wait_stream(sb_session* s, int64_t timeout_ms) {
     if (e == cudaSuccess) {
       if (s->used_tc) {
         int code = gemm_tcgen05_error();
-        if (code) {
-          // a kernel that gave up may have left split-K counters mid-count
-          if (s->dev->tile_counters) cudaMemset(s->dev->tile_counters, 0, kFixupCounters * sizeof(int));
+        if (code)
           return make_status(SB_STATUS_INTERNAL, "tensor-core kernel gave up on a bounded wait (code " +
                                                      std::to_string(code) + "); results are invalid");
-        }
       }
       return nullptr;
     }
@@ -515,7 +505,6 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
       a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
       a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
-      a.tile_counters = s->dev->tile_counters;
       size_t need = gemm_workspace(a, s->opts.precision);
       // a stream being captured into a graph must not allocate: the eager
       // call that precedes every capture sized the workspace
@@ -1123,8 +1112,6 @@ sb_status* sb_session_create(const sb_session_options* o, sb_session** out) {
   s->dev->ordinal = o->device_ordinal;
   SB_CUDA(cudaSetDevice(o->device_ordinal));
   SB_CUDA(cudaStreamCreateWithFlags(&s->dev->stream, cudaStreamNonBlocking));
-  SB_CUDA(cudaMalloc(&s->dev->tile_counters, kFixupCounters * sizeof(int)));
-  SB_CUDA(cudaMemset(s->dev->tile_counters, 0, kFixupCounters * sizeof(int)));
   if (o->world_size > 1 && (o->flags & SB_SESSION_FLAG_OVERLAP_ALLREDUCE)) {
     SB_CUDA(cudaStreamCreateWithFlags(&s->dev->comm_stream, cudaStreamNonBlocking));
     SB_CUDA(cudaEventCreateWithFlags(&s->dev->ready, cudaEventDisableTiming));

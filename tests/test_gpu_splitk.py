@@ -1,15 +1,12 @@
-"""Split-K GEMMs completed inside the tcgen05 kernel, on the GPU through the C
-ABI.
+"""Split-K GEMMs on the GPU through the C ABI.
 
-A GEMM whose 128 x 128 tiles do not cover the SMs is cut into K slices; the
-K slices of each output tile write partial sums to the workspace, and the
-epilogue warp that finishes a 32-row quadrant last adds the partials in slice
-order and writes the result.  Checked here: the result against an f64 product
-(TF32 operands: 2e-3 norm-relative; bf16 tensors: 1e-5), bit-identical
-results over repeated calls (the arrival counters reset themselves and the sum
-does not depend on which slice finishes last), every tile configuration, the
-weight-gradient layout X^T @ G, and a ragged edge (M, N not multiples of the
-tile).
+A GEMM whose 128 x 128 tiles do not cover the SMs is cut into K slices by a
+fixed rule on the shape; each slice's partial product goes to the workspace
+and a reduction kernel adds them in slice order.  Checked here: the result
+against an f64 product (TF32 operands: 2e-3 norm-relative; bf16 tensors:
+1e-5), bit-identical results over repeated calls, every tile configuration,
+the weight-gradient layout X^T @ G, and a ragged edge (M, N not multiples of
+the tile, N not a multiple of 4).
 """
 import os
 
