@@ -1208,6 +1208,7 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   c.vec = true;
   c.indent = 2;
   std::vector<int> outs;
+  std::vector<int> shadows;  // values whose operand shadows this kernel writes (X0, X1, ...)
   std::ostringstream rows;  // before the row loop: lane columns, column accumulators
   for (int j = 0; j < J; ++j)
     rows << "  const " << c.idx << " cL" << j << " = (lane + " << 32 * j << ") * 4;\n";
@@ -1295,6 +1296,22 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
           }
           c.body << "    *(float4*)(" << W << " + row * " << C << " + " << b << ") = make_float4(" << g[0] << ", "
                  << g[1] << ", " << g[2] << ", " << g[3] << ");\n";
+          auto sv = shadow_vals_.find(out_v);
+          if (sv != shadow_vals_.end()) {
+            // the operand shadow of the same four values
+            auto it = std::find(shadows.begin(), shadows.end(), out_v);
+            const int xi = (int)(it - shadows.begin());
+            if (it == shadows.end()) shadows.push_back(out_v);
+            const std::string X = "X" + std::to_string(xi);
+            if (sv->second == DType::BF16)
+              c.body << "    *(uint2*)(" << X << " + row * " << C << " + " << b << ") = make_uint2(sb_pack2(sb_bf16_bits("
+                     << g[0] << "), sb_bf16_bits(" << g[1] << ")), sb_pack2(sb_bf16_bits(" << g[2]
+                     << "), sb_bf16_bits(" << g[3] << ")));\n";
+            else
+              c.body << "    *(float4*)(" << X << " + row * " << C << " + " << b << ") = make_float4(sb_rna_tf32("
+                     << g[0] << "), sb_rna_tf32(" << g[1] << "), sb_rna_tf32(" << g[2] << "), sb_rna_tf32(" << g[3]
+                     << "));\n";
+          }
         }
         c.reg_kind[out_v] = 0;
       } else if (m.kind == 1) {
@@ -1416,9 +1433,14 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   // the per-block partials stay few while every warp slot is used
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, cols.empty() ? kMaxGrid : 148 * 8));
   const size_t np = c.leaves.size() + outs.size();
-  src_ << header(name, c, (int)outs.size() - 1 + (cols.empty() ? 0 : 1));
+  src_ << header(name, c, (int)outs.size() - 1 + (cols.empty() ? 0 : 1) + (int)shadows.size());
   for (size_t j = 0; j < outs.size(); ++j)
     src_ << "  float* __restrict__ O" << j << " = (float*)a.p[" << c.leaves.size() + j << "];\n";
+  for (size_t k = 0; k < shadows.size(); ++k) {
+    const char* t = shadow_vals_.at(shadows[k]) == DType::BF16 ? "unsigned short" : "float";
+    src_ << "  " << t << "* __restrict__ X" << k << " = (" << t << "*)a.p[" << np + (cols.empty() ? 0 : 1) + k
+         << "];\n";
+  }
   src_ << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
   src_ << rows.str();
   src_ << "  for (" << c.idx << " row = (" << c.idx << ")blockIdx.x * " << kThreads / 32 << " + warp; row < " << R
@@ -1447,6 +1469,7 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   st->leaves = c.leaves;
   st->root = outs[0];
   st->extra_roots.assign(outs.begin() + 1, outs.end());
+  st->shadow_values = shadows;
   st->block = kThreads;
   st->grid = grid;
   if (!cols.empty()) {

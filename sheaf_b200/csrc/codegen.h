@@ -19,6 +19,10 @@ class CodeGen {
   // Roots whose stored values are rounded to nearest TF32 (they feed tf32 GEMMs;
   // the tensor cores would otherwise truncate them).
   void set_round_roots(const std::vector<int>& roots) { round_roots_ = roots; }
+  // Values whose GEMM operand shadow (a TF32-rounded f32 or a bf16 copy) the
+  // producing row-group kernel writes as well, as it stores the value
+  // (Step::shadow_values); others get a separate conversion step.
+  void set_shadow_values(const std::map<int, DType>& v) { shadow_vals_ = v; }
 
   void gen_loop(const Op& root, Step* st);
   // Reduction `root`; with `epi`, the element-wise cluster rooted at epi (of
@@ -90,6 +94,7 @@ class CodeGen {
   std::vector<std::string> names_;
   std::vector<std::string> snippets_;
   std::vector<int> round_roots_;
+  std::map<int, DType> shadow_vals_;
 };
 
 const char* ctype_of(DType t);

@@ -181,6 +181,7 @@ GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws
   run.scm = g.N;
   run.scn = 1;
   run.round_out = 0;
+  run.epi = 0;  // partial sums: the epilogue applies to the total
   return run;
 }
 
@@ -191,7 +192,7 @@ GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws
 // configurations differ only in tiling, not in summation order), and the
 // fastest is kept.  The cost model's proposal stands while the stream is being
 // captured into a graph, or when the environment forces a configuration.
-using TuneKey = std::array<int64_t, 19>;
+using TuneKey = std::array<int64_t, 20>;
 std::mutex tune_mu;
 std::map<TuneKey, int> tune_cache;
 
@@ -199,7 +200,8 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
   if (tc_forced_config() >= 0) return proposed;
   const TuneKey key = {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
                        run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
-                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16};
+                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16,
+                       (int64_t)run.epi};
   std::lock_guard<std::mutex> lock(tune_mu);
   auto it = tune_cache.find(key);
   if (it != tune_cache.end()) return it->second;
@@ -232,9 +234,13 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
 
 }  // namespace
 
-cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
-  *used_tc = false;
-  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
+namespace {
+
+// The product itself; *fused reports whether the tensor-core kernel also
+// wrote the fused epilogue's output (unsplit launches only: split-K partials
+// must not pass through it).
+cudaError_t gemm_main(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
+                      bool* used_tc, bool* fused) {
   if (gemm_is_skinny(g)) return gemm_skinny(g, stream);
   // bf16 operands run on the tensor cores in every precision mode (their
   // products are exact in f32, so kind::f16 is the graph's arithmetic)
@@ -246,6 +252,7 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
       cudaError_t e = gemm_tcgen05(run, tuned_config(run, p.cfg, stream), stream);
       if (e == cudaSuccess) {
         *used_tc = true;
+        *fused = !split;
         if (!split) return cudaSuccess;
         return splitk_reduce((const float*)ws, g.c, p.splits, g.M, g.N, g.scm, g.round_out, stream);
       }
@@ -270,6 +277,7 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
         cudaError_t e = gemm_tcgen05(run, tuned_config(run, pd.plan.cfg, stream), stream);
         if (e != cudaSuccess) return e;
         *used_tc = true;
+        *fused = !split;
         if (!split) return cudaSuccess;
         return splitk_reduce((const float*)ws, g.c, pd.plan.splits, g.M, g.N, g.scm, g.round_out, stream);
       }
@@ -280,6 +288,21 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
   cudaError_t e = gemm_simt(split ? split_args(g, s.splits, s.k_chunk, ws) : g, stream);
   if (e != cudaSuccess || !split) return e;
   return splitk_reduce((const float*)ws, g.c, s.splits, g.M, g.N, g.scm, 0, stream);
+}
+
+}  // namespace
+
+cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
+  *used_tc = false;
+  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
+  // the fused epilogue's output is laid out densely like C (the unfused form
+  // below reads C as one contiguous array)
+  if (g.epi && (g.epi != kEpiGelu || !g.c2 || g.scn != 1 || g.scm != g.N || (g.batch > 1 && g.scb != g.M * g.N)))
+    return cudaErrorInvalidValue;
+  bool fused = false;
+  cudaError_t e = gemm_main(g, precision, ws, ws_bytes, stream, used_tc, &fused);
+  if (e != cudaSuccess || !g.epi || fused) return e;
+  return gelu_tanh(g.c, g.c2, g.batch * g.M * g.N, g.round_out2, stream);
 }
 
 }  // namespace sb

@@ -130,18 +130,19 @@ __device__ __forceinline__ void reg_fence16(uint32_t* r) {
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
 }
 
-// One 16-column chunk of this warp's 32 accumulator rows to C: through the
-// warp's double-buffered staging tile and a TMA store, or by plain stores.
-__device__ __forceinline__ void epilogue_chunk(const uint32_t* r, float* bufs, int lane, int* sb,
-                                               const CUtensorMap* tmC, bool c_tma, bool c3d, int z, float* cz,
-                                               int row0, int n, int M, int N, long long ldc, bool vec, bool zero,
-                                               int round_out) {
-  float v[16];
-#pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    v[q] = zero ? 0.f : __uint_as_float(r[q]);
-    if (round_out) v[q] = rna_tf32(v[q]);
-  }
+// Second output of the fused epilogue (Epi::epi == kEpiGelu): C2 = gelu(C).
+struct Epi {
+  const CUtensorMap* tm = nullptr;  // store map of C2 (when c_tma)
+  float* c = nullptr;               // C2 of this output slice
+  int epi = 0;
+  int round_out = 0;
+};
+
+// One 32 x 16 chunk of values (one row per lane) to C: through the warp's
+// double-buffered staging tile and a TMA store, or by plain stores.
+__device__ __forceinline__ void store_chunk16(const float* v, float* bufs, int lane, int* sb, const CUtensorMap* tmC,
+                                              bool c_tma, bool c3d, int z, float* cz, int row0, int n, int M, int N,
+                                              long long ldc, bool vec) {
   if (c_tma) {
     float* buf = bufs + *sb * 512;
     if (lane == 0) bulk_wait_read1();
@@ -162,6 +163,30 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* r, float* bufs, i
   }
 }
 
+// One 16-column chunk of this warp's 32 accumulator rows to C (optionally
+// rounded to TF32) and, with the fused epilogue, gelu of the same values to
+// C2 (gelu of the accumulator, before any rounding of C).
+__device__ __forceinline__ void epilogue_chunk(const uint32_t* r, float* bufs, int lane, int* sb,
+                                               const CUtensorMap* tmC, bool c_tma, bool c3d, int z, float* cz,
+                                               int row0, int n, int M, int N, long long ldc, bool vec, bool zero,
+                                               int round_out, const Epi& e2) {
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    v[q] = zero ? 0.f : __uint_as_float(r[q]);
+    if (round_out) v[q] = rna_tf32(v[q]);
+  }
+  store_chunk16(v, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n, M, N, ldc, vec);
+  if (e2.epi == kEpiGelu) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      v[q] = gelu_tanh_f(zero ? 0.f : __uint_as_float(r[q]));
+      if (e2.round_out) v[q] = rna_tf32(v[q]);
+    }
+    store_chunk16(v, bufs, lane, sb, e2.tm, c_tma, c3d, z, e2.c, row0, n, M, N, ldc, vec);
+  }
+}
+
 // Epilogue of one warp's 32 accumulator rows (TMEM lane quadrant at `acc`) to
 // rows row0..row0+31, columns n0..n0+BN-1 of output slice z.  With a C tensor
 // map (c_tma) each 32 x 16 chunk is staged in one of the warp's two 2 KB
@@ -174,7 +199,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* r, float* bufs, i
 template <int BN>
 __device__ __forceinline__ void epilogue_warp(uint32_t acc, float* bufs, int lane, int* sb, const CUtensorMap* tmC,
                                               bool c_tma, bool c3d, int z, float* cz, int row0, int n0, int M, int N,
-                                              long long ldc, bool vec, bool zero, int round_out) {
+                                              long long ldc, bool vec, bool zero, int round_out, const Epi& e2) {
   if (row0 >= M || n0 >= N) return;
   uint32_t r0[16], r1[16];
   tmem_ld16_async(acc, r0);
@@ -185,12 +210,13 @@ __device__ __forceinline__ void epilogue_warp(uint32_t acc, float* bufs, int lan
     const bool has1 = c + 16 < BN && n0 + c + 16 < N;
     const bool has2 = c + 32 < BN && n0 + c + 32 < N;
     if (has1) tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
-    epilogue_chunk(r0, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c, M, N, ldc, vec, zero, round_out);
+    epilogue_chunk(r0, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c, M, N, ldc, vec, zero, round_out, e2);
     if (!has1) break;
     tmem_wait_ld();
     reg_fence16(r1);
     if (has2) tmem_ld16_async(acc + (uint32_t)(c + 32), r0);
-    epilogue_chunk(r1, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c + 16, M, N, ldc, vec, zero, round_out);
+    epilogue_chunk(r1, bufs, lane, sb, tmC, c_tma, c3d, z, cz, row0, n0 + c + 16, M, N, ldc, vec, zero, round_out,
+                   e2);
     if (!has2) break;
     tmem_wait_ld();
     reg_fence16(r0);
@@ -219,7 +245,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                       long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                      int c3d, int round_out, int kchunk, Tiles tl, int* err) {
+                      int c3d, int round_out, int kchunk, Tiles tl,
+                      const __grid_constant__ CUtensorMap tmC2, float* C2, int epi, int round_out2, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   pdl_prologue();
@@ -230,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  float* epi = (float*)(smem + STAGES * S::STAGE);
+  float* epi_buf = (float*)(smem + STAGES * S::STAGE);
   uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE + S::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;   // [2]: MMA -> epilogue
@@ -367,8 +394,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       float* cz = C + (long long)z * scb;
       const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
       const uint32_t acc = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
-      epilogue_warp<BN>(acc, epi + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc, vec,
-                        kt1 <= kt0, round_out);
+      Epi e2;
+      e2.tm = &tmC2;
+      e2.c = C2 + (long long)z * scb;
+      e2.epi = epi;
+      e2.round_out = round_out2;
+      epilogue_warp<BN>(acc, epi_buf + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc,
+                        vec, kt1 <= kt0, round_out, e2);
       fence_before();
       mbar_arrive(&acc_empty[b]);
     }
@@ -396,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     gemm_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
                    long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                   int c3d, int round_out, int kchunk, Tiles tl, int* err) {
+                   int c3d, int round_out, int kchunk, Tiles tl,
+                   const __grid_constant__ CUtensorMap tmC2, float* C2, int epi, int round_out2, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -409,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  float* epi = (float*)(smem + STAGES * S::STAGE);
+  float* epi_buf = (float*)(smem + STAGES * S::STAGE);
   uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE + S::EPI_BYTES);  // leader: both CTAs' bytes
   uint64_t* empty = full + STAGES;                            // each CTA: slot free
   uint64_t* acc_full = empty + STAGES;                        // each CTA: accumulator ready
@@ -559,8 +592,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       float* cz = C + (long long)z * scb;
       const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
       const uint32_t accp = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
-      epilogue_warp<BN>(accp, epi + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc, vec,
-                        kt1 <= kt0, round_out);
+      Epi e2;
+      e2.tm = &tmC2;
+      e2.c = C2 + (long long)z * scb;
+      e2.epi = epi;
+      e2.round_out = round_out2;
+      epilogue_warp<BN>(accp, epi_buf + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc,
+                        vec, kt1 <= kt0, round_out, e2);
       fence_before();
       mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
     }
@@ -622,6 +660,16 @@ bool make_store_map(CUtensorMap* m, const GemmArgs& g) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Store maps of C and, with the fused epilogue, of C2 (laid out as C): both
+// or neither, so the epilogue uses one store path for the two outputs.
+bool store_maps(const GemmArgs& g, CUtensorMap* mc, CUtensorMap* mc2) {
+  if (!make_store_map(mc, g)) return false;
+  if (!g.epi) return true;
+  GemmArgs g2 = g;
+  g2.c = g.c2;
+  return make_store_map(mc2, g2);
+}
+
 int sm_count() {
   static int n = 0;
   if (!n) {
@@ -668,8 +716,8 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   if (!operand_maps<BF>(g, a_mn, b_mn, BN, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
     return cudaErrorNotSupported;
   const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
-  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
+  CUtensorMap tc_map = tb, tc_map2 = tb;  // placeholder contents when C (C2) has no store map
+  const int c_tma = store_maps(g, &tc_map, &tc_map2) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC>;
@@ -690,7 +738,8 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
   const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
   return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, ta, tb, tc_map, g.c, (int)g.M,
                     (int)g.N, (int)g.K, (long long)g.scb, (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d,
-                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, err);
+                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, tc_map2, g.epi ? g.c2 : g.c, g.epi,
+                    g.round_out2, err);
 }
 
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
@@ -705,8 +754,8 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   if (!operand_maps<BF>(g, a_mn, b_mn, BNH, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
     return cudaErrorNotSupported;
   const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  CUtensorMap tc_map = tb;  // placeholder contents when C has no store map
-  const int c_tma = make_store_map(&tc_map, g) ? 1 : 0;
+  CUtensorMap tc_map = tb, tc_map2 = tb;  // placeholder contents when C (C2) has no store map
+  const int c_tma = store_maps(g, &tc_map, &tc_map2) ? 1 : 0;
   const int c3d = g.batch > 1 ? 1 : 0;
   using S = Smem<BNH, STAGES>;
   auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC>;
@@ -741,7 +790,7 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
                             (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
-                            g.round_out, kchunk, tl, err);
+                            g.round_out, kchunk, tl, tc_map2, g.epi ? g.c2 : g.c, g.epi, g.round_out2, err);
 }
 
 int* error_word() { return tc_error_word(); }

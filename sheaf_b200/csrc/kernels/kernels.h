@@ -23,7 +23,14 @@ struct GemmArgs {
   // split-K (batch == 1 only): when > 0, "batch" index s computes the K range
   // [s*k_chunk, min(K, (s+1)*k_chunk)) into c + s*scb
   int64_t k_chunk = 0;
+  // fused epilogue: epi == kEpiGelu also writes c2 = gelu(C) elementwise
+  // (Sheaf's tanh form), c2 laid out as c, rounded to TF32 when round_out2
+  int epi = 0;
+  float* c2 = nullptr;
+  int round_out2 = 0;
 };
+
+constexpr int kEpiGelu = 1;
 
 // C[i] = sum_s P[s*M*N + i] over `splits` partial products (row-major M x N
 // partials, C with leading dimension ldc), optionally rounded to TF32.
@@ -50,6 +57,11 @@ cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t s
 
 // dst[i] = src[i] rounded to nearest TF32 (cvt.rna), n elements.
 cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream);
+
+// y = gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x *
+// x)))))) in f32, Sheaf's gelu (sheaf/lib/nn.shf) in its operation order;
+// optionally rounded to TF32.  The unfused form of the GEMM epilogue.
+cudaError_t gelu_tanh(const float* x, float* y, int64_t n, int round_tf32, cudaStream_t stream);
 
 // f32 FMA on CUDA cores; any strides.
 cudaError_t gemm_simt(const GemmArgs& g, cudaStream_t stream);

@@ -3,6 +3,7 @@
 
 #include "kernels.h"
 #include "pdl.h"
+#include "tc_common.h"
 
 namespace sb {
 namespace {
@@ -73,6 +74,26 @@ cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_
   if (blocks < 1) blocks = 1;
   if (blocks > 148 * 8) blocks = 148 * 8;
   return launch_pdl(round_tf32_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, n, n4);
+}
+
+namespace {
+
+__global__ void __launch_bounds__(256) gelu_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n,
+                                                   int round) {
+  pdl_prologue();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float g = tc::gelu_tanh_f(x[i]);
+    y[i] = round ? rna_tf32(g) : g;
+  }
+}
+
+}  // namespace
+
+cudaError_t gelu_tanh(const float* x, float* y, int64_t n, int round_tf32, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(gelu_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, x, y, n, round_tf32);
 }
 
 }  // namespace sb

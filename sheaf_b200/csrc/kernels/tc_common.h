@@ -348,6 +348,12 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
 }
 
+// Sheaf's gelu, (* 0.5 (* x (+ 1.0 (tanh (* 0.7978846 (+ x (* 0.044715 (* x
+// (* x x))))))))), evaluated in that order in f32.
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  return 0.5f * (x * (1.0f + tanhf(0.7978846f * (x + 0.044715f * (x * (x * x))))));
+}
+
 __device__ __forceinline__ float rna_tf32(float x) {
   uint32_t u;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));

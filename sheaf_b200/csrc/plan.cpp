@@ -937,6 +937,121 @@ void check_view_bounds(const Function& f, const View& v, const char* what) {
 
 namespace {
 
+// True when g is Sheaf's gelu of h, element by element: g's cone back to h
+// holds only element-wise ops and splat constants (no index maps), and its
+// value at sample points equals 0.5 x (1 + tanh(0.7978846 (x + 0.044715
+// x^3))) (sheaf/lib/nn.shf) to 1e-6.  The GEMM epilogue computes exactly
+// that form, so fusing it cannot change what is computed beyond rounding.
+bool is_gelu_of(const Function& f, int g, int h) {
+  if (f.value_types[g].dtype != DType::F32 || f.value_types[h].dtype != DType::F32 ||
+      f.value_types[g].shape != f.value_types[h].shape)
+    return false;
+  std::function<bool(int, double, double*)> eval = [&](int v, double x, double* out) -> bool {
+    if (v == h) {
+      *out = x;
+      return true;
+    }
+    const int pi = f.producer[v];
+    if (pi < 0) return false;
+    const Op& op = f.ops[pi];
+    if (op.kind == OpKind::Constant) {
+      if (op.values.size() != 1) return false;
+      *out = op.values[0];
+      return true;
+    }
+    if (op.kind == OpKind::BroadcastInDim) {
+      const int src = op.operands[0];
+      if (f.value_types[src].numel() != 1) return false;  // splat constants only
+      return eval(src, x, out);
+    }
+    if (f.value_types[v].shape != f.value_types[g].shape && f.value_types[v].numel() != 1) return false;
+    double a = 0, b = 0;
+    if (is_unary_elementwise(op.kind)) {
+      if (!eval(op.operands[0], x, &a)) return false;
+      switch (op.kind) {
+        case OpKind::Tanh: *out = std::tanh(a); return true;
+        case OpKind::Exp: *out = std::exp(a); return true;
+        case OpKind::Neg: *out = -a; return true;
+        case OpKind::Logistic: *out = 1.0 / (1.0 + std::exp(-a)); return true;
+        default: return false;
+      }
+    }
+    if (is_binary_elementwise(op.kind)) {
+      if (!eval(op.operands[0], x, &a) || !eval(op.operands[1], x, &b)) return false;
+      switch (op.kind) {
+        case OpKind::Add: *out = a + b; return true;
+        case OpKind::Sub: *out = a - b; return true;
+        case OpKind::Mul: *out = a * b; return true;
+        case OpKind::Div: *out = a / b; return true;
+        case OpKind::Pow: *out = std::pow(a, b); return true;
+        default: return false;
+      }
+    }
+    return false;
+  };
+  for (double x : {-4.5, -2.2, -1.0, -0.37, 0.0, 0.21, 0.8, 1.6, 3.3, 6.0}) {
+    double got = 0;
+    if (!eval(g, x, &got)) return false;
+    const double ref = 0.5 * x * (1.0 + std::tanh(0.7978846 * (x + 0.044715 * x * x * x)));
+    if (!(std::fabs(got - ref) <= 1e-6 * (1.0 + std::fabs(ref)))) return false;
+  }
+  return true;
+}
+
+// Fuses a loop step that computes only gelu of a GEMM step's result into the
+// GEMM's epilogue: the GEMM writes both h and gelu(h), and the loop step and
+// its launch (a read of h) are gone.  h keeps its own consumers (the gelu
+// VJP reads it).  Tensor-core modes only: in fp32 mode the GEMM runs on CUDA
+// cores and the epilogue would run as its separate unfused kernel anyway.
+void fuse_gemm_epilogues(const Function& f, Plan& plan, const std::vector<int>& round_roots,
+                         const std::set<int>& consts, std::map<int, int>& step_of_value) {
+  std::vector<char> drop(plan.steps.size(), 0);
+  std::map<int, int> gemm_step;  // GEMM result -> step
+  for (int si = 0; si < (int)plan.steps.size(); ++si) {
+    Step& st = plan.steps[si];
+    if (st.kind == StepKind::Gemm && st.gemm.epi == 0 && st.extra_roots.empty()) gemm_step[st.root] = si;
+    if (st.kind != StepKind::Loop || !st.finish_kernel.empty() || !st.extra_roots.empty() || st.scratch_elems ||
+        !st.shadow_values.empty())
+      continue;
+    int h = -1;
+    bool ok = true;
+    for (int l : st.leaves) {
+      if (consts.count(l)) continue;
+      if (h >= 0 && h != l) ok = false;
+      h = l;
+    }
+    if (!ok || h < 0) continue;
+    auto it = gemm_step.find(h);
+    if (it == gemm_step.end() || !is_gelu_of(f, st.root, h)) continue;
+    Step& gs = plan.steps[it->second];
+    gs.gemm.epi = kEpiGelu;
+    gs.gemm.round_out2 = std::find(round_roots.begin(), round_roots.end(), st.root) != round_roots.end();
+    gs.extra_roots.push_back(st.root);
+    gs.bytes_moved += st.elements * 4;
+    gemm_step.erase(it);
+    drop[si] = 1;
+  }
+  if (std::find(drop.begin(), drop.end(), 1) == drop.end()) return;
+  std::vector<Step> kept;
+  std::vector<int> new_index(plan.steps.size(), -1);
+  for (size_t si = 0; si < plan.steps.size(); ++si) {
+    if (drop[si]) continue;
+    new_index[si] = (int)kept.size();
+    kept.push_back(std::move(plan.steps[si]));
+  }
+  plan.steps = std::move(kept);
+  for (auto& [v, si] : step_of_value) {
+    if (new_index[si] >= 0) {
+      si = new_index[si];
+      continue;
+    }
+    // a fused loop's root: written by its GEMM step now
+    for (int k = 0; k < (int)plan.steps.size(); ++k)
+      for (int e : plan.steps[k].extra_roots)
+        if (e == v) si = k;
+  }
+}
+
 Plan plan_function(const Function& f, Precision prec) {
   verify(f);
   Planner pl(f, prec);
@@ -1041,6 +1156,14 @@ Plan plan_function(const Function& f, Precision prec) {
   }
   CodeGen cg(f, pl.cluster);
   cg.set_round_roots(round_roots);
+  {
+    // shadows of step results: written by the producing row-group kernel
+    // where it can (Step::shadow_values), else by a conversion step
+    std::map<int, DType> sv;
+    for (const Shadow& sh : plan.shadows)
+      if (pl.cluster[sh.value] != kParam) sv[sh.value] = sh.dtype;
+    cg.set_shadow_values(sv);
+  }
   std::map<int, int> step_of_value;
   // Consecutive loop / row-reduction steps over the same rows run as one row
   // group (CodeGen::gen_row_group): one launch, and each row's intermediates
@@ -1267,16 +1390,23 @@ Plan plan_function(const Function& f, Precision prec) {
     plan.steps.push_back(std::move(st));
   }
   flush();
+  if (prec == Precision::TF32 || prec == Precision::BF16) {
+    std::set<int> consts(plan.constants.begin(), plan.constants.end());
+    fuse_gemm_epilogues(f, plan, round_roots, consts, step_of_value);
+  }
   // conversion steps of the operand shadows, each right after the step that
   // writes its value
   if (!plan.shadows.empty()) {
     // drop shadows no GEMM reads (a bf16 shadow whose partner operand has none)
     {
       std::vector<char> used(plan.shadows.size(), 0);
-      for (const Step& st0 : plan.steps)
+      for (const Step& st0 : plan.steps) {
         if (st0.kind == StepKind::Gemm)
           for (int k : {st0.gemm.a_shadow, st0.gemm.b_shadow})
             if (k >= 0) used[k] = 1;
+        // a shadow a kernel writes keeps its buffer even if no GEMM reads it
+        for (int v : st0.shadow_values) used[shadow_of.at(v)] = 1;
+      }
       std::vector<int> remap(plan.shadows.size(), -1);
       std::vector<Shadow> kept;
       shadow_of.clear();
@@ -1314,10 +1444,17 @@ Plan plan_function(const Function& f, Precision prec) {
       std::vector<int> written{st0.root};
       written.insert(written.end(), st0.extra_roots.begin(), st0.extra_roots.end());
       new_index[si] = (int)steps.size();
+      for (int v : st0.shadow_values) {
+        const int k = shadow_of.at(v);
+        st0.shadow_outs.push_back(k);
+        plan.shadows[k].step = (int)steps.size();
+      }
+      const std::vector<int> fused = st0.shadow_values;
       steps.push_back(std::move(st0));
       for (int w : written) {
         auto it = shadow_of.find(w);
         if (it == shadow_of.end()) continue;
+        if (std::find(fused.begin(), fused.end(), w) != fused.end()) continue;  // written by the kernel
         Shadow& sh = plan.shadows[it->second];
         Step cs;
         cs.kind = StepKind::Convert;
@@ -1339,7 +1476,9 @@ Plan plan_function(const Function& f, Precision prec) {
         if (k >= 0) plan.shadows[k].last_use = std::max(plan.shadows[k].last_use, si);
     }
     for (const Shadow& sh : plan.shadows)
-      if (sh.step < 0) throw std::runtime_error("internal: operand shadow without a producing step");
+      if (sh.step < 0)
+        throw std::runtime_error("internal: operand shadow of %" + std::to_string(sh.value) +
+                                 " without a producing step");
   }
   plan.source = cg.source();
   plan.snippets = cg.snippets();

@@ -30,6 +30,10 @@ struct GemmDesc {
   bool round_out = false;                     // store the result rounded to TF32
   int a_shadow = -1, b_shadow = -1;           // read operand shadow Plan::shadows[i] instead
   bool bf16 = false;                          // both operands are read as bf16
+  // fused epilogue (kEpiGelu): the step also writes Step::extra_roots[0] =
+  // gelu(result), rounded to TF32 when round_out2
+  int epi = 0;
+  bool round_out2 = false;
 };
 
 // Copy of a GEMM operand in the form the tensor cores read, written by a
@@ -79,6 +83,11 @@ struct Step {
   int64_t bytes_moved = 0;      // algorithmic bytes (inputs read once + output)
   double flops = 0;
   int shadow = -1;              // Convert: index into Plan::shadows
+  // values whose operand shadows this step's kernel writes too (kernel
+  // arguments after the root, the extra roots and the scratch), and those
+  // shadows' indices into Plan::shadows, in the same order
+  std::vector<int> shadow_values;
+  std::vector<int> shadow_outs;
 };
 
 struct Plan {

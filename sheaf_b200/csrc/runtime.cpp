@@ -505,6 +505,11 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
       a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
       a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
+      if (g.epi) {
+        a.epi = g.epi;
+        a.c2 = (float*)ptr[st.extra_roots[0]];
+        a.round_out2 = g.round_out2 ? 1 : 0;
+      }
       size_t need = gemm_workspace(a, s->opts.precision);
       // a stream being captured into a graph must not allocate: the eager
       // call that precedes every capture sized the workspace
@@ -593,6 +598,7 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       scratch = (char*)lf->arena + plan.scratch_offset[si];
       args.push_back(scratch);
     }
+    for (int k : st.shadow_outs) args.push_back((char*)lf->arena + plan.shadows[k].offset);
     sb_status* e = launch_generated(lf->kern[si], args, st.grid, st.grid_y, st.block, stream);
     if (e) { return e; }
     if (st.splits > 1) {
@@ -1602,7 +1608,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   }
   std::ostringstream os;
   os.precision(17);
-  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn\n";
+  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi\n";
   static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert", "scatter"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
@@ -1610,7 +1616,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
     os << i << "," << kinds[(int)st.kind] << "," << step_name(st) << ","
        << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
        << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
-       << g.sbn << "\n";
+       << g.sbn << "," << g.epi << "\n";
   }
   std::string r = os.str();
   if (out_len) *out_len = r.size();

@@ -30,3 +30,37 @@ def test_bf16_plan_converts_gemm_operands():
     low = M.gpt_vag(M.NANOGPT, batch=2)
     s = _summary(low.text, "bf16")
     assert int(s["convert"]) > 0 and s["attention"] == "12"
+
+
+def test_gelu_is_fused_into_the_mlp_gemm_epilogue():
+    """nanoGPT value-and-grad and forward: each layer's c_fc GEMM writes both
+    its result and gelu of it (the gelu loop and its launch are gone); the
+    fp32 mode (CUDA-core GEMMs) keeps the loop."""
+    c = M.NANOGPT
+    for low in (M.gpt_vag(c, batch=2), M.gpt_fwd(c, batch=2)):
+        rows = S.plan_steps(low.text, low.qualified, "tf32")
+        fused = [r for r in rows if r["kind"] == "gemm" and r["epi"] == 1]
+        assert len(fused) == c.n_layer
+        # the c_fc product: [B*T, D] x [D, 4D]
+        assert all(r["N"] == 4 * c.n_embd and r["K"] == c.n_embd for r in fused)
+    rows = S.plan_steps(M.gpt_vag(c, batch=2).text, M.gpt_vag(c, batch=2).qualified, "fp32")
+    assert not [r for r in rows if r["epi"]]
+
+
+def test_gelu_matcher_rejects_other_functions():
+    """An erf-style or otherwise different activation after a GEMM is not
+    fused (the numeric check of the element-wise cone fails)."""
+    text = """module @notgelu {
+ func.func @f(%arg0: tensor<256x128xf32>, %arg1: tensor<128x512xf32>) -> tensor<256x512xf32> {
+    %0 = stablehlo.dot_general %arg0, %arg1, contracting_dims = [1] x [0] : (tensor<256x128xf32>, tensor<128x512xf32>) -> tensor<256x512xf32>
+    %c = stablehlo.constant dense<0.7978846> : tensor<f32>
+    %1 = stablehlo.broadcast_in_dim %c, dims = [] : (tensor<f32>) -> tensor<256x512xf32>
+    %2 = stablehlo.multiply %0, %1 : tensor<256x512xf32>
+    %3 = stablehlo.tanh %2 : tensor<256x512xf32>
+    %4 = stablehlo.multiply %0, %3 : tensor<256x512xf32>
+    return %4 : tensor<256x512xf32>
+ }
+}
+"""
+    rows = S.plan_steps(text, "notgelu.f", "tf32")
+    assert not [r for r in rows if r["epi"]]
