@@ -71,7 +71,8 @@ def _check(outs, ref, scalar_first=True):
     assert max(errs) <= 2e-3, errs
 
 
-@pytest.mark.parametrize("T", [128, 256])
+# up to GPT-2's context (1024) and one length past it
+@pytest.mark.parametrize("T", [128, 256, 1024, 1280])
 @pytest.mark.parametrize("causal", [True, False])
 def test_attention_value_and_grad(tf32_session, T, causal):
     low = attention_vag(2, 3, T, causal)
