@@ -1273,7 +1273,12 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
       const Op& root = *m.root;
       const Op& out_op = m.epi ? *m.epi : root;
       const int out_v = out_op.result;
-      if (out_op.type.dtype != DType::F32) return false;
+      // bf16 outputs: the registers hold the bf16-rounded f32 value (what
+      // later members read), the stores write its 16 bits
+      const bool bf = out_op.type.dtype == DType::BF16;
+      if (out_op.type.dtype != DType::F32 && !bf) return false;
+      if (bf && m.kind == 3) return false;
+      auto held = [&](const Op& o, const std::string& e) { return bf ? "sb_bf16_rn(" + e + ")" : store(o, e); };
       const std::string W = "O" + std::to_string(outs.size());
       outs.push_back(out_v);
       const std::string tag = "m" + std::to_string(mi) + "r";
@@ -1288,14 +1293,19 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
           std::string g[4];
           for (int k = 0; k < 4; ++k) {
             co.back() = lane_coord(b, k);
-            const Val v = reg(store(root, eval(c, root.result, co).name));
+            const Val v = reg(held(root, eval(c, root.result, co).name));
             // later members see the stored (possibly TF32-rounded) value
             c.memo[0][std::to_string(root.result) + "@" + join(co, ",")] = v;
             c.regs[std::to_string(out_v) + "@" + b + ":" + std::to_string(k)] = v;
             g[k] = v.name;
           }
-          c.body << "    *(float4*)(" << W << " + row * " << C << " + " << b << ") = make_float4(" << g[0] << ", "
-                 << g[1] << ", " << g[2] << ", " << g[3] << ");\n";
+          if (bf)
+            c.body << "    *(uint2*)(" << W << " + row * " << C << " + " << b << ") = make_uint2(sb_pack2(sb_bf16_bits("
+                   << g[0] << "), sb_bf16_bits(" << g[1] << ")), sb_pack2(sb_bf16_bits(" << g[2] << "), sb_bf16_bits("
+                   << g[3] << ")));\n";
+          else
+            c.body << "    *(float4*)(" << W << " + row * " << C << " + " << b << ") = make_float4(" << g[0] << ", "
+                   << g[1] << ", " << g[2] << ", " << g[3] << ");\n";
           auto sv = shadow_vals_.find(out_v);
           if (sv != shadow_vals_.end()) {
             // the operand shadow of the same four values
@@ -1318,9 +1328,9 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
         if (root.type.numel() != R) return false;
         std::vector<std::string> co = row_coords(root.type.shape, false, tag);
         c.root = root.result;
-        const Val v = reg(store(root, eval(c, root.result, co).name));
+        const Val v = reg(held(root, eval(c, root.result, co).name));
         c.memo[0][std::to_string(root.result) + "@" + join(co, ",")] = v;
-        c.body << "    if (lane == 0) " << W << "[row] = " << v.name << ";\n";
+        c.body << "    if (lane == 0) " << W << "[row] = " << (bf ? "sb_bf16_bits(" + v.name + ")" : v.name) << ";\n";
         c.regs[std::to_string(out_v) + "@row"] = v;
         c.reg_kind[out_v] = 1;
       } else if (m.kind == 3) {
@@ -1368,8 +1378,10 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
         const Type& in = f_.value_types[root.operands[0]];
         const auto& ish = in.shape;
         const int r = (int)ish.size();
+        // f32 accumulation of f32 or bf16 rows (a bf16 result is rounded once)
         if (r == 0 || ish.back() != C || root.dims.size() != 1 || root.dims[0] != r - 1 ||
-            root.type.dtype != DType::F32 || in.dtype != DType::F32 || root.type.numel() != R)
+            (root.type.dtype != DType::F32 && root.type.dtype != DType::BF16) ||
+            (in.dtype != DType::F32 && in.dtype != DType::BF16) || root.type.numel() != R)
           return false;
         const char* ident = root.body == ReduceBody::Add ? "0.f"
                             : root.body == ReduceBody::Max ? "__int_as_float(0xff800000)"
@@ -1404,18 +1416,20 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
         const bool saved_vec = c.vec;
         c.vec = false;
         const Val init = eval(c, root.operands[1], {});
-        const Val rv = reg(combine(acc, init.name));
+        const bool bf_red = root.type.dtype == DType::BF16;
+        const Val rv = reg(bf_red ? "sb_bf16_rn(" + combine(acc, init.name) + ")" : combine(acc, init.name));
         Val out = rv;
         if (m.epi) {
           std::string ev;
           const std::string code = epilogue_code(c, root, *m.epi, oc, 2, &ev, rv.name);
           c.body << code;
-          out = reg(store(*m.epi, ev));
+          out = reg(held(*m.epi, ev));
         } else {
-          out = reg(store(root, rv.name));
+          out = reg(held(root, rv.name));
         }
         c.vec = saved_vec;
-        c.body << "    if (lane == 0) " << W << "[row] = " << out.name << ";\n";
+        c.body << "    if (lane == 0) " << W << "[row] = " << (bf ? "sb_bf16_bits(" + out.name + ")" : out.name)
+               << ";\n";
         c.regs[std::to_string(out_v) + "@row"] = out;
         c.reg_kind[out_v] = 1;
       }
@@ -1434,8 +1448,10 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, cols.empty() ? kMaxGrid : 148 * 8));
   const size_t np = c.leaves.size() + outs.size();
   src_ << header(name, c, (int)outs.size() - 1 + (cols.empty() ? 0 : 1) + (int)shadows.size());
-  for (size_t j = 0; j < outs.size(); ++j)
-    src_ << "  float* __restrict__ O" << j << " = (float*)a.p[" << c.leaves.size() + j << "];\n";
+  for (size_t j = 0; j < outs.size(); ++j) {
+    const char* t = f_.value_types[outs[j]].dtype == DType::BF16 ? "unsigned short" : "float";
+    src_ << "  " << t << "* __restrict__ O" << j << " = (" << t << "*)a.p[" << c.leaves.size() + j << "];\n";
+  }
   for (size_t k = 0; k < shadows.size(); ++k) {
     const char* t = shadow_vals_.at(shadows[k]) == DType::BF16 ? "unsigned short" : "float";
     src_ << "  " << t << "* __restrict__ X" << k << " = (" << t << "*)a.p[" << np + (cols.empty() ? 0 : 1) + k
@@ -1512,7 +1528,7 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
   }
   st->elements = R * C;
   int64_t bytes = 0;
-  for (int o : outs) bytes += f_.value_types[o].numel() * 4;
+  for (int o : outs) bytes += f_.value_types[o].numel() * dtype_bytes(f_.value_types[o].dtype);
   for (int l : c.leaves) bytes += f_.value_types[l].numel() * dtype_bytes(f_.value_types[l].dtype);
   st->bytes_moved = bytes;
   return true;

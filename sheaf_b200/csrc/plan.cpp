@@ -1231,14 +1231,16 @@ Plan plan_function(const Function& f, Precision prec) {
   auto row_role = [&](size_t i, int64_t* R, int64_t* C, CodeGen::RowMember* m) {
     const Op& op = f.ops[i];
     const int v = op.result;
-    if (op.type.dtype != DType::F32) return -1;
+    // f32 or bf16 (computed in f32, rounded to bf16 per op as everywhere)
+    const bool bf = op.type.dtype == DType::BF16;
+    if (op.type.dtype != DType::F32 && !bf) return -1;
     const Op* red = nullptr;
     if (op.kind == OpKind::Reduce) red = &op;
     else if (pl.epilogue_of.count(v)) red = &f.ops[f.producer[pl.epilogue_of[v]]];
     if (red) {
       const auto& is = f.value_types[red->operands[0]].shape;
       // column reduction over every dim but the innermost
-      bool col = red == &op && is.size() >= 2 && red->dims.size() == is.size() - 1 &&
+      bool col = !bf && red == &op && is.size() >= 2 && red->dims.size() == is.size() - 1 &&
                  f.value_types[red->operands[0]].dtype == DType::F32;
       for (size_t d = 0; col && d + 1 < is.size(); ++d) col = red->dims[d] == (int64_t)d;
       if (col) {
@@ -1247,8 +1249,9 @@ Plan plan_function(const Function& f, Precision prec) {
         *m = {3, red, nullptr};
         return 3;
       }
+      const DType idt = f.value_types[red->operands[0]].dtype;
       if (red->dims.size() != 1 || is.empty() || red->dims[0] != (int64_t)is.size() - 1 ||
-          f.value_types[red->operands[0]].dtype != DType::F32)
+          (idt != DType::F32 && idt != DType::BF16))
         return -1;
       *R = red->type.numel();
       *C = is.back();
