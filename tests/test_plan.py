@@ -64,3 +64,23 @@ def test_gelu_matcher_rejects_other_functions():
 """
     rows = S.plan_steps(text, "notgelu.f", "tf32")
     assert not [r for r in rows if r["epi"]]
+
+
+def test_operand_shadows_written_by_their_producers():
+    """TF32: the residual-stream gradients that GEMMs and other steps both
+    read get TF32-rounded copies written by the row-group kernels that
+    produce them, so the plan has no separate conversion steps; bf16 mode
+    still converts the parameters (and values produced outside row groups).
+    Batch 8: 2048 rows (row groups start at 1024 rows)."""
+    low = M.gpt_vag(M.NANOGPT, batch=8)
+    assert int(_summary(low.text, "tf32").get("convert", "0")) == 0
+    n_bf16 = int(_summary(low.text, "bf16").get("convert", "0"))
+    assert 0 < n_bf16 < 75
+
+
+def test_bf16_softmax_is_one_row_group():
+    """A softmax over bf16 rows plans as one kernel, as the f32 one does."""
+    for dt in ("f32", "bf16"):
+        low = M.sweep_program("softmax", (4096, 768), False, dt)
+        s = _summary(low.text, "tf32")
+        assert s["loop"] == "1" and s["reduce"] == "0", (dt, s)
