@@ -57,18 +57,29 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const void* idx, int idx
   }
 }
 
-// hist[c][k] := rows of key k in chunks before c; total[k] := all rows of key k
+// hist[c][k] := rows of key k in chunks before c; total[k] := all rows of key k.
+// One warp per key: 32 chunks at a time, an exclusive scan across the lanes
+// (integer sums: the same result as a serial scan), a carry between groups.
 __global__ void __launch_bounds__(kThreads) colscan_kernel(int* __restrict__ hist, int* __restrict__ total,
                                                            int chunks, int v) {
   pdl_prologue();
-  for (int k = blockIdx.x * kThreads + threadIdx.x; k < v; k += gridDim.x * kThreads) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kWarps = kThreads / 32;
+  for (int64_t k = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); k < v; k += (int64_t)gridDim.x * kWarps) {
     int run = 0;
-    for (int c = 0; c < chunks; ++c) {
-      const int t = hist[(int64_t)c * v + k];
-      hist[(int64_t)c * v + k] = run;
-      run += t;
+    for (int c0 = 0; c0 < chunks; c0 += 32) {
+      const int c = c0 + lane;
+      const int t = c < chunks ? hist[(int64_t)c * v + k] : 0;
+      int incl = t;
+#pragma unroll
+      for (int s = 1; s < 32; s <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, s);
+        if (lane >= s) incl += y;
+      }
+      if (c < chunks) hist[(int64_t)c * v + k] = run + incl - t;
+      run += __shfl_sync(0xffffffffu, incl, 31);
     }
-    total[k] = run;
+    if (lane == 0) total[k] = run;
   }
 }
 
@@ -250,7 +261,7 @@ cudaError_t scatter_add_rows(const void* idx, bool idx_f32, const float* adj, fl
     e = launch_pdl(hist_kernel, dim3((unsigned)chunks), dim3(kThreads), 0, stream, idx, (int)idx_f32, n, (int)v, hist);
     if (e != cudaSuccess) return e;
   }
-  const unsigned vb = (unsigned)std::min<int64_t>((v + kThreads - 1) / kThreads, 148 * 8);
+  const unsigned vb = (unsigned)std::min<int64_t>((v + kThreads / 32 - 1) / (kThreads / 32), 148 * 8);
   e = launch_pdl(colscan_kernel, dim3(vb), dim3(kThreads), 0, stream, hist, total, (int)chunks, (int)v);
   if (e != cudaSuccess) return e;
   e = launch_pdl(offsets_kernel, dim3(1), dim3(1024), 0, stream, (const int*)total, offs, (int)v,
