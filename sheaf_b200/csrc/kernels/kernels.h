@@ -58,6 +58,17 @@ cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t s
 // dst[i] = src[i] rounded to nearest TF32 (cvt.rna), n elements.
 cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream);
 
+// Up to kRoundSegments such copies in one launch (the per-call TF32 copies of
+// a function's weights): segment i copies n[i] elements from src[i] to dst[i].
+constexpr int kRoundSegments = 48;
+struct RoundSegments {
+  const float* src[kRoundSegments];
+  float* dst[kRoundSegments];
+  int64_t n[kRoundSegments];
+  int count;
+};
+cudaError_t round_tf32_segments(const RoundSegments& segs, cudaStream_t stream);
+
 // y = gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x *
 // x)))))) in f32, Sheaf's gelu (sheaf/lib/nn.shf) in its operation order;
 // optionally rounded to TF32.  The unfused form of the GEMM epilogue.

@@ -66,6 +66,36 @@ cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t s
   return launch_pdl(bf16_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, src, dst, n, n8);
 }
 
+// Every block walks the segments in order with a grid-stride loop over each:
+// 4-wide where both pointers of a segment are 16-byte aligned, then the tail.
+__global__ void __launch_bounds__(256) round_tf32_segments_kernel(const RoundSegments s) {
+  pdl_prologue();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (int k = 0; k < s.count; ++k) {
+    const float* src = s.src[k];
+    float* dst = s.dst[k];
+    const int64_t n = s.n[k];
+    const int64_t n4 = ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0 ? n / 4 : 0;
+    for (int64_t i = t; i < n4; i += stride) {
+      const float4 v = reinterpret_cast<const float4*>(src)[i];
+      reinterpret_cast<float4*>(dst)[i] = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
+    }
+    for (int64_t i = n4 * 4 + t; i < n; i += stride) dst[i] = rna_tf32(src[i]);
+  }
+}
+
+cudaError_t round_tf32_segments(const RoundSegments& segs, cudaStream_t stream) {
+  if (segs.count <= 0) return cudaSuccess;
+  if (segs.count > kRoundSegments) return cudaErrorInvalidValue;
+  int64_t total = 0;
+  for (int k = 0; k < segs.count; ++k) total += segs.n[k];
+  int64_t blocks = (total / 4 + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(round_tf32_segments_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, segs);
+}
+
 cudaError_t round_tf32_copy(const float* src, float* dst, int64_t n, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   const bool aligned = ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0;

@@ -444,12 +444,20 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
   const Plan& plan = lf->plan;
   cudaStream_t stream = s->dev->stream;
   // TF32-rounded copies of parameters read by tensor-core GEMMs
+  // (kRoundSegments weights per launch: one launch for a typical model)
   std::map<int, const float*> rounded;
+  RoundSegments segs{};
   for (size_t j = 0; j < plan.rounded_params.size(); ++j) {
     int v = plan.rounded_params[j];
     float* dst = (float*)((char*)lf->arena + plan.rounded_offset[j]);
-    cudaError_t e = round_tf32_copy((const float*)ptr[v], dst, f.value_types[v].numel(), stream);
-    if (e != cudaSuccess) { return cuda_status(e, "round_tf32_copy"); }
+    segs.src[segs.count] = (const float*)ptr[v];
+    segs.dst[segs.count] = dst;
+    segs.n[segs.count] = f.value_types[v].numel();
+    if (++segs.count == kRoundSegments || j + 1 == plan.rounded_params.size()) {
+      cudaError_t e = round_tf32_segments(segs, stream);
+      if (e != cudaSuccess) { return cuda_status(e, "round_tf32_segments"); }
+      segs.count = 0;
+    }
     rounded[v] = dst;
   }
   std::vector<const void*> args;
