@@ -240,7 +240,21 @@ namespace {
 // wrote the fused epilogue's output (unsplit launches only: split-K partials
 // must not pass through it).
 cudaError_t gemm_main(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
-                      bool* used_tc, bool* fused) {
+                      bool* used_tc, bool* fused, SplitReduce* deferred) {
+  // the reduction of a split product: launched now, or described for the caller
+  auto reduce = [&](int64_t splits, int round) -> cudaError_t {
+    if (deferred) {
+      deferred->partials = (const float*)ws;
+      deferred->c = g.c;
+      deferred->splits = splits;
+      deferred->M = g.M;
+      deferred->N = g.N;
+      deferred->ldc = g.scm;
+      deferred->round = round;
+      return cudaSuccess;
+    }
+    return splitk_reduce((const float*)ws, g.c, splits, g.M, g.N, g.scm, round, stream);
+  };
   if (gemm_is_skinny(g)) return gemm_skinny(g, stream);
   // bf16 operands run on the tensor cores in every precision mode (their
   // products are exact in f32, so kind::f16 is the graph's arithmetic)
@@ -254,7 +268,7 @@ cudaError_t gemm_main(const GemmArgs& g, int precision, void* ws, size_t ws_byte
         *used_tc = true;
         *fused = !split;
         if (!split) return cudaSuccess;
-        return splitk_reduce((const float*)ws, g.c, p.splits, g.M, g.N, g.scm, g.round_out, stream);
+        return reduce(p.splits, g.round_out);
       }
       if (e != cudaErrorNotSupported) return e;
     } else {
@@ -279,7 +293,7 @@ cudaError_t gemm_main(const GemmArgs& g, int precision, void* ws, size_t ws_byte
         *used_tc = true;
         *fused = !split;
         if (!split) return cudaSuccess;
-        return splitk_reduce((const float*)ws, g.c, pd.plan.splits, g.M, g.N, g.scm, g.round_out, stream);
+        return reduce(pd.plan.splits, g.round_out);
       }
     }
   }
@@ -287,20 +301,23 @@ cudaError_t gemm_main(const GemmArgs& g, int precision, void* ws, size_t ws_byte
   const bool split = s.splits > 1 && ws && ws_bytes >= (size_t)(s.splits * g.M * g.N) * sizeof(float);
   cudaError_t e = gemm_simt(split ? split_args(g, s.splits, s.k_chunk, ws) : g, stream);
   if (e != cudaSuccess || !split) return e;
-  return splitk_reduce((const float*)ws, g.c, s.splits, g.M, g.N, g.scm, 0, stream);
+  return reduce(s.splits, 0);
 }
 
 }  // namespace
 
-cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc) {
+cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc,
+                 SplitReduce* deferred) {
   *used_tc = false;
+  if (deferred) *deferred = SplitReduce{};
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
   // the fused epilogue's output is laid out densely like C (the unfused form
   // below reads C as one contiguous array)
   if (g.epi && (g.epi != kEpiGelu || !g.c2 || g.scn != 1 || g.scm != g.N || (g.batch > 1 && g.scb != g.M * g.N)))
     return cudaErrorInvalidValue;
   bool fused = false;
-  cudaError_t e = gemm_main(g, precision, ws, ws_bytes, stream, used_tc, &fused);
+  // a fused epilogue applies to the reduced product: its split-K sum is not deferred
+  cudaError_t e = gemm_main(g, precision, ws, ws_bytes, stream, used_tc, &fused, g.epi ? nullptr : deferred);
   if (e != cudaSuccess || !g.epi || fused) return e;
   return gelu_tanh(g.c, g.c2, g.batch * g.M * g.N, g.round_out2, stream);
 }

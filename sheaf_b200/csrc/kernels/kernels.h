@@ -37,6 +37,24 @@ constexpr int kEpiGelu = 1;
 cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64_t M, int64_t N, int64_t ldc,
                           int round_tf32, cudaStream_t stream);
 
+// One split-K reduction left for later (see gemm): C[i] = sum over s of
+// partials[s*M*N + i], splits ascending, C with row stride ldc, rounded to
+// TF32 when round.  splits == 0: nothing pending.
+struct SplitReduce {
+  const float* partials = nullptr;
+  float* c = nullptr;
+  int64_t splits = 0, M = 0, N = 0, ldc = 0;
+  int round = 0;
+};
+// Up to kReduceSegments pending reductions in one launch, each with the
+// summation order of splitk_reduce (bit-identical results).
+constexpr int kReduceSegments = 32;
+struct ReduceSegments {
+  SplitReduce seg[kReduceSegments];
+  int count = 0;
+};
+cudaError_t splitk_reduce_segments(const ReduceSegments& r, cudaStream_t stream);
+
 // Split-K rule of the CUDA-core GEMM (shared by the session path and the
 // allocation-free entry point, so both compute identical partial sums).
 struct SimtSplit {
@@ -48,9 +66,14 @@ constexpr int64_t kSimtMaxM = 65535ll * 128;
 
 // Dispatch: precision 1 (TF32) tries the tcgen05 kernel, anything else or an
 // unsupported layout runs on CUDA cores; split-K through `ws` when the output
-// has few tiles.  *used_tc reports whether the tensor-core kernel ran.
+// has few tiles.  *used_tc reports whether the tensor-core kernel ran.  With
+// `deferred` set, a split product (without a fused epilogue) leaves its
+// partial sums in ws and describes their reduction in *deferred instead of
+// launching it: the caller runs it (splitk_reduce_segments) before C is read
+// and before ws is reused.
 size_t gemm_workspace(const GemmArgs& g, int precision);
-cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc);
+cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc,
+                 SplitReduce* deferred = nullptr);
 
 // dst[i] = bf16(src[i]), round to nearest even, n elements.
 cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t stream);

@@ -166,7 +166,56 @@ __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float4* __res
   *(float4*)(c + (size_t)row * ldc + col) = acc;
 }
 
+// Every block walks the reductions in order with a grid-stride loop over each
+// (4 outputs per thread where N, ldc and both buffers allow it); per output
+// the partials are added in ascending split order, as in the kernels above.
+__global__ void __launch_bounds__(256) splitk_reduce_segments_kernel(const ReduceSegments r) {
+  pdl_prologue();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (int k = 0; k < r.count; ++k) {
+    const SplitReduce& g = r.seg[k];
+    const int64_t mn = g.M * g.N;
+    const bool vec = g.N % 4 == 0 && g.ldc % 4 == 0 && (((uintptr_t)g.partials | (uintptr_t)g.c) & 15) == 0;
+    if (vec) {
+      const float4* p = reinterpret_cast<const float4*>(g.partials);
+      const int64_t mn4 = mn / 4, n4 = g.N / 4;
+      for (int64_t i4 = t; i4 < mn4; i4 += stride) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t s = 0; s < g.splits; ++s) {
+          const float4 v = p[s * mn4 + i4];
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        if (g.round) acc = make_float4(rna_tf32(acc.x), rna_tf32(acc.y), rna_tf32(acc.z), rna_tf32(acc.w));
+        const int64_t row = i4 / n4, col = (i4 - row * n4) * 4;
+        *(float4*)(g.c + row * g.ldc + col) = acc;
+      }
+    } else {
+      for (int64_t i = t; i < mn; i += stride) {
+        float acc = 0.f;
+        for (int64_t s = 0; s < g.splits; ++s) acc += g.partials[s * mn + i];
+        if (g.round) acc = rna_tf32(acc);
+        g.c[(i / g.N) * g.ldc + (i % g.N)] = acc;
+      }
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t splitk_reduce_segments(const ReduceSegments& r, cudaStream_t stream) {
+  if (r.count <= 0) return cudaSuccess;
+  if (r.count > kReduceSegments) return cudaErrorInvalidValue;
+  int64_t total = 0;
+  for (int k = 0; k < r.count; ++k) total += r.seg[k].M * r.seg[k].N;
+  int64_t blocks = (total / 4 + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(splitk_reduce_segments_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, r);
+}
 
 cudaError_t splitk_reduce(const float* partials, float* c, int64_t splits, int64_t M, int64_t N, int64_t ldc,
                           int round_tf32, cudaStream_t stream) {

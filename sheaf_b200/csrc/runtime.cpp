@@ -187,6 +187,9 @@ struct LoadedFunction {
   size_t arena_cap = 0;
   void* ws = nullptr;
   size_t ws_cap = 0;
+  // workspace that holds every deferred split-K partial set of a call at
+  // once (the next eager call grows the workspace to it)
+  size_t ws_want = 0;
   uint64_t calls = 0;
   // CUDA-graph replay (see run_graph)
   std::vector<std::shared_ptr<OutSlot>> slots;
@@ -435,11 +438,22 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
 
 // Enqueues a call's work on `stream`: TF32 copies of parameters, every plan
 // step, and the copies of outputs that no step writes (to outp[j]).  ptr holds
-// the device address of every materialized value.  before(si), if set, runs
-// before step si is enqueued (the data-parallel bucket flushes).  capturing:
-// the stream is being captured into a graph, so nothing may allocate.
+// the device address of every materialized value.  before(si, flush), if set,
+// runs before step si is enqueued (the data-parallel bucket flushes); it must
+// call flush() before a collective reads step outputs, so that deferred
+// split-K reductions are done.  capturing: the stream is being captured into
+// a graph, so nothing may allocate.
+//
+// Split-K reductions of GEMM steps are deferred and launched together (one
+// launch for up to kReduceSegments of them) when a step reads one of their
+// outputs, when the workspace is full, before a collective, and at the end:
+// the weight-gradient GEMMs of a backward pass, whose outputs no later step
+// reads, share one reduction launch.  Their partial sums stay in disjoint
+// parts of the workspace until then.  Profiled calls reduce right away, so
+// that every step's time includes its own reduction.
+using BeforeStep = std::function<sb_status*(size_t, const std::function<sb_status*()>&)>;
 sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& ptr, const std::vector<void*>& outp,
-                         const std::function<sb_status*(size_t)>& before, bool capturing) {
+                         const BeforeStep& before, bool capturing) {
   const Function& f = *lf->plan.fn;
   const Plan& plan = lf->plan;
   cudaStream_t stream = s->dev->stream;
@@ -460,11 +474,34 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
     }
     rounded[v] = dst;
   }
+  ReduceSegments red;
+  std::vector<int> red_vals;  // values the pending reductions write
+  size_t ws_off = 0;          // workspace bytes held by pending partial sums
+  size_t ws_run = 0;          // the same, not counting flushes forced by a full workspace
+  const bool defer = !s->profiling;
+  const std::function<sb_status*()> flush_red = [&]() -> sb_status* {
+    if (red.count) {
+      cudaError_t e = splitk_reduce_segments(red, stream);
+      if (e != cudaSuccess) return cuda_status(e, "splitk_reduce_segments");
+      red.count = 0;
+      red_vals.clear();
+    }
+    ws_off = 0;
+    return nullptr;
+  };
   std::vector<const void*> args;
   for (size_t si = 0; si < plan.steps.size(); ++si) {
     if (before)
-      if (sb_status* e = before(si)) return e;
+      if (sb_status* e = before(si, flush_red)) return e;
     const Step& st = plan.steps[si];
+    if (!red_vals.empty()) {
+      bool reads = false;
+      for (int l : st.leaves) reads |= std::find(red_vals.begin(), red_vals.end(), l) != red_vals.end();
+      if (reads) {
+        if (sb_status* e = flush_red()) return e;
+        ws_run = 0;
+      }
+    }
     if (!ptr[st.root] && st.elements) { return make_status(SB_STATUS_INTERNAL, "unplaced value"); }
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     if (s->profiling) {
@@ -518,7 +555,9 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
         a.c2 = (float*)ptr[st.extra_roots[0]];
         a.round_out2 = g.round_out2 ? 1 : 0;
       }
-      size_t need = gemm_workspace(a, s->opts.precision);
+      const size_t need = (gemm_workspace(a, s->opts.precision) + 255) & ~(size_t)255;
+      if (ws_off + need > lf->ws_cap)
+        if (sb_status* e = flush_red()) return e;  // the pending partials' space is free again
       // a stream being captured into a graph must not allocate: the eager
       // call that precedes every capture sized the workspace
       if (need > lf->ws_cap && capturing) return make_status(SB_STATUS_UNAVAILABLE, "workspace grows during capture");
@@ -528,9 +567,20 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
         else lf->ws_cap = need;
       }
       bool tc = false;
-      cudaError_t e = gemm(a, s->opts.precision, lf->ws, lf->ws_cap, stream, &tc);
+      SplitReduce d;
+      cudaError_t e = gemm(a, s->opts.precision, lf->ws ? (char*)lf->ws + ws_off : nullptr,
+                           lf->ws ? lf->ws_cap - ws_off : 0, stream, &tc, defer ? &d : nullptr);
       if (tc) s->used_tc = true;
       if (e != cudaSuccess) { return cuda_status(e, "gemm"); }
+      if (defer && d.splits > 0) {
+        red.seg[red.count++] = d;
+        red_vals.push_back(st.root);
+        ws_off += need;
+        ws_run += need;
+        lf->ws_want = std::max(lf->ws_want, ws_run);
+        if (red.count == kReduceSegments)
+          if (sb_status* e2 = flush_red()) return e2;
+      }
       continue;
     }
     if (st.kind == StepKind::Scatter) {
@@ -613,6 +663,14 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
       if (e) { return e; }
     }
+  }
+  if (sb_status* e = flush_red()) return e;
+  // room for every deferred partial set of a call, for the calls that follow
+  // (a captured call cannot allocate)
+  if (!capturing && lf->ws_want > lf->ws_cap) {
+    if (lf->ws) cudaFreeAsync(lf->ws, stream);
+    if (cudaMallocAsync(&lf->ws, lf->ws_want, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+    else lf->ws_cap = lf->ws_want;
   }
   // outputs not written by a step: copies
   for (size_t j = 0; j < f.returns.size(); ++j) {
@@ -734,9 +792,12 @@ sb_status* capture_reductions(sb_session* s, LoadedFunction* lf, const int32_t* 
     const int v = f.returns[j];
     return ((size_t)f.value_types[v].numel() * 4 + 255) & ~size_t(255);
   };
+  const std::function<sb_status*()>* red_flush = nullptr;  // deferred split-K reductions (during the steps)
   auto flush = [&]() -> sb_status* {
     if (!open) return nullptr;
     open = false;
+    if (red_flush)
+      if (sb_status* st = (*red_flush)()) return st;
     if (overlap) {
       SB_CUDA(cudaEventRecord(s->dev->ready, stream));
       SB_CUDA(cudaStreamWaitEvent(cs, s->dev->ready, 0));
@@ -773,10 +834,13 @@ sb_status* capture_reductions(sb_session* s, LoadedFunction* lf, const int32_t* 
     return nullptr;
   };
   slot->buckets.clear();
-  const std::function<sb_status*(size_t)> before = [&](size_t si) -> sb_status* {
+  const BeforeStep before = [&](size_t si, const std::function<sb_status*()>& fl) -> sb_status* {
+    red_flush = &fl;
     return (overlap && si > 0) ? queue((int)si - 1) : nullptr;
   };
-  if (sb_status* st = enqueue_steps(s, lf, ptr, outp, before, true)) return st;
+  sb_status* est = enqueue_steps(s, lf, ptr, outp, before, true);
+  red_flush = nullptr;
+  if (est) return est;
   if (sb_status* st = queue((int)plan.steps.size())) return st;
   if (sb_status* st = flush()) return st;
   if (overlap && forked) {
@@ -1000,8 +1064,11 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
       ready_at[std::max(plan.output_step[j], last[v])].push_back((int)j);
     }
   }
+  const std::function<sb_status*()>* red_flush = nullptr;  // deferred split-K reductions (during the steps)
   auto flush_bucket = [&]() -> sb_status* {
     if (bucket.empty()) return nullptr;
+    if (red_flush)
+      if (sb_status* st = (*red_flush)()) return st;
     const NcclApi& api = nccl_api();
     if (!s->nccl.comm) return make_status(SB_STATUS_FAILED_PRECONDITION, "NCCL communicator is not available");
     SB_CUDA(cudaEventRecord(s->dev->ready, stream));
@@ -1024,7 +1091,8 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
     comm_used = true;
     return nccl_settle(s);
   };
-  const std::function<sb_status*(size_t)> before = [&](size_t si) -> sb_status* {
+  const BeforeStep before = [&](size_t si, const std::function<sb_status*()>& fl) -> sb_status* {
+    red_flush = &fl;
     if (!overlap || si == 0) return nullptr;
     for (int j : ready_at[si - 1]) {
       bucket.push_back(j);
@@ -1036,7 +1104,9 @@ sb_status* run_function(sb_session* s, LoadedFunction* lf, sb_buffer* const* in,
   {
     std::vector<void*> outp(outs.size());
     for (size_t j = 0; j < outs.size(); ++j) outp[j] = outs[j]->ptr;
-    if (sb_status* e = enqueue_steps(s, lf, ptr, outp, before, false)) { cleanup(); return e; }
+    sb_status* e = enqueue_steps(s, lf, ptr, outp, before, false);
+    red_flush = nullptr;
+    if (e) { cleanup(); return e; }
   }
   // data-parallel combine of outputs
   if (overlap) {
