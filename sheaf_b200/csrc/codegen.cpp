@@ -1525,6 +1525,16 @@ bool CodeGen::gen_row_group(const std::vector<RowMember>& ms, int64_t R, int64_t
     st->finish_grid = (C + 7) / 8;
     st->splits = grid;
     st->scratch_elems = (int64_t)cols.size() * grid * C;
+    // plain column sums can also be finished by the batched kernel, which adds
+    // in the same order (block partials by ry then the 32-lane tree, + 0)
+    bool plain = true;
+    for (const ColRed& cr : cols)
+      plain = plain && cr.op->body == ReduceBody::Add && cr.init_code.empty() &&
+              cr.init_val == "__int_as_float(0x00000000)" && store(*cr.op, "x_") == "x_" &&
+              cr.op->type.dtype == DType::F32;
+    if (plain)
+      for (size_t q = 0; q < cols.size(); ++q) st->col_finish.push_back({cols[q].out, (int64_t)q * grid * C});
+    st->col_C = C;
   }
   st->elements = R * C;
   int64_t bytes = 0;

@@ -55,6 +55,21 @@ struct ReduceSegments {
 };
 cudaError_t splitk_reduce_segments(const ReduceSegments& r, cudaStream_t stream);
 
+// Column sums finished later: out[c] = sum over parts p of s[p*C + c] for
+// c < C, added as a row group's finish kernel adds them (parts split over 32
+// lanes with stride 32, in order, then a fixed 32-lane tree, then + 0.0f).
+struct ColSum {
+  const float* s = nullptr;
+  float* out = nullptr;
+  int C = 0, parts = 0;
+};
+constexpr int kColSegments = 32;
+struct ColSums {
+  ColSum seg[kColSegments];
+  int count = 0;
+};
+cudaError_t col_sum_segments(const ColSums& r, cudaStream_t stream);
+
 // Split-K rule of the CUDA-core GEMM (shared by the session path and the
 // allocation-free entry point, so both compute identical partial sums).
 struct SimtSplit {

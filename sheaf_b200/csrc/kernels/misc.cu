@@ -204,7 +204,45 @@ __global__ void __launch_bounds__(256) splitk_reduce_segments_kernel(const Reduc
   }
 }
 
+// Block b finishes 8 columns of one sum: blocks [blk0[k], blk0[k+1]) belong
+// to sum k (C/8 blocks each).
+struct ColSumLaunch {
+  ColSums r;
+  int blk0[kColSegments + 1];
+};
+
+__global__ void __launch_bounds__(256) col_sum_segments_kernel(const ColSumLaunch l) {
+  pdl_prologue();
+  __shared__ float part_[32][8];
+  int k = 0;
+  while (k + 1 < l.r.count && (int)blockIdx.x >= l.blk0[k + 1]) ++k;
+  const ColSum& g = l.r.seg[k];
+  const int cx = threadIdx.x & 7, ry = threadIdx.x >> 3;
+  const int col = ((int)blockIdx.x - l.blk0[k]) * 8 + cx;
+  float v = 0.f;
+  if (col < g.C)
+    for (int b = ry; b < g.parts; b += 32) v = v + g.s[(int64_t)b * g.C + col];
+  part_[ry][cx] = v;
+  __syncthreads();
+  for (int w = 16; w > 0; w >>= 1) {
+    if (ry < w) part_[ry][cx] = part_[ry][cx] + part_[ry + w][cx];
+    __syncthreads();
+  }
+  if (ry == 0 && col < g.C) g.out[col] = part_[0][cx] + 0.0f;
+}
+
 }  // namespace
+
+cudaError_t col_sum_segments(const ColSums& r, cudaStream_t stream) {
+  if (r.count <= 0) return cudaSuccess;
+  if (r.count > kColSegments) return cudaErrorInvalidValue;
+  ColSumLaunch l;
+  l.r = r;
+  l.blk0[0] = 0;
+  for (int k = 0; k < r.count; ++k) l.blk0[k + 1] = l.blk0[k] + (r.seg[k].C + 7) / 8;
+  if (l.blk0[r.count] <= 0) return cudaSuccess;
+  return launch_pdl(col_sum_segments_kernel, dim3((unsigned)l.blk0[r.count]), dim3(256), 0, stream, l);
+}
 
 cudaError_t splitk_reduce_segments(const ReduceSegments& r, cudaStream_t stream) {
   if (r.count <= 0) return cudaSuccess;

@@ -1507,6 +1507,18 @@ Plan plan_function(const Function& f, Precision prec) {
   std::vector<int> last_use(NV, -1);
   for (int s = 0; s < (int)plan.steps.size(); ++s)
     for (int l : plan.steps[s].leaves) last_use[l] = std::max(last_use[l], s);
+  // a row group's column sums whose outputs no later step reads may be
+  // finished at the end of the call (batched): their partials live until then
+  for (int s = 0; s < (int)plan.steps.size(); ++s) {
+    Step& st = plan.steps[s];
+    if (st.col_finish.empty()) continue;
+    bool read_later = false;
+    for (const Step::ColFinish& cf : st.col_finish) {
+      const int v = cf.out == 0 ? st.root : st.extra_roots[cf.out - 1];
+      read_later = read_later || last_use[v] > s;
+    }
+    st.finish_deferred = !read_later;
+  }
   for (int s = 0; s < (int)plan.steps.size(); ++s) {
     // a conversion step writes a shadow (placed below), not its root value
     if (plan.steps[s].kind == StepKind::Convert) continue;
@@ -1517,12 +1529,14 @@ Plan plan_function(const Function& f, Precision prec) {
       int64_t bytes = f.value_types[v].numel() * dtype_bytes(f.value_types[v].dtype);
       iv.push_back({bytes, s, std::max(s, last_use[v]), v, -1});
     }
+    const int scratch_end = plan.steps[s].finish_deferred ? (int)plan.steps.size() - 1 : s;
     if (plan.steps[s].scratch_elems && !pl.returned[plan.steps[s].root])
-      iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
+      iv.push_back({plan.steps[s].scratch_elems * 4, s, scratch_end, -1, s});
   }
   for (int s = 0; s < (int)plan.steps.size(); ++s)
     if (plan.steps[s].scratch_elems && pl.returned[plan.steps[s].root])
-      iv.push_back({plan.steps[s].scratch_elems * 4, s, s, -1, s});
+      iv.push_back({plan.steps[s].scratch_elems * 4, s,
+                    plan.steps[s].finish_deferred ? (int)plan.steps.size() - 1 : s, -1, s});
   int last_gemm = -1;
   for (int s2 = 0; s2 < (int)plan.steps.size(); ++s2)
     if (plan.steps[s2].kind == StepKind::Gemm || plan.steps[s2].kind == StepKind::Attn) last_gemm = s2;

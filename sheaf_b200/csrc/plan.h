@@ -88,6 +88,18 @@ struct Step {
   // shadows' indices into Plan::shadows, in the same order
   std::vector<int> shadow_values;
   std::vector<int> shadow_outs;
+  // Column reductions of a row group whose finish is a plain column sum (f32,
+  // zero init, no rounding): per reduction, its output's index among root and
+  // extra roots and the offset (floats) of its block partials in the scratch.
+  // With finish_deferred (no later step reads the outputs) the runtime may
+  // add the partials later, batched with other steps' (col_sum_segments).
+  struct ColFinish {
+    int out = 0;
+    int64_t offset = 0;
+  };
+  std::vector<ColFinish> col_finish;
+  int64_t col_C = 0;
+  bool finish_deferred = false;
 };
 
 struct Plan {

@@ -479,13 +479,19 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
   size_t ws_off = 0;          // workspace bytes held by pending partial sums
   size_t ws_run = 0;          // the same, not counting flushes forced by a full workspace
   const bool defer = !s->profiling;
+  ColSums cols;  // deferred finishes of row-group column sums
   const std::function<sb_status*()> flush_red = [&]() -> sb_status* {
     if (red.count) {
       cudaError_t e = splitk_reduce_segments(red, stream);
       if (e != cudaSuccess) return cuda_status(e, "splitk_reduce_segments");
       red.count = 0;
-      red_vals.clear();
     }
+    if (cols.count) {
+      cudaError_t e = col_sum_segments(cols, stream);
+      if (e != cudaSuccess) return cuda_status(e, "col_sum_segments");
+      cols.count = 0;
+    }
+    red_vals.clear();
     ws_off = 0;
     return nullptr;
   };
@@ -660,6 +666,21 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
     sb_status* e = launch_generated(lf->kern[si], args, st.grid, st.grid_y, st.block, stream);
     if (e) { return e; }
     if (st.splits > 1) {
+      if (defer && st.finish_deferred && (int)st.col_finish.size() <= kColSegments) {
+        // column sums no later step reads: added with other steps' at the next flush
+        if (cols.count + (int)st.col_finish.size() > kColSegments)
+          if (sb_status* e2 = flush_red()) return e2;
+        for (const Step::ColFinish& cf : st.col_finish) {
+          const int v = cf.out == 0 ? st.root : st.extra_roots[cf.out - 1];
+          ColSum& c = cols.seg[cols.count++];
+          c.s = (const float*)scratch + cf.offset;
+          c.out = (float*)ptr[v];
+          c.C = (int)st.col_C;
+          c.parts = (int)st.splits;
+          red_vals.push_back(v);
+        }
+        continue;
+      }
       e = launch_generated(lf->fin[si], args, st.finish_grid, 1, st.block, stream);
       if (e) { return e; }
     }
@@ -1686,7 +1707,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   }
   std::ostringstream os;
   os.precision(17);
-  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi\n";
+  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi,deferred_sums\n";
   static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert", "scatter"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
@@ -1694,7 +1715,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
     os << i << "," << kinds[(int)st.kind] << "," << step_name(st) << ","
        << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
        << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
-       << g.sbn << "," << g.epi << "\n";
+       << g.sbn << "," << g.epi << "," << (st.finish_deferred ? st.col_finish.size() : 0) << "\n";
   }
   std::string r = os.str();
   if (out_len) *out_len = r.size();

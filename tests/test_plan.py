@@ -84,3 +84,11 @@ def test_bf16_softmax_is_one_row_group():
         low = M.sweep_program("softmax", (4096, 768), False, dt)
         s = _summary(low.text, "tf32")
         assert s["loop"] == "1" and s["reduce"] == "0", (dt, s)
+
+
+def test_layer_norm_weight_gradient_sums_are_finished_in_one_batch():
+    """The 13 column sums of the nanoGPT step (LayerNorm weight gradients,
+    outputs no later step reads) are marked for the runtime's batched finish."""
+    low = M.gpt_vag(M.NANOGPT, batch=8)
+    rows = S.plan_steps(low.text, low.qualified, "tf32")
+    assert sum(r["deferred_sums"] for r in rows) == 2 * M.NANOGPT.n_layer + 1
