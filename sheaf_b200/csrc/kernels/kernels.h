@@ -107,6 +107,16 @@ struct RoundSegments {
 };
 cudaError_t round_tf32_segments(const RoundSegments& segs, cudaStream_t stream);
 
+// The same for bf16 copies (round to nearest even): consecutive conversion
+// steps of a call (the bf16 copies of its weights) in one launch.
+struct Bf16Segments {
+  const float* src[kRoundSegments];
+  uint16_t* dst[kRoundSegments];
+  int64_t n[kRoundSegments];
+  int count;
+};
+cudaError_t bf16_segments(const Bf16Segments& segs, cudaStream_t stream);
+
 // y = gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x *
 // x)))))) in f32, Sheaf's gelu (sheaf/lib/nn.shf) in its operation order;
 // optionally rounded to TF32.  The unfused form of the GEMM epilogue.

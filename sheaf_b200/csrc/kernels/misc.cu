@@ -85,6 +85,41 @@ __global__ void __launch_bounds__(256) round_tf32_segments_kernel(const RoundSeg
   }
 }
 
+// bf16 copies: 8 elements per step where both pointers of a segment are
+// 16-byte aligned, then the tail, round to nearest even as bf16_kernel.
+__global__ void __launch_bounds__(256) bf16_segments_kernel(const Bf16Segments s) {
+  pdl_prologue();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (int k = 0; k < s.count; ++k) {
+    const float* src = s.src[k];
+    uint16_t* dst = s.dst[k];
+    const int64_t n = s.n[k];
+    const int64_t n8 = ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0 ? n / 8 : 0;
+    for (int64_t i = t; i < n8; i += stride) {
+      const float4 a = reinterpret_cast<const float4*>(src)[2 * i];
+      const float4 b = reinterpret_cast<const float4*>(src)[2 * i + 1];
+      reinterpret_cast<uint4*>(dst)[i] =
+          make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+    }
+    for (int64_t i = n8 * 8 + t; i < n; i += stride) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(src[i]);
+      dst[i] = *reinterpret_cast<const uint16_t*>(&h);
+    }
+  }
+}
+
+cudaError_t bf16_segments(const Bf16Segments& segs, cudaStream_t stream) {
+  if (segs.count <= 0) return cudaSuccess;
+  if (segs.count > kRoundSegments) return cudaErrorInvalidValue;
+  int64_t total = 0;
+  for (int k = 0; k < segs.count; ++k) total += segs.n[k];
+  int64_t blocks = (total / 8 + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  return launch_pdl(bf16_segments_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, segs);
+}
+
 cudaError_t round_tf32_segments(const RoundSegments& segs, cudaStream_t stream) {
   if (segs.count <= 0) return cudaSuccess;
   if (segs.count > kRoundSegments) return cudaErrorInvalidValue;

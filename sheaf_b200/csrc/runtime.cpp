@@ -480,6 +480,7 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
   size_t ws_run = 0;          // the same, not counting flushes forced by a full workspace
   const bool defer = !s->profiling;
   ColSums cols;  // deferred finishes of row-group column sums
+  Bf16Segments cvt{};  // consecutive bf16 operand-shadow conversions
   const std::function<sb_status*()> flush_red = [&]() -> sb_status* {
     if (red.count) {
       cudaError_t e = splitk_reduce_segments(red, stream);
@@ -531,6 +532,22 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       const Shadow& sh = plan.shadows[st.shadow];
       char* dst = (char*)lf->arena + sh.offset;
       const float* src = (const float*)ptr[sh.value];
+      if (defer && sh.dtype == DType::BF16) {
+        // consecutive bf16 conversions (the weights' copies at the start of
+        // a call) go out as one launch
+        cvt.src[cvt.count] = src;
+        cvt.dst[cvt.count] = (uint16_t*)dst;
+        cvt.n[cvt.count] = st.elements;
+        ++cvt.count;
+        const bool more = si + 1 < plan.steps.size() && plan.steps[si + 1].kind == StepKind::Convert &&
+                          plan.shadows[plan.steps[si + 1].shadow].dtype == DType::BF16;
+        if (!more || cvt.count == kRoundSegments) {
+          cudaError_t e = bf16_segments(cvt, stream);
+          cvt.count = 0;
+          if (e != cudaSuccess) { return cuda_status(e, "operand shadows"); }
+        }
+        continue;
+      }
       cudaError_t e = sh.dtype == DType::BF16 ? bf16_copy(src, (uint16_t*)dst, st.elements, stream)
                                               : round_tf32_copy(src, (float*)dst, st.elements, stream);
       if (e != cudaSuccess) { return cuda_status(e, "operand shadow"); }
