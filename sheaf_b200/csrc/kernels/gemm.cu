@@ -195,29 +195,33 @@ GemmArgs split_args(const GemmArgs& g, int64_t splits, int64_t k_chunk, void* ws
 using TuneKey = std::array<int64_t, 20>;
 std::mutex tune_mu;
 std::map<TuneKey, int> tune_cache;
+std::map<std::array<int64_t, 40>, int> tune_pair_cache;
 
-int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
-  if (tc_forced_config() >= 0) return proposed;
-  const TuneKey key = {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
-                       run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
-                       (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16,
-                       (int64_t)run.epi};
-  std::lock_guard<std::mutex> lock(tune_mu);
-  auto it = tune_cache.find(key);
-  if (it != tune_cache.end()) return it->second;
+TuneKey tune_key(const GemmArgs& run) {
+  return {run.batch, run.M, run.N, run.K, run.sab, run.sam, run.sak, run.sbb, run.sbk, run.sbn,
+          run.scb, run.scm, run.scn, run.k_chunk, run.round_out, (int64_t)((uintptr_t)run.a & 15),
+          (int64_t)((uintptr_t)run.b & 15), (int64_t)((uintptr_t)run.c & 15), (int64_t)run.bf16,
+          (int64_t)run.epi};
+}
+
+// The fastest configuration for which run_cfg(c) succeeds, each timed twice
+// after one warm-up run; -1 while the stream is being captured or when no
+// configuration ran.
+template <typename F>
+int measure_configs(F run_cfg, cudaStream_t stream) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return proposed;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return -1;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
     if (e0) cudaEventDestroy(e0);
-    return proposed;
+    return -1;
   }
-  int best = proposed;
+  int best = -1;
   float best_ms = 1e30f;
   for (int c = 0; c < tc_num_configs(); ++c) {
-    if (gemm_tcgen05(run, c, stream) != cudaSuccess) continue;
+    if (run_cfg(c) != cudaSuccess) continue;
     cudaEventRecord(e0, stream);
-    bool ok = gemm_tcgen05(run, c, stream) == cudaSuccess && gemm_tcgen05(run, c, stream) == cudaSuccess;
+    bool ok = run_cfg(c) == cudaSuccess && run_cfg(c) == cudaSuccess;
     cudaEventRecord(e1, stream);
     float ms = 0.f;
     if (!ok || cudaEventSynchronize(e1) != cudaSuccess || cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) continue;
@@ -228,7 +232,35 @@ int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
   }
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  return best;
+}
+
+int tuned_config(const GemmArgs& run, int proposed, cudaStream_t stream) {
+  if (tc_forced_config() >= 0) return proposed;
+  const TuneKey key = tune_key(run);
+  std::lock_guard<std::mutex> lock(tune_mu);
+  auto it = tune_cache.find(key);
+  if (it != tune_cache.end()) return it->second;
+  const int best = measure_configs([&](int c) { return gemm_tcgen05(run, c, stream); }, stream);
+  if (best < 0) return proposed;
   tune_cache[key] = best;
+  return best;
+}
+
+// The same for the launch of two products: keyed by both signatures, timed as
+// one launch.
+int tuned_pair_config(const GemmArgs run[2], int proposed, cudaStream_t stream) {
+  if (tc_forced_config() >= 0) return proposed;
+  std::array<int64_t, 40> key;
+  const TuneKey k0 = tune_key(run[0]), k1 = tune_key(run[1]);
+  std::copy(k0.begin(), k0.end(), key.begin());
+  std::copy(k1.begin(), k1.end(), key.begin() + k0.size());
+  std::lock_guard<std::mutex> lock(tune_mu);
+  auto it = tune_pair_cache.find(key);
+  if (it != tune_pair_cache.end()) return it->second;
+  const int best = measure_configs([&](int c) { return gemm_tcgen05_group(run, 2, c, stream); }, stream);
+  if (best < 0) return proposed;
+  tune_pair_cache[key] = best;
   return best;
 }
 
@@ -320,6 +352,45 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
   cudaError_t e = gemm_main(g, precision, ws, ws_bytes, stream, used_tc, &fused, g.epi ? nullptr : deferred);
   if (e != cudaSuccess || !g.epi || fused) return e;
   return gelu_tanh(g.c, g.c2, g.batch * g.M * g.N, g.round_out2, stream);
+}
+
+cudaError_t gemm_pair(const GemmArgs g[2], int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
+                      SplitReduce deferred[2]) {
+  deferred[0] = SplitReduce{};
+  deferred[1] = SplitReduce{};
+  GemmArgs run[2];
+  TcPlan plan[2];
+  size_t off = 0;
+  for (int q = 0; q < 2; ++q) {
+    const GemmArgs& a = g[q];
+    if (a.M <= 0 || a.N <= 0 || a.batch <= 0 || a.epi || a.bf16 != g[0].bf16 || gemm_is_skinny(a))
+      return cudaErrorNotSupported;
+    if (precision != 1 && !a.bf16) return cudaErrorNotSupported;
+    if (!tc_plan(a, &plan[q])) return cudaErrorNotSupported;
+    run[q] = a;
+    if (plan[q].splits > 1) {
+      const size_t need = (size_t)(plan[q].splits * a.M * a.N) * sizeof(float);
+      if (!ws || off + need > ws_bytes) return cudaErrorNotSupported;
+      run[q] = split_args(a, plan[q].splits, plan[q].k_chunk, (char*)ws + off);
+      off += (need + 255) & ~(size_t)255;
+    }
+  }
+  // the cost model's proposal for the larger product stands where nothing is measured
+  const double f0 = (double)g[0].M * g[0].N * g[0].K * g[0].batch, f1 = (double)g[1].M * g[1].N * g[1].K * g[1].batch;
+  const int cfg = tuned_pair_config(run, f0 >= f1 ? plan[0].cfg : plan[1].cfg, stream);
+  cudaError_t e = gemm_tcgen05_group(run, 2, cfg, stream);
+  if (e != cudaSuccess) return e;
+  for (int q = 0; q < 2; ++q) {
+    if (plan[q].splits <= 1) continue;
+    deferred[q].partials = run[q].c;
+    deferred[q].c = g[q].c;
+    deferred[q].splits = plan[q].splits;
+    deferred[q].M = g[q].M;
+    deferred[q].N = g[q].N;
+    deferred[q].ldc = g[q].scm;
+    deferred[q].round = g[q].round_out;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace sb

@@ -91,6 +91,54 @@ struct Tiles {
   }
 };
 
+// One product of a launch: its operand and store maps and the scalars the
+// three roles read (C = C2's layout; kchunk in K steps, 0 when not split).
+struct GemmProblem {
+  CUtensorMap tmA, tmB, tmC, tmC2;
+  float* C;
+  float* C2;
+  long long scb, ldc;
+  int M, N, K;
+  int a_mn, b_mn, a3d, b3d, a_chunks, b_chunks, c_tma, c3d, round_out, kchunk, epi, round_out2;
+  Tiles tl;
+};
+
+// The products of one launch: the tiles of problem 0, then those of problem
+// 1, as one persistent tile sequence, so that independent GEMMs (a layer's
+// dX and dW in a backward pass) fill the SMs together and cost one launch.
+// Every problem has the same store path (all TMA stores or none), so a warp's
+// staging buffers are never written by plain stores while a TMA store of the
+// other problem still reads them.
+struct GemmGroup {
+  GemmProblem p[kGemmGroupMax];
+  int count;
+  int start[kGemmGroupMax + 1];  // first tile of problem q; start[count] = all tiles
+};
+
+// Tile t of a group: problem q, output slice z, tile origin (m0, n0), K steps
+// [kt0, kt1) and the operand slice zab that the loads address (0 for a split
+// product, whose slices are K ranges of one operand pair).
+struct TileAt {
+  int q, z, m0, n0, kt0, kt1, zab;
+};
+template <int BKE>
+__device__ __forceinline__ TileAt locate(const GemmGroup& g, int t, int bn) {
+  TileAt a;
+  a.q = (g.count > 1 && t >= g.start[1]) ? 1 : 0;
+  const GemmProblem& P = g.p[a.q];
+  P.tl.at(t - g.start[a.q], &a.z, &a.m0, &a.n0, bn);
+  const int ktiles = (P.K + BKE - 1) / BKE;
+  a.kt0 = 0;
+  a.kt1 = ktiles;
+  a.zab = a.z;
+  if (P.kchunk > 0) {
+    a.kt0 = a.z * P.kchunk;
+    a.kt1 = min(a.kt0 + P.kchunk, ktiles);
+    a.zab = 0;
+  }
+  return a;
+}
+
 // Epilogue store of a 32-row x 16-column chunk held one row per lane (v =
 // columns col0..col0+15 of row row0 + lane).  The warp passes it through its
 // 2 KB shared-memory slot so that each store instruction writes 8 rows x 64
@@ -242,11 +290,7 @@ __host__ __device__ constexpr uint32_t tmem_cols(int n) { return n <= 32 ? 32u :
 
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
-                      long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                      int c3d, int round_out, int kchunk, Tiles tl,
-                      const __grid_constant__ CUtensorMap tmC2, float* C2, int epi, int round_out2, int* err) {
+    gemm_tcgen05_kernel(const __grid_constant__ GemmGroup grp, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   pdl_prologue();
@@ -269,8 +313,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   // K values per 128-byte stage row (also M/N values per 128-byte row of an
   // MN-major tile): 32 f32 or 64 bf16
   constexpr int BKE = BF ? 64 : 32;
-  const int ktiles_all = (K + BKE - 1) / BKE;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
+  const int total = grp.start[grp.count];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -291,50 +335,37 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // K range of output slice z
-  auto krange = [&](int z, int* kt0, int* kt1, int* zab) {
-    *kt0 = 0;
-    *kt1 = ktiles_all;
-    *zab = z;
-    if (kchunk > 0) {
-      *kt0 = z * kchunk;
-      *kt1 = min(*kt0 + kchunk, ktiles_all);
-      *zab = 0;
-    }
-  };
-
   if (warp == 0) {
     if (lane == 0) {
       // ring position: slot s, phase ph (advanced after each K step)
       int it = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x) {
-        int z, m0, n0, kt0, kt1, zab;
-        tl.at(t, &z, &m0, &n0, BN);
-        krange(z, &kt0, &kt1, &zab);
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileAt at = locate<BKE>(grp, t, BN);
+        const GemmProblem& P = grp.p[at.q];
+        for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
           mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
-          if (!a_mn) {
-            tma_ld(a, &tmA, &full[s], kt * BKE, m0, zab, a3d);
-          } else if (a_chunks) {
-            tma_ld_chunks(a, &tmA, &full[s], kt * BKE, m0 / BKE, zab, a3d);
+          if (!P.a_mn) {
+            tma_ld(a, &P.tmA, &full[s], kt * BKE, at.m0, at.zab, P.a3d);
+          } else if (P.a_chunks) {
+            tma_ld_chunks(a, &P.tmA, &full[s], kt * BKE, at.m0 / BKE, at.zab, P.a3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / BKE; ++j)
-              tma_ld(a + j * BKE * 128, &tmA, &full[s], m0 + BKE * j, kt * BKE, zab, a3d);
+              tma_ld(a + j * BKE * 128, &P.tmA, &full[s], at.m0 + BKE * j, kt * BKE, at.zab, P.a3d);
           }
-          if (!b_mn) {
-            tma_ld(b, &tmB, &full[s], kt * BKE, n0, zab, b3d);
-          } else if (b_chunks) {
-            tma_ld_chunks(b, &tmB, &full[s], kt * BKE, n0 / BKE, zab, b3d);
+          if (!P.b_mn) {
+            tma_ld(b, &P.tmB, &full[s], kt * BKE, at.n0, at.zab, P.b3d);
+          } else if (P.b_chunks) {
+            tma_ld_chunks(b, &P.tmB, &full[s], kt * BKE, at.n0 / BKE, at.zab, P.b3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / BKE; ++j)
-              tma_ld(b + j * BKE * 128, &tmB, &full[s], n0 + BKE * j, kt * BKE, zab, b3d);
+              tma_ld(b + j * BKE * 128, &P.tmB, &full[s], at.n0 + BKE * j, kt * BKE, at.zab, P.b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -342,23 +373,22 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = BF ? idesc_bf16(BM, BN, a_mn, b_mn) : idesc_tf32(BM, BN, a_mn, b_mn);
-      // descriptors of slot 0, K slice 0 (see the CTA-pair kernel)
-      const uint64_t a_d0 = a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
-      const uint64_t b_d0 = b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
-      const uint64_t a_kk = a_mn ? kMnStep<BF> : 32 >> 4, b_kk = b_mn ? kMnStep<BF> : 32 >> 4;
       int it = 0, j = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tl.total && ok; t += gridDim.x, ++j) {
-        int z, m0, n0, kt0, kt1, zab;
-        tl.at(t, &z, &m0, &n0, BN);
-        krange(z, &kt0, &kt1, &zab);
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++j) {
+        const TileAt at = locate<BKE>(grp, t, BN);
+        const GemmProblem& P = grp.p[at.q];
+        const uint32_t idesc = BF ? idesc_bf16(BM, BN, P.a_mn, P.b_mn) : idesc_tf32(BM, BN, P.a_mn, P.b_mn);
+        // descriptors of slot 0, K slice 0 (see the CTA-pair kernel)
+        const uint64_t a_d0 = P.a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
+        const uint64_t b_d0 = P.b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
+        const uint64_t a_kk = P.a_mn ? kMnStep<BF> : 32 >> 4, b_kk = P.b_mn ? kMnStep<BF> : 32 >> 4;
         const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
         if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+        for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
           fence_after();
           // K-major: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B apart; the
@@ -369,8 +399,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (BF) mma_bf16(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-            else mma_tf32(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            if (BF) mma_bf16(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > at.kt0 || kk > 0) ? 1u : 0u);
+            else mma_tf32(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > at.kt0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -383,28 +413,27 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
     const int quad = warp & 3;
     int j = 0, sb = 0;
-    for (int t = blockIdx.x; t < tl.total; t += gridDim.x, ++j) {
-      int z, m0, n0, kt0, kt1, zab;
-      tl.at(t, &z, &m0, &n0, BN);
-      krange(z, &kt0, &kt1, &zab);
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++j) {
+      const TileAt at = locate<BKE>(grp, t, BN);
+      const GemmProblem& P = grp.p[at.q];
       const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
       fence_after();
-      const int row0 = m0 + quad * 32;
-      float* cz = C + (long long)z * scb;
-      const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
+      const int row0 = at.m0 + quad * 32;
+      float* cz = P.C + (long long)at.z * P.scb;
+      const bool vec = (P.ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
       const uint32_t acc = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
       Epi e2;
-      e2.tm = &tmC2;
-      e2.c = C2 + (long long)z * scb;
-      e2.epi = epi;
-      e2.round_out = round_out2;
-      epilogue_warp<BN>(acc, epi_buf + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc,
-                        vec, kt1 <= kt0, round_out, e2);
+      e2.tm = &P.tmC2;
+      e2.c = P.C2 + (long long)at.z * P.scb;
+      e2.epi = P.epi;
+      e2.round_out = P.round_out2;
+      epilogue_warp<BN>(acc, epi_buf + (warp - 2) * 1024, lane, &sb, &P.tmC, P.c_tma, P.c3d, at.z, cz, row0, at.n0,
+                        P.M, P.N, P.ldc, vec, at.kt1 <= at.kt0, P.round_out, e2);
       fence_before();
       mbar_arrive(&acc_empty[b]);
     }
-    if (c_tma && lane == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   }
   fence_before();
   __syncthreads();
@@ -425,11 +454,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 // peer's epilogue releases an accumulator with a remote mbarrier arrive.
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, float* C, int M, int N, int K, long long scb,
-                   long long ldc, int a_mn, int b_mn, int a3d, int b3d, int a_chunks, int b_chunks, int c_tma,
-                   int c3d, int round_out, int kchunk, Tiles tl,
-                   const __grid_constant__ CUtensorMap tmC2, float* C2, int epi, int round_out2, int* err) {
+    gemm_tcgen05_pair(const __grid_constant__ GemmGroup grp, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -457,8 +482,8 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   // K values per 128-byte stage row (also M/N values per 128-byte row of an
   // MN-major tile): 32 f32 or 64 bf16
   constexpr int BKE = BF ? 64 : 32;
-  const int ktiles_all = (K + BKE - 1) / BKE;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
+  const int total = grp.start[grp.count];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -480,16 +505,6 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto krange = [&](int z, int* kt0, int* kt1, int* zab) {
-    *kt0 = 0;
-    *kt1 = ktiles_all;
-    *zab = z;
-    if (kchunk > 0) {
-      *kt0 = z * kchunk;
-      *kt1 = min(*kt0 + kchunk, ktiles_all);
-      *zab = 0;
-    }
-  };
   auto ld = [&](void* dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z, bool is3d) {
     if (is3d) tma_load_3d_pair(dst, map, bar, x, y, z);
     else tma_load_2d_pair(dst, map, bar, x, y);
@@ -506,32 +521,32 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       uint32_t ph = 0;
       const uint32_t full_leader = cluster_addr(&full[0], 0);
       bool ok = true;
-      for (int t = pair; t < tl.total && ok; t += npairs) {
-        int z, m0, n0, kt0, kt1, zab;
-        tl.at(t, &z, &m0, &n0, BN);
-        krange(z, &kt0, &kt1, &zab);
-        const int ma = m0 + (int)rank * BM, nb = n0 + (int)rank * BNH;
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+      for (int t = pair; t < total && ok; t += npairs) {
+        const TileAt at = locate<BKE>(grp, t, BN);
+        const GemmProblem& P = grp.p[at.q];
+        const int ma = at.m0 + (int)rank * BM, nb = at.n0 + (int)rank * BNH;
+        for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
           if (leader) mbar_expect_tx(&full[s], 2u * (uint32_t)S::STAGE);
           const uint32_t bar = full_leader + (uint32_t)(s * 8);
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
-          if (!a_mn) {
-            ld(a, &tmA, bar, kt * BKE, ma, zab, a3d);
-          } else if (a_chunks) {
-            ld_chunks(a, &tmA, bar, kt * BKE, ma / BKE, zab, a3d);
+          if (!P.a_mn) {
+            ld(a, &P.tmA, bar, kt * BKE, ma, at.zab, P.a3d);
+          } else if (P.a_chunks) {
+            ld_chunks(a, &P.tmA, bar, kt * BKE, ma / BKE, at.zab, P.a3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / BKE; ++j) ld(a + j * BKE * 128, &tmA, bar, ma + BKE * j, kt * BKE, zab, a3d);
+            for (int j = 0; j < BM / BKE; ++j) ld(a + j * BKE * 128, &P.tmA, bar, ma + BKE * j, kt * BKE, at.zab, P.a3d);
           }
-          if (!b_mn) {
-            ld(b, &tmB, bar, kt * BKE, nb, zab, b3d);
-          } else if (b_chunks) {
-            ld_chunks(b, &tmB, bar, kt * BKE, nb / BKE, zab, b3d);
+          if (!P.b_mn) {
+            ld(b, &P.tmB, bar, kt * BKE, nb, at.zab, P.b3d);
+          } else if (P.b_chunks) {
+            ld_chunks(b, &P.tmB, bar, kt * BKE, nb / BKE, at.zab, P.b3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BNH / BKE; ++j) ld(b + j * BKE * 128, &tmB, bar, nb + BKE * j, kt * BKE, zab, b3d);
+            for (int j = 0; j < BNH / BKE; ++j)
+              ld(b + j * BKE * 128, &P.tmB, bar, nb + BKE * j, kt * BKE, at.zab, P.b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -539,35 +554,34 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      const uint32_t idesc = BF ? idesc_bf16(2 * BM, BN, a_mn, b_mn) : idesc_tf32(2 * BM, BN, a_mn, b_mn);
-      // descriptors of slot 0, K slice 0; a slot adds its byte offset and a
-      // K slice 32 B (K-major) or 1024 / 2048 B (MN-major tf32 / bf16), in
-      // 16-byte units, to the start-address field (shared addresses stay below
-      // 2^18, no carry)
-      const uint64_t a_d0 = a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
-      const uint64_t b_d0 = b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
-      const uint64_t a_kk = a_mn ? kMnStep<BF> : 32 >> 4, b_kk = b_mn ? kMnStep<BF> : 32 >> 4;
       const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
       int it = 0, j = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = pair; t < tl.total && ok; t += npairs, ++j) {
-        int z, m0, n0, kt0, kt1, zab;
-        tl.at(t, &z, &m0, &n0, BN);
-        krange(z, &kt0, &kt1, &zab);
+      for (int t = pair; t < total && ok; t += npairs, ++j) {
+        const TileAt at = locate<BKE>(grp, t, BN);
+        const GemmProblem& P = grp.p[at.q];
+        const uint32_t idesc = BF ? idesc_bf16(2 * BM, BN, P.a_mn, P.b_mn) : idesc_tf32(2 * BM, BN, P.a_mn, P.b_mn);
+        // descriptors of slot 0, K slice 0; a slot adds its byte offset and a
+        // K slice 32 B (K-major) or 1024 / 2048 B (MN-major tf32 / bf16), in
+        // 16-byte units, to the start-address field (shared addresses stay below
+        // 2^18, no carry)
+        const uint64_t a_d0 = P.a_mn ? mn_desc<BF>(smem_u32(sA)) : smem_desc(smem_u32(sA), 16, 1024, 2);
+        const uint64_t b_d0 = P.b_mn ? mn_desc<BF>(smem_u32(sB)) : smem_desc(smem_u32(sB), 16, 1024, 2);
+        const uint64_t a_kk = P.a_mn ? kMnStep<BF> : 32 >> 4, b_kk = P.b_mn ? kMnStep<BF> : 32 >> 4;
         const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
         if (use > 0 && !mbar_wait(&acc_empty[b], (uint32_t)(use - 1) & 1u, abort_flag, err, 4)) break;
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+        for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (!mbar_wait(&full[s], ph, abort_flag, err, 2)) { ok = false; break; }
           fence_after();
           const uint64_t ad = a_d0 + (uint64_t)((s * S::A_BYTES) >> 4);
           const uint64_t bd = b_d0 + (uint64_t)((s * S::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (BF) mma_bf16_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-            else mma_tf32_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            if (BF) mma_bf16_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > at.kt0 || kk > 0) ? 1u : 0u);
+            else mma_tf32_pair(acc, ad + kk * a_kk, bd + kk * b_kk, idesc, (kt > at.kt0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_pair(empty0 + (uint32_t)(s * 8));
           mma_commit_pair(empty1 + (uint32_t)(s * 8));
@@ -581,28 +595,27 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   } else {
     const int quad = warp & 3;
     int j = 0, sb = 0;
-    for (int t = pair; t < tl.total; t += npairs, ++j) {
-      int z, m0, n0, kt0, kt1, zab;
-      tl.at(t, &z, &m0, &n0, BN);
-      krange(z, &kt0, &kt1, &zab);
+    for (int t = pair; t < total; t += npairs, ++j) {
+      const TileAt at = locate<BKE>(grp, t, BN);
+      const GemmProblem& P = grp.p[at.q];
       const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
       fence_after();
-      const int row0 = m0 + (int)rank * BM + quad * 32;
-      float* cz = C + (long long)z * scb;
-      const bool vec = (ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
+      const int row0 = at.m0 + (int)rank * BM + quad * 32;
+      float* cz = P.C + (long long)at.z * P.scb;
+      const bool vec = (P.ldc & 3) == 0 && (((uintptr_t)cz) & 15) == 0;
       const uint32_t accp = tmem + (uint32_t)(b * BN) + ((uint32_t)(quad * 32) << 16);
       Epi e2;
-      e2.tm = &tmC2;
-      e2.c = C2 + (long long)z * scb;
-      e2.epi = epi;
-      e2.round_out = round_out2;
-      epilogue_warp<BN>(accp, epi_buf + (warp - 2) * 1024, lane, &sb, &tmC, c_tma, c3d, z, cz, row0, n0, M, N, ldc,
-                        vec, kt1 <= kt0, round_out, e2);
+      e2.tm = &P.tmC2;
+      e2.c = P.C2 + (long long)at.z * P.scb;
+      e2.epi = P.epi;
+      e2.round_out = P.round_out2;
+      epilogue_warp<BN>(accp, epi_buf + (warp - 2) * 1024, lane, &sb, &P.tmC, P.c_tma, P.c3d, at.z, cz, row0, at.n0,
+                        P.M, P.N, P.ldc, vec, at.kt1 <= at.kt0, P.round_out, e2);
       fence_before();
       mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
     }
-    if (c_tma && lane == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   }
   fence_before();
   __syncthreads();
@@ -705,20 +718,75 @@ bool operand_maps(const GemmArgs& g, bool a_mn, bool b_mn, int bn_cta, CUtensorM
   return ok;
 }
 
-template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
-cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
+// Problem g of a launch whose tiles are bm_tile x bn_tile with bn_cta columns
+// of B loaded per CTA: operand and store maps and scalars.  false when a map
+// cannot be encoded or the problem has too many tiles.
+template <bool BF>
+bool fill_problem(const GemmArgs& g, bool a_mn, bool b_mn, int bn_cta, int bm_tile, int bn_tile, GemmProblem* P) {
   constexpr int BKE = BF ? 64 : 32;
-  // an MN-major tile is loaded in whole 128-byte-wide chunks
-  if (BF && b_mn && BN % BKE) return cudaErrorNotSupported;
-  CUtensorMap ta, tb;
   int a_chunks = 0, b_chunks = 0;
   bool a3d = false, b3d = false;
-  if (!operand_maps<BF>(g, a_mn, b_mn, BN, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
-    return cudaErrorNotSupported;
-  const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  CUtensorMap tc_map = tb, tc_map2 = tb;  // placeholder contents when C (C2) has no store map
-  const int c_tma = store_maps(g, &tc_map, &tc_map2) ? 1 : 0;
-  const int c3d = g.batch > 1 ? 1 : 0;
+  if (!operand_maps<BF>(g, a_mn, b_mn, bn_cta, &P->tmA, &P->tmB, &a_chunks, &b_chunks, &a3d, &b3d)) return false;
+  P->tmC = P->tmB;  // placeholder contents when C (C2) has no store map
+  P->tmC2 = P->tmB;
+  P->c_tma = store_maps(g, &P->tmC, &P->tmC2) ? 1 : 0;
+  P->C = g.c;
+  P->C2 = g.epi ? g.c2 : g.c;
+  P->scb = g.scb;
+  P->ldc = g.scm;
+  P->M = (int)g.M;
+  P->N = (int)g.N;
+  P->K = (int)g.K;
+  P->a_mn = a_mn;
+  P->b_mn = b_mn;
+  P->a3d = a3d;
+  P->b3d = b3d;
+  P->a_chunks = a_chunks;
+  P->b_chunks = b_chunks;
+  P->c3d = g.batch > 1 ? 1 : 0;
+  P->round_out = g.round_out;
+  P->kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
+  P->epi = g.epi;
+  P->round_out2 = g.round_out2;
+  P->tl.bm = bm_tile;
+  P->tl.m_tiles = (int)((g.M + bm_tile - 1) / bm_tile);
+  P->tl.n_tiles = (int)((g.N + bn_tile - 1) / bn_tile);
+  P->tl.per_z = P->tl.m_tiles * P->tl.n_tiles;
+  const int64_t total = (int64_t)P->tl.per_z * g.batch;
+  if (total > (1ll << 30)) return false;
+  P->tl.total = (int)total;
+  return true;
+}
+
+// The launch description of problems gs[0..n): their tile ranges one after
+// the other, one store path for all (TMA stores only when every problem has
+// its store maps).
+template <bool BF>
+bool make_group(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int bn_cta, int bm_tile, int bn_tile,
+                GemmGroup* G) {
+  G->count = n;
+  G->start[0] = 0;
+  bool all_tma = true;
+  for (int q = 0; q < n; ++q) {
+    if (!fill_problem<BF>(gs[q], a_mn[q], b_mn[q], bn_cta, bm_tile, bn_tile, &G->p[q])) return false;
+    all_tma = all_tma && G->p[q].c_tma;
+    const int64_t end = (int64_t)G->start[q] + G->p[q].tl.total;
+    if (end > (1ll << 30)) return false;
+    G->start[q + 1] = (int)end;
+  }
+  if (!all_tma)
+    for (int q = 0; q < n; ++q) G->p[q].c_tma = 0;
+  return true;
+}
+
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+cudaError_t launch(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int* err, cudaStream_t stream) {
+  constexpr int BKE = BF ? 64 : 32;
+  // an MN-major tile is loaded in whole 128-byte-wide chunks
+  for (int q = 0; q < n; ++q)
+    if (BF && b_mn[q] && BN % BKE) return cudaErrorNotSupported;
+  GemmGroup G{};
+  if (!make_group<BF>(gs, a_mn, b_mn, n, BN, BM, BN, &G)) return cudaErrorNotSupported;
   using S = Smem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
@@ -727,36 +795,21 @@ cudaError_t launch(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  Tiles tl;
-  tl.bm = BM;
-  tl.m_tiles = (int)((g.M + BM - 1) / BM);
-  tl.n_tiles = (int)((g.N + BN - 1) / BN);
-  tl.per_z = tl.m_tiles * tl.n_tiles;
-  const int64_t total = (int64_t)tl.per_z * g.batch;
-  if (total > (1ll << 30)) return cudaErrorNotSupported;
-  tl.total = (int)total;
-  const int grid = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count());
-  return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, ta, tb, tc_map, g.c, (int)g.M,
-                    (int)g.N, (int)g.K, (long long)g.scb, (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d,
-                    a_chunks, b_chunks, c_tma, c3d, g.round_out, kchunk, tl, tc_map2, g.epi ? g.c2 : g.c, g.epi,
-                    g.round_out2, err);
+  const int grid = (int)std::min<int64_t>(G.start[n], (int64_t)PER_SM * sm_count());
+  if (grid <= 0) return cudaSuccess;
+  return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, G, err);
 }
 
 template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
-cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaStream_t stream) {
+cudaError_t launch_pair(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int* err,
+                        cudaStream_t stream) {
   constexpr int BNH = BN / 2;
   constexpr int BKE = BF ? 64 : 32;
   // each CTA loads BN / 2 columns of B: whole 128-byte chunks when MN-major
-  if (b_mn && BNH % BKE) return cudaErrorNotSupported;
-  CUtensorMap ta, tb;
-  int a_chunks = 0, b_chunks = 0;
-  bool a3d = false, b3d = false;
-  if (!operand_maps<BF>(g, a_mn, b_mn, BNH, &ta, &tb, &a_chunks, &b_chunks, &a3d, &b3d))
-    return cudaErrorNotSupported;
-  const int kchunk = g.k_chunk > 0 ? (int)(g.k_chunk / BKE) : 0;
-  CUtensorMap tc_map = tb, tc_map2 = tb;  // placeholder contents when C (C2) has no store map
-  const int c_tma = store_maps(g, &tc_map, &tc_map2) ? 1 : 0;
-  const int c3d = g.batch > 1 ? 1 : 0;
+  for (int q = 0; q < n; ++q)
+    if (b_mn[q] && BNH % BKE) return cudaErrorNotSupported;
+  GemmGroup G{};
+  if (!make_group<BF>(gs, a_mn, b_mn, n, BNH, 2 * BM, BN, &G)) return cudaErrorNotSupported;
   using S = Smem<BNH, STAGES>;
   auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC>;
   static bool attr_set = false;
@@ -765,15 +818,8 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  Tiles tl;
-  tl.bm = 2 * BM;
-  tl.m_tiles = (int)((g.M + 2 * BM - 1) / (2 * BM));
-  tl.n_tiles = (int)((g.N + BN - 1) / BN);
-  tl.per_z = tl.m_tiles * tl.n_tiles;
-  const int64_t total = (int64_t)tl.per_z * g.batch;
-  if (total > (1ll << 30)) return cudaErrorNotSupported;
-  tl.total = (int)total;
-  const int pairs = (int)std::min<int64_t>(total, (int64_t)PER_SM * sm_count() / 2);
+  const int pairs = (int)std::min<int64_t>(G.start[n], (int64_t)PER_SM * sm_count() / 2);
+  if (pairs <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kThreads);
@@ -788,9 +834,7 @@ cudaError_t launch_pair(const GemmArgs& g, bool a_mn, bool b_mn, int* err, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   launch_counter().fetch_add(1, std::memory_order_relaxed);
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_map, g.c, (int)g.M, (int)g.N, (int)g.K, (long long)g.scb,
-                            (long long)g.scm, (int)a_mn, (int)b_mn, (int)a3d, (int)b3d, a_chunks, b_chunks, c_tma, c3d,
-                            g.round_out, kchunk, tl, tc_map2, g.epi ? g.c2 : g.c, g.epi, g.round_out2, err);
+  return cudaLaunchKernelEx(&cfg, kern, G, err);
 }
 
 int* error_word() { return tc_error_word(); }
@@ -982,32 +1026,36 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
   return p->cfg >= 0;
 }
 
-cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) {
-  bool a_mn, b_mn;
-  if (!tc_layout(g, &a_mn, &b_mn)) return cudaErrorNotSupported;
+cudaError_t gemm_tcgen05_group(const GemmArgs* gs, int n, int cfg, cudaStream_t stream) {
+  if (n < 1 || n > kGemmGroupMax) return cudaErrorInvalidValue;
+  bool a_mn[kGemmGroupMax], b_mn[kGemmGroupMax];
+  for (int q = 0; q < n; ++q)
+    if (!tc_layout(gs[q], &a_mn[q], &b_mn[q]) || gs[q].bf16 != gs[0].bf16) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
-  if (g.bf16) {
+  if (gs[0].bf16) {
     switch (cfg) {
-      case 0: return launch<true, 64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-      case 1: return launch<true, 128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
-      case 2: return launch_pair<true, 128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-      case 3: return launch_pair<true, 192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-      case 4: return launch_pair<true, 256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-      case 5: return launch_pair<true, 256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
+      case 0: return launch<true, 64, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+      case 1: return launch<true, 128, 3, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+      case 2: return launch_pair<true, 128, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+      case 3: return launch_pair<true, 192, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
+      case 4: return launch_pair<true, 256, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
+      case 5: return launch_pair<true, 256, 6, 1, 2>(gs, a_mn, b_mn, n, err, stream);
     }
     return cudaErrorNotSupported;
   }
   switch (cfg) {
-    case 0: return launch<false, 64, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 1: return launch<false, 128, 3, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 2: return launch_pair<false, 128, 4, 2, 2>(g, a_mn, b_mn, err, stream);
-    case 3: return launch_pair<false, 192, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-    case 4: return launch_pair<false, 256, 3, 2, 1>(g, a_mn, b_mn, err, stream);
-    case 5: return launch_pair<false, 256, 6, 1, 2>(g, a_mn, b_mn, err, stream);
+    case 0: return launch<false, 64, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+    case 1: return launch<false, 128, 3, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+    case 2: return launch_pair<false, 128, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
+    case 3: return launch_pair<false, 192, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
+    case 4: return launch_pair<false, 256, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
+    case 5: return launch_pair<false, 256, 6, 1, 2>(gs, a_mn, b_mn, n, err, stream);
   }
   return cudaErrorNotSupported;
 }
+
+cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) { return gemm_tcgen05_group(&g, 1, cfg, stream); }
 
 int gemm_tcgen05_error() {
   int* p = error_word();

@@ -90,6 +90,20 @@ size_t gemm_workspace(const GemmArgs& g, int precision);
 cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cudaStream_t stream, bool* used_tc,
                  SplitReduce* deferred = nullptr);
 
+// Two independent GEMMs (neither reads the other's output) in one tensor-core
+// launch: the tiles of g[0], then those of g[1], one persistent tile sequence,
+// with the configuration measured for the pair.  For the products of a
+// backward pass whose tiles alone would leave SMs idle (a layer's dX and dW).
+// Each split product leaves its partial sums in its part of ws (the first
+// gemm_workspace(g[0]) bytes, rounded up to 256, then g[1]'s) and describes
+// their reduction in deferred[q]; both products' results are as gemm() gives
+// them.  cudaErrorNotSupported (nothing launched) when either product needs
+// another path: CUDA cores, padded operands, a fused epilogue, or operands of
+// different types; the caller then runs them one by one.
+constexpr int kGemmGroupMax = 2;
+cudaError_t gemm_pair(const GemmArgs g[2], int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
+                      SplitReduce deferred[2]);
+
 // dst[i] = bf16(src[i]), round to nearest even, n elements.
 cudaError_t bf16_copy(const float* src, uint16_t* dst, int64_t n, cudaStream_t stream);
 
@@ -148,6 +162,9 @@ bool tc_plan(const GemmArgs& g, TcPlan* plan);
 int tc_num_configs();
 int tc_forced_config();
 cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream);
+// The same for n <= kGemmGroupMax products of one operand type in one launch
+// (g[q] already split where its plan split K).
+cudaError_t gemm_tcgen05_group(const GemmArgs* g, int n, int cfg, cudaStream_t stream);
 // Non-zero when a tcgen05 kernel gave up on a bounded wait (GEMM 1: ring slot,
 // 2: operand tiles, 3: accumulator; attention 11..35) or found its shared
 // memory window misaligned (9), or the row scatter-add found inconsistent

@@ -436,6 +436,17 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
   return nullptr;
 }
 
+// SHEAF_B200_GEMM_PAIRS=0: every GEMM step in its own launch (for
+// comparisons; pairing changes no result, since a product's summation order
+// depends only on its shape).
+bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SHEAF_B200_GEMM_PAIRS");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
 // Enqueues a call's work on `stream`: TF32 copies of parameters, every plan
 // step, and the copies of outputs that no step writes (to outp[j]).  ptr holds
 // the device address of every materialized value.  before(si, flush), if set,
@@ -451,6 +462,10 @@ sb_status* launch_generated(cudaKernel_t k, const std::vector<const void*>& ptrs
 // reads, share one reduction launch.  Their partial sums stay in disjoint
 // parts of the workspace until then.  Profiled calls reduce right away, so
 // that every step's time includes its own reduction.
+//
+// Two consecutive GEMM steps, the second not reading the first's result,
+// run as one tensor-core launch (gemm_pair) where both allow it; profiled
+// calls launch every step on its own.
 using BeforeStep = std::function<sb_status*(size_t, const std::function<sb_status*()>&)>;
 sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& ptr, const std::vector<void*>& outp,
                          const BeforeStep& before, bool capturing) {
@@ -495,6 +510,33 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
     red_vals.clear();
     ws_off = 0;
     return nullptr;
+  };
+  // the GEMM of step st: operand addresses (view offsets count elements of
+  // the buffer read: f32, or bf16 for bf16 operands and bf16 shadows)
+  auto gemm_args = [&](const Step& st) {
+    const GemmDesc& g = st.gemm;
+    GemmArgs a;
+    auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
+      const int64_t es = g.bf16 ? 2 : 4;
+      if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset + w.offset * es);
+      const char* base = rnd ? (const char*)rounded[w.value] : (const char*)ptr[w.value];
+      return (const float*)(base + w.offset * es);
+    };
+    a.a = operand(g.a, g.a_rounded, g.a_shadow);
+    a.b = operand(g.b, g.b_rounded, g.b_shadow);
+    a.bf16 = g.bf16 ? 1 : 0;
+    a.c = (float*)ptr[st.root];
+    a.round_out = g.round_out ? 1 : 0;
+    a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
+    a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
+    a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
+    a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
+    if (g.epi) {
+      a.epi = g.epi;
+      a.c2 = (float*)ptr[st.extra_roots[0]];
+      a.round_out2 = g.round_out2 ? 1 : 0;
+    }
+    return a;
   };
   std::vector<const void*> args;
   for (size_t si = 0; si < plan.steps.size(); ++si) {
@@ -554,29 +596,51 @@ sb_status* enqueue_steps(sb_session* s, LoadedFunction* lf, std::vector<void*>& 
       continue;
     }
     if (st.kind == StepKind::Gemm) {
-      const GemmDesc& g = st.gemm;
-      GemmArgs a;
-      // operand address: view offsets count elements of the buffer read (f32,
-      // or bf16 for bf16 operands and bf16 shadows)
-      auto operand = [&](const View& w, bool rnd, int shadow) -> const float* {
-        const int64_t es = g.bf16 ? 2 : 4;
-        if (shadow >= 0) return (const float*)((char*)lf->arena + plan.shadows[shadow].offset + w.offset * es);
-        const char* base = rnd ? (const char*)rounded[w.value] : (const char*)ptr[w.value];
-        return (const float*)(base + w.offset * es);
-      };
-      a.a = operand(g.a, g.a_rounded, g.a_shadow);
-      a.b = operand(g.b, g.b_rounded, g.b_shadow);
-      a.bf16 = g.bf16 ? 1 : 0;
-      a.c = (float*)ptr[st.root];
-      a.round_out = g.round_out ? 1 : 0;
-      a.batch = g.batch; a.M = g.M; a.N = g.N; a.K = g.K;
-      a.sab = g.sab; a.sam = g.sam; a.sak = g.sak;
-      a.sbb = g.sbb; a.sbk = g.sbk; a.sbn = g.sbn;
-      a.scb = g.M * g.N; a.scm = g.N; a.scn = 1;
-      if (g.epi) {
-        a.epi = g.epi;
-        a.c2 = (float*)ptr[st.extra_roots[0]];
-        a.round_out2 = g.round_out2 ? 1 : 0;
+      GemmArgs a = gemm_args(st);
+      // the next step, a GEMM that does not read this one's result, shares the
+      // launch (a layer's dX and dW in a backward pass)
+      if (defer && gemm_pairs_enabled() && si + 1 < plan.steps.size() && plan.steps[si + 1].kind == StepKind::Gemm &&
+          !st.gemm.epi && !plan.steps[si + 1].gemm.epi) {
+        const Step& nx = plan.steps[si + 1];
+        const bool indep = std::find(nx.leaves.begin(), nx.leaves.end(), st.root) == nx.leaves.end();
+        GemmArgs ab[2] = {a, gemm_args(nx)};
+        const size_t n0 = (gemm_workspace(ab[0], s->opts.precision) + 255) & ~(size_t)255;
+        const size_t n1 = (gemm_workspace(ab[1], s->opts.precision) + 255) & ~(size_t)255;
+        if (indep && !(capturing && n0 + n1 > lf->ws_cap)) {
+          bool reads = false;
+          for (int l : nx.leaves) reads |= std::find(red_vals.begin(), red_vals.end(), l) != red_vals.end();
+          if (reads || red.count + 2 > kReduceSegments || ws_off + n0 + n1 > lf->ws_cap) {
+            if (sb_status* e = flush_red()) return e;
+            if (reads) ws_run = 0;
+          }
+          if (n0 + n1 > lf->ws_cap) {
+            if (lf->ws) cudaFreeAsync(lf->ws, stream);
+            if (cudaMallocAsync(&lf->ws, n0 + n1, stream) != cudaSuccess) { lf->ws = nullptr; lf->ws_cap = 0; }
+            else lf->ws_cap = n0 + n1;
+          }
+          SplitReduce d2[2];
+          cudaError_t e = gemm_pair(ab, s->opts.precision, lf->ws ? (char*)lf->ws + ws_off : nullptr,
+                                    lf->ws ? lf->ws_cap - ws_off : 0, stream, d2);
+          if (e == cudaSuccess) {
+            s->used_tc = true;
+            const int roots[2] = {st.root, nx.root};
+            for (int q = 0; q < 2; ++q)
+              if (d2[q].splits > 0) {
+                red.seg[red.count++] = d2[q];
+                red_vals.push_back(roots[q]);
+              }
+            ws_off += n0 + n1;
+            ws_run += n0 + n1;
+            lf->ws_want = std::max(lf->ws_want, ws_run);
+            if (red.count == kReduceSegments)
+              if (sb_status* e2 = flush_red()) return e2;
+            ++si;  // the next step ran in this launch; its collectives are due now
+            if (before)
+              if (sb_status* e2 = before(si, flush_red)) return e2;
+            continue;
+          }
+          if (e != cudaErrorNotSupported) return cuda_status(e, "gemm pair");
+        }
       }
       const size_t need = (gemm_workspace(a, s->opts.precision) + 255) & ~(size_t)255;
       if (ws_off + need > lf->ws_cap)
