@@ -109,10 +109,14 @@ struct GemmProblem {
 // Every problem has the same store path (all TMA stores or none), so a warp's
 // staging buffers are never written by plain stores while a TMA store of the
 // other problem still reads them.
+// NP = 1 for a single product: the kernel then indexes a constant problem
+// (parameters read as directly as scalar kernel arguments) and takes a
+// parameter block of one problem.
+template <int NP>
 struct GemmGroup {
-  GemmProblem p[kGemmGroupMax];
+  GemmProblem p[NP];
   int count;
-  int start[kGemmGroupMax + 1];  // first tile of problem q; start[count] = all tiles
+  int start[NP + 1];  // first tile of problem q; start[count] = all tiles
 };
 
 // Tile t of a group: problem q, output slice z, tile origin (m0, n0), K steps
@@ -121,10 +125,10 @@ struct GemmGroup {
 struct TileAt {
   int q, z, m0, n0, kt0, kt1, zab;
 };
-template <int BKE>
-__device__ __forceinline__ TileAt locate(const GemmGroup& g, int t, int bn) {
+template <int BKE, int NP>
+__device__ __forceinline__ TileAt locate(const GemmGroup<NP>& g, int t, int bn) {
   TileAt a;
-  a.q = (g.count > 1 && t >= g.start[1]) ? 1 : 0;
+  a.q = (NP > 1 && t >= g.start[NP > 1 ? 1 : 0]) ? 1 : 0;
   const GemmProblem& P = g.p[a.q];
   P.tl.at(t - g.start[a.q], &a.z, &a.m0, &a.n0, bn);
   const int ktiles = (P.K + BKE - 1) / BKE;
@@ -288,9 +292,9 @@ constexpr uint64_t kMnStep = BF ? (2048 >> 4) : (1024 >> 4);
 // TMEM allocations are powers of two of at least 32 columns.
 __host__ __device__ constexpr uint32_t tmem_cols(int n) { return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u; }
 
-template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC, int NP>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tcgen05_kernel(const __grid_constant__ GemmGroup grp, int* err) {
+    gemm_tcgen05_kernel(const __grid_constant__ GemmGroup<NP> grp, int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   pdl_prologue();
@@ -314,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   // MN-major tile): 32 f32 or 64 bf16
   constexpr int BKE = BF ? 64 : 32;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
-  const int total = grp.start[grp.count];
+  const int total = grp.start[NP];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -342,30 +346,35 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const TileAt at = locate<BKE>(grp, t, BN);
+        const TileAt at = locate<BKE, NP>(grp, t, BN);
+        // this problem's operand description, read once per tile (not per K step)
         const GemmProblem& P = grp.p[at.q];
+        const CUtensorMap* tA = &P.tmA;
+        const CUtensorMap* tB = &P.tmB;
+        const int a_mn = P.a_mn, b_mn = P.b_mn, a_chunks = P.a_chunks, b_chunks = P.b_chunks;
+        const bool a3d = P.a3d, b3d = P.b3d;
         for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
           mbar_expect_tx(&full[s], (uint32_t)S::STAGE);
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
-          if (!P.a_mn) {
-            tma_ld(a, &P.tmA, &full[s], kt * BKE, at.m0, at.zab, P.a3d);
-          } else if (P.a_chunks) {
-            tma_ld_chunks(a, &P.tmA, &full[s], kt * BKE, at.m0 / BKE, at.zab, P.a3d);
+          if (!a_mn) {
+            tma_ld(a, tA, &full[s], kt * BKE, at.m0, at.zab, a3d);
+          } else if (a_chunks) {
+            tma_ld_chunks(a, tA, &full[s], kt * BKE, at.m0 / BKE, at.zab, a3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / BKE; ++j)
-              tma_ld(a + j * BKE * 128, &P.tmA, &full[s], at.m0 + BKE * j, kt * BKE, at.zab, P.a3d);
+              tma_ld(a + j * BKE * 128, tA, &full[s], at.m0 + BKE * j, kt * BKE, at.zab, a3d);
           }
-          if (!P.b_mn) {
-            tma_ld(b, &P.tmB, &full[s], kt * BKE, at.n0, at.zab, P.b3d);
-          } else if (P.b_chunks) {
-            tma_ld_chunks(b, &P.tmB, &full[s], kt * BKE, at.n0 / BKE, at.zab, P.b3d);
+          if (!b_mn) {
+            tma_ld(b, tB, &full[s], kt * BKE, at.n0, at.zab, b3d);
+          } else if (b_chunks) {
+            tma_ld_chunks(b, tB, &full[s], kt * BKE, at.n0 / BKE, at.zab, b3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / BKE; ++j)
-              tma_ld(b + j * BKE * 128, &P.tmB, &full[s], at.n0 + BKE * j, kt * BKE, at.zab, P.b3d);
+              tma_ld(b + j * BKE * 128, tB, &full[s], at.n0 + BKE * j, kt * BKE, at.zab, b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -377,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++j) {
-        const TileAt at = locate<BKE>(grp, t, BN);
+        const TileAt at = locate<BKE, NP>(grp, t, BN);
         const GemmProblem& P = grp.p[at.q];
         const uint32_t idesc = BF ? idesc_bf16(BM, BN, P.a_mn, P.b_mn) : idesc_tf32(BM, BN, P.a_mn, P.b_mn);
         // descriptors of slot 0, K slice 0 (see the CTA-pair kernel)
@@ -414,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     const int quad = warp & 3;
     int j = 0, sb = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++j) {
-      const TileAt at = locate<BKE>(grp, t, BN);
+      const TileAt at = locate<BKE, NP>(grp, t, BN);
       const GemmProblem& P = grp.p[at.q];
       const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
@@ -452,9 +461,9 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
 // (BN = 256) fewer operand bytes per FLOP than the 128 x 128 single-CTA tile.
 // Completion is signalled to both CTAs with one non-multicast commit each; the
 // peer's epilogue releases an accumulator with a remote mbarrier arrive.
-template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC, int NP>
 __global__ void __launch_bounds__(kThreads, PER_SM)
-    gemm_tcgen05_pair(const __grid_constant__ GemmGroup grp, int* err) {
+    gemm_tcgen05_pair(const __grid_constant__ GemmGroup<NP> grp, int* err) {
   constexpr int BNH = BN / 2;
   using S = Smem<BNH, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -483,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
   // MN-major tile): 32 f32 or 64 bf16
   constexpr int BKE = BF ? 64 : 32;
   constexpr uint32_t TMEM_COLS = tmem_cols(ACC * BN);
-  const int total = grp.start[grp.count];
+  const int total = grp.start[NP];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -522,8 +531,13 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       const uint32_t full_leader = cluster_addr(&full[0], 0);
       bool ok = true;
       for (int t = pair; t < total && ok; t += npairs) {
-        const TileAt at = locate<BKE>(grp, t, BN);
+        const TileAt at = locate<BKE, NP>(grp, t, BN);
+        // this problem's operand description, read once per tile (not per K step)
         const GemmProblem& P = grp.p[at.q];
+        const CUtensorMap* tA = &P.tmA;
+        const CUtensorMap* tB = &P.tmB;
+        const int a_mn = P.a_mn, b_mn = P.b_mn, a_chunks = P.a_chunks, b_chunks = P.b_chunks;
+        const bool a3d = P.a3d, b3d = P.b3d;
         const int ma = at.m0 + (int)rank * BM, nb = at.n0 + (int)rank * BNH;
         for (int kt = at.kt0; kt < at.kt1; ++kt, ++it) {
           if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, abort_flag, err, 1)) { ok = false; break; }
@@ -531,22 +545,22 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
           const uint32_t bar = full_leader + (uint32_t)(s * 8);
           uint8_t* a = sA + s * S::A_BYTES;
           uint8_t* b = sB + s * S::B_BYTES;
-          if (!P.a_mn) {
-            ld(a, &P.tmA, bar, kt * BKE, ma, at.zab, P.a3d);
-          } else if (P.a_chunks) {
-            ld_chunks(a, &P.tmA, bar, kt * BKE, ma / BKE, at.zab, P.a3d);
+          if (!a_mn) {
+            ld(a, tA, bar, kt * BKE, ma, at.zab, a3d);
+          } else if (a_chunks) {
+            ld_chunks(a, tA, bar, kt * BKE, ma / BKE, at.zab, a3d);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / BKE; ++j) ld(a + j * BKE * 128, &P.tmA, bar, ma + BKE * j, kt * BKE, at.zab, P.a3d);
+            for (int j = 0; j < BM / BKE; ++j) ld(a + j * BKE * 128, tA, bar, ma + BKE * j, kt * BKE, at.zab, a3d);
           }
-          if (!P.b_mn) {
-            ld(b, &P.tmB, bar, kt * BKE, nb, at.zab, P.b3d);
-          } else if (P.b_chunks) {
-            ld_chunks(b, &P.tmB, bar, kt * BKE, nb / BKE, at.zab, P.b3d);
+          if (!b_mn) {
+            ld(b, tB, bar, kt * BKE, nb, at.zab, b3d);
+          } else if (b_chunks) {
+            ld_chunks(b, tB, bar, kt * BKE, nb / BKE, at.zab, b3d);
           } else {
 #pragma unroll
             for (int j = 0; j < BNH / BKE; ++j)
-              ld(b + j * BKE * 128, &P.tmB, bar, nb + BKE * j, kt * BKE, at.zab, P.b3d);
+              ld(b + j * BKE * 128, tB, bar, nb + BKE * j, kt * BKE, at.zab, b3d);
           }
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
@@ -559,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = pair; t < total && ok; t += npairs, ++j) {
-        const TileAt at = locate<BKE>(grp, t, BN);
+        const TileAt at = locate<BKE, NP>(grp, t, BN);
         const GemmProblem& P = grp.p[at.q];
         const uint32_t idesc = BF ? idesc_bf16(2 * BM, BN, P.a_mn, P.b_mn) : idesc_tf32(2 * BM, BN, P.a_mn, P.b_mn);
         // descriptors of slot 0, K slice 0; a slot adds its byte offset and a
@@ -596,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, PER_SM)
     const int quad = warp & 3;
     int j = 0, sb = 0;
     for (int t = pair; t < total; t += npairs, ++j) {
-      const TileAt at = locate<BKE>(grp, t, BN);
+      const TileAt at = locate<BKE, NP>(grp, t, BN);
       const GemmProblem& P = grp.p[at.q];
       const int b = ACC == 2 ? (j & 1) : 0, use = ACC == 2 ? (j >> 1) : j;
       if (!mbar_wait(&acc_full[b], (uint32_t)use & 1u, abort_flag, err, 3)) break;
@@ -761,9 +775,10 @@ bool fill_problem(const GemmArgs& g, bool a_mn, bool b_mn, int bn_cta, int bm_ti
 // The launch description of problems gs[0..n): their tile ranges one after
 // the other, one store path for all (TMA stores only when every problem has
 // its store maps).
-template <bool BF>
+template <bool BF, int NP>
 bool make_group(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int bn_cta, int bm_tile, int bn_tile,
-                GemmGroup* G) {
+                GemmGroup<NP>* G) {
+  if (n != NP) return false;
   G->count = n;
   G->start[0] = 0;
   bool all_tma = true;
@@ -779,16 +794,16 @@ bool make_group(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, i
   return true;
 }
 
-template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC, int NP>
 cudaError_t launch(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int* err, cudaStream_t stream) {
   constexpr int BKE = BF ? 64 : 32;
   // an MN-major tile is loaded in whole 128-byte-wide chunks
   for (int q = 0; q < n; ++q)
     if (BF && b_mn[q] && BN % BKE) return cudaErrorNotSupported;
-  GemmGroup G{};
-  if (!make_group<BF>(gs, a_mn, b_mn, n, BN, BM, BN, &G)) return cudaErrorNotSupported;
+  GemmGroup<NP> G{};
+  if (!make_group<BF, NP>(gs, a_mn, b_mn, n, BN, BM, BN, &G)) return cudaErrorNotSupported;
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC>;
+  auto kern = gemm_tcgen05_kernel<BF, BN, STAGES, PER_SM, ACC, NP>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -800,7 +815,7 @@ cudaError_t launch(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n
   return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), S::BYTES, stream, G, err);
 }
 
-template <bool BF, int BN, int STAGES, int PER_SM, int ACC>
+template <bool BF, int BN, int STAGES, int PER_SM, int ACC, int NP>
 cudaError_t launch_pair(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int n, int* err,
                         cudaStream_t stream) {
   constexpr int BNH = BN / 2;
@@ -808,10 +823,10 @@ cudaError_t launch_pair(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, 
   // each CTA loads BN / 2 columns of B: whole 128-byte chunks when MN-major
   for (int q = 0; q < n; ++q)
     if (b_mn[q] && BNH % BKE) return cudaErrorNotSupported;
-  GemmGroup G{};
-  if (!make_group<BF>(gs, a_mn, b_mn, n, BNH, 2 * BM, BN, &G)) return cudaErrorNotSupported;
+  GemmGroup<NP> G{};
+  if (!make_group<BF, NP>(gs, a_mn, b_mn, n, BNH, 2 * BM, BN, &G)) return cudaErrorNotSupported;
   using S = Smem<BNH, STAGES>;
-  auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC>;
+  auto kern = gemm_tcgen05_pair<BF, BN, STAGES, PER_SM, ACC, NP>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -1026,6 +1041,25 @@ bool tc_plan(const GemmArgs& g, TcPlan* p) {
   return p->cfg >= 0;
 }
 
+namespace {
+
+// Configuration cfg (the kCfgs table) with NP products per launch.
+template <bool BF, int NP>
+cudaError_t launch_cfg(const GemmArgs* gs, const bool* a_mn, const bool* b_mn, int cfg, int* err,
+                       cudaStream_t stream) {
+  switch (cfg) {
+    case 0: return launch<BF, 64, 4, 2, 2, NP>(gs, a_mn, b_mn, NP, err, stream);
+    case 1: return launch<BF, 128, 3, 2, 2, NP>(gs, a_mn, b_mn, NP, err, stream);
+    case 2: return launch_pair<BF, 128, 4, 2, 2, NP>(gs, a_mn, b_mn, NP, err, stream);
+    case 3: return launch_pair<BF, 192, 3, 2, 1, NP>(gs, a_mn, b_mn, NP, err, stream);
+    case 4: return launch_pair<BF, 256, 3, 2, 1, NP>(gs, a_mn, b_mn, NP, err, stream);
+    case 5: return launch_pair<BF, 256, 6, 1, 2, NP>(gs, a_mn, b_mn, NP, err, stream);
+  }
+  return cudaErrorNotSupported;
+}
+
+}  // namespace
+
 cudaError_t gemm_tcgen05_group(const GemmArgs* gs, int n, int cfg, cudaStream_t stream) {
   if (n < 1 || n > kGemmGroupMax) return cudaErrorInvalidValue;
   bool a_mn[kGemmGroupMax], b_mn[kGemmGroupMax];
@@ -1033,26 +1067,11 @@ cudaError_t gemm_tcgen05_group(const GemmArgs* gs, int n, int cfg, cudaStream_t 
     if (!tc_layout(gs[q], &a_mn[q], &b_mn[q]) || gs[q].bf16 != gs[0].bf16) return cudaErrorNotSupported;
   int* err = error_word();
   if (!err) return cudaErrorNotSupported;
-  if (gs[0].bf16) {
-    switch (cfg) {
-      case 0: return launch<true, 64, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-      case 1: return launch<true, 128, 3, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-      case 2: return launch_pair<true, 128, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-      case 3: return launch_pair<true, 192, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
-      case 4: return launch_pair<true, 256, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
-      case 5: return launch_pair<true, 256, 6, 1, 2>(gs, a_mn, b_mn, n, err, stream);
-    }
-    return cudaErrorNotSupported;
-  }
-  switch (cfg) {
-    case 0: return launch<false, 64, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-    case 1: return launch<false, 128, 3, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-    case 2: return launch_pair<false, 128, 4, 2, 2>(gs, a_mn, b_mn, n, err, stream);
-    case 3: return launch_pair<false, 192, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
-    case 4: return launch_pair<false, 256, 3, 2, 1>(gs, a_mn, b_mn, n, err, stream);
-    case 5: return launch_pair<false, 256, 6, 1, 2>(gs, a_mn, b_mn, n, err, stream);
-  }
-  return cudaErrorNotSupported;
+  if (gs[0].bf16)
+    return n == 1 ? launch_cfg<true, 1>(gs, a_mn, b_mn, cfg, err, stream)
+                  : launch_cfg<true, 2>(gs, a_mn, b_mn, cfg, err, stream);
+  return n == 1 ? launch_cfg<false, 1>(gs, a_mn, b_mn, cfg, err, stream)
+                : launch_cfg<false, 2>(gs, a_mn, b_mn, cfg, err, stream);
 }
 
 cudaError_t gemm_tcgen05(const GemmArgs& g, int cfg, cudaStream_t stream) { return gemm_tcgen05_group(&g, 1, cfg, stream); }
