@@ -7,7 +7,9 @@
 //
 // Persistent: PER_SM CTAs per SM walk the 128 x BN output tiles t = blockIdx.x,
 // blockIdx.x + gridDim.x, ... (grouped order, see Tiles, so CTAs that run
-// together share A and B tiles in L2).  192 threads, warp-specialized:
+// together share A and B tiles in L2).  A launch computes one product or two
+// independent ones (GemmGroup: the tiles of the first, then those of the
+// second, in the same sequence).  192 threads, warp-specialized:
 //   warp 0      TMA producer (one lane): 128B-swizzled K slices of A and B into
 //               a STAGES-deep shared-memory ring that runs across tiles,
 //               completion via mbarrier transaction bytes;
