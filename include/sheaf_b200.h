@@ -243,10 +243,12 @@ SB_API sb_status* sb_nccl_get_unique_id(uint8_t out_id[128]);
 SB_API sb_status* sb_module_inspect(const char* text, size_t length, int32_t precision,
                                     char* report, size_t report_capacity);
 /* CSV of the execution plan of one function, one row per step:
- * step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi,deferred_sums
+ * step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi,deferred_sums,root_offset
  * (epi: 1 when a GEMM step also writes gelu of its result, fused into its
  * epilogue; deferred_sums: column sums of a row group that the runtime may
- * finish later, batched with other steps') */
+ * finish later, batched with other steps'; root_offset: byte offset of the
+ * step's result in the call's work arena, -1 for a returned value, which has
+ * a buffer of its own) */
 SB_API sb_status* sb_module_plan_steps(const char* text, size_t length, const char* function, int32_t precision,
                                        char* out, size_t capacity, size_t* out_length);
 /* Writes the generated CUDA source of one function (for diagnostics). */

@@ -354,10 +354,50 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
   return gelu_tanh(g.c, g.c2, g.batch * g.M * g.N, g.round_out2, stream);
 }
 
+namespace {
+
+// Bytes [lo, hi) that a strided rows x cols (x batch) array of es-byte
+// elements spans; ok = false for a negative stride (no span is claimed).
+struct Span {
+  uintptr_t lo = 0, hi = 0;
+  bool ok = true;
+};
+
+Span span_of(const void* p, int64_t batch, int64_t sb, int64_t rows, int64_t sr, int64_t cols, int64_t sc,
+             int64_t es) {
+  Span r;
+  if ((batch > 1 && sb < 0) || (rows > 1 && sr < 0) || (cols > 1 && sc < 0)) {
+    r.ok = false;
+    return r;
+  }
+  const int64_t last = (batch - 1) * sb + (rows - 1) * sr + (cols - 1) * sc;
+  r.lo = (uintptr_t)p;
+  r.hi = r.lo + (uintptr_t)((last + 1) * es);
+  return r;
+}
+
+bool apart(const Span& x, const Span& y) { return x.ok && y.ok && (x.hi <= y.lo || y.hi <= x.lo); }
+
+// The products of a pair run at the same time, so neither may write memory
+// that the other reads or writes.  A plan frees a value's memory after its
+// last reader, so the second product's output may have been placed where the
+// first product's operand was, which is safe only one step after the other.
+bool independent(const GemmArgs& w, const GemmArgs& r) {
+  const int64_t es = r.bf16 ? 2 : 4;
+  const Span out = span_of(w.c, w.batch, w.scb, w.M, w.scm, w.N, w.scn, 4);
+  const Span ra = span_of(r.a, r.batch, r.sab, r.M, r.sam, r.K, r.sak, es);
+  const Span rb = span_of(r.b, r.batch, r.sbb, r.K, r.sbk, r.N, r.sbn, es);
+  const Span rc = span_of(r.c, r.batch, r.scb, r.M, r.scm, r.N, r.scn, 4);
+  return apart(out, ra) && apart(out, rb) && apart(out, rc);
+}
+
+}  // namespace
+
 cudaError_t gemm_pair(const GemmArgs g[2], int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
                       SplitReduce deferred[2]) {
   deferred[0] = SplitReduce{};
   deferred[1] = SplitReduce{};
+  if (!independent(g[0], g[1]) || !independent(g[1], g[0])) return cudaErrorNotSupported;
   GemmArgs run[2];
   TcPlan plan[2];
   size_t off = 0;

@@ -98,8 +98,9 @@ cudaError_t gemm(const GemmArgs& g, int precision, void* ws, size_t ws_bytes, cu
 // gemm_workspace(g[0]) bytes, rounded up to 256, then g[1]'s) and describes
 // their reduction in deferred[q]; both products' results are as gemm() gives
 // them.  cudaErrorNotSupported (nothing launched) when either product needs
-// another path: CUDA cores, padded operands, a fused epilogue, or operands of
-// different types; the caller then runs them one by one.
+// another path (CUDA cores, padded operands, a fused epilogue, operands of
+// different types) or when either writes memory that the other reads or
+// writes (the two run at the same time); the caller then runs them one by one.
 constexpr int kGemmGroupMax = 2;
 cudaError_t gemm_pair(const GemmArgs g[2], int precision, void* ws, size_t ws_bytes, cudaStream_t stream,
                       SplitReduce deferred[2]);

@@ -1791,7 +1791,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
   }
   std::ostringstream os;
   os.precision(17);
-  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi,deferred_sums\n";
+  os << "step,kind,kernel,elements,bytes,flops,batch,M,N,K,sab,sam,sak,sbb,sbk,sbn,epi,deferred_sums,root_offset\n";
   static const char* kinds[] = {"loop", "reduce", "gemm", "attention", "sort", "convert", "scatter"};
   for (size_t i = 0; i < p.steps.size(); ++i) {
     const Step& st = p.steps[i];
@@ -1799,7 +1799,8 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
     os << i << "," << kinds[(int)st.kind] << "," << step_name(st) << ","
        << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
        << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
-       << g.sbn << "," << g.epi << "," << (st.finish_deferred ? st.col_finish.size() : 0) << "\n";
+       << g.sbn << "," << g.epi << "," << (st.finish_deferred ? st.col_finish.size() : 0) << ","
+       << p.value_offset[st.root] << "\n";
   }
   std::string r = os.str();
   if (out_len) *out_len = r.size();

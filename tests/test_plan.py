@@ -92,3 +92,25 @@ def test_layer_norm_weight_gradient_sums_are_finished_in_one_batch():
     low = M.gpt_vag(M.NANOGPT, batch=8)
     rows = S.plan_steps(low.text, low.qualified, "tf32")
     assert sum(r["deferred_sums"] for r in rows) == 2 * M.NANOGPT.n_layer + 1
+
+
+def test_second_gemm_may_take_first_gemms_operand_memory():
+    """A value's arena memory is free after its last reader, so a GEMM's result
+    may be placed where the previous GEMM's operand was (here dX = G @ W takes
+    the memory of X*X, read last by dW = G^T @ (X*X)).  That is why the runtime
+    launches two GEMM steps together only when neither writes memory that the
+    other reads (they run at the same time)."""
+    T, I, O = 2048, 384, 1152
+    g, w, x = f"tensor<{T}x{O}xf32>", f"tensor<{O}x{I}xf32>", f"tensor<{T}x{I}xf32>"
+    dw, gt = f"tensor<{O}x{I}xf32>", f"tensor<{O}x{T}xf32>"
+    text = (f"module @reuse {{\n func.func @f(%arg0: {g}, %arg1: {w}, %arg2: {x}) -> ({dw}, {x}) {{\n"
+            f"    %t = stablehlo.multiply %arg2, %arg2 : {x}\n"
+            f"    %gt = stablehlo.transpose %arg0, dims = [1, 0] : ({g}) -> {gt}\n"
+            f"    %dw = stablehlo.dot_general %gt, %t, contracting_dims = [1] x [0] : ({gt}, {x}) -> {dw}\n"
+            f"    %dx = stablehlo.dot_general %arg0, %arg1, contracting_dims = [1] x [0] : ({g}, {w}) -> {x}\n"
+            f"    %y = stablehlo.add %dx, %dx : {x}\n"
+            f"    return %dw, %y : {dw}, {x}\n }}\n}}\n")
+    rows = S.plan_steps(text, "reuse.f", "tf32")
+    assert [r["kind"] for r in rows] == ["loop", "gemm", "gemm", "loop"]
+    assert rows[1]["root_offset"] == -1  # dW is returned: a buffer of its own
+    assert rows[2]["root_offset"] == rows[0]["root_offset"] >= 0
