@@ -247,8 +247,8 @@ SB_API sb_status* sb_module_inspect(const char* text, size_t length, int32_t pre
  * (epi: 1 when a GEMM step also writes gelu of its result, fused into its
  * epilogue; deferred_sums: column sums of a row group that the runtime may
  * finish later, batched with other steps'; root_offset: byte offset of the
- * step's result in the call's work arena, -1 for a returned value, which has
- * a buffer of its own) */
+ * step's result (of the copy, for an operand conversion) in the call's work
+ * arena, -1 for a returned value, which has a buffer of its own) */
 SB_API sb_status* sb_module_plan_steps(const char* text, size_t length, const char* function, int32_t precision,
                                        char* out, size_t capacity, size_t* out_length);
 /* Writes the generated CUDA source of one function (for diagnostics). */

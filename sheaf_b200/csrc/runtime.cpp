@@ -1800,7 +1800,7 @@ sb_status* sb_module_plan_steps(const char* text, size_t len, const char* fn, in
        << st.elements << "," << st.bytes_moved << "," << st.flops << "," << g.batch << "," << g.M << "," << g.N
        << "," << g.K << "," << g.sab << "," << g.sam << "," << g.sak << "," << g.sbb << "," << g.sbk << ","
        << g.sbn << "," << g.epi << "," << (st.finish_deferred ? st.col_finish.size() : 0) << ","
-       << p.value_offset[st.root] << "\n";
+       << (st.kind == StepKind::Convert ? p.shadows[st.shadow].offset : p.value_offset[st.root]) << "\n";
   }
   std::string r = os.str();
   if (out_len) *out_len = r.size();
